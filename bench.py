@@ -1,0 +1,419 @@
+"""MoE-layer throughput of the fused NF4 expert path on B200.
+
+Default workload (N=1): BASELINE config 2, OLMoE-1B-7B geometry bs=1 decode --
+16 MoE layers (E=64, H=2048, I=1024, top-8 softmax router), random-init NF4
+experts (N(0, 0.02) bf16 weights quantized on the device). One step = one
+decode token through all 16 MoE layers (router + fused expert layer each),
+with a fresh synthetic token per layer and step. ``value`` is MoE-layer
+tokens/s (layers x tokens / s: the throughput of one MoE layer, the unit of the
+reference's own per-layer numbers) with inputs resident in HBM, timed over
+CUDA-graph replays; ``e2e`` is the same metric through the public Python API
+(eager calls) with pinned-host -> device copies of every step's inputs and a
+device -> host read of its outputs inside the timed region.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+       [--workload olmoe-decode|qwen3-prefill]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+WORKLOADS = {
+    # name: (E, H, I, k, tokens per layer, layers, router norm)
+    "olmoe-decode": dict(E=64, H=2048, I=1024, k=8, T=1, layers=16, norm=False, lora=0,
+                         desc="OLMoE-1B-7B geometry (config 2): 16 MoE layers, E=64, H=2048, I=1024, top-8, bs=1 decode"),
+    "qwen3-prefill": dict(E=128, H=2048, I=768, k=8, T=4096, layers=4, norm=True, lora=16,
+                          desc="Qwen3-30B-A3B geometry (config 3): E=128, H=2048, I=768, top-8, T=4096, LoRA r=16"),
+}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+# --------------------------------------------------------------------------- #
+# our arm
+# --------------------------------------------------------------------------- #
+def build_layers(pkg, wl, dev, seed=0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    layers = []
+    for _ in range(wl["layers"]):
+        gate_up = (torch.randn(wl["E"], 2 * wl["I"], wl["H"], generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        down = (torch.randn(wl["E"], wl["H"], wl["I"], generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        mod = pkg.Experts4bit.from_float(gate_up, down)
+        del gate_up, down
+        router = (torch.randn(wl["E"], wl["H"], generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        lora = None
+        if wl["lora"]:
+            r = wl["lora"]
+            lm = pkg.ExpertsLoRA(mod, r=r, alpha=16, dtype=torch.bfloat16).to(dev)
+            with torch.no_grad():
+                for p in (lm.gate_up_lora_A, lm.gate_up_lora_B, lm.down_lora_A, lm.down_lora_B):
+                    p.copy_(torch.randn(p.shape, generator=g, device=dev) * 0.01)
+            lora = (lm.gate_up_lora_A.data, lm.gate_up_lora_B.data, lm.down_lora_A.data, lm.down_lora_B.data,
+                    lm.scaling)
+            mod = lm.eval()
+        layers.append((mod, router, lora))
+    torch.cuda.synchronize()
+    return layers
+
+
+def run_ours(args, wl, world, rank, local):
+    import importlib
+    import ctypes
+    pkg = importlib.import_module("experts4bit-qlora_b200")
+    N = pkg._native
+    ops = pkg.ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layers = build_layers(pkg, wl, dev, seed=rank)
+    Lc, T, H = wl["layers"], wl["T"], wl["H"]
+    pool = 8
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    X = torch.randn(pool, Lc, T, H, generator=g, device=dev).to(torch.bfloat16)
+    outs = torch.empty(Lc, T, H, dtype=torch.bfloat16, device=dev)
+    base = lambda m: m.base if hasattr(m, "base") else m  # noqa: E731
+    ws = N.workspaces.get(dev, max(ops.moe_workspace_bytes(wl["E"], H, wl["I"], wl["k"], T, lora_rank=wl["lora"]),
+                                   1 << 20), "bench")
+    rws = N.workspaces.get(dev, N.lib().e4b_router_workspace_bytes(T, wl["E"]), "bench_router")
+    topw = torch.empty(Lc, T, wl["k"], dtype=torch.float32, device=dev)
+    topi = torch.empty(Lc, T, wl["k"], dtype=torch.int64, device=dev)
+    L = N.lib()
+    nstage = N.MOE_STAGE_EVENTS
+
+    def layer_call(li, x, events=None):
+        mod, router, lora = layers[li]
+        b = base(mod)
+        N.check(L.e4b_router_topk(x.data_ptr(), N.BF16, router.data_ptr(), N.BF16, T, H, wl["E"], wl["k"],
+                                  N.SOFTMAX_THEN_TOPK, int(wl["norm"]), None, topi[li].data_ptr(), topw[li].data_ptr(),
+                                  rws.data_ptr(), rws.numel(), torch.cuda.current_stream().cuda_stream), "router")
+        d = ops.MoeDesc_from(wl["E"], H, wl["I"], wl["k"], T, True, torch.bfloat16, torch.float32, torch.bfloat16,
+                             lora)
+        t = N.MoeTensors()
+        t.hidden, t.topk_idx, t.topk_w = x.data_ptr(), topi[li].data_ptr(), topw[li].data_ptr()
+        t.gate_up_packed, t.gate_up_absmax = b.gate_up_proj.data_ptr(), b.gate_up_absmax.data_ptr()
+        t.down_packed, t.down_absmax = b.down_proj.data_ptr(), b.down_absmax.data_ptr()
+        if lora is not None:
+            t.gate_up_lora_A, t.gate_up_lora_B, t.down_lora_A, t.down_lora_B = (m.data_ptr() for m in lora[:4])
+        t.out = outs[li].data_ptr()
+        if events is not None:
+            arr = (ctypes.c_void_p * nstage)(*[e.cuda_event for e in events])
+            t.stage_events = ctypes.cast(arr, ctypes.c_void_p)
+            layer_call._keep = arr
+        N.check(L.e4b_moe_forward(ctypes.byref(d), ctypes.byref(t), ws.data_ptr(), ws.numel(),
+                                  torch.cuda.current_stream().cuda_stream), "moe")
+
+    def step(s, events=None):
+        xs = X[s % pool]
+        for li in range(Lc):
+            layer_call(li, xs[li], events[li] if events is not None else None)
+
+    # --- capture one graph per pool slot (device-resident inputs) ----------------
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for s in range(pool):
+            step(s)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graphs = []
+    for s in range(pool):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step(s)
+        graphs.append(gr)
+    for w in range(max(args.warmup, 3)):
+        graphs[w % pool].replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if world == 1 else local) as clocks:
+        torch.cuda.synchronize()
+        start.record()
+        for s in range(args.steps):
+            graphs[s % pool].replay()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t_ = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t_.item())
+    units = args.steps * T * Lc * world
+    value = units / (ms / 1e3)
+
+    # --- per-stage kernel times, live, from event nodes inside replayed graphs ----
+    ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(nstage)] for _ in range(Lc)]
+    gt = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gt):
+        step(0, ev)
+    stage_ms = [[] for _ in range(nstage - 1)]
+    for rep in range(max(5, min(args.steps, 20))):
+        gt.replay()
+        torch.cuda.synchronize()
+        for li in range(Lc):
+            for si in range(nstage - 1):
+                stage_ms[si].append(ev[li][si].elapsed_time(ev[li][si + 1]))
+    stage_names = ["permute", "lora_a_x", "gate_up", "lora_a_h", "down", "combine"]
+    stage_avg_us = {n: 1e3 * statistics.mean(v) for n, v in zip(stage_names, stage_ms)}
+
+    # algorithmic bytes of the dominant kernel (gate_up grouped GEMM), per launch
+    E, I, k = wl["E"], wl["I"], wl["k"]
+    n1 = 2 * I
+    per_expert_gu = n1 * H // 2 + n1 * H // 64 * 4
+    per_expert_dn = H * I // 2 + H * I // 64 * 4
+    # unique experts touched per layer (measured from the routing of the timed inputs)
+    uniq = []
+    for s in range(min(pool, 8)):
+        for li in range(Lc):
+            uniq.append(int(torch.unique(_route_idx(pkg, layers[li][1], X[s][li], wl)).numel()))
+    mean_uniq = statistics.mean(uniq)
+    gu_bytes = mean_uniq * per_expert_gu + T * H * 2 + T * k * I * 2
+    dn_bytes = mean_uniq * per_expert_dn + T * k * I * 2 + T * k * H * 2
+    peaks, peak_kind = load_peaks()
+    if wl["T"] <= 16:
+        bound, unit = "hbm", "GB/s"
+        achieved = gu_bytes / (stage_avg_us["gate_up"] * 1e-6) / 1e9
+        peak = peaks["hbm_gbs"]
+    else:
+        bound, unit = "tensor", "TFLOP/s"
+        flops = 2.0 * T * k * H * n1
+        achieved = flops / (stage_avg_us["gate_up"] * 1e-6) / 1e12
+        peak = peaks["bf16_tflops"]
+    roofline = {"bound": bound, "kernel": "nf4 grouped gate_up (SwiGLU fused)", "achieved": round(achieved, 1),
+                "peak": peak, "peak_source": peak_kind, "unit": unit, "frac": round(achieved / peak, 4),
+                "traffic": None, "algorithmic_bytes_per_launch": int(gu_bytes),
+                "kernel_us": round(stage_avg_us["gate_up"], 3),
+                "down_kernel_us": round(stage_avg_us["down"], 3),
+                "down_achieved": round(dn_bytes / (stage_avg_us["down"] * 1e-6) / 1e9, 1) if bound == "hbm" else None,
+                "layer_bytes": int(gu_bytes + dn_bytes + wl["E"] * H * 2),
+                "stage_us": {k_: round(v, 3) for k_, v in stage_avg_us.items()}}
+
+    # --- e2e through the public API: pinned H2D in, eager calls, D2H out ----------
+    e2e = run_e2e(pkg, layers, wl, dev, args, X)
+    if world > 1:
+        t_ = torch.tensor([e2e["ms"]], device=dev)
+        torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
+        e2e["ms"] = float(t_.item())
+    e2e_value = args.steps * T * Lc * world / (e2e["ms"] / 1e3)
+
+    launches_per_layer = 2 + (5 if wl["lora"] else 3) + 1  # router 2; permute, [lora], gate_up, down, combine
+    result = {
+        "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights quantized to NF4; N(0,1) tokens)",
+        "config": {"workload": args.workload, "desc": wl["desc"], "tokens_per_layer": T, "layers_per_step": Lc,
+                   "experts": wl["E"], "hidden": H, "intermediate": I, "top_k": k, "lora_rank": wl["lora"],
+                   "parallelism": "replicas" if world > 1 else "single-gpu",
+                   "l2": "inputs larger than L2: each step touches %.0f MB of expert weights" %
+                         (Lc * (gu_bytes + dn_bytes) / 1e6),
+                   "timing": "CUDA-graph replay of the step, CUDA events, max over ranks"},
+        "model_tokens_per_s": round(value / Lc, 1),
+        "roofline": roofline,
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
+                "d2h_bytes_per_step": e2e["d2h"], "path": "public API (route + enable_fast module call), eager"},
+        "gpu_launches": launches_per_layer * Lc * args.steps,
+        "clocks": clocks.summary(),
+        "unique_experts_per_layer": round(mean_uniq, 2),
+    }
+    if rank == 0:
+        result["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
+    return result
+
+
+def _route_idx(pkg, router, x, wl):
+    w, idx = pkg.route(x, router, wl["k"], norm_topk_prob=wl["norm"])
+    return idx
+
+
+def run_e2e(pkg, layers, wl, dev, args, X):
+    Lc, T, H = wl["layers"], wl["T"], wl["H"]
+    pool = X.shape[0]
+    host_in = torch.empty(pool, Lc, T, H, dtype=torch.bfloat16, pin_memory=True)
+    host_in.copy_(X.cpu())
+    host_out = torch.empty(Lc, T, H, dtype=torch.bfloat16, pin_memory=True)
+    for mod, _, _ in layers:
+        pkg.enable_fast(mod)
+
+    def one(s):
+        xs = host_in[s % pool].to(dev, non_blocking=True)
+        outs = []
+        with torch.no_grad():
+            for li in range(Lc):
+                mod, router, _ = layers[li]
+                w, idx = pkg.route(xs[li], router, wl["k"], norm_topk_prob=wl["norm"])
+                outs.append(mod(xs[li], idx, w))
+        host_out.copy_(torch.stack(outs), non_blocking=True)
+
+    for s in range(max(args.warmup, 3)):
+        one(s)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(args.steps):
+        one(s)
+    b.record()
+    torch.cuda.synchronize()
+    return {"ms": a.elapsed_time(b), "h2d": Lc * T * H * 2, "d2h": Lc * T * H * 2}
+
+
+# --------------------------------------------------------------------------- #
+# CPU baseline: the reference's per-expert loop restated on CPU (oracle port)
+# --------------------------------------------------------------------------- #
+def cpu_baseline(wl, seconds=15.0, threads=None):
+    """Times the reference loop (``ExpertsNbit.forward``, experts4bit_qlora/_vendor/experts.py:468-516,
+    restated in oracle/moe.py) on the host cores, on a bounded sample of the same workload:
+    one layer of the workload's geometry, its T tokens per call, repeated for ~``seconds``."""
+    from oracle import moe as M
+    from oracle.nf4 import quantize_stack
+
+    ncores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads or ncores)
+    g = torch.Generator().manual_seed(0)
+    E, H, I, k = wl["E"], wl["H"], wl["I"], wl["k"]
+    T = min(wl["T"], 128)
+    # quantize a handful of distinct experts and reuse them (quantization is not timed)
+    ne = min(E, 8)
+    gp, ga = quantize_stack((torch.randn(ne, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16))
+    dp, da = quantize_stack((torch.randn(ne, H, I, generator=g) * 0.02).to(torch.bfloat16))
+    rep = (E + ne - 1) // ne
+    st = {"gate_up_packed": gp.repeat(rep, 1)[:E], "gate_up_absmax": ga.repeat(rep, 1)[:E],
+          "down_packed": dp.repeat(rep, 1)[:E], "down_absmax": da.repeat(rep, 1)[:E],
+          "E": E, "H": H, "I": I, "has_gate": True}
+    router = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    n_tok = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        w, idx = M.route_on_host(M.router_logits_f32(x, router), k, M.SOFTMAX_THEN_TOPK, wl["norm"])
+        M.reference_forward(st, x, idx, w, torch.bfloat16)
+        n_tok += T
+    dt = time.perf_counter() - t0
+    return {"value": round(n_tok / dt, 2), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"reference per-expert loop (oracle port, torch CPU) on one {E}-expert layer, {T} token(s) "
+                      f"per call, {n_tok} tokens in {dt:.1f} s"}
+
+
+def run_reference(args, wl, rank):
+    if rank != 0:
+        return None
+    cb = cpu_baseline(wl, seconds=max(5.0, min(60.0, 2.0 * args.steps)))
+    return {"metric": "MoE-layer tokens/s", "value": cb["value"], "unit": "tokens/s", "impl": "reference",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": args.workload, "desc": wl["desc"]},
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="olmoe-decode", choices=sorted(WORKLOADS))
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        res = run_reference(args, wl, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    res = run_ours(args, wl, world, rank, local)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

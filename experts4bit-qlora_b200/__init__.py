@@ -1,0 +1,28 @@
+"""experts4bit-b200: the fused-expert forward of experts4bit-qlora, B200-native.
+
+Drop-in names (same constructors, state_dict layout and patch semantics as the
+reference's ``experts4bit_qlora`` package): ``ExpertsNbit``, ``Experts4bit``,
+``ExpertsLoRA``, ``enable_fast``, ``disable_fast``, ``fast_available``,
+``normalize_quant_type``. The hot path is libe4b.so (hand-written sm_100a CUDA
+behind the C ABI in include/e4b.h), reached through ctypes.
+
+The package directory is named ``experts4bit-qlora_b200``; import it with
+``importlib.import_module("experts4bit-qlora_b200")``. After that first import
+it is also registered as ``experts4bit_qlora_b200``.
+"""
+import sys as _sys
+
+from . import _native, ops  # noqa: F401
+from .experts import Experts4bit, ExpertsNbit, normalize_quant_type
+from .fast import disable_fast, enable_fast, fast_available
+from .lora import ExpertsLoRA
+from .router import route, TopKRouter
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "Experts4bit", "ExpertsNbit", "ExpertsLoRA", "enable_fast", "disable_fast", "fast_available",
+    "normalize_quant_type", "route", "TopKRouter", "ops",
+]
+
+_sys.modules.setdefault("experts4bit_qlora_b200", _sys.modules[__name__])

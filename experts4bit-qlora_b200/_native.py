@@ -1,0 +1,178 @@
+"""ctypes binding of libe4b.so (the C ABI declared in include/e4b.h).
+
+The fused path has no CPU fallback: if the library is missing, every call
+raises ``NativeLibraryError``. torch is used only for device memory and the
+current CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libe4b.so")
+
+E4B_OK = 0
+E4B_ERR_EXPERT_INDEX = 6
+BF16, F16, F32 = 0, 1, 2
+SOFTMAX_THEN_TOPK, TOPK_THEN_SOFTMAX = 0, 1
+EPI_NONE, EPI_SWIGLU, EPI_SILU = 0, 1, 2
+
+# Every symbol include/e4b.h exports, in declaration order.
+EXPORTED_SYMBOLS = (
+    "e4b_status_string", "e4b_abi_version",
+    "e4b_nf4_quantize", "e4b_nf4_dequantize", "e4b_nf4_quantize_host", "e4b_nf4_dequantize_host",
+    "e4b_router_workspace_bytes", "e4b_router_topk",
+    "e4b_permute_workspace_bytes", "e4b_permute",
+    "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
+    "e4b_combine",
+    "e4b_moe_workspace_bytes", "e4b_moe_forward",
+    "e4b_read_device_error",
+)
+
+
+class NativeLibraryError(RuntimeError):
+    """libe4b.so is missing or failed to load: the fused path cannot run."""
+
+
+class E4BError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {status_string(status)} (status {status})")
+
+
+class MoeDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "num_experts", "hidden", "intermediate", "top_k", "tokens", "has_gate", "act_dtype",
+        "weight_dtype", "out_dtype", "lora_rank", "lora_dtype")] + [("lora_scaling", ctypes.c_float)]
+
+
+class MoeTensors(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "hidden", "topk_idx", "topk_w", "gate_up_packed", "gate_up_absmax", "down_packed", "down_absmax",
+        "gate_up_lora_A", "gate_up_lora_B", "down_lora_A", "down_lora_B", "out", "stage_events")]
+
+MOE_STAGE_EVENTS = 7
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def _declare(lib):
+    P, I, SZ, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_int64, ctypes.c_float
+    sig = {
+        "e4b_status_string": (ctypes.c_char_p, [I]),
+        "e4b_abi_version": (I, []),
+        "e4b_nf4_quantize": (I, [P, I, I64, P, P, P]),
+        "e4b_nf4_dequantize": (I, [P, P, I64, P, I, P]),
+        "e4b_nf4_quantize_host": (I, [P, I, I64, P, P]),
+        "e4b_nf4_dequantize_host": (I, [P, P, I64, P, I]),
+        "e4b_router_workspace_bytes": (SZ, [I, I]),
+        "e4b_router_topk": (I, [P, I, P, I, I, I, I, I, I, I, P, P, P, P, SZ, P]),
+        "e4b_permute_workspace_bytes": (SZ, [I, I, I]),
+        "e4b_permute": (I, [P, I, I, I, P, P, P, P, SZ, P]),
+        "e4b_grouped_gemm_workspace_bytes": (SZ, [I, I, I, I]),
+        "e4b_grouped_nf4_gemm": (I, [P, I, P, P, P, P, I, I, I, I, I, P, P, SZ, P]),
+        "e4b_combine": (I, [P, I, P, P, I, I, I, I, P, I, P]),
+        "e4b_moe_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
+        "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
+        "e4b_read_device_error": (I, [P, P, ctypes.POINTER(I)]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    del F
+
+
+def lib():
+    """The loaded library; raises NativeLibraryError when it is not built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise NativeLibraryError(
+                        f"{LIB_PATH} is not built; run `python -c 'import __graft_entry__ as g; g.build()'` "
+                        "(or experts4bit-qlora_b200/build.py). There is no CPU fallback for the fused path.")
+                try:
+                    l = ctypes.CDLL(LIB_PATH)
+                except OSError as e:
+                    raise NativeLibraryError(f"failed to load {LIB_PATH}: {e}") from e
+                _declare(l)
+                if l.e4b_abi_version() != 1:
+                    raise NativeLibraryError("libe4b.so ABI version mismatch; rebuild it")
+                _lib = l
+    return _lib
+
+
+def available() -> bool:
+    try:
+        lib()
+        return True
+    except NativeLibraryError:
+        return False
+
+
+def status_string(status: int) -> str:
+    try:
+        return lib().e4b_status_string(int(status)).decode()
+    except NativeLibraryError:
+        return "native library unavailable"
+
+
+def check(status: int, what: str) -> None:
+    if status != E4B_OK:
+        raise E4BError(status, what)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return BF16
+    if dt == torch.float16:
+        return F16
+    if dt == torch.float32:
+        return F32
+    raise TypeError(f"unsupported dtype {dt}")
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _Workspaces:
+    """One grow-only workspace per (device, purpose), owned by torch's allocator.
+
+    Reusing a buffer keeps its address stable across calls, which CUDA-graph
+    replay needs. Calls on one device that share a purpose must be
+    stream-ordered (the library is stream-ordered; this cache is not a pool).
+    """
+
+    def __init__(self):
+        self._bufs: dict[tuple[int, str], torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int, purpose: str = "moe") -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), purpose)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            self._bufs[key] = buf
+        return buf
+
+
+workspaces = _Workspaces()
+
+
+def read_device_error(ws: torch.Tensor) -> int:
+    out = ctypes.c_int(0)
+    check(lib().e4b_read_device_error(ws.data_ptr(), stream_handle(ws.device), ctypes.byref(out)),
+          "e4b_read_device_error")
+    return out.value

@@ -1,0 +1,32 @@
+// Internal launch interface of the grouped NF4 GEMV (decode regime).
+#pragma once
+#include "common.cuh"
+
+namespace e4b {
+
+struct GemvArgs {
+  const void* a;             // activations, rows of K elements (act dtype)
+  const int32_t* a_rows;     // nullable: sorted row r reads a[a_rows[r]]
+  const uint8_t* packed;     // [E, N, K/2]
+  const float* absmax;       // [E, N, K/64]
+  const int32_t* offsets;    // [E+1] sorted-row start of each expert
+  const int32_t* active;     // [E] active expert ids (ascending)
+  const int32_t* num_active; // [1]
+  int E, N, K;
+  int epilogue;              // e4b_epilogue
+  void* out;                 // [R, Nout] act dtype
+  int Nout;
+  const float* lora_xa;      // [R, rank] = scaling * (a_row . A^T), fp32 (nullable)
+  const void* lora_B;        // [E, N, rank] (lora_dtype)
+  int lora_dtype, rank;
+  int tiles_per_expert;      // MMA row tiles per expert
+  int max_tasks;             // upper bound on tasks (max active experts x tiles)
+  int* err;
+};
+
+// Tokens per expert handled without re-reading the weights.
+constexpr int kGemvMaxCols = 16;
+
+e4b_status launch_gemv(const GemvArgs& g, int act_dtype, int max_rows_per_expert, cudaStream_t s);
+
+}  // namespace e4b

@@ -1,0 +1,23 @@
+// Internal launch interface of the LoRA-A pre-pass.
+#pragma once
+#include "common.cuh"
+
+namespace e4b {
+
+struct LoraAArgs {
+  const void* a;             // activations (act dtype), rows of K
+  const int32_t* a_rows;     // nullable gather map (sorted row -> source row)
+  const void* loraA;         // [E, rank, K] (lora dtype)
+  const int32_t* offsets;    // [E+1]
+  const int32_t* tile_start; // [E+1] prefix of ceil(count / kLoraRows)
+  int E, K, rank, lora_dtype;
+  float scaling;
+  float* xa;                 // [R, rank] fp32 = scaling * (a_row . A[e]^T)
+  int max_tiles;
+};
+constexpr int kLoraRows = 32;
+constexpr int kLoraMaxRank = 64;
+
+e4b_status launch_lora_a(const LoraAArgs& g, int act_dtype, cudaStream_t s);
+
+}  // namespace e4b

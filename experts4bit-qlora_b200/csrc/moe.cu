@@ -1,0 +1,303 @@
+// Whole expert layer and the standalone grouped GEMM entry point.
+//
+// e4b_moe_forward is the device-side replacement of fused_experts_forward /
+// fused_experts_lora_forward (experts4bit_qlora/engines/fast.py:100-257):
+//   permute (no host sync) -> [LoRA-A of x] -> grouped gate_up GEMM with the
+//   LoRA delta and SwiGLU fused -> [LoRA-A of h] -> grouped down GEMM with its
+//   LoRA delta -> weighted fixed-order combine.
+// All launches are stream-ordered on the caller's stream; nothing is allocated.
+#include "common.cuh"
+#include "gemv.cuh"
+#include "lora.cuh"
+#include "permute.cuh"
+#include "umma.cuh"
+
+namespace e4b {
+
+struct MoeLayout {
+  size_t offsets, active, num_active, tile_a, tile_b, inv, sorted_token, h, down_rows, xa_gu, xa_dn, umma, total;
+};
+
+static MoeLayout moe_layout(const e4b_moe_desc& d) {
+  MoeLayout L{};
+  const size_t R = (size_t)d.tokens * d.top_k;
+  const size_t E = d.num_experts;
+  const size_t es = 2;  // act dtypes are 16-bit
+  size_t o = kErrBytes;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align_up(o + bytes, 256);
+    return at;
+  };
+  L.offsets = take((E + 1) * 4);
+  L.active = take(E * 4);
+  L.num_active = take(4);
+  L.tile_a = take((E + 1) * 4);
+  L.tile_b = take((E + 1) * 4);
+  L.inv = take(R * 4);
+  L.sorted_token = take(R * 4);
+  L.h = take(R * d.intermediate * es);
+  L.down_rows = take(R * d.hidden * es);
+  L.xa_gu = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
+  L.xa_dn = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
+  L.umma = take(umma_workspace_bytes(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate));
+  L.total = o;
+  return L;
+}
+
+__global__ void active_from_offsets_kernel(const int32_t* __restrict__ offsets, int E, int32_t* __restrict__ active,
+                                           int32_t* __restrict__ num_active) {
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int e = 0; e < E; ++e)
+      if (offsets[e + 1] > offsets[e]) active[n++] = e;
+    *num_active = n;
+  }
+}
+
+static bool desc_ok(const e4b_moe_desc& d) {
+  if (d.num_experts <= 0 || d.num_experts > 1024 || d.hidden <= 0 || d.intermediate <= 0) return false;
+  if (d.top_k <= 0 || d.top_k > d.num_experts || d.tokens < 0) return false;
+  if ((int64_t)d.tokens * d.top_k > (1 << 30)) return false;
+  return true;
+}
+
+}  // namespace e4b
+
+using namespace e4b;
+
+extern "C" const char* e4b_status_string(e4b_status s) {
+  switch (s) {
+    case E4B_OK: return "ok";
+    case E4B_ERR_INVALID_ARG: return "invalid argument (null pointer or inconsistent sizes)";
+    case E4B_ERR_UNSUPPORTED: return "unsupported configuration (dtype, blocksize, K % 64, or rank)";
+    case E4B_ERR_WORKSPACE: return "workspace missing or too small";
+    case E4B_ERR_ALIGNMENT: return "pointer not 16-byte aligned";
+    case E4B_ERR_CUDA: return "CUDA launch or query failed";
+    case E4B_ERR_EXPERT_INDEX: return "top-k expert index outside [0, num_experts)";
+  }
+  return "unknown status";
+}
+
+extern "C" int e4b_abi_version(void) { return 1; }
+
+extern "C" e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out) {
+  if (!workspace || !error_out) return E4B_ERR_INVALID_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  int v = 0;
+  if (cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return E4B_ERR_CUDA;
+  if (cudaMemsetAsync(workspace, 0, sizeof(int), s) != cudaSuccess) return E4B_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return E4B_ERR_CUDA;
+  *error_out = v;
+  return E4B_OK;
+}
+
+extern "C" size_t e4b_grouped_gemm_workspace_bytes(int R, int E, int N, int K) {
+  (void)R;
+  (void)N;
+  (void)K;
+  if (E <= 0) return 0;
+  return kErrBytes + align_up((size_t)(E + 1) * 4, 256);
+}
+
+extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int32_t* a_rows, const uint8_t* packed,
+                                           const float* absmax, const int32_t* offsets, int E, int R, int N, int K,
+                                           int epilogue, void* out, void* workspace, size_t workspace_bytes,
+                                           void* stream) {
+  if (E <= 0 || E > 1024 || R < 0 || N <= 0 || K <= 0) return E4B_ERR_INVALID_ARG;
+  if (!is_act_dtype(a_dtype) || K % 64) return E4B_ERR_UNSUPPORTED;
+  if (epilogue == E4B_EPI_SWIGLU ? (N % 32) : (N % 16)) return E4B_ERR_UNSUPPORTED;
+  if (epilogue < E4B_EPI_NONE || epilogue > E4B_EPI_SILU) return E4B_ERR_INVALID_ARG;
+  if (R == 0) return E4B_OK;
+  if (!a || !packed || !absmax || !offsets || !out) return E4B_ERR_INVALID_ARG;
+  if (!aligned16(a) || !aligned16(packed)) return E4B_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < e4b_grouped_gemm_workspace_bytes(R, E, N, K)) return E4B_ERR_WORKSPACE;
+  cudaStream_t s = (cudaStream_t)stream;
+  char* ws = static_cast<char*>(workspace);
+  int32_t* active = reinterpret_cast<int32_t*>(ws + kErrBytes);
+  int32_t* num_active = reinterpret_cast<int32_t*>(ws + 4);  // second word of the error block
+  active_from_offsets_kernel<<<1, 32, 0, s>>>(offsets, E, active, num_active);
+  if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
+  GemvArgs g{};
+  g.a = a;
+  g.a_rows = a_rows;
+  g.packed = packed;
+  g.absmax = absmax;
+  g.offsets = offsets;
+  g.active = active;
+  g.num_active = num_active;
+  g.E = E;
+  g.N = N;
+  g.K = K;
+  g.epilogue = epilogue;
+  g.out = out;
+  g.Nout = epilogue == E4B_EPI_SWIGLU ? N / 2 : N;
+  g.tiles_per_expert = epilogue == E4B_EPI_SWIGLU ? N / 16 : N / 16;
+  g.max_tasks = (R < E ? R : E) * g.tiles_per_expert;
+  g.err = reinterpret_cast<int*>(ws);
+  return launch_gemv(g, a_dtype, R, s);
+}
+
+extern "C" size_t e4b_moe_workspace_bytes(const e4b_moe_desc* desc) {
+  if (!desc || !desc_ok(*desc)) return 0;
+  return moe_layout(*desc).total;
+}
+
+extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tensors* t, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  if (!desc || !t || !desc_ok(*desc)) return E4B_ERR_INVALID_ARG;
+  const e4b_moe_desc& d = *desc;
+  if (!is_act_dtype(d.act_dtype) || !is_any_dtype(d.weight_dtype) || !is_any_dtype(d.out_dtype))
+    return E4B_ERR_UNSUPPORTED;
+  if (d.hidden % 64 || d.intermediate % 64) return E4B_ERR_UNSUPPORTED;
+  if (d.lora_rank < 0 || d.lora_rank > kLoraMaxRank) return E4B_ERR_UNSUPPORTED;
+  if (d.lora_rank > 0 && !is_any_dtype(d.lora_dtype)) return E4B_ERR_UNSUPPORTED;
+  const int T = d.tokens, k = d.top_k, E = d.num_experts, H = d.hidden, I = d.intermediate;
+  if (T == 0) return E4B_OK;
+  if (!t->hidden || !t->topk_idx || !t->topk_w || !t->gate_up_packed || !t->gate_up_absmax || !t->down_packed ||
+      !t->down_absmax || !t->out)
+    return E4B_ERR_INVALID_ARG;
+  if (d.lora_rank > 0 && (!t->gate_up_lora_A || !t->gate_up_lora_B || !t->down_lora_A || !t->down_lora_B))
+    return E4B_ERR_INVALID_ARG;
+  if (!aligned16(t->hidden) || !aligned16(t->gate_up_packed) || !aligned16(t->down_packed) || !aligned16(t->out))
+    return E4B_ERR_ALIGNMENT;
+  const MoeLayout L = moe_layout(d);
+  if (!workspace || workspace_bytes < L.total) return E4B_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return E4B_ERR_ALIGNMENT;
+  cudaStream_t s = (cudaStream_t)stream;
+  char* ws = static_cast<char*>(workspace);
+  int* err = reinterpret_cast<int*>(ws);
+  const int R = T * k;
+  const int n1 = d.has_gate ? 2 * I : I;
+
+  auto mark = [&](int i) {
+    if (!t->stage_events || !t->stage_events[i]) return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cs);
+    cudaEvent_t ev = (cudaEvent_t)t->stage_events[i];
+    if (cs == cudaStreamCaptureStatusActive)
+      cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal);
+    else
+      cudaEventRecord(ev, s);
+  };
+  mark(0);
+  PermuteArgs pa{};
+  pa.topk_idx = t->topk_idx;
+  pa.T = T;
+  pa.k = k;
+  pa.E = E;
+  pa.inv = reinterpret_cast<int32_t*>(ws + L.inv);
+  pa.sorted_token = reinterpret_cast<int32_t*>(ws + L.sorted_token);
+  pa.offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  pa.active = reinterpret_cast<int32_t*>(ws + L.active);
+  pa.num_active = reinterpret_cast<int32_t*>(ws + L.num_active);
+  pa.tile_start_a = reinterpret_cast<int32_t*>(ws + L.tile_a);
+  pa.tile_start_b = reinterpret_cast<int32_t*>(ws + L.tile_b);
+  pa.tile_a = kLoraRows;
+  pa.tile_b = kUmmaTokens;
+  pa.err = err;
+  pa.reset_err = 1;
+  e4b_status st = launch_permute(pa, s);
+  if (st != E4B_OK) return st;
+  mark(1);
+
+  void* h = ws + L.h;
+  void* down_rows = ws + L.down_rows;
+  float* xa_gu = reinterpret_cast<float*>(ws + L.xa_gu);
+  float* xa_dn = reinterpret_cast<float*>(ws + L.xa_dn);
+  const int max_active = R < E ? R : E;
+  const int lora_tiles = R / kLoraRows + max_active;
+
+  if (d.lora_rank > 0) {
+    LoraAArgs la{};
+    la.a = t->hidden;
+    la.a_rows = pa.sorted_token;
+    la.loraA = t->gate_up_lora_A;
+    la.offsets = pa.offsets;
+    la.tile_start = pa.tile_start_a;
+    la.E = E;
+    la.K = H;
+    la.rank = d.lora_rank;
+    la.lora_dtype = d.lora_dtype;
+    la.scaling = d.lora_scaling;
+    la.xa = xa_gu;
+    la.max_tiles = lora_tiles;
+    if ((st = launch_lora_a(la, d.act_dtype, s)) != E4B_OK) return st;
+  }
+  mark(2);
+
+  const bool use_umma = umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype);
+  GemvArgs g{};
+  g.a = t->hidden;
+  g.a_rows = pa.sorted_token;
+  g.packed = t->gate_up_packed;
+  g.absmax = t->gate_up_absmax;
+  g.offsets = pa.offsets;
+  g.active = pa.active;
+  g.num_active = pa.num_active;
+  g.E = E;
+  g.N = n1;
+  g.K = H;
+  g.epilogue = d.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
+  g.out = h;
+  g.Nout = I;
+  g.lora_xa = d.lora_rank > 0 ? xa_gu : nullptr;
+  g.lora_B = t->gate_up_lora_B;
+  g.lora_dtype = d.lora_dtype;
+  g.rank = d.lora_rank;
+  g.tiles_per_expert = n1 / 16;
+  g.max_tasks = max_active * g.tiles_per_expert;
+  g.err = err;
+  if (use_umma) {
+    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
+    st = launch_umma(u, d.act_dtype, s);
+  } else {
+    st = launch_gemv(g, d.act_dtype, T, s);
+  }
+  if (st != E4B_OK) return st;
+  mark(3);
+
+  if (d.lora_rank > 0) {
+    LoraAArgs la{};
+    la.a = h;
+    la.a_rows = nullptr;
+    la.loraA = t->down_lora_A;
+    la.offsets = pa.offsets;
+    la.tile_start = pa.tile_start_a;
+    la.E = E;
+    la.K = I;
+    la.rank = d.lora_rank;
+    la.lora_dtype = d.lora_dtype;
+    la.scaling = d.lora_scaling;
+    la.xa = xa_dn;
+    la.max_tiles = lora_tiles;
+    if ((st = launch_lora_a(la, d.act_dtype, s)) != E4B_OK) return st;
+  }
+  mark(4);
+
+  g.a = h;
+  g.a_rows = nullptr;
+  g.packed = t->down_packed;
+  g.absmax = t->down_absmax;
+  g.N = H;
+  g.K = I;
+  g.epilogue = E4B_EPI_NONE;
+  g.out = down_rows;
+  g.Nout = H;
+  g.lora_xa = d.lora_rank > 0 ? xa_dn : nullptr;
+  g.lora_B = t->down_lora_B;
+  g.tiles_per_expert = H / 16;
+  g.max_tasks = max_active * g.tiles_per_expert;
+  if (use_umma) {
+    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
+    st = launch_umma(u, d.act_dtype, s);
+  } else {
+    st = launch_gemv(g, d.act_dtype, T, s);
+  }
+  if (st != E4B_OK) return st;
+  mark(5);
+
+  st = e4b_combine(down_rows, d.act_dtype, pa.inv, t->topk_w, d.weight_dtype, T, k, H, t->out, d.out_dtype, stream);
+  mark(6);
+  return st;
+}

@@ -1,0 +1,168 @@
+// Permutation (R2): the device-side replacement for engines/fast.py:126-135.
+//
+// order = argsort(flat top-k ids, stable); counts = bincount; offsets =
+// exclusive scan -- computed in one CTA of 32 warps with no host round trip.
+// Each warp owns a contiguous segment of the flat array, so ranks within an
+// expert follow flat order exactly (stable): pass 1 counts per (warp, expert),
+// pass 2 scans expert-major / warp-minor, pass 3 re-walks each segment in order
+// and places every entry with __match_any_sync ranks.
+#include "common.cuh"
+#include "permute.cuh"
+
+namespace e4b {
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* smem_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) smem_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? smem_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) smem_warp[lane] = w;
+  }
+  __syncthreads();
+  const int before = (warp ? smem_warp[warp - 1] : 0) + x - v;
+  if (total) *total = smem_warp[nw - 1];
+  __syncthreads();
+  return before;
+}
+
+__global__ void __launch_bounds__(1024)
+permute_kernel(PermuteArgs a) {
+  extern __shared__ int wc[];           // [32][E]
+  __shared__ int s_scan[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int E = a.E;
+  const int n = a.T * a.k;
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) wc[i] = 0;
+  if (a.reset_err && threadIdx.x == 0 && a.err) *a.err = 0;
+  __syncthreads();
+  const int seg = (n + 31) / 32;
+  const int s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
+  const unsigned lt = (1u << lane) - 1u;
+  // pass 1: per-warp counts
+  for (int base = s0; base < s1; base += 32) {
+    const int i = base + lane;
+    const bool valid = i < s1;
+    int e = 0;
+    if (valid) {
+      const int64_t raw = a.topk_idx[i];
+      e = (int)raw;
+      if (raw < 0 || raw >= E) {
+        raise_error(a.err, E4B_ERR_EXPERT_INDEX);
+        e = raw < 0 ? 0 : E - 1;
+      }
+    }
+    const unsigned act = __ballot_sync(0xffffffffu, valid);
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1) & act;
+    if (valid && (peers & lt) == 0) wc[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  // pass 2: counts, offsets, per-warp bases (one expert per thread, E <= 1024)
+  {
+    const int e = threadIdx.x;
+    int c = 0;
+    if (e < E) {
+      for (int w = 0; w < 32; ++w) {
+        const int t = wc[w * E + e];
+        wc[w * E + e] = c;           // exclusive prefix over warps
+        c += t;
+      }
+    }
+    int tot;
+    const int off = block_exclusive_scan(c, s_scan, &tot);
+    if (e < E) {
+      a.offsets[e] = off;
+      for (int w = 0; w < 32; ++w) wc[w * E + e] += off;
+    }
+    if (threadIdx.x == 0) a.offsets[E] = n;
+    // active-expert list and tile prefixes
+    const int pos = block_exclusive_scan(c > 0 ? 1 : 0, s_scan, &tot);
+    if (e < E && c > 0 && a.active) a.active[pos] = e;
+    if (threadIdx.x == 0 && a.num_active) *a.num_active = tot;
+    for (int j = 0; j < 2; ++j) {
+      int* ts = j == 0 ? a.tile_start_a : a.tile_start_b;
+      const int bm = j == 0 ? a.tile_a : a.tile_b;
+      if (!ts) continue;
+      const int nt = e < E ? (c + bm - 1) / bm : 0;
+      const int p = block_exclusive_scan(nt, s_scan, &tot);
+      if (e < E) ts[e] = p;
+      if (threadIdx.x == 0) ts[E] = tot;
+    }
+  }
+  __syncthreads();
+  // pass 3: place every entry (stable)
+  for (int base = s0; base < s1; base += 32) {
+    const int i = base + lane;
+    const bool valid = i < s1;
+    int e = 0;
+    if (valid) {
+      const int64_t raw = a.topk_idx[i];
+      e = raw < 0 ? 0 : (raw >= E ? E - 1 : (int)raw);
+    }
+    const unsigned act = __ballot_sync(0xffffffffu, valid);
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1) & act;
+    int pos = 0;
+    if (valid) pos = wc[warp * E + e] + __popc(peers & lt);
+    __syncwarp();
+    if (valid && (peers & lt) == 0) wc[warp * E + e] += __popc(peers);
+    __syncwarp();
+    if (valid) {
+      if (a.order) a.order[pos] = i;
+      if (a.inv) a.inv[i] = pos;
+      if (a.sorted_token) a.sorted_token[pos] = i / a.k;
+    }
+  }
+}
+
+size_t permute_smem_bytes(int E) { return (size_t)32 * E * sizeof(int); }
+
+e4b_status launch_permute(const PermuteArgs& a, cudaStream_t s) {
+  const size_t smem = permute_smem_bytes(a.E);
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return E4B_ERR_CUDA;
+  }
+  permute_kernel<<<1, 1024, smem, s>>>(a);
+  return launch_status();
+}
+
+}  // namespace e4b
+
+using namespace e4b;
+
+extern "C" size_t e4b_permute_workspace_bytes(int T, int k, int E) {
+  (void)T;
+  (void)k;
+  if (E < 0) return 0;
+  return kErrBytes;
+}
+
+extern "C" e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, int32_t* order, int32_t* inv,
+                                  int32_t* offsets, void* workspace, size_t workspace_bytes, void* stream) {
+  if (T < 0 || k <= 0 || E <= 0 || E > 1024 || (int64_t)T * k > (1 << 30)) return E4B_ERR_INVALID_ARG;
+  if (!offsets || (T > 0 && !topk_idx)) return E4B_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < e4b_permute_workspace_bytes(T, k, E)) return E4B_ERR_WORKSPACE;
+  PermuteArgs a{};
+  a.topk_idx = topk_idx;
+  a.T = T;
+  a.k = k;
+  a.E = E;
+  a.order = order;
+  a.inv = inv;
+  a.offsets = offsets;
+  a.err = static_cast<int*>(workspace);
+  a.reset_err = 1;
+  return launch_permute(a, (cudaStream_t)stream);
+}

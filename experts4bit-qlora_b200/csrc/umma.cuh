@@ -1,0 +1,22 @@
+// Internal launch interface of the tcgen05 grouped NF4 GEMM (prefill regime).
+#pragma once
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace e4b {
+
+constexpr int kUmmaTokens = 128;   // token tile (UMMA N) per CTA
+
+struct UmmaArgs {
+  GemvArgs g;                      // operands, epilogue and LoRA, as for the GEMV
+  const int32_t* tile_start;       // [E+1] prefix of ceil(count / kUmmaTokens)
+  int max_tiles;
+  void* scratch;
+};
+
+size_t umma_workspace_bytes(int T, int k, int E, int H, int I);
+bool umma_eligible(int T, int k, int E, int H, int I, int has_gate, int act_dtype);
+UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k);
+e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s);
+
+}  // namespace e4b

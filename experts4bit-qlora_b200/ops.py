@@ -1,0 +1,222 @@
+"""Tensor-level wrappers over the C ABI (include/e4b.h).
+
+Each function validates shapes on the host, takes device memory from torch,
+and launches on torch's current stream without synchronising. These are the
+calls the module classes and the tests use.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+
+
+def _cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} must be a CUDA tensor (the fused path has no CPU implementation)")
+
+
+# --------------------------------------------------------------------------- #
+# NF4 codec
+# --------------------------------------------------------------------------- #
+def nf4_quantize(w: torch.Tensor, blocksize: int = 64):
+    """Blockwise NF4 of ``w`` (any shape, numel % 64 == 0) -> (packed u8 [n/2], absmax f32 [n/64]).
+
+    Runs the CUDA kernel for CUDA tensors and the library's host routine for CPU
+    tensors; both produce the same bytes."""
+    if blocksize != 64:
+        raise ValueError("only blocksize 64 is built")
+    w = w.detach().contiguous()
+    if w.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        w = w.float()
+    n = w.numel()
+    if n % 64:
+        raise ValueError(f"element count {n} is not a multiple of 64")
+    packed = torch.empty(n // 2, dtype=torch.uint8, device=w.device)
+    absmax = torch.empty(n // 64, dtype=torch.float32, device=w.device)
+    L = N.lib()
+    if w.is_cuda:
+        N.check(L.e4b_nf4_quantize(w.data_ptr(), N.dtype_code(w.dtype), n, packed.data_ptr(), absmax.data_ptr(),
+                                   N.stream_handle(w.device)), "e4b_nf4_quantize")
+    else:
+        N.check(L.e4b_nf4_quantize_host(w.data_ptr(), N.dtype_code(w.dtype), n, packed.data_ptr(),
+                                        absmax.data_ptr()), "e4b_nf4_quantize_host")
+    return packed, absmax
+
+
+def nf4_dequantize(packed: torch.Tensor, absmax: torch.Tensor, shape, dtype=torch.bfloat16) -> torch.Tensor:
+    """``dtype(code[q] * absmax)``, reshaped to ``shape``."""
+    packed = packed.contiguous()
+    absmax = absmax.contiguous().float()
+    n = packed.numel() * 2
+    out = torch.empty(n, dtype=dtype, device=packed.device)
+    L = N.lib()
+    if packed.is_cuda:
+        N.check(L.e4b_nf4_dequantize(packed.data_ptr(), absmax.data_ptr(), n, out.data_ptr(), N.dtype_code(dtype),
+                                     N.stream_handle(packed.device)), "e4b_nf4_dequantize")
+    else:
+        N.check(L.e4b_nf4_dequantize_host(packed.data_ptr(), absmax.data_ptr(), n, out.data_ptr(),
+                                          N.dtype_code(dtype)), "e4b_nf4_dequantize_host")
+    return out.view(*shape)
+
+
+# --------------------------------------------------------------------------- #
+# Router, permutation, grouped GEMM, combine
+# --------------------------------------------------------------------------- #
+def router_topk(x: torch.Tensor, router_weight: torch.Tensor, k: int, kind: int = N.SOFTMAX_THEN_TOPK,
+                norm_topk_prob: bool = False, return_logits: bool = False):
+    """fp32 router logits of ``x [T,H]`` against ``router_weight [E,H]`` and the
+    deterministic top-k. Returns ``(weights f32 [T,k], idx i64 [T,k])`` (+ logits)."""
+    _cuda(x, "x")
+    x = x.contiguous()
+    wr = router_weight.contiguous()
+    T, H = x.shape
+    E = wr.shape[0]
+    dev = x.device
+    idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if return_logits else None
+    L = N.lib()
+    nbytes = L.e4b_router_workspace_bytes(T, E)
+    ws = N.workspaces.get(dev, nbytes, "router")
+    N.check(L.e4b_router_topk(x.data_ptr(), N.dtype_code(x.dtype), wr.data_ptr(), N.dtype_code(wr.dtype), T, H, E, k,
+                              kind, int(norm_topk_prob), N.ptr(logits), idx.data_ptr(), w.data_ptr(),
+                              ws.data_ptr(), ws.numel(), N.stream_handle(dev)), "e4b_router_topk")
+    return (w, idx, logits) if return_logits else (w, idx)
+
+
+def permute(top_k_index: torch.Tensor, num_experts: int):
+    """Device permutation: ``(order i32 [T*k], inv i32 [T*k], offsets i32 [E+1])``."""
+    _cuda(top_k_index, "top_k_index")
+    idx = top_k_index.contiguous().long()
+    T, k = idx.shape
+    dev = idx.device
+    order = torch.empty(T * k, dtype=torch.int32, device=dev)
+    inv = torch.empty(T * k, dtype=torch.int32, device=dev)
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    L = N.lib()
+    ws = N.workspaces.get(dev, L.e4b_permute_workspace_bytes(T, k, num_experts), "permute")
+    N.check(L.e4b_permute(idx.data_ptr(), T, k, num_experts, order.data_ptr(), inv.data_ptr(), offsets.data_ptr(),
+                          ws.data_ptr(), ws.numel(), N.stream_handle(dev)), "e4b_permute")
+    return order, inv, offsets
+
+
+def grouped_nf4_gemm(a: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, offsets: torch.Tensor,
+                     a_rows: torch.Tensor | None = None, epilogue: int = N.EPI_NONE) -> torch.Tensor:
+    """Grouped NF4 GEMM: ``packed [E,N,K/2]``, ``absmax [E,N,K/64]``, expert-sorted rows
+    delimited by ``offsets [E+1]`` (int32). Returns ``[R, N]`` (``[R, N/2]`` for SwiGLU)."""
+    _cuda(a, "a")
+    a = a.contiguous()
+    E, Nn, Kh = packed.shape
+    K = Kh * 2
+    R = int(a_rows.numel()) if a_rows is not None else a.shape[0]
+    n_out = Nn // 2 if epilogue == N.EPI_SWIGLU else Nn
+    out = torch.empty(R, n_out, dtype=a.dtype, device=a.device)
+    L = N.lib()
+    ws = N.workspaces.get(a.device, L.e4b_grouped_gemm_workspace_bytes(R, E, Nn, K), "gemm")
+    offs = offsets.to(torch.int32).contiguous()
+    rows = a_rows.to(torch.int32).contiguous() if a_rows is not None else None
+    N.check(L.e4b_grouped_nf4_gemm(a.data_ptr(), N.dtype_code(a.dtype), N.ptr(rows), packed.contiguous().data_ptr(),
+                                   absmax.contiguous().data_ptr(), offs.data_ptr(), E, R, Nn, K, epilogue,
+                                   out.data_ptr(), ws.data_ptr(), ws.numel(), N.stream_handle(a.device)),
+            "e4b_grouped_nf4_gemm")
+    return out
+
+
+def combine(rows: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, tokens: int, k: int,
+            out_dtype=torch.bfloat16) -> torch.Tensor:
+    _cuda(rows, "rows")
+    rows = rows.contiguous()
+    H = rows.shape[1]
+    out = torch.empty(tokens, H, dtype=out_dtype, device=rows.device)
+    w = w.contiguous()
+    N.check(N.lib().e4b_combine(rows.data_ptr(), N.dtype_code(rows.dtype), inv.to(torch.int32).contiguous().data_ptr(),
+                                w.data_ptr(), N.dtype_code(w.dtype), tokens, k, H, out.data_ptr(),
+                                N.dtype_code(out_dtype), N.stream_handle(rows.device)), "e4b_combine")
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# Whole layer
+# --------------------------------------------------------------------------- #
+def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor,
+                gate_up_packed: torch.Tensor, gate_up_absmax: torch.Tensor, down_packed: torch.Tensor,
+                down_absmax: torch.Tensor, num_experts: int, intermediate: int, has_gate: bool = True,
+                out_dtype=None, lora=None, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                check_errors: bool = False) -> torch.Tensor:
+    """One fused expert layer through ``e4b_moe_forward``.
+
+    ``hidden [T,H]`` must already be in the compute dtype (bf16/fp16).
+    ``lora`` = ``(A_gu [E,r,H], B_gu [E,n1,r], A_dn [E,r,I], B_dn [E,H,r], scaling)`` or None.
+    """
+    _cuda(hidden, "hidden_states")
+    if hidden.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("hidden must be bf16 or fp16 (the compute dtype)")
+    hidden = hidden.contiguous()
+    idx = top_k_index.contiguous()
+    if idx.dtype != torch.int64:
+        idx = idx.long()
+    w = top_k_weights.contiguous()
+    if w.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        w = w.float()
+    T, H = hidden.shape
+    k = idx.shape[1]
+    out_dtype = out_dtype or hidden.dtype
+    if out is None:
+        out = torch.empty(T, H, dtype=out_dtype, device=hidden.device)
+    d = MoeDesc_from(num_experts, H, intermediate, k, T, has_gate, hidden.dtype, w.dtype, out_dtype, lora)
+    t = N.MoeTensors()
+    t.hidden, t.topk_idx, t.topk_w = hidden.data_ptr(), idx.data_ptr(), w.data_ptr()
+    t.gate_up_packed, t.gate_up_absmax = gate_up_packed.data_ptr(), gate_up_absmax.data_ptr()
+    t.down_packed, t.down_absmax = down_packed.data_ptr(), down_absmax.data_ptr()
+    keep = []
+    if lora is not None:
+        A_gu, B_gu, A_dn, B_dn, _ = lora
+        mats = [m.contiguous() for m in (A_gu, B_gu, A_dn, B_dn)]
+        keep = mats
+        t.gate_up_lora_A, t.gate_up_lora_B, t.down_lora_A, t.down_lora_B = (m.data_ptr() for m in mats)
+    t.out = out.data_ptr()
+    L = N.lib()
+    nbytes = L.e4b_moe_workspace_bytes(ctypes.byref(d))
+    if nbytes == 0:
+        raise ValueError("invalid expert-layer geometry for the fused kernel")
+    ws = workspace if workspace is not None else N.workspaces.get(hidden.device, nbytes, "moe")
+    if ws.numel() < nbytes:
+        raise ValueError(f"workspace of {ws.numel()} bytes < required {nbytes}")
+    N.check(L.e4b_moe_forward(ctypes.byref(d), ctypes.byref(t), ws.data_ptr(), ws.numel(),
+                              N.stream_handle(hidden.device)), "e4b_moe_forward")
+    del keep
+    if check_errors:
+        err = N.read_device_error(ws)
+        if err:
+            raise N.E4BError(err, "e4b_moe_forward (device)")
+    return out
+
+
+def MoeDesc_from(E, H, I, k, T, has_gate, act_dtype, w_dtype, out_dtype, lora) -> N.MoeDesc:
+    d = N.MoeDesc()
+    d.num_experts, d.hidden, d.intermediate, d.top_k, d.tokens = E, H, I, k, T
+    d.has_gate = int(bool(has_gate))
+    d.act_dtype = N.dtype_code(act_dtype)
+    d.weight_dtype = N.dtype_code(w_dtype)
+    d.out_dtype = N.dtype_code(out_dtype)
+    if lora is not None:
+        A_gu = lora[0]
+        d.lora_rank = A_gu.shape[1]
+        d.lora_dtype = N.dtype_code(A_gu.dtype)
+        d.lora_scaling = float(lora[4])
+    return d
+
+
+def moe_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16, lora_rank=0) -> int:
+    d = N.MoeDesc()
+    d.num_experts, d.hidden, d.intermediate, d.top_k, d.tokens = E, H, I, k, T
+    d.has_gate = int(bool(has_gate))
+    d.act_dtype = N.dtype_code(act_dtype)
+    d.weight_dtype = N.F32
+    d.out_dtype = N.dtype_code(act_dtype)
+    d.lora_rank = lora_rank
+    d.lora_dtype = N.F32
+    return N.lib().e4b_moe_workspace_bytes(ctypes.byref(d))

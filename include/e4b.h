@@ -1,0 +1,190 @@
+/*
+ * e4b.h -- C ABI of the B200 fused-expert library (libe4b.so).
+ *
+ * The reference (experts4bit-qlora) has no C ABI: its kernel boundary is a
+ * Python call into grouped-nf4-gemm / bitsandbytes. Each entry point below
+ * replaces one such call (or one stage of experts4bit_qlora/engines/fast.py)
+ * and is cited to the reference line it stands in for. A maintainer binds them
+ * with ctypes; the Python package in this repository does
+ * exactly that.
+ *
+ * Conventions
+ *   - Every pointer is a DEVICE pointer unless the name ends in _host.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Every call is stream-ordered, never synchronises the host, and is
+ *     therefore capturable in a CUDA graph. The library allocates nothing.
+ *   - Return codes, never exceptions or device traps. Invalid expert ids found
+ *     on the device are clamped for memory safety and reported through the
+ *     device error word at the start of the workspace (e4b_read_device_error).
+ *   - Layouts are the reference's storage contract
+ *     (experts4bit_qlora/_vendor/experts.py:244-269): per expert, row-major
+ *     [out, in] NF4 with two codes per byte (first element in the high nibble)
+ *     and one fp32 absmax per 64 consecutive elements.
+ */
+#ifndef E4B_H_
+#define E4B_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define E4B_API __attribute__((visibility("default")))
+#else
+#define E4B_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  E4B_OK = 0,
+  E4B_ERR_INVALID_ARG = 1,    /* null pointer, negative or inconsistent size */
+  E4B_ERR_UNSUPPORTED = 2,    /* dtype / blocksize / K%64 / rank outside what the kernels take */
+  E4B_ERR_WORKSPACE = 3,      /* workspace missing or smaller than *_workspace_bytes() */
+  E4B_ERR_ALIGNMENT = 4,      /* a pointer is not 16-byte aligned */
+  E4B_ERR_CUDA = 5,           /* a CUDA launch or query failed */
+  E4B_ERR_EXPERT_INDEX = 6    /* device-reported: a top-k index outside [0, E) */
+} e4b_status;
+
+typedef enum { E4B_BF16 = 0, E4B_F16 = 1, E4B_F32 = 2 } e4b_dtype;
+
+typedef enum {
+  E4B_SOFTMAX_THEN_TOPK = 0,  /* OLMoE / Qwen3-MoE / Mixtral */
+  E4B_TOPK_THEN_SOFTMAX = 1   /* gpt-oss */
+} e4b_router_kind;
+
+typedef enum { E4B_EPI_NONE = 0, E4B_EPI_SWIGLU = 1, E4B_EPI_SILU = 2 } e4b_epilogue;
+
+E4B_API const char* e4b_status_string(e4b_status s);
+/* ABI version: bumped when a signature or a struct below changes. */
+E4B_API int e4b_abi_version(void);
+
+/* ---- NF4 codec ---------------------------------------------------------- */
+
+/* Replaces bitsandbytes.functional.quantize_4bit(w, blocksize=64,
+ * compress_statistics=False, quant_type="nf4") as called per expert by
+ * ExpertsNbit._quantize_stack (_vendor/experts.py:408-426). n % 64 == 0.
+ * w: n elements of `w_dtype`; packed: n/2 bytes; absmax: n/64 fp32. */
+E4B_API e4b_status e4b_nf4_quantize(const void* w, int w_dtype, int64_t n, uint8_t* packed, float* absmax,
+                            void* stream);
+
+/* Replaces bitsandbytes.functional.dequantize_4bit as called by
+ * ExpertsNbit._dequantize_expert (_vendor/experts.py:447-457):
+ * out[i] = out_dtype(code[q_i] * absmax[i/64]) with one round-to-nearest-even. */
+E4B_API e4b_status e4b_nf4_dequantize(const uint8_t* packed, const float* absmax, int64_t n, void* out, int out_dtype,
+                              void* stream);
+
+/* Host (CPU) versions of the two calls above for modules built on CPU; they
+ * produce the same bytes as the device kernels. */
+E4B_API e4b_status e4b_nf4_quantize_host(const void* w_host, int w_dtype, int64_t n, uint8_t* packed_host,
+                                 float* absmax_host);
+E4B_API e4b_status e4b_nf4_dequantize_host(const uint8_t* packed_host, const float* absmax_host, int64_t n,
+                                   void* out_host, int out_dtype);
+
+/* ---- Router (R1) --------------------------------------------------------- */
+
+/* Replaces transformers' OlmoeTopKRouter.forward (F.linear + fp32 softmax +
+ * topk + optional renorm) with the rule of engines/cpu_router.py:100-119:
+ * fp32 logits, stable descending order with ties to the LOWER expert id.
+ * x [T,H] (x_dtype bf16/f16), w_router [E,H] (w_dtype bf16/f16/f32).
+ * logits_out [T,E] fp32 is optional (NULL); topk_idx [T,k] int64; topk_w [T,k] fp32.
+ * E <= 1024, k <= 32, k <= E. workspace: e4b_router_workspace_bytes(T,E). */
+E4B_API size_t e4b_router_workspace_bytes(int T, int E);
+E4B_API e4b_status e4b_router_topk(const void* x, int x_dtype, const void* w_router, int w_dtype, int T, int H, int E,
+                           int k, int kind, int norm_topk_prob, float* logits_out, int64_t* topk_idx,
+                           float* topk_w, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Permutation (R2) ---------------------------------------------------- */
+
+/* Replaces engines/fast.py:126-135 (stable argsort of the flat indices,
+ * bincount, nonzero, and the two .tolist() host syncs) with one device pass.
+ * order [T*k]: order[r] = flat index (t*k+s) of sorted row r, stable within an
+ * expert; inv [T*k]: inv[t*k+s] = r; offsets [E+1]: row start of each expert.
+ * Any of order/inv may be NULL. workspace: e4b_permute_workspace_bytes. */
+E4B_API size_t e4b_permute_workspace_bytes(int T, int k, int E);
+E4B_API e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, int32_t* order, int32_t* inv,
+                       int32_t* offsets, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Grouped NF4 GEMM (R3, R4, R6) --------------------------------------- */
+
+/* Replaces nf4_grouped.gemm_4bit_grouped(a, packed.view(E,N,K/2),
+ * absmax.view(E,N,K/64), sizes, expert_ids) (engines/fast.py:137-156) and,
+ * with epilogue = E4B_EPI_SWIGLU, lora._epilogue (lora.py:102-128) fused on it.
+ * a [R,K] (a_dtype bf16/f16): rows grouped by expert, expert e owning rows
+ * [offsets[e], offsets[e+1]); with a_rows != NULL, row r is read from
+ * a[a_rows[r]] instead (the permutation gather of fast.py:135 fused in).
+ * out [R, N_out] in a_dtype, N_out = N/2 for SWIGLU (silu(gate)*up, gate = rows
+ * [0, N/2)), else N. K % 64 == 0, N % 16 == 0 (N % 32 for SWIGLU).
+ * workspace: e4b_grouped_gemm_workspace_bytes. */
+E4B_API size_t e4b_grouped_gemm_workspace_bytes(int R, int E, int N, int K);
+E4B_API e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int32_t* a_rows, const uint8_t* packed,
+                                const float* absmax, const int32_t* offsets, int E, int R, int N, int K,
+                                int epilogue, void* out, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/* ---- Combine (R7) -------------------------------------------------------- */
+
+/* Replaces engines/fast.py:158-160 + _scatter_combine (:260-278): out[t] =
+ * sum over s = 0..k-1 (in slot order, fp32) of w[t,s] * rows[inv[t*k+s]].
+ * rows [T*k, H] (rows_dtype), w [T,k] (w_dtype), out [T,H] (out_dtype). No
+ * atomics: bit-identical across runs. */
+E4B_API e4b_status e4b_combine(const void* rows, int rows_dtype, const int32_t* inv, const void* w, int w_dtype, int T,
+                       int k, int H, void* out, int out_dtype, void* stream);
+
+/* ---- Whole expert layer (R2-R7 + LoRA R5) -------------------------------- */
+
+typedef struct {
+  int num_experts;        /* E */
+  int hidden;             /* H: in-features of gate_up, out-features of down */
+  int intermediate;       /* I: in-features of down */
+  int top_k;              /* k */
+  int tokens;             /* T */
+  int has_gate;           /* 1: gate_up is [2I,H] (SwiGLU); 0: [I,H] (SiLU) */
+  int act_dtype;          /* hidden / compute dtype: E4B_BF16 or E4B_F16 */
+  int weight_dtype;       /* top_k_weights dtype: bf16 / f16 / f32 */
+  int out_dtype;          /* output dtype (the caller's input dtype) */
+  int lora_rank;          /* 0 = no adapter */
+  int lora_dtype;         /* adapter dtype: E4B_F32 or E4B_BF16 (or E4B_F16) */
+  float lora_scaling;     /* alpha / r */
+} e4b_moe_desc;
+
+typedef struct {
+  const void* hidden;              /* [T,H] act_dtype */
+  const int64_t* topk_idx;         /* [T,k] */
+  const void* topk_w;              /* [T,k] weight_dtype */
+  const uint8_t* gate_up_packed;   /* [E, n1*H/2], n1 = 2I (has_gate) or I */
+  const float* gate_up_absmax;     /* [E, n1*H/64] */
+  const uint8_t* down_packed;      /* [E, H*I/2] */
+  const float* down_absmax;        /* [E, H*I/64] */
+  const void* gate_up_lora_A;      /* [E, r, H]   (NULL if lora_rank == 0) */
+  const void* gate_up_lora_B;      /* [E, n1, r] */
+  const void* down_lora_A;         /* [E, r, I] */
+  const void* down_lora_B;         /* [E, H, r] */
+  void* out;                       /* [T,H] out_dtype */
+  /* Optional profiling hook (NULL normally): E4B_MOE_STAGE_EVENTS cudaEvent_t
+   * handles recorded on `stream` before the permutation and after each of the
+   * stages permute, LoRA-A(x), gate_up, LoRA-A(h), down, combine. While the
+   * stream is being captured they are recorded as graph nodes, so a replayed
+   * graph yields per-stage device times. */
+  void* const* stage_events;
+} e4b_moe_tensors;
+
+#define E4B_MOE_STAGE_EVENTS 7
+
+/* Replaces fused_experts_forward / fused_experts_lora_forward
+ * (engines/fast.py:100-160, :163-257) end to end: permutation, grouped
+ * gate_up GEMM (+ LoRA delta before the activation) with SwiGLU, grouped down
+ * GEMM (+ LoRA delta), weighted deterministic combine. No host sync. */
+E4B_API size_t e4b_moe_workspace_bytes(const e4b_moe_desc* desc);
+E4B_API e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tensors* t, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Reads (and clears) the device error word of a workspace used by the calls
+ * above. Synchronises `stream`; for debugging and tests, not the hot path. */
+E4B_API e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* E4B_H_ */

@@ -1,0 +1,150 @@
+"""GPU: each stage of the fused path against the CPU oracle, through the C ABI.
+
+Integer/byte/index stages (quantize, dequantize, top-k indices, permutation)
+must be bit-exact; floating-point stages carry their tolerance in the test.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+from oracle import moe as M
+from oracle import nf4 as N
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def ops(e4b):
+    assert e4b._native.available(), "libe4b.so must be built (no fallback)"
+    return e4b.ops
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("n", [64, 64 * 1000, 2048 * 2048])
+def test_dequantize_bit_exact(ops, dtype, n):
+    g = torch.Generator().manual_seed(n)
+    packed = torch.randint(0, 256, (n // 2,), dtype=torch.uint8, generator=g)
+    absmax = torch.rand(n // 64, generator=g) * 3
+    absmax[::7] = 0.0
+    got = ops.nf4_dequantize(packed.to(DEV), absmax.to(DEV), (n,), dtype).cpu()
+    ref = torch.from_numpy(N.dequantize_nf4_f32(packed.numpy(), absmax.numpy())).to(dtype)
+    assert torch.equal(got.view(torch.uint8), ref.view(torch.uint8))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_quantize_bit_exact_device_and_host(ops, dtype):
+    g = torch.Generator().manual_seed(1)
+    w = (torch.randn(96, 640, generator=g) * 0.02).to(dtype)
+    w[3, :64] = 0.0                                   # an all-zero block
+    t = N.nf4_thresholds()
+    w[5, :64] = torch.from_numpy(np.r_[t, np.ones(64 - 15, np.float32)]).to(dtype)  # values on midpoints
+    p_ref, a_ref = N.quantize_nf4(w)
+    p_dev, a_dev = ops.nf4_quantize(w.to(DEV))
+    p_host, a_host = ops.nf4_quantize(w)
+    assert np.array_equal(p_dev.cpu().numpy(), p_ref) and np.array_equal(a_dev.cpu().numpy(), a_ref)
+    assert np.array_equal(p_host.numpy(), p_ref) and np.array_equal(a_host.numpy(), a_ref)
+
+
+@pytest.mark.parametrize("name", ["small", "olmoe_like", "ragged"])
+def test_dequantize_matches_reference_golden(ops, name):
+    import os
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", f"{name}.npz")))
+    case = C.build(name)
+    st = case["st"]
+    e = st["E"] - 1
+    got = ops.nf4_dequantize(st["gate_up_packed"][e].to(DEV), st["gate_up_absmax"][e].to(DEV),
+                             (2 * st["I"], st["H"]), torch.bfloat16).cpu()
+    assert np.array_equal(got.view(torch.int16).numpy().view(np.uint16), g[f"dequant_gu_e{e}"])
+
+
+@pytest.mark.parametrize("T,E,k,H", [(1, 64, 8, 2048), (37, 128, 8, 2048), (300, 8, 2, 4096), (5, 256, 8, 7168),
+                                     (64, 64, 1, 256)])
+@pytest.mark.parametrize("kind,norm", [(0, False), (0, True), (1, False)])
+def test_router_topk_bit_exact_on_same_logits(ops, T, E, k, H, kind, norm):
+    g = torch.Generator().manual_seed(T * 7 + E)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    wr = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    wr[E // 2] = wr[E // 3]                      # exact logit ties between two experts
+    w, idx, logits = ops.router_topk(x.to(DEV), wr.to(DEV), k, kind, norm, return_logits=True)
+    logits = logits.cpu()
+    ref_logits = M.router_logits_f32(x, wr)
+    assert torch.allclose(logits, ref_logits, rtol=1e-4, atol=1e-4)
+    # bit-exact indices on identical fp32 logits (the tie rule)
+    kname = M.SOFTMAX_THEN_TOPK if kind == 0 else M.TOPK_THEN_SOFTMAX
+    rw, ridx = M.route_on_host(logits, k, kname, norm)
+    assert torch.equal(idx.cpu(), ridx)
+    torch.testing.assert_close(w.cpu(), rw, rtol=2e-6, atol=1e-7)
+
+
+def test_router_tie_known_answer(ops):
+    """engines/cpu_router.py tie rule: logits [1,3,3,.5,3,2], k=3 -> [1,2,4]."""
+    logits = torch.tensor([[1.0, 3.0, 3.0, 0.5, 3.0, 2.0]])
+    # x = e_0 (one-hot), W_r[:, 0] = logits -> fp32 logits are exactly the vector
+    H = 64
+    x = torch.zeros(1, H, dtype=torch.bfloat16)
+    x[0, 0] = 1.0
+    wr = torch.zeros(6, H, dtype=torch.bfloat16)
+    wr[:, 0] = logits[0].to(torch.bfloat16)
+    w, idx = ops.router_topk(x.to(DEV), wr.to(DEV), 3)
+    assert idx.cpu().tolist() == [[1, 2, 4]]
+
+
+@pytest.mark.parametrize("T,k,E", [(1, 8, 64), (5, 8, 64), (4096, 8, 128), (8192, 2, 8), (16384, 8, 256),
+                                   (33, 4, 16), (0, 2, 4), (3, 3, 1000)])
+def test_permute_bit_exact(ops, T, k, E):
+    g = torch.Generator().manual_seed(T + E)
+    idx = torch.randint(0, E, (T, k), generator=g)
+    if T > 4:
+        idx[: T // 2] = idx[0]                     # many equal rows -> long equal runs
+    order, inv, offsets = ops.permute(idx.to(DEV), E)
+    r_order, tok, pos, counts, r_off = M.permute(idx, E)
+    assert torch.equal(order.cpu().long(), r_order)
+    assert torch.equal(offsets.cpu().long(), r_off)
+    inv_ref = torch.empty_like(r_order)
+    inv_ref[r_order] = torch.arange(T * k)
+    assert torch.equal(inv.cpu().long(), inv_ref)
+
+
+@pytest.mark.parametrize("E,NN,K,m,epi", [(4, 256, 128, 1, 0), (8, 512, 1024, 3, 1), (3, 128, 2048, 8, 2),
+                                           (5, 256, 768, 13, 1), (4, 128, 128, 40, 0), (2, 4096, 1024, 1, 0)])
+def test_grouped_gemm_vs_fp32(ops, E, NN, K, m, epi):
+    g = torch.Generator().manual_seed(E * NN + K + m)
+    w = torch.randn(E, NN, K, generator=g) * 0.05
+    packed, absmax = N.quantize_stack(w)
+    counts = torch.randint(0, m + 1, (E,), generator=g)
+    counts[0] = m
+    R = int(counts.sum())
+    a = torch.randn(R, K, generator=g).to(torch.bfloat16)
+    offsets = torch.zeros(E + 1, dtype=torch.int32)
+    offsets[1:] = torch.cumsum(counts, 0)
+    out = ops.grouped_nf4_gemm(a.to(DEV), packed.view(E, NN, K // 2).to(DEV), absmax.view(E, NN, K // 64).to(DEV),
+                               offsets.to(DEV), epilogue=epi).cpu().float()
+    Wf = M.dequant_stack_f32(packed, absmax, (NN, K))
+    ref = torch.empty(R, NN // 2 if epi == 1 else NN)
+    for e in range(E):
+        lo, hi = int(offsets[e]), int(offsets[e + 1])
+        y = a[lo:hi].float() @ Wf[e].t()
+        if epi == 1:
+            y = torch.nn.functional.silu(y[:, : NN // 2]) * y[:, NN // 2:]
+        elif epi == 2:
+            y = torch.nn.functional.silu(y)
+        ref[lo:hi] = y
+    mx, mean = M.rel_errors(out, ref)
+    assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
+
+
+@pytest.mark.parametrize("T,k,H", [(1, 8, 2048), (7, 2, 4096), (64, 8, 128)])
+def test_combine_fixed_order(ops, T, k, H):
+    g = torch.Generator().manual_seed(T)
+    E = 16
+    idx = torch.randint(0, E, (T, k), generator=g)
+    order, tok, pos, counts, off = M.permute(idx, E)
+    rows = torch.randn(T * k, H, generator=g).to(torch.bfloat16)
+    w = torch.rand(T, k, generator=g)
+    inv = torch.empty(T * k, dtype=torch.int32)
+    inv[order] = torch.arange(T * k, dtype=torch.int32)
+    got = ops.combine(rows.to(DEV), inv.to(DEV), w.to(DEV), T, k, torch.float32).cpu()
+    ref = M.scatter_combine(rows, w[tok, pos], order, T, k, torch.float32)
+    torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)
