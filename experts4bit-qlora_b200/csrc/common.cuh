@@ -53,6 +53,20 @@ __device__ __forceinline__ float load_as_f32(const void* p, int dtype, int64_t i
   }
 }
 
+// Store with the fp16 range guarded: values beyond +-65504 saturate and raise
+// E4B_ERR_RANGE (a bf16 store never saturates).
+template <typename T> __device__ __forceinline__ T store_cast(float v, int* err);
+template <> __device__ __forceinline__ __nv_bfloat16 store_cast<__nv_bfloat16>(float v, int*) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half store_cast<__half>(float v, int* err) {
+  if (fabsf(v) > 65504.f) {
+    raise_error(err, E4B_ERR_RANGE);
+    v = copysignf(65504.f, v);
+  }
+  return __float2half_rn(v);
+}
+
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + __expf(-g)); }
 
 // Streaming 64-bit global load that does not allocate in L1 (weights are read once).

@@ -15,6 +15,10 @@
 // straight into register A fragments of mma.sync m16n8k16 whose B operand is
 // the activations (<= 8 tokens per n8 tile). The block's partial sum is scaled
 // by its fp32 absmax in fp32, so the code -> weight scaling never rounds.
+// The MMA runs in fp16: the 16 codes carry 11 significant bits there (bf16
+// would round them by up to 2^-8, a systematic per-code error that costs
+// ~1.4e-3 of relative output error), and the activations arrive as fp16 with a
+// per-row power-of-two scale (convert.cu) that keeps them in range exactly.
 // The K dimension is permuted consistently on A and B (both sides read the
 // same physical elements), which lets each lane's bytes stay contiguous.
 #include "gemv.cuh"
@@ -72,8 +76,9 @@ __device__ __forceinline__ float lora_delta(const GemvArgs& g, int e, int row, i
   return d;
 }
 
-template <typename T, int NT>
+template <typename OutT, int NT>
 __global__ void __launch_bounds__(kGemvThreads, 3) nf4_gemv_kernel(GemvArgs g) {
+  using T = __half;
   extern __shared__ __align__(16) uint32_t smem[];
   const char* lut = reinterpret_cast<const char*>(smem);
   float* red = reinterpret_cast<float*>(reinterpret_cast<char*>(smem) + kLutBytes);  // [warps][NT][4][32]
@@ -221,19 +226,24 @@ __global__ void __launch_bounds__(kGemvThreads, 3) nf4_gemv_kernel(GemvArgs g) {
             if (m < M) {
               const int64_t srow = row0 + m;
               float va = c[h], vb = c[2 + h];
+              if (g.a_scale) {
+                const float sc = g.a_scale[g.a_rows ? g.a_rows[srow] : srow];
+                va *= sc;
+                vb *= sc;
+              }
               if (g.rank) {
                 va += lora_delta(g, e, rA, srow);
                 vb += lora_delta(g, e, rB, srow);
               }
-              T* o = reinterpret_cast<T*>(g.out) + srow * g.Nout;
+              OutT* o = reinterpret_cast<OutT*>(g.out) + srow * g.Nout;
               if (g.epilogue == E4B_EPI_SWIGLU) {
-                o[tile * 8 + gq] = from_f32<T>(silu_f32(va) * vb);
+                o[tile * 8 + gq] = store_cast<OutT>(silu_f32(va) * vb, g.err);
               } else if (g.epilogue == E4B_EPI_SILU) {
-                o[rA] = from_f32<T>(silu_f32(va));
-                o[rB] = from_f32<T>(silu_f32(vb));
+                o[rA] = store_cast<OutT>(silu_f32(va), g.err);
+                o[rB] = store_cast<OutT>(silu_f32(vb), g.err);
               } else {
-                o[rA] = from_f32<T>(va);
-                o[rB] = from_f32<T>(vb);
+                o[rA] = store_cast<OutT>(va, g.err);
+                o[rB] = store_cast<OutT>(vb, g.err);
               }
             }
           }
@@ -244,7 +254,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) nf4_gemv_kernel(GemvArgs g) {
   }
 }
 
-template <typename T, int NT>
+template <typename OutT, int NT>
 static e4b_status launch_one(const GemvArgs& g, cudaStream_t s) {
   const int smem = kLutBytes + kGemvWarps * NT * 4 * 32 * (int)sizeof(float);
   int dev = 0;
@@ -254,7 +264,7 @@ static e4b_status launch_one(const GemvArgs& g, cudaStream_t s) {
   static int sm_count[64] = {0};
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(configured & bit)) {
-    if (cudaFuncSetAttribute(nf4_gemv_kernel<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+    if (cudaFuncSetAttribute(nf4_gemv_kernel<OutT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return E4B_ERR_CUDA;
     cudaDeviceGetAttribute(&sm_count[dev & 63], cudaDevAttrMultiProcessorCount, dev);
@@ -263,13 +273,13 @@ static e4b_status launch_one(const GemvArgs& g, cudaStream_t s) {
   int grid = sm_count[dev & 63] * 3;
   if (g.max_tasks < grid) grid = g.max_tasks;
   if (grid < 1) return E4B_OK;
-  nf4_gemv_kernel<T, NT><<<grid, kGemvThreads, smem, s>>>(g);
+  nf4_gemv_kernel<OutT, NT><<<grid, kGemvThreads, smem, s>>>(g);
   return launch_status();
 }
 
-e4b_status launch_gemv(const GemvArgs& g, int act_dtype, int max_rows_per_expert, cudaStream_t s) {
+e4b_status launch_gemv(const GemvArgs& g, int max_rows_per_expert, cudaStream_t s) {
   const bool two = max_rows_per_expert > 8;
-  if (act_dtype == E4B_BF16)
+  if (g.out_dtype == E4B_BF16)
     return two ? launch_one<__nv_bfloat16, 2>(g, s) : launch_one<__nv_bfloat16, 1>(g, s);
   return two ? launch_one<__half, 2>(g, s) : launch_one<__half, 1>(g, s);
 }

@@ -5,7 +5,8 @@
 namespace e4b {
 
 struct GemvArgs {
-  const void* a;             // activations, rows of K elements (act dtype)
+  const void* a;             // activations, rows of K elements, fp16 (see convert.cuh)
+  const float* a_scale;      // nullable: per source row power-of-two scale of `a`
   const int32_t* a_rows;     // nullable: sorted row r reads a[a_rows[r]]
   const uint8_t* packed;     // [E, N, K/2]
   const float* absmax;       // [E, N, K/64]
@@ -14,7 +15,8 @@ struct GemvArgs {
   const int32_t* num_active; // [1]
   int E, N, K;
   int epilogue;              // e4b_epilogue
-  void* out;                 // [R, Nout] act dtype
+  void* out;                 // [R, Nout] out_dtype (bf16 or fp16; fp16 saturates and flags)
+  int out_dtype;
   int Nout;
   const float* lora_xa;      // [R, rank] = scaling * (a_row . A^T), fp32 (nullable)
   const void* lora_B;        // [E, N, rank] (lora_dtype)
@@ -27,6 +29,6 @@ struct GemvArgs {
 // Tokens per expert handled without re-reading the weights.
 constexpr int kGemvMaxCols = 16;
 
-e4b_status launch_gemv(const GemvArgs& g, int act_dtype, int max_rows_per_expert, cudaStream_t s);
+e4b_status launch_gemv(const GemvArgs& g, int max_rows_per_expert, cudaStream_t s);
 
 }  // namespace e4b

@@ -7,6 +7,7 @@
 //   LoRA delta -> weighted fixed-order combine.
 // All launches are stream-ordered on the caller's stream; nothing is allocated.
 #include "common.cuh"
+#include "convert.cuh"
 #include "gemv.cuh"
 #include "lora.cuh"
 #include "permute.cuh"
@@ -15,7 +16,8 @@
 namespace e4b {
 
 struct MoeLayout {
-  size_t offsets, active, num_active, tile_a, tile_b, inv, sorted_token, h, down_rows, xa_gu, xa_dn, umma, total;
+  size_t offsets, active, num_active, tile_a, tile_b, inv, sorted_token, x16, x_scale, h, down_rows, xa_gu, xa_dn,
+      umma, total;
 };
 
 static MoeLayout moe_layout(const e4b_moe_desc& d) {
@@ -36,13 +38,47 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   L.tile_b = take((E + 1) * 4);
   L.inv = take(R * 4);
   L.sorted_token = take(R * 4);
-  L.h = take(R * d.intermediate * es);
+  L.x16 = take((size_t)d.tokens * d.hidden * 2);
+  L.x_scale = take((size_t)d.tokens * 4);
+  L.h = take(R * d.intermediate * 2);
   L.down_rows = take(R * d.hidden * es);
   L.xa_gu = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
   L.xa_dn = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
   L.umma = take(umma_workspace_bytes(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate));
   L.total = o;
   return L;
+}
+
+__global__ void __launch_bounds__(256) convert_kernel(ConvertArgs c) {
+  convert_rows_to_f16(c.src, c.src_dtype, c.dst, c.scale, c.rows, c.K, blockIdx.x * 8 + (threadIdx.x >> 5),
+                      gridDim.x * 8);
+}
+
+// As convert_kernel, but row r of the output is source row rows_map[r].
+__global__ void __launch_bounds__(256) gather_convert_kernel(ConvertArgs c, const int32_t* __restrict__ rows_map) {
+  const int lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < c.rows; r += gridDim.x * 8) {
+    const int64_t src = rows_map[r];
+    float m = 0.f;
+    for (int k = lane; k < c.K; k += 32) m = fmaxf(m, fabsf(load_as_f32(c.src, c.src_dtype, src * c.K + k)));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int sh = 0;
+    if (m > 32768.f) {
+      int ex;
+      frexpf(m / 32768.f, &ex);
+      sh = ex;
+    }
+    const float inv = ldexpf(1.f, -sh);
+    for (int k = lane; k < c.K; k += 32)
+      c.dst[(int64_t)r * c.K + k] = __float2half_rn(load_as_f32(c.src, c.src_dtype, src * c.K + k) * inv);
+    if (lane == 0) c.scale[r] = ldexpf(1.f, sh);
+  }
+}
+
+static int conv_ctas_for(int rows, int warps_per_cta) {
+  int c = (rows + warps_per_cta - 1) / warps_per_cta;
+  return c < 1 ? 1 : (c > 148 * 4 ? 148 * 4 : c);
 }
 
 __global__ void active_from_offsets_kernel(const int32_t* __restrict__ offsets, int E, int32_t* __restrict__ active,
@@ -75,6 +111,7 @@ extern "C" const char* e4b_status_string(e4b_status s) {
     case E4B_ERR_ALIGNMENT: return "pointer not 16-byte aligned";
     case E4B_ERR_CUDA: return "CUDA launch or query failed";
     case E4B_ERR_EXPERT_INDEX: return "top-k expert index outside [0, num_experts)";
+    case E4B_ERR_RANGE: return "an intermediate activation exceeded the fp16 range (+-65504) and was saturated";
   }
   return "unknown status";
 }
@@ -93,11 +130,10 @@ extern "C" e4b_status e4b_read_device_error(void* workspace, void* stream, int* 
 }
 
 extern "C" size_t e4b_grouped_gemm_workspace_bytes(int R, int E, int N, int K) {
-  (void)R;
   (void)N;
-  (void)K;
-  if (E <= 0) return 0;
-  return kErrBytes + align_up((size_t)(E + 1) * 4, 256);
+  if (E <= 0 || R < 0 || K <= 0) return 0;
+  return kErrBytes + align_up((size_t)(E + 1) * 4, 256) + align_up((size_t)R * K * 2, 256) +
+         align_up((size_t)R * 4, 256);
 }
 
 extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int32_t* a_rows, const uint8_t* packed,
@@ -116,11 +152,30 @@ extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int
   char* ws = static_cast<char*>(workspace);
   int32_t* active = reinterpret_cast<int32_t*>(ws + kErrBytes);
   int32_t* num_active = reinterpret_cast<int32_t*>(ws + 4);  // second word of the error block
+  __half* a16 = reinterpret_cast<__half*>(ws + kErrBytes + align_up((size_t)(E + 1) * 4, 256));
+  float* a_scale = reinterpret_cast<float*>(reinterpret_cast<char*>(a16) + align_up((size_t)R * K * 2, 256));
   active_from_offsets_kernel<<<1, 32, 0, s>>>(offsets, E, active, num_active);
   if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
+  // source rows of `a`: R rows, or (with a gather map) up to max(a_rows)+1 -- converted lazily
+  // by converting R rows of the gathered order into a16 and dropping the map.
+  ConvertArgs cv{};
+  cv.src = a;
+  cv.src_dtype = a_dtype;
+  cv.dst = a16;
+  cv.scale = a_scale;
+  cv.rows = R;
+  cv.K = K;
+  if (a_rows) {
+    gather_convert_kernel<<<conv_ctas_for(R, 8), 256, 0, s>>>(cv, a_rows);
+  } else {
+    convert_kernel<<<conv_ctas_for(R, 8), 256, 0, s>>>(cv);
+  }
+  if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
   GemvArgs g{};
-  g.a = a;
-  g.a_rows = a_rows;
+  g.a = a16;
+  g.a_scale = a_scale;
+  g.a_rows = nullptr;
+  g.out_dtype = a_dtype;
   g.packed = packed;
   g.absmax = absmax;
   g.offsets = offsets;
@@ -135,7 +190,7 @@ extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int
   g.tiles_per_expert = epilogue == E4B_EPI_SWIGLU ? N / 16 : N / 16;
   g.max_tasks = (R < E ? R : E) * g.tiles_per_expert;
   g.err = reinterpret_cast<int*>(ws);
-  return launch_gemv(g, a_dtype, R, s);
+  return launch_gemv(g, R, s);
 }
 
 extern "C" size_t e4b_moe_workspace_bytes(const e4b_moe_desc* desc) {
@@ -197,6 +252,15 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   pa.tile_b = kUmmaTokens;
   pa.err = err;
   pa.reset_err = 1;
+  __half* x16 = reinterpret_cast<__half*>(ws + L.x16);
+  float* x_scale = reinterpret_cast<float*>(ws + L.x_scale);
+  pa.conv.src = t->hidden;
+  pa.conv.src_dtype = d.act_dtype;
+  pa.conv.dst = x16;
+  pa.conv.scale = x_scale;
+  pa.conv.rows = T;
+  pa.conv.K = H;
+  pa.conv_ctas = conv_ctas_for(T, 32);
   e4b_status st = launch_permute(pa, s);
   if (st != E4B_OK) return st;
   mark(1);
@@ -228,7 +292,8 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
 
   const bool use_umma = umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype);
   GemvArgs g{};
-  g.a = t->hidden;
+  g.a = x16;
+  g.a_scale = x_scale;
   g.a_rows = pa.sorted_token;
   g.packed = t->gate_up_packed;
   g.absmax = t->gate_up_absmax;
@@ -240,6 +305,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   g.K = H;
   g.epilogue = d.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
   g.out = h;
+  g.out_dtype = E4B_F16;
   g.Nout = I;
   g.lora_xa = d.lora_rank > 0 ? xa_gu : nullptr;
   g.lora_B = t->gate_up_lora_B;
@@ -252,14 +318,14 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
     st = launch_umma(u, d.act_dtype, s);
   } else {
-    st = launch_gemv(g, d.act_dtype, T, s);
+    st = launch_gemv(g, T, s);
   }
   if (st != E4B_OK) return st;
   mark(3);
 
   if (d.lora_rank > 0) {
     LoraAArgs la{};
-    la.a = h;
+    la.a = h;  // fp16
     la.a_rows = nullptr;
     la.loraA = t->down_lora_A;
     la.offsets = pa.offsets;
@@ -271,11 +337,12 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     la.scaling = d.lora_scaling;
     la.xa = xa_dn;
     la.max_tiles = lora_tiles;
-    if ((st = launch_lora_a(la, d.act_dtype, s)) != E4B_OK) return st;
+    if ((st = launch_lora_a(la, E4B_F16, s)) != E4B_OK) return st;
   }
   mark(4);
 
   g.a = h;
+  g.a_scale = nullptr;
   g.a_rows = nullptr;
   g.packed = t->down_packed;
   g.absmax = t->down_absmax;
@@ -283,6 +350,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   g.K = I;
   g.epilogue = E4B_EPI_NONE;
   g.out = down_rows;
+  g.out_dtype = d.act_dtype;
   g.Nout = H;
   g.lora_xa = d.lora_rank > 0 ? xa_dn : nullptr;
   g.lora_B = t->down_lora_B;
@@ -292,7 +360,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
     st = launch_umma(u, d.act_dtype, s);
   } else {
-    st = launch_gemv(g, d.act_dtype, T, s);
+    st = launch_gemv(g, T, s);
   }
   if (st != E4B_OK) return st;
   mark(5);

@@ -39,6 +39,11 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* smem_warp, int* 
 
 __global__ void __launch_bounds__(1024)
 permute_kernel(PermuteArgs a) {
+  if (blockIdx.x > 0) {  // conversion CTAs: one row per warp
+    convert_rows_to_f16(a.conv.src, a.conv.src_dtype, a.conv.dst, a.conv.scale, a.conv.rows, a.conv.K,
+                        (blockIdx.x - 1) * (blockDim.x >> 5) + (threadIdx.x >> 5), a.conv_ctas * (blockDim.x >> 5));
+    return;
+  }
   extern __shared__ int wc[];           // [32][E]
   __shared__ int s_scan[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -134,7 +139,7 @@ e4b_status launch_permute(const PermuteArgs& a, cudaStream_t s) {
     if (cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return E4B_ERR_CUDA;
   }
-  permute_kernel<<<1, 1024, smem, s>>>(a);
+  permute_kernel<<<1 + (a.conv.src ? a.conv_ctas : 0), 1024, smem, s>>>(a);
   return launch_status();
 }
 

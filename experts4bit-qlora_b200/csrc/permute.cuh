@@ -1,6 +1,7 @@
 // Internal launch interface of the permutation kernel (shared with moe.cu).
 #pragma once
 #include "common.cuh"
+#include "convert.cuh"
 
 namespace e4b {
 
@@ -18,6 +19,8 @@ struct PermuteArgs {
   int tile_a, tile_b;
   int* err;                 // device error word
   int reset_err;            // zero *err before validating (first kernel of a call)
+  ConvertArgs conv;         // optional: rows converted to fp16 by CTAs 1.. of the same launch
+  int conv_ctas;
 };
 
 size_t permute_smem_bytes(int E);

@@ -148,3 +148,40 @@ def test_combine_fixed_order(ops, T, k, H):
     got = ops.combine(rows.to(DEV), inv.to(DEV), w.to(DEV), T, k, torch.float32).cpu()
     ref = M.scatter_combine(rows, w[tok, pos], order, T, k, torch.float32)
     torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("K", [128, 2048])
+def test_gemv_matches_fp16_code_model_to_one_ulp(ops, K):
+    """The decode GEMV computes sum_b absmax_b * sum_i fp16(code_i) * fp16(x_i) in fp32; check it
+    against that model (evaluated in fp64) to within one bf16 ulp of the output."""
+    E, NN, m = 2, 256, 5
+    g = torch.Generator().manual_seed(K)
+    w = torch.randn(E, NN, K, generator=g) * 0.05
+    packed, absmax = N.quantize_stack(w)
+    a = torch.randn(E * m, K, generator=g).to(torch.bfloat16)
+    offsets = torch.tensor([0, m, 2 * m], dtype=torch.int32)
+    out = ops.grouped_nf4_gemm(a.to(DEV), packed.view(E, NN, K // 2).to(DEV), absmax.view(E, NN, K // 64).to(DEV),
+                               offsets.to(DEV)).cpu().double()
+    q = torch.from_numpy(N.unpack_nf4(packed.numpy().reshape(-1)).astype(np.int64)).view(E, NN, K)
+    c16 = torch.from_numpy(N.NF4_CODE).to(torch.float16).double()
+    Wm = (c16[q].view(E, NN, K // 64, 64) * absmax.double().view(E, NN, K // 64, 1)).view(E, NN, K)
+    model = torch.cat([a[e * m:(e + 1) * m].double() @ Wm[e].t() for e in range(E)])
+    ulp = (model.abs().float().to(torch.bfloat16).float().double() * 2.0 ** -7).clamp_min(1e-30)
+    assert ((out - model).abs() / ulp).max().item() <= 1.0
+
+
+def test_gemv_rows_beyond_fp16_range_are_scaled_exactly(ops):
+    E, NN, K = 1, 128, 256
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(E, NN, K, generator=g) * 0.05
+    packed, absmax = N.quantize_stack(w)
+    a = torch.randn(3, K, generator=g)
+    a[1] *= 1e6                                 # far beyond fp16's 65504
+    a = a.to(torch.bfloat16)
+    offsets = torch.tensor([0, 3], dtype=torch.int32)
+    out = ops.grouped_nf4_gemm(a.to(DEV), packed.view(E, NN, K // 2).to(DEV), absmax.view(E, NN, K // 64).to(DEV),
+                               offsets.to(DEV)).cpu().float()
+    ref = a.float() @ M.dequant_stack_f32(packed, absmax, (NN, K))[0].t()
+    for r in range(3):
+        mx, mean = M.rel_errors(out[r], ref[r])
+        assert mx <= 1e-2 and mean <= 2e-3, (r, mx, mean)
