@@ -227,7 +227,8 @@ def run_ours(args, wl, world, rank, local):
     value = units / (ms / 1e3)
 
     # --- per-stage kernel times, live, from event nodes inside replayed graphs ----
-    ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(nstage)] for _ in range(Lc)]
+    cudart = _cudart()
+    ev = [[_RawEvent(cudart) for _ in range(nstage)] for _ in range(Lc)]
     gt = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gt):
         step(0, ev)
@@ -237,7 +238,7 @@ def run_ours(args, wl, world, rank, local):
         torch.cuda.synchronize()
         for li in range(Lc):
             for si in range(nstage - 1):
-                stage_ms[si].append(ev[li][si].elapsed_time(ev[li][si + 1]))
+                stage_ms[si].append(ev[li][si].elapsed_ms(ev[li][si + 1]))
     stage_names = ["permute", "lora_a_x", "gate_up", "lora_a_h", "down", "combine"]
     stage_avg_us = {n: 1e3 * statistics.mean(v) for n, v in zip(stage_names, stage_ms)}
 
@@ -274,7 +275,7 @@ def run_ours(args, wl, world, rank, local):
                 "stage_us": {k_: round(v, 3) for k_, v in stage_avg_us.items()}}
 
     # --- e2e through the public API: pinned H2D in, eager calls, D2H out ----------
-    e2e = run_e2e(pkg, layers, wl, dev, args, X)
+    e2e = run_e2e(pkg, layers, wl, dev, args, X) if not args.skip_e2e else {"ms": float("nan"), "h2d": 0, "d2h": 0}
     if world > 1:
         t_ = torch.tensor([e2e["ms"]], device=dev)
         torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
@@ -301,9 +302,41 @@ def run_ours(args, wl, world, rank, local):
         "clocks": clocks.summary(),
         "unique_experts_per_layer": round(mean_uniq, 2),
     }
-    if rank == 0:
+    if rank == 0 and args.cpu_seconds > 0:
         result["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
     return result
+
+
+def _cudart():
+    import ctypes
+    for name in ("/usr/local/cuda/lib64/libcudart.so", "libcudart.so", "libcudart.so.12"):
+        try:
+            return ctypes.CDLL(name)
+        except OSError:
+            continue
+    raise RuntimeError("libcudart not found")
+
+
+class _RawEvent:
+    """A timing cudaEvent_t owned here (torch's Event refuses elapsed_time on events
+    recorded outside torch, e.g. by the library's graph event-record nodes)."""
+
+    def __init__(self, cudart):
+        import ctypes
+        self._rt = cudart
+        h = ctypes.c_void_p()
+        if cudart.cudaEventCreate(ctypes.byref(h)) != 0:
+            raise RuntimeError("cudaEventCreate failed")
+        self.cuda_event = h.value
+
+    def elapsed_ms(self, other):
+        import ctypes
+        out = ctypes.c_float()
+        rc = self._rt.cudaEventElapsedTime(ctypes.byref(out), ctypes.c_void_p(self.cuda_event),
+                                           ctypes.c_void_p(other.cuda_event))
+        if rc != 0:
+            raise RuntimeError(f"cudaEventElapsedTime failed ({rc})")
+        return out.value
 
 
 def _route_idx(pkg, router, x, wl):
@@ -398,9 +431,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="olmoe-decode", choices=sorted(WORKLOADS))
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="0 skips the CPU baseline")
+    ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling)")
+    ap.add_argument("--skip-e2e", action="store_true", help="skip the public-API e2e leg (profiling)")
     args = ap.parse_args()
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.layers:
+        wl["layers"] = args.layers
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         res = run_reference(args, wl, rank)

@@ -31,4 +31,15 @@ constexpr int kGemvMaxCols = 16;
 
 e4b_status launch_gemv(const GemvArgs& g, int max_rows_per_expert, cudaStream_t s);
 
+// Streaming variant (gemv_stream.cu): activation rows [x_rows, K] staged in
+// shared memory, weights streamed by per-warp bulk-copy rings.
+bool gemv_stream_eligible(const GemvArgs& g, int x_rows, int max_rows_per_expert);
+e4b_status launch_gemv_stream(const GemvArgs& g, int x_rows, int max_rows_per_expert, cudaStream_t s);
+
+// Picks the streaming kernel when eligible, else the general one.
+inline e4b_status launch_gemv_auto(const GemvArgs& g, int x_rows, int max_rows_per_expert, cudaStream_t s) {
+  if (gemv_stream_eligible(g, x_rows, max_rows_per_expert)) return launch_gemv_stream(g, x_rows, max_rows_per_expert, s);
+  return launch_gemv(g, max_rows_per_expert, s);
+}
+
 }  // namespace e4b

@@ -24,7 +24,6 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   MoeLayout L{};
   const size_t R = (size_t)d.tokens * d.top_k;
   const size_t E = d.num_experts;
-  const size_t es = 2;  // act dtypes are 16-bit
   size_t o = kErrBytes;
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -41,7 +40,7 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   L.x16 = take((size_t)d.tokens * d.hidden * 2);
   L.x_scale = take((size_t)d.tokens * 4);
   L.h = take(R * d.intermediate * 2);
-  L.down_rows = take(R * d.hidden * es);
+  L.down_rows = take(R * d.hidden * 2);
   L.xa_gu = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
   L.xa_dn = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
   L.umma = take(umma_workspace_bytes(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate));
@@ -112,6 +111,7 @@ extern "C" const char* e4b_status_string(e4b_status s) {
     case E4B_ERR_CUDA: return "CUDA launch or query failed";
     case E4B_ERR_EXPERT_INDEX: return "top-k expert index outside [0, num_experts)";
     case E4B_ERR_RANGE: return "an intermediate activation exceeded the fp16 range (+-65504) and was saturated";
+    case E4B_ERR_TIMEOUT: return "a bounded device wait on an asynchronous copy timed out";
   }
   return "unknown status";
 }
@@ -190,7 +190,7 @@ extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int
   g.tiles_per_expert = epilogue == E4B_EPI_SWIGLU ? N / 16 : N / 16;
   g.max_tasks = (R < E ? R : E) * g.tiles_per_expert;
   g.err = reinterpret_cast<int*>(ws);
-  return launch_gemv(g, R, s);
+  return launch_gemv_auto(g, R, R, s);
 }
 
 extern "C" size_t e4b_moe_workspace_bytes(const e4b_moe_desc* desc) {
@@ -318,7 +318,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
     st = launch_umma(u, d.act_dtype, s);
   } else {
-    st = launch_gemv(g, T, s);
+    st = launch_gemv_auto(g, T, T, s);
   }
   if (st != E4B_OK) return st;
   mark(3);
@@ -350,7 +350,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   g.K = I;
   g.epilogue = E4B_EPI_NONE;
   g.out = down_rows;
-  g.out_dtype = d.act_dtype;
+  g.out_dtype = E4B_F16;  // fp16 rows: one bf16 rounding (the final output) instead of two
   g.Nout = H;
   g.lora_xa = d.lora_rank > 0 ? xa_dn : nullptr;
   g.lora_B = t->down_lora_B;
@@ -360,12 +360,12 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
     st = launch_umma(u, d.act_dtype, s);
   } else {
-    st = launch_gemv(g, T, s);
+    st = launch_gemv_auto(g, R, T, s);
   }
   if (st != E4B_OK) return st;
   mark(5);
 
-  st = e4b_combine(down_rows, d.act_dtype, pa.inv, t->topk_w, d.weight_dtype, T, k, H, t->out, d.out_dtype, stream);
+  st = e4b_combine(down_rows, E4B_F16, pa.inv, t->topk_w, d.weight_dtype, T, k, H, t->out, d.out_dtype, stream);
   mark(6);
   return st;
 }

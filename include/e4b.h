@@ -45,7 +45,8 @@ typedef enum {
   E4B_ERR_ALIGNMENT = 4,      /* a pointer is not 16-byte aligned */
   E4B_ERR_CUDA = 5,           /* a CUDA launch or query failed */
   E4B_ERR_EXPERT_INDEX = 6,   /* device-reported: a top-k index outside [0, E) */
-  E4B_ERR_RANGE = 7           /* device-reported: an intermediate activation beyond +-65504 saturated */
+  E4B_ERR_RANGE = 7,          /* device-reported: an intermediate activation beyond +-65504 saturated */
+  E4B_ERR_TIMEOUT = 8         /* device-reported: a bounded wait on an async copy gave up */
 } e4b_status;
 
 typedef enum { E4B_BF16 = 0, E4B_F16 = 1, E4B_F32 = 2 } e4b_dtype;

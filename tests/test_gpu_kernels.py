@@ -150,10 +150,12 @@ def test_combine_fixed_order(ops, T, k, H):
     torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)
 
 
-@pytest.mark.parametrize("K", [128, 2048])
+@pytest.mark.parametrize("K", [128, 768, 2048])
 def test_gemv_matches_fp16_code_model_to_one_ulp(ops, K):
-    """The decode GEMV computes sum_b absmax_b * sum_i fp16(code_i) * fp16(x_i) in fp32; check it
-    against that model (evaluated in fp64) to within one bf16 ulp of the output."""
+    """The decode GEMV computes sum_b absmax_b * sum_i fp16(code_i) * fp16(x_i) with fp32 tensor-core
+    accumulation; check it against that model (evaluated in fp64) to within one bf16 ulp of the
+    output plus an accumulation floor of 2^-16 of the row's scale (tensor-core fp32 sums are not
+    round-to-nearest, which shows on outputs near zero)."""
     E, NN, m = 2, 256, 5
     g = torch.Generator().manual_seed(K)
     w = torch.randn(E, NN, K, generator=g) * 0.05
@@ -166,8 +168,9 @@ def test_gemv_matches_fp16_code_model_to_one_ulp(ops, K):
     c16 = torch.from_numpy(N.NF4_CODE).to(torch.float16).double()
     Wm = (c16[q].view(E, NN, K // 64, 64) * absmax.double().view(E, NN, K // 64, 1)).view(E, NN, K)
     model = torch.cat([a[e * m:(e + 1) * m].double() @ Wm[e].t() for e in range(E)])
-    ulp = (model.abs().float().to(torch.bfloat16).float().double() * 2.0 ** -7).clamp_min(1e-30)
-    assert ((out - model).abs() / ulp).max().item() <= 1.0
+    ulp = model.abs().float().to(torch.bfloat16).float().double() * 2.0 ** -7
+    floor = 2.0 ** -16 * model.abs().amax(dim=1, keepdim=True)
+    assert ((out - model).abs() <= ulp + floor).all()
 
 
 def test_gemv_rows_beyond_fp16_range_are_scaled_exactly(ops):
