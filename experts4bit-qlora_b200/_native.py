@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
     "e4b_combine",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
+    "e4b_moe_forward_static",
     "e4b_read_device_error",
 )
 
@@ -80,6 +81,7 @@ def _declare(lib):
         "e4b_combine": (I, [P, I, P, P, I, I, I, I, P, I, P]),
         "e4b_moe_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
         "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
+        "e4b_moe_forward_static": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P]),
         "e4b_read_device_error": (I, [P, P, ctypes.POINTER(I)]),
     }
     for name, (res, args) in sig.items():

@@ -46,7 +46,8 @@ typedef enum {
   E4B_ERR_CUDA = 5,           /* a CUDA launch or query failed */
   E4B_ERR_EXPERT_INDEX = 6,   /* device-reported: a top-k index outside [0, E) */
   E4B_ERR_RANGE = 7,          /* device-reported: an intermediate activation beyond +-65504 saturated */
-  E4B_ERR_TIMEOUT = 8         /* device-reported: a bounded wait on an async copy gave up */
+  E4B_ERR_TIMEOUT = 8,        /* device-reported: a bounded wait on an async copy gave up */
+  E4B_ERR_STATIC_SCRATCH = 9  /* layer needs more scratch than e4b_moe_forward_static's fixed array */
 } e4b_status;
 
 typedef enum { E4B_BF16 = 0, E4B_F16 = 1, E4B_F32 = 2 } e4b_dtype;
@@ -181,6 +182,18 @@ typedef struct {
 E4B_API size_t e4b_moe_workspace_bytes(const e4b_moe_desc* desc);
 E4B_API e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tensors* t, void* workspace,
                            size_t workspace_bytes, void* stream);
+
+/* No counterpart in the reference. Same layer as e4b_moe_forward for callers
+ * that cannot allocate device memory (a host framework that owns all device
+ * allocations, a plugin host that forbids cudaMalloc after start-up): the
+ * scratch is a fixed library-owned device array of E4B_STATIC_SCRATCH_BYTES
+ * held on every GPU that loads the library. Layers needing more
+ * (e4b_moe_workspace_bytes) are refused with E4B_ERR_STATIC_SCRATCH. The first
+ * call on a device looks up the array's address and should come before any
+ * stream capture there. All calls on a device share the array: calls that
+ * overlap on the GPU race. Allocates nothing. */
+#define E4B_STATIC_SCRATCH_BYTES (16u << 20)
+E4B_API e4b_status e4b_moe_forward_static(const e4b_moe_desc* desc, const e4b_moe_tensors* t, void* stream);
 
 /* Reads (and clears) the device error word of a workspace used by the calls
  * above. Synchronises `stream`; for debugging and tests, not the hot path. */
