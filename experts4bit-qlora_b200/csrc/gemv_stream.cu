@@ -2,48 +2,83 @@
 //
 // Same arithmetic as gemv.cu (fp16 code pairs from a lane-replicated table,
 // mma.sync m16n8k16 with the activations as the n8 operand, fp32 per-block
-// absmax scaling), organised for HBM bandwidth:
+// absmax scaling), organised for HBM bandwidth and short dependency chains:
 //  * one persistent CTA per SM builds the pair table once (32 KB: entry e of
 //    lane l at (e << 7) | (l << 2), so no two lanes of a warp share a bank) and
 //    stages the layer's activation rows in shared memory once;
-//  * each of the 8 warps owns whole 16-row weight tiles (full K, no cross-warp
-//    reduction) and streams them in 512-element chunks through its own
-//    3-slot ring: lanes 0-15 bulk-copy one weight row each, lanes 16-31 the
-//    matching absmax rows, completion tracked by one mbarrier per slot. Up to
-//    3 x 4.6 KB are in flight per warp, ~100 KB per SM, independent of the
-//    register file;
-//  * shared-memory rows are padded (weights 288 B, absmax 48 B, activations
-//    2K+16 B) so every fragment read is bank-conflict free.
+//  * the CTA's 16 warps form 8 pairs; a pair owns whole 16-row weight tiles
+//    (full K) and streams them in 512-element chunks through its own 3-slot
+//    ring, each warp of the pair taking half of every chunk's blocks and the
+//    two halves summed through shared memory once per tile (fixed order). A
+//    chunk is four TMA tile loads completing on one mbarrier: for each
+//    8-row group, a 3-D box {128 B, 2 lines, 8 rows} of packed bytes with
+//    128-byte swizzle, and a 2-D box {8 floats, 8 rows} of absmax. Because row
+//    r of a group lands on shared-memory line 2r + c, the swizzle spreads the
+//    eight rows of a half-warp over all banks: the fragment reads are
+//    conflict free;
+//  * a warp's four blocks of a chunk are unrolled with all packed words loaded
+//    first, so the table lookups of different blocks overlap; a table address
+//    is one shift and one lop3.
 // Waits are bounded; a timed-out wait reports E4B_ERR_TIMEOUT and the warp
 // drains its in-flight copies (again bounded) before leaving.
 #include "async.cuh"
 #include "gemv.cuh"
+#include "tmap.cuh"
+
+// Profiling instrumentation, compiled only with -DE4B_TRACE: per-warp %globaltimer
+// stamps at phase boundaries, read back with e4b_trace_read.
+#ifdef E4B_TRACE
+__device__ unsigned long long g_trace[148 * 8 * 8];
+extern "C" __attribute__((visibility("default"))) int e4b_trace_read(unsigned long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, g_trace, n * sizeof(unsigned long long));
+}
+#define TRACE(i)                                                     \
+  if (lane == 0 && (warp & 1) == 0 && blockIdx.x < 148) {            \
+    unsigned long long t_;                                           \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));          \
+    g_trace[(blockIdx.x * 8 + (warp >> 1)) * 8 + (i)] = t_;          \
+  }
+#else
+#define TRACE(i)
+#endif
 
 namespace e4b {
 
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kPairs = 8;                   // warp pairs per CTA
+constexpr int kWarps = 2 * kPairs;
 constexpr int kThreads = kWarps * 32;
 constexpr int kSlots = 3;
-constexpr int kChunk = 512;                            // K elements per chunk
-constexpr int kWPitch = kChunk / 2 + 32;               // 288 B per weight row (== 32 mod 128)
-constexpr int kAPitch = 48;                            // absmax row: 8 floats + pad (bank spread)
-constexpr int kSlotBytes = 16 * kWPitch + 16 * kAPitch;  // 5376
-constexpr int kLut = 256 * 128;                        // 32 KB pair table
-constexpr int kXBudget = 64 * 1024;                    // activation rows staged per CTA
+constexpr int kChunk = 512;                 // K elements per chunk = 2 lines of 128 B per row
+constexpr int kBoxW = 8 * 2 * 128;          // one 8-row group of packed bytes
+constexpr int kBoxA = 8 * 8 * 4;            // one 8-row group of absmax (8 blocks)
+constexpr int kSlotBytes = 5120;            // 2 x kBoxW + 2 x kBoxA, padded to keep 1024-B alignment
+constexpr uint32_t kItemTx = 2 * kBoxW + 2 * kBoxA;
+constexpr int kLut = 256 * 128;             // 32 KB pair table
+constexpr int kXBudget = 64 * 1024;         // activation rows staged per CTA
+constexpr int kXRegs = kXBudget / 16 / kThreads;  // 16-byte activation vectors per thread
 
 struct Smem {
   static constexpr int lut = 0;
   static constexpr int x = kLut;
-  static constexpr int slots = kLut + kXBudget;
-  static constexpr int bars = slots + kWarps * kSlots * kSlotBytes;
-  static constexpr int total = bars + kWarps * kSlots * 8;
+  static constexpr int slots = kLut + kXBudget;  // 96 KB: 1024-aligned for the swizzled boxes
+  static constexpr int red = slots + kPairs * kSlots * kSlotBytes;
+  static constexpr int bars = red + kPairs * 32 * 8 * 4;
+  static constexpr int total = bars + kPairs * kSlots * 8;
 };
 
-__device__ __forceinline__ uint32_t lut2(const char* lut, uint32_t word, int pos, uint32_t lane4) {
-  const uint32_t byte = (word >> (8 * pos)) & 0xffu;
-  return *reinterpret_cast<const uint32_t*>(lut + ((byte << 7) | lane4));
+// Table entry address of byte POS of `word` for this lane: ((byte << 7) | lane4).
+template <int POS>
+__device__ __forceinline__ uint32_t lut_addr(uint32_t word, uint32_t lane4) {
+  const uint32_t sh = POS == 0 ? (word << 7) : (word >> (8 * POS - 7));
+  uint32_t a;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(a) : "r"(sh), "r"(0x7F80u), "r"(lane4));  // (sh & m) | lane4
+  return a;
+}
+template <int POS>
+__device__ __forceinline__ uint32_t lut2(const char* lut, uint32_t word, uint32_t lane4) {
+  return *reinterpret_cast<const uint32_t*>(lut + lut_addr<POS>(word, lane4));
 }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -53,172 +88,236 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void mma16816_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 struct Tile {
   int e, row0, M, tile;
 };
 
-__device__ __forceinline__ bool tile_of(const GemvArgs& g, int t, int num_active, Tile& out) {
+__device__ __forceinline__ void tile_of(const GemvArgs& g, int t, Tile& out) {
   const int j = t / g.tiles_per_expert;
-  if (t >= g.max_tasks || j >= num_active) return false;
   out.tile = t - j * g.tiles_per_expert;
   out.e = g.active[j];
   out.row0 = g.offsets[out.e];
   out.M = g.offsets[out.e + 1] - out.row0;
-  return true;
 }
 
-// MMA row r (0..15) of a tile -> weight row.
-__device__ __forceinline__ int weight_row(const GemvArgs& g, int tile, int r) {
-  if (g.epilogue == E4B_EPI_SWIGLU) return r < 8 ? tile * 8 + r : (g.N >> 1) + tile * 8 + (r - 8);
-  return tile * 16 + r;
+// First weight row of 8-row group h (0: MMA rows 0-7, 1: MMA rows 8-15) of a tile.
+__device__ __forceinline__ int group_row(const GemvArgs& g, int tile, int h) {
+  if (g.epilogue == E4B_EPI_SWIGLU) return h == 0 ? tile * 8 : (g.N >> 1) + tile * 8;
+  return tile * 16 + 8 * h;
+}
+
+// Byte offset of lane (row r of the group, quad lane q) 8-byte piece of block b in a
+// 128-byte-swizzled box whose shared address is `box`. The swizzle XORs the 16-byte
+// unit index with bits 7-9 of the shared address, so it is computed from the address.
+__device__ __forceinline__ int wofs(uint32_t box, int r, int q, int b) {
+  const int line = 2 * r + (b >> 2);  // a 128-byte line holds four 32-byte blocks
+  const int unit = (((b & 3) << 1) | (q >> 1)) ^ (((box >> 7) + line) & 7);
+  return line * 128 + (unit << 4) + ((q & 1) << 3);
 }
 
 }  // namespace
 
 template <typename OutT, int NT>
-__global__ void __launch_bounds__(kThreads, 1) nf4_gemv_stream_kernel(GemvArgs g, int x_rows) {
-  extern __shared__ __align__(128) char smem[];
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_gemv_stream_kernel(GemvArgs g, int x_rows, const __grid_constant__ CUtensorMap wmap,
+                           const __grid_constant__ CUtensorMap amap) {
+  extern __shared__ __align__(1024) char smem[];
   char* lut = smem + Smem::lut;
   __half* xs = reinterpret_cast<__half*>(smem + Smem::x);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int pair = warp >> 1, member = warp & 1;
   const int gq = lane >> 2, q = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
   const int K = g.K;
   const int xpitch = K + 8;  // halves: 2K + 16 bytes
-  char* myslots = smem + Smem::slots + warp * kSlots * kSlotBytes;
-  uint64_t* mybars = reinterpret_cast<uint64_t*>(smem + Smem::bars) + warp * kSlots;
+  char* myslots = smem + Smem::slots + pair * kSlots * kSlotBytes;
+  float* red = reinterpret_cast<float*>(smem + Smem::red) + pair * 32 * 8;
+  uint64_t* mybars = reinterpret_cast<uint64_t*>(smem + Smem::bars) + pair * kSlots;
+  const bool leader = member == 0 && lane == 0;  // issues this pair's copies
 
-  if (lane == 0)
+  TRACE(0);
+  // activation rows into registers first: their latency overlaps everything below
+  const __half* A = reinterpret_cast<const __half*>(g.a);
+  const int xvec = x_rows * (K / 8);
+  uint4 xr[kXRegs];
+#pragma unroll
+  for (int i = 0; i < kXRegs; ++i) {
+    const int v = threadIdx.x + i * kThreads;
+    if (v < xvec) {
+      const int r = v / (K / 8), c8 = v - r * (K / 8);
+      xr[i] = *reinterpret_cast<const uint4*>(A + (int64_t)r * K + c8 * 8);
+    }
+  }
+  if (leader) {
     for (int s = 0; s < kSlots; ++s) mbar_init(&mybars[s], 1);
-  fence_proxy_async();
-  __syncwarp();
+    fence_proxy_async();
+  }
 
   const int num_active = *g.num_active;
-  const int nwarps = gridDim.x * kWarps;
+  const int npairs = gridDim.x * kPairs;
   const int chunks = (K + kChunk - 1) / kChunk;
+  const int gp = blockIdx.x * kPairs + pair;
+  // items of this pair in closed form: tiles gp, gp + npairs, ... below the limit, x chunks
+  const int limit = min(g.max_tasks, num_active * g.tiles_per_expert);
+  const int total_items = (limit > gp ? (limit - gp + npairs - 1) / npairs : 0) * chunks;
 
-  // item n of this warp = (tile index n / chunks, chunk n % chunks)
-  auto issue = [&](int n) {
-    Tile tl;
-    if (!tile_of(g, blockIdx.x * kWarps + warp + (n / chunks) * nwarps, num_active, tl)) return;
+  auto issue = [&](int n) {  // leader only
+    const int t = gp + (n / chunks) * npairs;
+    const int j = t / g.tiles_per_expert;
+    const int tile = t - j * g.tiles_per_expert;
+    const int rowbase = g.active[j] * g.N;
     const int c = n % chunks;
-    const int kc = min(kChunk, K - c * kChunk);
-    const int s = n % kSlots;
-    char* slot = myslots + s * kSlotBytes;
-    if (lane == 0) mbar_arrive_expect_tx(&mybars[s], 16u * (kc / 2) + 16u * (kc / 16));
-    __syncwarp();
-    const int r = lane & 15;
-    const int64_t wrow = (int64_t)tl.e * g.N + weight_row(g, tl.tile, r);
-    if (lane < 16) {
-      bulk_g2s(slot + r * kWPitch, g.packed + wrow * (K / 2) + c * (kChunk / 2), kc / 2, &mybars[s]);
-    } else {
-      bulk_g2s(slot + 16 * kWPitch + r * kAPitch, g.absmax + wrow * (K / 64) + c * (kChunk / 64), kc / 16,
-               &mybars[s]);
+    char* slot = myslots + (n % kSlots) * kSlotBytes;
+    uint64_t* bar = &mybars[n % kSlots];
+    mbar_arrive_expect_tx(bar, kItemTx);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r0 = rowbase + group_row(g, tile, h);
+      tma_load_3d(slot + h * kBoxW, &wmap, 0, 2 * c, r0, bar);
+      tma_load_2d(slot + 2 * kBoxW + h * kBoxA, &amap, 8 * c, r0, bar);
     }
   };
 
-  // Prefetch the first items before the shared tables are built.
-  int total_items = 0;
-  {
-    Tile tl;
-    int tiles = 0;
-    while (tile_of(g, blockIdx.x * kWarps + warp + tiles * nwarps, num_active, tl)) ++tiles;
-    total_items = tiles * chunks;
-  }
-  for (int n = 0; n < kSlots && n < total_items; ++n) issue(n);
+  TRACE(1);
+  if (leader)
+    for (int n = 0; n < kSlots && n < total_items; ++n) issue(n);
+  TRACE(2);
+  Tile tl;
+  if (total_items > 0) tile_of(g, gp, tl);
 
-  // Pair table and activation rows (all threads).
-  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-    const int e = i >> 5, l = i & 31;
-    reinterpret_cast<uint32_t*>(lut)[e * 32 + l] = pack2<__half>(c_nf4[e >> 4], c_nf4[e & 15]);
-  }
+  // Pair table (warp shuffles of the 16 codes), then the activation rows.
   {
-    const __half* A = reinterpret_cast<const __half*>(g.a);
-    const int vec = K / 8;
-    for (int i = threadIdx.x; i < x_rows * vec; i += blockDim.x) {
-      const int r = i / vec, v = i - r * vec;
-      *reinterpret_cast<uint4*>(xs + r * xpitch + v * 8) =
-          *reinterpret_cast<const uint4*>(A + (int64_t)r * K + v * 8);
+    const float code = c_nf4[lane & 15];
+#pragma unroll 4
+    for (int e = warp; e < 256; e += kWarps) {
+      const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
+      reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
+    }
+#pragma unroll
+    for (int i = 0; i < kXRegs; ++i) {
+      const int v = threadIdx.x + i * kThreads;
+      if (v < xvec) {
+        const int r = v / (K / 8), c8 = v - r * (K / 8);
+        *reinterpret_cast<uint4*>(xs + r * xpitch + c8 * 8) = xr[i];
+      }
     }
   }
   __syncthreads();
+  TRACE(3);
 
   float acc[NT][4];
-  bool ok = true;
+  bool dead = false;  // a wait timed out: stop computing but keep the pair's barriers matched
   for (int n = 0; n < total_items; ++n) {
     const int c = n % chunks;
-    Tile tl;
-    tile_of(g, blockIdx.x * kWarps + warp + (n / chunks) * nwarps, num_active, tl);
     if (c == 0) {
+      if (n > 0) tile_of(g, gp + (n / chunks) * npairs, tl);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
     }
     const int s = n % kSlots;
-    if (!mbar_wait(&mybars[s], (n / kSlots) & 1)) {
+    if (!dead && !mbar_wait(&mybars[s], (n / kSlots) & 1)) {
       raise_error(g.err, E4B_ERR_TIMEOUT);
-      // drain: items n .. n+kSlots-1 may still be in flight; wait for them (bounded) before leaving
-      for (int m = n; m < n + kSlots && m < total_items; ++m) (void)mbar_wait(&mybars[m % kSlots], (m / kSlots) & 1);
-      ok = false;
-      break;
+      dead = true;
     }
-    const char* slot = myslots + s * kSlotBytes;
-    const int kc = min(kChunk, K - c * kChunk);
-    // token rows of this tile's n8 column tiles (tokens >= M read row 0 and are discarded)
-    const __half* xrow[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int m = nt * 8 + gq;
-      int src = 0;
-      if (m < tl.M) src = g.a_rows ? g.a_rows[tl.row0 + m] : tl.row0 + m;
-      xrow[nt] = xs + src * xpitch + c * kChunk + q * 16;
-    }
-#pragma unroll 2
-    for (int b = 0; b < kc / 64; ++b) {
-      const uint2 wa = *reinterpret_cast<const uint2*>(slot + gq * kWPitch + b * 32 + q * 8);
-      const uint2 wb = *reinterpret_cast<const uint2*>(slot + (gq + 8) * kWPitch + b * 32 + q * 8);
-      const float sa = *reinterpret_cast<const float*>(slot + 16 * kWPitch + gq * kAPitch + b * 4);
-      const float sb = *reinterpret_cast<const float*>(slot + 16 * kWPitch + (gq + 8) * kAPitch + b * 4);
-      uint4 xf[NT][2];
+    if (n == 0) TRACE(4);
+    if (!dead) {
+      const char* slot = myslots + s * kSlotBytes;
+      const int nb = min(kChunk, K - c * kChunk) / 64;
+      // token rows of this tile's n8 column tiles (tokens >= M read row 0 and are discarded)
+      const __half* xrow[NT];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        xf[nt][0] = *reinterpret_cast<const uint4*>(xrow[nt] + b * 64);
-        xf[nt][1] = *reinterpret_cast<const uint4*>(xrow[nt] + b * 64 + 8);
+        const int m = nt * 8 + gq;
+        int src = 0;
+        if (m < tl.M) src = g.a_rows ? g.a_rows[tl.row0 + m] : tl.row0 + m;
+        xrow[nt] = xs + src * xpitch + c * kChunk + q * 16;
       }
-      float p[NT][4];
+      // this member's blocks of the chunk: b = 4 * member + i (absmax floats 4*member..+3)
+      const float4 sa4 = reinterpret_cast<const float4*>(slot + 2 * kBoxW + gq * 32)[member];
+      const float4 sb4 = reinterpret_cast<const float4*>(slot + 2 * kBoxW + kBoxA + gq * 32)[member];
+      const float sa[4] = {sa4.x, sa4.y, sa4.z, sa4.w}, sb[4] = {sb4.x, sb4.y, sb4.z, sb4.w};
+      uint2 wa[4], wb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int b = 4 * member + i;
+        wa[i] = *reinterpret_cast<const uint2*>(slot + wofs(smem_u32(slot), gq, q, b));
+        wb[i] = *reinterpret_cast<const uint2*>(slot + kBoxW + wofs(smem_u32(slot + kBoxW), gq, q, b));
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int b = 4 * member + i;
+        if (b >= nb) break;
+        uint4 xf[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          xf[nt][0] = *reinterpret_cast<const uint4*>(xrow[nt] + b * 64);
+          xf[nt][1] = *reinterpret_cast<const uint4*>(xrow[nt] + b * 64 + 8);
+        }
+        float p[NT][4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint32_t w0 = jj < 2 ? wa[i].x : wa[i].y, w1 = jj < 2 ? wb[i].x : wb[i].y;
+          uint32_t a0, a1, a2, a3;
+          if (jj & 1) {
+            a0 = lut2<2>(lut, w0, lane4); a2 = lut2<3>(lut, w0, lane4);
+            a1 = lut2<2>(lut, w1, lane4); a3 = lut2<3>(lut, w1, lane4);
+          } else {
+            a0 = lut2<0>(lut, w0, lane4); a2 = lut2<1>(lut, w0, lane4);
+            a1 = lut2<0>(lut, w1, lane4); a3 = lut2<1>(lut, w1, lane4);
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xf[nt][jj >> 1]);
+            if (jj == 0)
+              mma16816_zero(p[nt], a0, a1, a2, a3, xw[0], xw[1]);
+            else
+              mma16816(p[nt], a0, a1, a2, a3, xw[(jj & 1) * 2], xw[(jj & 1) * 2 + 1]);
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          acc[nt][0] = fmaf(p[nt][0], sa[i], acc[nt][0]);
+          acc[nt][1] = fmaf(p[nt][1], sa[i], acc[nt][1]);
+          acc[nt][2] = fmaf(p[nt][2], sb[i], acc[nt][2]);
+          acc[nt][3] = fmaf(p[nt][3], sb[i], acc[nt][3]);
+        }
+      }
+    }
+    const bool last = c == chunks - 1;
+    if (last && member == 1) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) p[nt][r] = 0.f;
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const uint32_t w0 = jj < 2 ? wa.x : wa.y, w1 = jj < 2 ? wb.x : wb.y;
-        const int p0 = (jj & 1) * 2;
-        const uint32_t a0 = lut2(lut, w0, p0, lane4), a2 = lut2(lut, w0, p0 + 1, lane4);
-        const uint32_t a1 = lut2(lut, w1, p0, lane4), a3 = lut2(lut, w1, p0 + 1, lane4);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xf[nt][jj >> 1]);
-          mma16816(p[nt], a0, a1, a2, a3, xw[(jj & 1) * 2], xw[(jj & 1) * 2 + 1]);
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        acc[nt][0] = fmaf(p[nt][0], sa, acc[nt][0]);
-        acc[nt][1] = fmaf(p[nt][1], sa, acc[nt][1]);
-        acc[nt][2] = fmaf(p[nt][2], sb, acc[nt][2]);
-        acc[nt][3] = fmaf(p[nt][3], sb, acc[nt][3]);
-      }
+        for (int r = 0; r < 4; ++r) red[(nt * 4 + r) * 32 + lane] = acc[nt][r];
     }
-    // slot consumed: hand it back to the copy engine, refill with item n + kSlots
+    // both members are done with the slot (and member 1's partial sums are written)
     fence_proxy_async();
-    __syncwarp();
-    if (n + kSlots < total_items) issue(n + kSlots);
+    named_barrier(1 + pair, 64);
+    if (n == 0) TRACE(5);
+    if (leader && !dead && n + kSlots < total_items) issue(n + kSlots);
+    if (n == 0) TRACE(7);
 
-    if (c == chunks - 1) {  // epilogue of the tile
-      const int rA = weight_row(g, tl.tile, gq), rB = weight_row(g, tl.tile, gq + 8);
+    if (last && member == 0 && !dead) {  // epilogue of the tile
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[nt][r] += red[(nt * 4 + r) * 32 + lane];
+      const int rA = group_row(g, tl.tile, 0) + gq, rB = group_row(g, tl.tile, 1) + gq;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -253,12 +352,17 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_gemv_stream_kernel(GemvArgs g
         }
     }
   }
-  (void)ok;
+  if (dead && leader) {
+    // drain (bounded) whatever may still be in flight before the CTA's shared memory goes away
+    for (int m = 0; m < total_items && m < kSlots; ++m) (void)mbar_wait(&mybars[m], 0);
+  }
+  TRACE(6);
 }
 
 bool gemv_stream_eligible(const GemvArgs& g, int x_rows, int max_rows_per_expert) {
   return g.K % 256 == 0 && max_rows_per_expert <= 16 && (int64_t)x_rows * (g.K + 8) * 2 <= kXBudget &&
-         g.epilogue >= E4B_EPI_NONE && g.epilogue <= E4B_EPI_SILU;
+         g.epilogue >= E4B_EPI_NONE && g.epilogue <= E4B_EPI_SILU && (int64_t)g.E * g.N < (1ll << 31) &&
+         encode_tiled_fn() != nullptr;
 }
 
 template <typename OutT, int NT>
@@ -276,10 +380,24 @@ static e4b_status launch_stream_one(const GemvArgs& g, int x_rows, cudaStream_t 
     configured |= bit;
   }
   int grid = sm_count[dev & 63];
-  const int need = (g.max_tasks + kWarps - 1) / kWarps;
+  const int need = (g.max_tasks + kPairs - 1) / kPairs;
   if (need < grid) grid = need;
   if (grid < 1) return E4B_OK;
-  nf4_gemv_stream_kernel<OutT, NT><<<grid, kThreads, Smem::total, s>>>(g, x_rows);
+  // packed bytes as [rows][K/256 lines][128 B]; absmax as [rows][K/64]
+  const cuuint64_t rows = (cuuint64_t)g.E * g.N;
+  CUtensorMap wmap, amap;
+  const cuuint64_t wdims[3] = {128, (cuuint64_t)(g.K / 256), rows};
+  const cuuint64_t wstr[2] = {128, (cuuint64_t)(g.K / 2)};
+  const cuuint32_t wbox[3] = {128, 2, 8};
+  const cuuint64_t adims[2] = {(cuuint64_t)(g.K / 64), rows};
+  const cuuint64_t astr[1] = {(cuuint64_t)(g.K / 64) * 4};
+  const cuuint32_t abox[2] = {8, 8};
+  if (!encode_tiled(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, g.packed, wdims, wstr, wbox,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tiled(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, g.absmax, adims, astr, abox,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+    return E4B_ERR_CUDA;
+  nf4_gemv_stream_kernel<OutT, NT><<<grid, kThreads, Smem::total, s>>>(g, x_rows, wmap, amap);
   return launch_status();
 }
 
