@@ -6,22 +6,39 @@
 
 namespace e4b {
 
+constexpr int kMaxK = 32;
+
 template <typename TR, typename TO>
 __global__ void __launch_bounds__(256) combine_kernel(const TR* __restrict__ rows, const int32_t* __restrict__ inv,
                                                       const void* __restrict__ w, int w_dtype, int k, int H,
                                                       TO* __restrict__ out) {
+  // the token's k (row, weight) pairs first, then every row load at once: two
+  // dependent memory round trips per token instead of one per slot
+  __shared__ int64_t s_row[kMaxK];
+  __shared__ float s_w[kMaxK];
   const int t = blockIdx.x;
+  if (threadIdx.x < k) {
+    s_row[threadIdx.x] = (int64_t)inv[(int64_t)t * k + threadIdx.x] * H;
+    s_w[threadIdx.x] = load_as_f32(w, w_dtype, (int64_t)t * k + threadIdx.x);
+  }
+  __syncthreads();
   for (int h = threadIdx.x * 8; h < H; h += blockDim.x * 8) {
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int s = 0; s < k; ++s) {
-      const int64_t r = inv[(int64_t)t * k + s];
-      const float ws = load_as_f32(w, w_dtype, (int64_t)t * k + s);
-      const uint4 v = *reinterpret_cast<const uint4*>(rows + r * H + h);
-      const TR* vv = reinterpret_cast<const TR*>(&v);
+    for (int s0 = 0; s0 < k; s0 += 8) {
+      uint4 v[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(to_f32(vv[i]), ws, acc[i]);
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < k) v[u] = *reinterpret_cast<const uint4*>(rows + s_row[s0 + u] + h);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + u >= k) break;
+        const TR* vv = reinterpret_cast<const TR*>(&v[u]);
+        const float ws = s_w[s0 + u];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(to_f32(vv[i]), ws, acc[i]);  // slot order
+      }
     }
     TO o[8];
 #pragma unroll
@@ -52,7 +69,7 @@ using namespace e4b;
 
 extern "C" e4b_status e4b_combine(const void* rows, int rows_dtype, const int32_t* inv, const void* w, int w_dtype,
                                   int T, int k, int H, void* out, int out_dtype, void* stream) {
-  if (T < 0 || k <= 0 || H <= 0) return E4B_ERR_INVALID_ARG;
+  if (T < 0 || k <= 0 || k > kMaxK || H <= 0) return E4B_ERR_INVALID_ARG;
   if (!is_act_dtype(rows_dtype) || !is_any_dtype(w_dtype) || !is_any_dtype(out_dtype) || H % 8)
     return E4B_ERR_UNSUPPORTED;
   if (T == 0) return E4B_OK;

@@ -55,23 +55,10 @@ __global__ void __launch_bounds__(256) convert_kernel(ConvertArgs c) {
 
 // As convert_kernel, but row r of the output is source row rows_map[r].
 __global__ void __launch_bounds__(256) gather_convert_kernel(ConvertArgs c, const int32_t* __restrict__ rows_map) {
-  const int lane = threadIdx.x & 31;
   for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < c.rows; r += gridDim.x * 8) {
     const int64_t src = rows_map[r];
-    float m = 0.f;
-    for (int k = lane; k < c.K; k += 32) m = fmaxf(m, fabsf(load_as_f32(c.src, c.src_dtype, src * c.K + k)));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    int sh = 0;
-    if (m > 32768.f) {
-      int ex;
-      frexpf(m / 32768.f, &ex);
-      sh = ex;
-    }
-    const float inv = ldexpf(1.f, -sh);
-    for (int k = lane; k < c.K; k += 32)
-      c.dst[(int64_t)r * c.K + k] = __float2half_rn(load_as_f32(c.src, c.src_dtype, src * c.K + k) * inv);
-    if (lane == 0) c.scale[r] = ldexpf(1.f, sh);
+    convert_rows_to_f16(reinterpret_cast<const char*>(c.src) + src * c.K * 2, c.src_dtype, c.dst + (int64_t)r * c.K,
+                        c.scale + r, 1, c.K, 0, 1);
   }
 }
 
@@ -92,7 +79,7 @@ __global__ void active_from_offsets_kernel(const int32_t* __restrict__ offsets, 
 
 static bool desc_ok(const e4b_moe_desc& d) {
   if (d.num_experts <= 0 || d.num_experts > 1024 || d.hidden <= 0 || d.intermediate <= 0) return false;
-  if (d.top_k <= 0 || d.top_k > d.num_experts || d.tokens < 0) return false;
+  if (d.top_k <= 0 || d.top_k > 32 || d.top_k > d.num_experts || d.tokens < 0) return false;
   if ((int64_t)d.tokens * d.top_k > (1 << 30)) return false;
   return true;
 }

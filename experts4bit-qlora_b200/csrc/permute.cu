@@ -37,11 +37,75 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* smem_warp, int* 
   return before;
 }
 
+// Whole permutation in one warp when T*k <= 32 (decode): lane i holds flat entry i;
+// ranks, counts, offsets and the active list come from shuffles, with no block
+// barriers and no shared memory.
+__device__ void permute_one_warp(const PermuteArgs& a) {
+  const int lane = threadIdx.x & 31;
+  const int E = a.E, n = a.T * a.k;
+  if (a.reset_err && lane == 0 && a.err) *a.err = 0;
+  __syncwarp();
+  int e = 0x7fffffff;
+  if (lane < n) {
+    const int64_t raw = a.topk_idx[lane];
+    e = (int)raw;
+    if (raw < 0 || raw >= E) {
+      raise_error(a.err, E4B_ERR_EXPERT_INDEX);
+      e = raw < 0 ? 0 : E - 1;
+    }
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const bool valid = lane < n;
+  const bool lead = valid && (peers & ((1u << lane) - 1u)) == 0;  // first entry of its expert
+  const int cnt = __popc(peers);
+  int below = 0, distinct_below = 0;  // entries / experts with a smaller id
+  for (int j = 0; j < n; ++j) {
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    below += ej < e;
+  }
+  const unsigned leaders = __ballot_sync(0xffffffffu, lead);
+  for (int j = 0; j < n; ++j) {
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    distinct_below += ((leaders >> j) & 1u) && ej < e;
+  }
+  if (valid) {
+    const int pos = below + __popc(peers & ((1u << lane) - 1u));
+    if (a.order) a.order[pos] = lane;
+    if (a.inv) a.inv[lane] = pos;
+    if (a.sorted_token) a.sorted_token[pos] = lane / a.k;
+    if (lead && a.active) a.active[distinct_below] = e;
+  }
+  if (lane == 0 && a.num_active) *a.num_active = __popc(leaders);
+  // per-expert prefix arrays over all E experts
+  for (int x0 = 0; x0 <= E; x0 += 32) {  // warp-uniform trip count: every shuffle has all lanes
+    const int x = x0 + lane;
+    int off = 0, ta = 0, tb = 0;
+    for (int j = 0; j < 32; ++j) {
+      const int ej = __shfl_sync(0xffffffffu, e, j);
+      const int cj = __shfl_sync(0xffffffffu, cnt, j);
+      off += (j < n) && ej < x;
+      if (((leaders >> j) & 1u) && ej < x) {
+        ta += (cj + a.tile_a - 1) / max(a.tile_a, 1);
+        tb += (cj + a.tile_b - 1) / max(a.tile_b, 1);
+      }
+    }
+    if (x <= E) {
+      a.offsets[x] = off;
+      if (a.tile_start_a) a.tile_start_a[x] = ta;
+      if (a.tile_start_b) a.tile_start_b[x] = tb;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(1024)
 permute_kernel(PermuteArgs a) {
   if (blockIdx.x > 0) {  // conversion CTAs: one row per warp
     convert_rows_to_f16(a.conv.src, a.conv.src_dtype, a.conv.dst, a.conv.scale, a.conv.rows, a.conv.K,
                         (blockIdx.x - 1) * (blockDim.x >> 5) + (threadIdx.x >> 5), a.conv_ctas * (blockDim.x >> 5));
+    return;
+  }
+  if (a.T * a.k <= 32) {
+    if (threadIdx.x < 32) permute_one_warp(a);
     return;
   }
   extern __shared__ int wc[];           // [32][E]

@@ -44,16 +44,29 @@ router_logits_kernel(const void* __restrict__ x, int x_dtype, const void* __rest
   float acc[kRouterTT];
 #pragma unroll
   for (int j = 0; j < kRouterTT; ++j) acc[j] = 0.f;
-  for (int h = lane * 8; h < H; h += 256) {
-    float wv[8];
-    load8_f32(wr, w_dtype, (int64_t)e * H + h, wv);
+  for (int h0 = 0; h0 < H; h0 += 256 * 4) {  // four 256-element strips per lane in flight
+    float wv[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int h = h0 + u * 256 + lane * 8;
+      if (h < H) load8_f32(wr, w_dtype, (int64_t)e * H + h, wv[u]);
+    }
 #pragma unroll
     for (int j = 0; j < kRouterTT; ++j) {
       if (t0 + j < T) {
-        float xv[8];
-        load8_f32(x, x_dtype, (int64_t)(t0 + j) * H + h, xv);
+        float xv[4][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[j] = fmaf(xv[i], wv[i], acc[j]);
+        for (int u = 0; u < 4; ++u) {
+          const int h = h0 + u * 256 + lane * 8;
+          if (h < H) load8_f32(x, x_dtype, (int64_t)(t0 + j) * H + h, xv[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (h0 + u * 256 + lane * 8 < H) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[j] = fmaf(xv[u][i], wv[u][i], acc[j]);
+          }
+        }
       }
     }
   }
