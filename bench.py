@@ -38,6 +38,8 @@ WORKLOADS = {
                          desc="OLMoE-1B-7B geometry (config 2): 16 MoE layers, E=64, H=2048, I=1024, top-8, bs=1 decode"),
     "qwen3-prefill": dict(E=128, H=2048, I=768, k=8, T=4096, layers=4, norm=True, lora=16,
                           desc="Qwen3-30B-A3B geometry (config 3): E=128, H=2048, I=768, top-8, T=4096, LoRA r=16"),
+    "qwen3-prefill-base": dict(E=128, H=2048, I=768, k=8, T=4096, layers=4, norm=True, lora=0,
+                               desc="Qwen3-30B-A3B geometry, T=4096, frozen NF4 experts without adapters"),
 }
 
 

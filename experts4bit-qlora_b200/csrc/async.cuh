@@ -71,4 +71,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int c0, 
       : "memory");
 }
 
+// Four rows (y0..y3) of a 2-D tensor, box {x extent, 1 row}, into consecutive box rows of dst.
+__device__ __forceinline__ void tma_gather4(void* dst, const void* map, int x, int y0, int y1, int y2, int y3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 }  // namespace e4b

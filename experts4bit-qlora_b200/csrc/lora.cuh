@@ -5,7 +5,8 @@
 namespace e4b {
 
 struct LoraAArgs {
-  const void* a;             // activations (act dtype), rows of K
+  const __half* a;           // activations, fp16 rows of K
+  const float* a_scale;      // nullable: per source row power-of-two scale of `a`
   const int32_t* a_rows;     // nullable gather map (sorted row -> source row)
   const void* loraA;         // [E, rank, K] (lora dtype)
   const int32_t* offsets;    // [E+1]
@@ -15,9 +16,9 @@ struct LoraAArgs {
   float* xa;                 // [R, rank] fp32 = scaling * (a_row . A[e]^T)
   int max_tiles;
 };
-constexpr int kLoraRows = 32;
+constexpr int kLoraRows = 64;
 constexpr int kLoraMaxRank = 64;
 
-e4b_status launch_lora_a(const LoraAArgs& g, int act_dtype, cudaStream_t s);
+e4b_status launch_lora_a(const LoraAArgs& g, cudaStream_t s);
 
 }  // namespace e4b

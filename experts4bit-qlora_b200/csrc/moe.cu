@@ -37,8 +37,9 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   L.tile_b = take((E + 1) * 4);
   L.inv = take(R * 4);
   L.sorted_token = take(R * 4);
-  L.x16 = take((size_t)d.tokens * d.hidden * 2);
-  L.x_scale = take((size_t)d.tokens * 4);
+  // fp16 activations: T rows (decode path) or R expert-sorted rows (tensor-core path)
+  L.x16 = take(R * d.hidden * 2);
+  L.x_scale = take(R * 4);
   L.h = take(R * d.intermediate * 2);
   L.down_rows = take(R * d.hidden * 2);
   L.xa_gu = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
@@ -250,8 +251,21 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   pa.conv.rows = T;
   pa.conv.K = H;
   pa.conv_ctas = conv_ctas_for(T, 32);
+  const bool use_umma = umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype, d.lora_rank);
+  if (use_umma) pa.conv.src = nullptr;  // converted below, in expert-sorted order
   e4b_status st = launch_permute(pa, s);
   if (st != E4B_OK) return st;
+  if (use_umma) {  // xs[r] = fp16(x[sorted_token[r]]): contiguous rows per expert for the TMA tiles
+    ConvertArgs cv{};
+    cv.src = t->hidden;
+    cv.src_dtype = d.act_dtype;
+    cv.dst = x16;
+    cv.scale = x_scale;
+    cv.rows = R;
+    cv.K = H;
+    gather_convert_kernel<<<conv_ctas_for(R, 8), 256, 0, s>>>(cv, pa.sorted_token);
+    if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
+  }
   mark(1);
 
   void* h = ws + L.h;
@@ -263,8 +277,9 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
 
   if (d.lora_rank > 0) {
     LoraAArgs la{};
-    la.a = t->hidden;
-    la.a_rows = pa.sorted_token;
+    la.a = x16;
+    la.a_scale = x_scale;
+    la.a_rows = use_umma ? nullptr : pa.sorted_token;
     la.loraA = t->gate_up_lora_A;
     la.offsets = pa.offsets;
     la.tile_start = pa.tile_start_a;
@@ -275,15 +290,14 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     la.scaling = d.lora_scaling;
     la.xa = xa_gu;
     la.max_tiles = lora_tiles;
-    if ((st = launch_lora_a(la, d.act_dtype, s)) != E4B_OK) return st;
+    if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
   }
   mark(2);
 
-  const bool use_umma = umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype);
   GemvArgs g{};
   g.a = x16;
   g.a_scale = x_scale;
-  g.a_rows = pa.sorted_token;
+  g.a_rows = use_umma ? nullptr : pa.sorted_token;
   g.packed = t->gate_up_packed;
   g.absmax = t->gate_up_absmax;
   g.offsets = pa.offsets;
@@ -304,7 +318,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   g.max_tasks = max_active * g.tiles_per_expert;
   g.err = err;
   if (use_umma) {
-    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
+    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k, R);
     st = launch_umma(u, d.act_dtype, s);
   } else {
     st = launch_gemv_auto(g, T, T, s);
@@ -314,7 +328,8 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
 
   if (d.lora_rank > 0) {
     LoraAArgs la{};
-    la.a = h;  // fp16
+    la.a = reinterpret_cast<const __half*>(h);
+    la.a_scale = nullptr;
     la.a_rows = nullptr;
     la.loraA = t->down_lora_A;
     la.offsets = pa.offsets;
@@ -326,7 +341,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     la.scaling = d.lora_scaling;
     la.xa = xa_dn;
     la.max_tiles = lora_tiles;
-    if ((st = launch_lora_a(la, E4B_F16, s)) != E4B_OK) return st;
+    if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
   }
   mark(4);
 
@@ -346,7 +361,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   g.tiles_per_expert = H / 16;
   g.max_tasks = max_active * g.tiles_per_expert;
   if (use_umma) {
-    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k);
+    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k, R);
     st = launch_umma(u, d.act_dtype, s);
   } else {
     st = launch_gemv_auto(g, R, T, s);

@@ -1,21 +1,506 @@
-// tcgen05 grouped NF4 GEMM for the prefill regime.
+// tcgen05 grouped NF4 GEMM for the prefill regime (many tokens per expert).
+//
+// Replaces grouped-nf4-gemm's gemm_4bit_grouped at prefill shapes
+// (experts4bit_qlora/engines/fast.py:137-156) with the gate_up epilogue
+// (lora._epilogue, lora.py:102-128) and the LoRA delta (lora.py:251-256) fused.
+//
+// D[feature, token] = W_e[feature, :] . X[token, :] on the 5th-generation tensor
+// cores: the NF4 weight tile is the M = 128 operand, a tile of 128 tokens of
+// the same expert the N = 128 operand, fp32 accumulators live in tensor memory.
+// For SwiGLU the CTA tile is 128 output features: 128 gate rows and the 128
+// matching up rows accumulate into two TMEM accumulators, so silu(gate) * up
+// happens in registers in the epilogue.
+//
+// One persistent CTA per SM, 16 warps with fixed roles, 64-wide K chunks (one
+// quantization block per row per chunk) through three rings of their own depth --
+// packed weights 4 deep, activation tiles 5 deep, decoded A tiles 2 deep:
+//   warp 0      TMA: packed NF4 bytes of the tile's rows (2-D boxes {32 B, 128 rows});
+//   warp 1      TMA of the 128 token rows (fp16, expert-sorted), one box per chunk,
+//               landing in the 128-byte-swizzled K-major operand layout;
+//   warp 3      allocates TMEM, issues tcgen05.mma (one thread), commits;
+//   warps 4-11  NF4 -> fp16 decode: one thread per weight row, 32 pair-table
+//               lookups per chunk, scaled by the block's absmax, stored into the
+//               swizzled A operand;
+//   warps 12-15 epilogue: tcgen05.ld of the finished accumulators (double
+//               buffered, so it overlaps the next tile's MMAs), activation
+//               scale, LoRA delta, activation, fp16 / bf16 stores.
+// Tiles are ordered (expert, feature tile, token tile) so CTAs that run at the
+// same time share the weight tile through L2. Every wait is bounded; a timeout
+// raises E4B_ERR_TIMEOUT and all roles run to the common exit (TMEM is freed).
+#include "async.cuh"
 #include "umma.cuh"
+#include "tmap.cuh"
+
+// Profiling instrumentation, compiled only with -DE4B_TRACE: per-CTA cycles each role
+// spends waiting (clock64), read back with e4b_umma_stats_read.
+#ifdef E4B_TRACE
+__device__ unsigned long long g_umma_stats[148 * 8];
+extern "C" __attribute__((visibility("default"))) int e4b_umma_stats_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_umma_stats, sizeof(g_umma_stats));
+}
+#define STAT_WAIT(slot, expr)                                                        \
+  ({                                                                                 \
+    const long long t0_ = clock64();                                                 \
+    const bool ok_ = (expr);                                                         \
+    if (blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 8 + (slot)], (unsigned long long)(clock64() - t0_)); \
+    ok_;                                                                             \
+  })
+#else
+#define STAT_WAIT(slot, expr) (expr)
+#endif
 
 namespace e4b {
 
+namespace {
+
+constexpr int kSW = 4;  // packed-weight ring depth (HBM latency)
+constexpr int kSB = 5;  // activation ring depth (L2 latency of the gathers)
+constexpr int kSA = 2;  // decoded-A ring depth (produced on chip)
+constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA N)
+constexpr int kRows = 128;          // weight rows per group (UMMA M)
+constexpr int kKc = 64;             // K per chunk
+constexpr int kThreads = 512;
+constexpr int kWBytes = kRows * kKc / 2;        // 4 KB packed per group
+constexpr int kABytes = kRows * kKc * 2;        // 16 KB fp16 per group
+constexpr int kBBytes = kTok * kKc * 2;         // 16 KB fp16
+constexpr int kLut = 256 * 128;
+constexpr int kEpiMaxRank = 16;  // LoRA ranks above this take the streaming path
+
+struct Smem {
+  static constexpr int lut = 0;
+  static constexpr int a = kLut;                                  // [stage][group] 16 KB, 1024-aligned
+  static constexpr int b = a + kSA * 2 * kABytes;                 // [stage] 16 KB
+  static constexpr int w = b + kSB * kBBytes;                     // [stage][group] 4 KB
+  static constexpr int epi = w + kSW * 2 * kWBytes;                // epilogue staging
+  static constexpr int bars = epi + kTok * (1 + kEpiMaxRank) * 4;
+  // full_w, w_empty [kSW]; full_b, b_empty [kSB]; a_ready, a_empty [kSA]; acc_full, acc_empty [2]
+  static constexpr int nbars = 2 * kSW + 2 * kSB + 2 * kSA + 4;
+  static constexpr int tmem_slot = bars + nbars * 8;
+  static constexpr int tables = tmem_slot + 16;                   // tile_start and offsets, E <= 1024
+  static constexpr int total = tables + 2 * 1025 * 4;
+};
+
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait that remembers a timeout: after the first timeout every later
+// wait of this thread returns at once, so all roles reach the common exit.
+struct Waiter {
+  bool dead = false;
+  int* err;
+  __device__ bool wait(uint64_t* bar, uint32_t parity) {
+    if (dead) return false;
+    if (mbar_wait(bar, parity)) return true;
+    dead = true;
+    raise_error(err, E4B_ERR_TIMEOUT);
+    return false;
+  }
+};
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte swizzle shared-memory matrix descriptor (rows of 128 B, 8-row groups 1024 B apart).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3fff);          // start address
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;                // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;                          // descriptor version
+  d |= (uint64_t)2 << 61;                          // layout: 128-byte swizzle
+  return d;
+}
+
+// kind::f16 instruction descriptor: fp16 A and B, fp32 D, both K-major, M = 128, N = kTok.
+__device__ __forceinline__ uint32_t idesc_f16() {
+  return (1u << 4) | ((uint32_t)(kTok >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(dtmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct TileInfo {
+  int e, row0, M, ft, tt;
+};
+
+// Tile t -> (expert, token tile, feature tile); tiles ordered (expert, feature tile, token tile).
+// ts (prefix of ceil(count / kTok)) and offs are the shared-memory copies of the expert tables.
+__device__ __forceinline__ void tile_info(const int32_t* ts, const int32_t* offs, int E, int nft, int t,
+                                          TileInfo& ti) {
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {  // last e with ts[e] * nft <= t
+    const int mid = (lo + hi + 1) >> 1;
+    if (ts[mid] * nft <= t) lo = mid; else hi = mid - 1;
+  }
+  ti.e = lo;
+  const int local = t - ts[lo] * nft;
+  const int ntt = ts[lo + 1] - ts[lo];
+  ti.ft = local / ntt;
+  ti.tt = local - ti.ft * ntt;
+  ti.row0 = offs[lo];
+  ti.M = offs[lo + 1] - ti.row0;
+}
+
+}  // namespace
+
+template <typename OutT, int GROUPS>
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_umma_kernel(UmmaArgs u, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap) {
+  extern __shared__ __align__(1024) char smem[];
+#ifdef E4B_TRACE
+  const long long t_start = clock64();
+#endif
+  const GemvArgs& g = u.g;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  char* lut = smem + Smem::lut;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::bars);
+  uint64_t* full_w = bars;
+  uint64_t* w_empty = full_w + kSW;
+  uint64_t* full_b = w_empty + kSW;
+  uint64_t* b_empty = full_b + kSB;
+  uint64_t* a_ready = b_empty + kSB;
+  uint64_t* a_empty = a_ready + kSA;
+  uint64_t* acc_full = a_empty + kSA;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Smem::tmem_slot);
+  int32_t* s_ts = reinterpret_cast<int32_t*>(smem + Smem::tables);
+  int32_t* s_offs = s_ts + 1025;
+  for (int i = tid; i <= u.g.E; i += kThreads) {
+    s_ts[i] = u.tile_start[i];
+    s_offs[i] = u.g.offsets[i];
+  }
+
+  const int nft = GROUPS == 2 ? (g.N / 2) / kRows : g.N / kRows;  // feature tiles per expert
+  const int kchunks = g.K / kKc;
+  const int total_tiles = u.tile_start[g.E] * nft;
+  Waiter wt{false, g.err};
+
+  if (tid == 0) {
+    for (int s = 0; s < kSW; ++s) {
+      mbar_init(&full_w[s], 1);
+      mbar_init(&w_empty[s], 256);
+    }
+    for (int s = 0; s < kSB; ++s) {
+      mbar_init(&full_b[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < kSA; ++s) {
+      mbar_init(&a_ready[s], 256);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    fence_proxy_async();
+  }
+  if (warp == 3) {  // 512 TMEM columns: two buffers x (gate, up) x 128 fp32 columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  {  // pair table: entry e of lane l at (e << 7) | (l << 2)
+    const float code = c_nf4[lane & 15];
+    for (int e = warp; e < 256; e += kThreads / 32) {
+      const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
+      reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer: packed weight rows -------------------------------------
+    if (lane == 0) {
+      int n = 0;
+      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+        TileInfo ti;
+        tile_info(s_ts, s_offs, g.E, nft, t, ti);
+        for (int c = 0; c < kchunks; ++c, ++n) {
+          const int s = n % kSW;
+          if (!STAT_WAIT(0, wt.wait(&w_empty[s], ((n / kSW) & 1) ^ 1))) break;
+          mbar_arrive_expect_tx(&full_w[s], GROUPS * kWBytes);
+#pragma unroll
+          for (int h = 0; h < GROUPS; ++h) {
+            const int row = ti.e * g.N + (h == 0 ? ti.ft * kRows : (g.N / 2) + ti.ft * kRows);
+            tma_load_2d(smem + Smem::w + (s * 2 + h) * kWBytes, &wmap, c * (kKc / 2), row, &full_w[s]);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- activation tiles: one TMA box {64 halves, 128 rows} per chunk ------------
+    // The rows of an expert are contiguous (expert-sorted activations); rows past its end belong
+    // to the next expert or are zero-filled past the matrix, and are discarded by the epilogue.
+    if (lane == 0) {
+      int n = 0;
+      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+        TileInfo ti;
+        tile_info(s_ts, s_offs, g.E, nft, t, ti);
+        for (int c = 0; c < kchunks; ++c, ++n) {
+          const int s = n % kSB;
+          if (!STAT_WAIT(1, wt.wait(&b_empty[s], ((n / kSB) & 1) ^ 1))) break;
+          mbar_arrive_expect_tx(&full_b[s], kBBytes);
+          tma_load_2d(smem + Smem::b + s * kBBytes, &bmap, c * kKc, ti.row0 + ti.tt * kTok, &full_b[s]);
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // idle
+  } else if (warp == 3) {
+    // ---------------- MMA issuer -------------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16();
+      int n = 0, it = 0;
+      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        if (!STAT_WAIT(4, wt.wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1))) break;
+        tc_fence_after();
+        for (int c = 0; c < kchunks; ++c, ++n) {
+          const int s = n % kSB, sa = n % kSA;
+          if (!STAT_WAIT(2, wt.wait(&full_b[s], (n / kSB) & 1))) break;
+          if (!STAT_WAIT(3, wt.wait(&a_ready[sa], (n / kSA) & 1))) break;
+          tc_fence_after();
+          const uint32_t bsm = smem_u32(smem + Smem::b + s * kBBytes);
+#pragma unroll
+          for (int h = 0; h < GROUPS; ++h) {
+            const uint32_t asm_ = smem_u32(smem + Smem::a + (sa * 2 + h) * kABytes);
+            const uint32_t d = tmem + buf * 256 + h * 128;
+#pragma unroll
+            for (int kk = 0; kk < kKc / 16; ++kk)
+              umma_f16(d, sw128_desc(asm_ + kk * 32), sw128_desc(bsm + kk * 32), idesc, (c | kk) != 0);
+          }
+          umma_commit(&b_empty[s]);
+          umma_commit(&a_empty[sa]);
+        }
+        umma_commit(&acc_full[buf]);
+      }
+    }
+  } else if (warp < 12) {
+    // ---------------- NF4 decode: one weight row per thread ---------------------------------
+    const int d = tid - 128;          // 0..255
+    const int h = d >> 7, r = d & 127;  // group, row within the tile
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    int n = 0;
+    for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+      TileInfo ti;
+      tile_info(s_ts, s_offs, g.E, nft, t, ti);
+      const int row = h == 0 ? ti.ft * kRows + r : (g.N / 2) + ti.ft * kRows + r;
+      const float* am = g.absmax + ((int64_t)ti.e * g.N + row) * (g.K / 64);
+      float am_next = h < GROUPS ? __ldg(am) : 0.f;
+      for (int c = 0; c < kchunks; ++c, ++n) {
+        const int s = n % kSW, sa = n % kSA;
+        const float a = am_next;
+        if (h < GROUPS && c + 1 < kchunks) am_next = __ldg(am + c + 1);
+        if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (n / kSW) & 1)) : wt.wait(&full_w[s], (n / kSW) & 1))) break;
+        uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
+        if (h < GROUPS) {
+          const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
+          p0 = reinterpret_cast<const uint4*>(wsrc)[0];
+          p1 = reinterpret_cast<const uint4*>(wsrc)[1];
+        }
+        fence_proxy_async();
+        mbar_arrive(&w_empty[s]);  // packed bytes are in registers: the slot can be refilled
+        if (!wt.wait(&a_empty[sa], ((n / kSA) & 1) ^ 1)) break;
+        if (h < GROUPS) {
+          const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+          const __half2 sc = __float2half2_rn(a);
+          char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
+          const int swz = (smem_u32(adst) >> 7) & 7;  // 128-byte swizzle follows the shared address
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {  // 16-byte unit q = 8 elements = packed word q
+            uint32_t o[4];
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+              const uint32_t byte = (words[q] >> (8 * bb)) & 0xffu;
+              uint32_t pr = *reinterpret_cast<const uint32_t*>(lut + ((byte << 7) | lane4));
+              __half2 v = __hmul2(*reinterpret_cast<__half2*>(&pr), sc);
+              o[bb] = *reinterpret_cast<uint32_t*>(&v);
+            }
+            *reinterpret_cast<uint4*>(adst + ((q ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        fence_proxy_async();
+        mbar_arrive(&a_ready[sa]);
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM -> registers -> global ---------------------------------
+    // Per tile, the 128 tokens' activation scales and LoRA-A vectors are staged once in shared
+    // memory (read back as broadcasts); each thread keeps its feature's LoRA-B rows in registers.
+    const int ew = warp - 12;          // TMEM lanes 32*ew .. 32*ew+31
+    const int r = ew * 32 + lane;      // row within the tile
+    float* s_sc = reinterpret_cast<float*>(smem + Smem::epi);
+    float* s_xa = s_sc + kTok;         // [kTok][rank]
+    const int rank = g.rank;
+    int it = 0;
+    for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
+      TileInfo ti;
+      tile_info(s_ts, s_offs, g.E, nft, t, ti);
+      const int buf = it & 1;
+      const int rowA = ti.ft * kRows + r;
+      const int rowB = (g.N / 2) + ti.ft * kRows + r;
+      const int feat = ti.ft * kRows + r;  // output column
+      {  // token r of the tile: scale and LoRA-A vector
+        const int m = ti.tt * kTok + r;
+        float sc = 1.f;
+        if (m < ti.M) {
+          const int64_t srow = ti.row0 + m;
+          if (g.a_scale) sc = g.a_scale[g.a_rows ? g.a_rows[srow] : srow];
+          for (int j = 0; j < rank; ++j) s_xa[r * rank + j] = g.lora_xa[srow * rank + j];
+        }
+        s_sc[r] = sc;
+      }
+      float lb_a[kEpiMaxRank], lb_b[kEpiMaxRank];
+#pragma unroll
+      for (int j = 0; j < kEpiMaxRank; ++j) {
+        lb_a[j] = j < rank ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + rowA) * rank + j) : 0.f;
+        lb_b[j] = (GROUPS == 2 && j < rank) ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + rowB) * rank + j)
+                                            : 0.f;
+      }
+      named_bar(1, 128);
+      if (!(r == 0 ? STAT_WAIT(6, wt.wait(&acc_full[buf], (it >> 1) & 1)) : wt.wait(&acc_full[buf], (it >> 1) & 1))) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + buf * 256;
+      for (int c0 = 0; c0 < kTok; c0 += 16) {
+        float va[16], vb[16];
+        tmem_ld16(tbase + c0, va);
+        if (GROUPS == 2) tmem_ld16(tbase + 128 + c0, vb);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int m = ti.tt * kTok + c0 + i;
+          if (m >= ti.M) break;
+          const int64_t srow = ti.row0 + m;
+          const float sc = s_sc[c0 + i];
+          float xa = va[i] * sc, xb = GROUPS == 2 ? vb[i] * sc : 0.f;
+          if (rank) {  // rank is a multiple of 4 here: 128-bit broadcast reads of the token's vector
+            const float4* la = reinterpret_cast<const float4*>(s_xa + (c0 + i) * rank);
+#pragma unroll
+            for (int j4 = 0; j4 < kEpiMaxRank / 4; ++j4) {
+              if (4 * j4 >= rank) break;
+              const float4 l = la[j4];
+              xa = fmaf(l.x, lb_a[4 * j4], fmaf(l.y, lb_a[4 * j4 + 1], fmaf(l.z, lb_a[4 * j4 + 2], fmaf(l.w, lb_a[4 * j4 + 3], xa))));
+              if (GROUPS == 2)
+                xb = fmaf(l.x, lb_b[4 * j4], fmaf(l.y, lb_b[4 * j4 + 1], fmaf(l.z, lb_b[4 * j4 + 2], fmaf(l.w, lb_b[4 * j4 + 3], xb))));
+            }
+          }
+          OutT* o = reinterpret_cast<OutT*>(g.out) + srow * g.Nout;
+          if (g.epilogue == E4B_EPI_SWIGLU)
+            o[feat] = store_cast<OutT>(silu_f32(xa) * xb, g.err);
+          else if (g.epilogue == E4B_EPI_SILU)
+            o[feat] = store_cast<OutT>(silu_f32(xa), g.err);
+          else
+            o[feat] = store_cast<OutT>(xa, g.err);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      named_bar(1, 128);  // staging of the next tile may overwrite s_sc / s_xa
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 3) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+#ifdef E4B_TRACE
+  if (tid == 0 && blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 8 + 7], (unsigned long long)(clock64() - t_start));
+#endif
+}
+
 size_t umma_workspace_bytes(int, int, int, int, int) { return 0; }
 
-bool umma_eligible(int, int, int, int, int, int, int) { return false; }
+bool umma_eligible(int T, int k, int E, int H, int I, int has_gate, int act_dtype, int lora_rank) {
+  (void)k;
+  (void)E;
+  (void)act_dtype;
+  if (T <= 16) return false;  // the streaming GEMV owns decode shapes
+  if (H % kKc || I % kKc) return false;
+  // feature tiles of 128: gate_up produces I features (SwiGLU) or I (SiLU); down produces H
+  if (I % kRows || H % kRows) return false;
+  (void)has_gate;
+  if (lora_rank > kEpiMaxRank || lora_rank % 4) return false;
+  return encode_tiled_fn() != nullptr;
+}
 
-UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k) {
+UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k, int x_rows) {
   UmmaArgs u{};
   u.g = g;
   u.tile_start = tile_start;
   u.max_tiles = (T * k) / kUmmaTokens + (g.E < T * k ? g.E : T * k);
+  u.x_rows = x_rows;
   u.scratch = scratch;
   return u;
 }
 
-e4b_status launch_umma(const UmmaArgs&, int, cudaStream_t) { return E4B_ERR_UNSUPPORTED; }
+template <typename OutT, int GROUPS>
+static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return E4B_ERR_CUDA;
+  static unsigned long long configured = 0;
+  static int sm_count[64] = {0};
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured & bit)) {
+    if (cudaFuncSetAttribute(nf4_umma_kernel<OutT, GROUPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Smem::total) != cudaSuccess)
+      return E4B_ERR_CUDA;
+    cudaDeviceGetAttribute(&sm_count[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+    configured |= bit;
+  }
+  const GemvArgs& g = u.g;
+  const int nft = GROUPS == 2 ? (g.N / 2) / kRows : g.N / kRows;
+  int grid = sm_count[dev & 63];
+  const int bound = u.max_tiles * nft;
+  if (bound < grid) grid = bound;
+  if (grid < 1) return E4B_OK;
+  CUtensorMap wmap;  // packed bytes [E*N rows][K/2 bytes], box {32 B, 128 rows}
+  const cuuint64_t dims[2] = {(cuuint64_t)(g.K / 2), (cuuint64_t)g.E * g.N};
+  const cuuint64_t str[1] = {(cuuint64_t)(g.K / 2)};
+  const cuuint32_t box[2] = {kKc / 2, kRows};
+  if (!encode_tiled(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, g.packed, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return E4B_ERR_CUDA;
+  if (g.a_rows) return E4B_ERR_UNSUPPORTED;  // activations must be expert-sorted rows
+  CUtensorMap bmap;  // fp16 activation rows [x_rows][K], box {64 halves, 128 rows}, 128-byte swizzle
+  const cuuint64_t bdims[2] = {(cuuint64_t)g.K, (cuuint64_t)u.x_rows};
+  const cuuint64_t bstr[1] = {(cuuint64_t)g.K * 2};
+  const cuuint32_t bbox[2] = {kKc, kTok};
+  if (!encode_tiled(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.a, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B))
+    return E4B_ERR_CUDA;
+  nf4_umma_kernel<OutT, GROUPS><<<grid, kThreads, Smem::total, s>>>(u, wmap, bmap);
+  return launch_status();
+}
+
+e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s) {
+  (void)act_dtype;
+  const bool two = u.g.epilogue == E4B_EPI_SWIGLU;
+  if (u.g.out_dtype == E4B_BF16)
+    return two ? launch_groups<__nv_bfloat16, 2>(u, s) : launch_groups<__nv_bfloat16, 1>(u, s);
+  return two ? launch_groups<__half, 2>(u, s) : launch_groups<__half, 1>(u, s);
+}
 
 }  // namespace e4b

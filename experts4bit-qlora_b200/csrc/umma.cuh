@@ -11,12 +11,13 @@ struct UmmaArgs {
   GemvArgs g;                      // operands, epilogue and LoRA, as for the GEMV
   const int32_t* tile_start;       // [E+1] prefix of ceil(count / kUmmaTokens)
   int max_tiles;
+  int x_rows;                      // rows of the activation matrix g.a
   void* scratch;
 };
 
 size_t umma_workspace_bytes(int T, int k, int E, int H, int I);
-bool umma_eligible(int T, int k, int E, int H, int I, int has_gate, int act_dtype);
-UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k);
+bool umma_eligible(int T, int k, int E, int H, int I, int has_gate, int act_dtype, int lora_rank);
+UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k, int x_rows);
 e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s);
 
 }  // namespace e4b
