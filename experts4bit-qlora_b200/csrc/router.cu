@@ -7,6 +7,23 @@
 namespace e4b {
 
 constexpr int kRouterWarps = 8;   // experts per CTA (one warp each)
+
+template <typename T> __device__ __forceinline__ void mma_act(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                              uint32_t a3, uint32_t b0, uint32_t b1);
+template <> __device__ __forceinline__ void mma_act<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                                   uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <> __device__ __forceinline__ void mma_act<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                            uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 constexpr int kRouterTT = 4;      // tokens per CTA
 
 template <int N>
@@ -76,6 +93,67 @@ router_logits_kernel(const void* __restrict__ x, int x_dtype, const void* __rest
 #pragma unroll
     for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
     if (lane == 0 && t0 + j < T) logits[(int64_t)(t0 + j) * E + e] = a;
+  }
+}
+
+// Many tokens: logits as a tensor-core GEMM. A CTA takes 64 tokens x 64 experts; its
+// 4 warps each own 16 tokens x 64 experts (8 n8 tiles of mma.sync m16n8k16, bf16
+// or fp16 operands, fp32 accumulation); 64-wide K chunks of x and W_r are staged in
+// padded shared memory (fp32 weights are rounded to the activation type there).
+template <typename T>
+__global__ void __launch_bounds__(128) router_logits_mma_kernel(const T* __restrict__ x, const void* __restrict__ wr,
+                                                                int w_dtype, int Tn, int H, int E,
+                                                                float* __restrict__ logits) {
+  constexpr int P = 72;  // padded row, halves
+  __shared__ __align__(16) T xs[64][P];
+  __shared__ __align__(16) T ws[64][P];
+  const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, q = lane & 3;
+  float acc[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+  for (int k0 = 0; k0 < H; k0 += 64) {
+    for (int i = threadIdx.x; i < 64 * 8; i += 128) {
+      const int rr = i >> 3, v = i & 7;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (t0 + rr < Tn) val = *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + rr) * H + k0 + v * 8);
+      *reinterpret_cast<uint4*>(&xs[rr][v * 8]) = val;
+    }
+    for (int i = threadIdx.x; i < 64 * 64; i += 128) {
+      const int rr = i >> 6, kk = i & 63;
+      const float v = e0 + rr < E ? load_as_f32(wr, w_dtype, (int64_t)(e0 + rr) * H + k0 + kk) : 0.f;
+      ws[rr][kk] = from_f32<T>(v);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int ks = 0; ks < 64; ks += 16) {
+      const int rw = warp * 16 + gq;
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&xs[rw][ks + 2 * q]);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(&xs[rw + 8][ks + 2 * q]);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&xs[rw][ks + 2 * q + 8]);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(&xs[rw + 8][ks + 2 * q + 8]);
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&ws[n * 8 + gq][ks + 2 * q]);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&ws[n * 8 + gq][ks + 2 * q + 8]);
+        mma_act<T>(acc[n], a0, a1, a2, a3, b0, b1);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int t = t0 + warp * 16 + gq + 8 * h;
+    if (t >= Tn) continue;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int e = e0 + n * 8 + 2 * q + c;
+        if (e < E) logits[(int64_t)t * E + e] = acc[n][2 * h + c];
+      }
   }
 }
 
@@ -179,8 +257,17 @@ extern "C" e4b_status e4b_router_topk(const void* x, int x_dtype, const void* w_
     logits = reinterpret_cast<float*>(static_cast<char*>(workspace) + kErrBytes);
   }
   cudaStream_t s = (cudaStream_t)stream;
-  dim3 g1((E + kRouterWarps - 1) / kRouterWarps, (T + kRouterTT - 1) / kRouterTT);
-  router_logits_kernel<<<g1, kRouterWarps * 32, 0, s>>>(x, x_dtype, w_router, w_dtype, T, H, E, logits);
+  if (T > 16 && H % 64 == 0) {
+    dim3 g1((T + 63) / 64, (E + 63) / 64);
+    if (x_dtype == E4B_BF16)
+      router_logits_mma_kernel<__nv_bfloat16><<<g1, 128, 0, s>>>((const __nv_bfloat16*)x, w_router, w_dtype, T, H, E,
+                                                                 logits);
+    else
+      router_logits_mma_kernel<__half><<<g1, 128, 0, s>>>((const __half*)x, w_router, w_dtype, T, H, E, logits);
+  } else {
+    dim3 g1((E + kRouterWarps - 1) / kRouterWarps, (T + kRouterTT - 1) / kRouterTT);
+    router_logits_kernel<<<g1, kRouterWarps * 32, 0, s>>>(x, x_dtype, w_router, w_dtype, T, H, E, logits);
+  }
   const int warps = 8;
   const int g2 = (T + warps - 1) / warps;
   if (E <= 32)
