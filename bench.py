@@ -40,6 +40,10 @@ WORKLOADS = {
                           desc="Qwen3-30B-A3B geometry (config 3): E=128, H=2048, I=768, top-8, T=4096, LoRA r=16"),
     "qwen3-prefill-base": dict(E=128, H=2048, I=768, k=8, T=4096, layers=4, norm=True, lora=0,
                                desc="Qwen3-30B-A3B geometry, T=4096, frozen NF4 experts without adapters"),
+    # T is the GLOBAL token count per layer, split over the ranks (strong scaling)
+    "mixtral-ep": dict(E=8, H=4096, I=14336, k=2, T=8192, layers=32, norm=True, lora=0, ep=True,
+                       desc="Mixtral-8x7B geometry (config 4): 32 MoE layers, E=8, H=4096, I=14336, top-2, "
+                            "T=8192 tokens per layer sharded over the ranks, experts sharded over the ranks"),
 }
 
 
@@ -315,6 +319,167 @@ def run_ours(args, wl, world, rank, local):
     return result
 
 
+def build_ep_layers(pkg, wl, dev, rank, world):
+    """The rank's expert slice of every layer. Expert e of layer l is drawn from its own
+    seed, so a slice holds the same weights whatever the world size."""
+    ep = pkg.ep
+    E, H, I = wl["E"], wl["H"], wl["I"]
+    El = E // world
+    shards, routers = [], []
+    for li in range(wl["layers"]):
+        parts = {"gu": [], "gua": [], "dn": [], "dna": []}
+        for e in range(rank * El, (rank + 1) * El):
+            g = torch.Generator(device=dev).manual_seed(1_000_003 * li + e)
+            for key, shape in (("gu", (2 * I, H)), ("dn", (H, I))):
+                w = (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                packed, absmax = pkg.ops.nf4_quantize(w)
+                parts[key].append(packed)
+                parts[key + "a"].append(absmax)
+                del w
+        shards.append(ep.ExpertShard(torch.stack(parts["gu"]), torch.stack(parts["gua"]), torch.stack(parts["dn"]),
+                                     torch.stack(parts["dna"]), rank * El, El))
+        g = torch.Generator(device=dev).manual_seed(7_000_001 + li)
+        routers.append((torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    torch.cuda.synchronize()
+    return shards, routers
+
+
+def run_ep(args, wl, world, rank, local):
+    """Expert-parallel layer over `world` ranks (config 4). One step = one MoE layer over
+    the T global tokens (layers cycled), T/world tokens and E/world experts per rank;
+    exchanges are NCCL all-to-alls over NVLink. Not graph-captured: the row splits need
+    one host sync per layer."""
+    import importlib
+    pkg = importlib.import_module("experts4bit-qlora_b200")
+    N = pkg._native
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if wl["E"] % world:
+        raise SystemExit(f"{wl['E']} experts do not split over {world} ranks")
+    E, H, I, k, Lc = wl["E"], wl["H"], wl["I"], wl["k"], wl["layers"]
+    T = wl["T"] // world
+    shards, routers = build_ep_layers(pkg, wl, dev, rank, world)
+    layers = [pkg.ExpertParallelMoE(sh, E, H, I, True) for sh in shards]
+    pool = 4
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    X = torch.randn(pool, T, H, generator=g, device=dev).to(torch.bfloat16)
+
+    def step(s, x=None):
+        li = s % Lc
+        x = X[s % pool] if x is None else x
+        w, idx = pkg.route(x, routers[li], k, norm_topk_prob=wl["norm"])
+        return layers[li](x, idx, w)
+
+    for s in range(max(args.warmup, 3)):
+        step(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        start.record()
+        for s in range(args.steps):
+            step(s)
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t_ = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t_.item())
+    value = args.steps * wl["T"] / (ms / 1e3)
+
+    # per-stage device times of this rank's expert side, from the library's stage events
+    cudart = _cudart()
+    nst = N.MOE_STAGE_EVENTS
+    stage_ms = [[] for _ in range(nst - 1)]
+    recv_rows = []
+    for rep in range(4):
+        li = rep % Lc
+        x = X[rep % pool]
+        w, idx = pkg.route(x, routers[li], k, norm_topk_prob=wl["norm"])
+        lay = layers[li]
+        send, counts, inv = lay.stages.dispatch(x, idx)
+        rc, ss, rs = lay.exchange_counts(counts)
+        rows = torch.empty(sum(rs), H, dtype=send.dtype, device=dev)
+        if world > 1:
+            torch.distributed.all_to_all_single(rows, send, rs, ss)
+        else:
+            rows.copy_(send)
+        ev = [_RawEvent(cudart) for _ in range(nst)]
+        lay.stages.experts(rows, rc, events=[e.cuda_event for e in ev])
+        torch.cuda.synchronize()
+        for si in range(nst - 1):
+            stage_ms[si].append(ev[si].elapsed_ms(ev[si + 1]))
+        recv_rows.append(rows.shape[0])
+    names = ["plan", "convert", "gate_up", "lora_a_h", "down", "scatter"]
+    st_us = {n: 1e3 * statistics.mean(v) for n, v in zip(names, stage_ms)}
+    Rr = statistics.mean(recv_rows)
+    gu_flops = 2.0 * Rr * H * 2 * I
+    peaks, peak_kind = load_peaks()
+    peak = peaks["bf16_tflops"]
+    achieved = gu_flops / (st_us["gate_up"] * 1e-6) / 1e12
+    roofline = {"bound": "tensor", "kernel": "nf4 grouped gate_up (SwiGLU fused), tcgen05, rank 0 expert side",
+                "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": None, "kernel_us": round(st_us["gate_up"], 1),
+                "down_kernel_us": round(st_us["down"], 1),
+                "down_achieved_tflops": round(2.0 * Rr * H * I / (st_us["down"] * 1e-6) / 1e12, 1),
+                "rows_received": int(Rr), "stage_us": {n: round(v, 1) for n, v in st_us.items()},
+                "nvlink_bytes_per_layer_per_rank": int(2 * T * k * H * 2 * (world - 1) / world)}
+
+    # e2e through the public API: pinned host tokens in, route + layer, output back to the host
+    host_in = torch.empty(pool, T, H, dtype=torch.bfloat16, pin_memory=True)
+    host_in.copy_(X.cpu())
+    host_out = torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True)
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def one(s):
+        x = host_in[s % pool].to(dev, non_blocking=True)
+        with torch.no_grad():
+            y = step(s, x)
+        host_out.copy_(y, non_blocking=True)
+
+    for s in range(3):
+        one(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(e2e_steps):
+        one(s)
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    if world > 1:
+        t_ = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t_.item())
+    layer_gb = wl["E"] * (2 * I * H + H * I) * (0.5 + 4 / 64) / 1e9
+    result = {
+        "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights quantized to NF4; N(0,1) tokens; random router)",
+        "config": {"workload": args.workload, "desc": wl["desc"], "tokens_per_layer": wl["T"],
+                   "tokens_per_rank": T, "layers_cycled": Lc, "experts": E, "hidden": H, "intermediate": I,
+                   "top_k": k, "parallelism": f"ep{world}" if world > 1 else "single-gpu",
+                   "l2": "inputs larger than L2: each step reads a %.0f MB layer slice per rank" %
+                         (layer_gb * 1e3 / world),
+                   "timing": "CUDA events around K eager steps, max over ranks"},
+        "roofline": roofline,
+        "e2e": {"value": round(e2e_steps * wl["T"] / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2 * world, "d2h_bytes_per_step": T * H * 2 * world,
+                "path": "public API (route + ExpertParallelMoE), pinned host tokens in, outputs out"},
+        "gpu_launches": 10 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        result["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
+    return result
+
+
 def _cudart():
     import ctypes
     for name in ("/usr/local/cuda/lib64/libcudart.so", "libcudart.so", "libcudart.so.12"):
@@ -397,9 +562,10 @@ def cpu_baseline(wl, seconds=15.0, threads=None):
     torch.set_num_threads(threads or ncores)
     g = torch.Generator().manual_seed(0)
     E, H, I, k = wl["E"], wl["H"], wl["I"], wl["k"]
-    T = min(wl["T"], 128)
+    big = H * I > 16 * 2**20
+    T = min(wl["T"], 16 if big else 128)
     # quantize a handful of distinct experts and reuse them (quantization is not timed)
-    ne = min(E, 8)
+    ne = 1 if big else min(E, 8)
     gp, ga = quantize_stack((torch.randn(ne, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16))
     dp, da = quantize_stack((torch.randn(ne, H, I, generator=g) * 0.02).to(torch.bfloat16))
     rep = (E + ne - 1) // ne
@@ -438,11 +604,15 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="olmoe-decode", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="auto", choices=["auto"] + sorted(WORKLOADS),
+                    help="auto: olmoe-decode on one GPU, mixtral-ep (expert parallel) on several")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="0 skips the CPU baseline")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling)")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the public-API e2e leg (profiling)")
     args = ap.parse_args()
+    if args.workload == "auto":
+        world_env = int(os.environ.get("WORLD_SIZE", "1"))
+        args.workload = "mixtral-ep" if max(world_env, args.gpus) > 1 else "olmoe-decode"
     wl = dict(WORKLOADS[args.workload])
     if args.layers:
         wl["layers"] = args.layers
@@ -453,7 +623,7 @@ def main():
             print(json.dumps(res), flush=True)
         return
     world, rank, local = dist_setup(args.gpus)
-    res = run_ours(args, wl, world, rank, local)
+    res = (run_ep if wl.get("ep") else run_ours)(args, wl, world, rank, local)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

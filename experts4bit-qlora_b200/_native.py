@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "e4b_combine",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
     "e4b_moe_forward_static",
+    "e4b_ep_dispatch_workspace_bytes", "e4b_ep_dispatch", "e4b_ep_experts_workspace_bytes", "e4b_ep_experts",
     "e4b_read_device_error",
 )
 
@@ -82,6 +83,10 @@ def _declare(lib):
         "e4b_moe_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
         "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
         "e4b_moe_forward_static": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P]),
+        "e4b_ep_dispatch_workspace_bytes": (SZ, [I, I, I]),
+        "e4b_ep_dispatch": (I, [P, I, P, I, I, I, I, P, P, P, P, SZ, P]),
+        "e4b_ep_experts_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc), I]),
+        "e4b_ep_experts": (I, [ctypes.POINTER(MoeDesc), I, P, ctypes.POINTER(MoeTensors), P, SZ, P]),
         "e4b_read_device_error": (I, [P, P, ctypes.POINTER(I)]),
     }
     for name, (res, args) in sig.items():

@@ -12,6 +12,7 @@
 #include "lora.cuh"
 #include "permute.cuh"
 #include "umma.cuh"
+#include "moe_stages.cuh"
 
 namespace e4b {
 
@@ -63,7 +64,13 @@ __global__ void __launch_bounds__(256) gather_convert_kernel(ConvertArgs c, cons
   }
 }
 
-static int conv_ctas_for(int rows, int warps_per_cta) {
+e4b_status launch_gather_convert(const ConvertArgs& c, const int32_t* rows_map, cudaStream_t s) {
+  if (c.rows <= 0) return E4B_OK;
+  gather_convert_kernel<<<conv_ctas_for(c.rows, 8), 256, 0, s>>>(c, rows_map);
+  return launch_status();
+}
+
+int conv_ctas_for(int rows, int warps_per_cta) {
   int c = (rows + warps_per_cta - 1) / warps_per_cta;
   return c < 1 ? 1 : (c > 148 * 4 ? 148 * 4 : c);
 }
@@ -76,6 +83,119 @@ __global__ void active_from_offsets_kernel(const int32_t* __restrict__ offsets, 
       if (offsets[e + 1] > offsets[e]) active[n++] = e;
     *num_active = n;
   }
+}
+
+void mark_stage(const e4b_moe_tensors* t, int i, cudaStream_t s) {
+  if (!t->stage_events || !t->stage_events[i]) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(s, &cs);
+  cudaEvent_t ev = (cudaEvent_t)t->stage_events[i];
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, s);
+}
+
+e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, const ExpertRows& x, cudaStream_t s) {
+  const int E = d.num_experts, H = d.hidden, I = d.intermediate, R = x.R;
+  const int n1 = d.has_gate ? 2 * I : I;
+  const int max_active = R < E ? R : E;
+  const int lora_tiles = R / kLoraRows + max_active;
+  e4b_status st = E4B_OK;
+  if (d.lora_rank > 0) {
+    LoraAArgs la{};
+    la.a = x.x16;
+    la.a_scale = x.x_scale;
+    la.a_rows = x.a_rows;
+    la.loraA = t->gate_up_lora_A;
+    la.offsets = x.offsets;
+    la.tile_start = x.tile_a;
+    la.E = E;
+    la.K = H;
+    la.rank = d.lora_rank;
+    la.lora_dtype = d.lora_dtype;
+    la.scaling = d.lora_scaling;
+    la.xa = x.xa_gu;
+    la.max_tiles = lora_tiles;
+    if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
+  }
+  mark_stage(t, 2, s);
+
+  GemvArgs g{};
+  g.a = x.x16;
+  g.a_scale = x.x_scale;
+  g.a_rows = x.a_rows;
+  g.packed = t->gate_up_packed;
+  g.absmax = t->gate_up_absmax;
+  g.offsets = x.offsets;
+  g.active = x.active;
+  g.num_active = x.num_active;
+  g.E = E;
+  g.N = n1;
+  g.K = H;
+  g.epilogue = d.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
+  g.out = x.h;
+  g.out_dtype = E4B_F16;
+  g.Nout = I;
+  g.lora_xa = d.lora_rank > 0 ? x.xa_gu : nullptr;
+  g.lora_B = t->gate_up_lora_B;
+  g.lora_dtype = d.lora_dtype;
+  g.rank = d.lora_rank;
+  g.tiles_per_expert = n1 / 16;
+  g.max_tasks = max_active * g.tiles_per_expert;
+  g.err = x.err;
+  if (x.use_umma) {
+    UmmaArgs u = umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R);
+    st = launch_umma(u, d.act_dtype, s);
+  } else {
+    st = launch_gemv_auto(g, x.x_rows, x.max_rows_per_expert, s);
+  }
+  if (st != E4B_OK) return st;
+  mark_stage(t, 3, s);
+
+  if (d.lora_rank > 0) {
+    LoraAArgs la{};
+    la.a = reinterpret_cast<const __half*>(x.h);
+    la.a_scale = nullptr;
+    la.a_rows = nullptr;
+    la.loraA = t->down_lora_A;
+    la.offsets = x.offsets;
+    la.tile_start = x.tile_a;
+    la.E = E;
+    la.K = I;
+    la.rank = d.lora_rank;
+    la.lora_dtype = d.lora_dtype;
+    la.scaling = d.lora_scaling;
+    la.xa = x.xa_dn;
+    la.max_tiles = lora_tiles;
+    if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
+  }
+  mark_stage(t, 4, s);
+
+  g.a = x.h;
+  g.a_scale = nullptr;
+  g.a_rows = nullptr;
+  g.packed = t->down_packed;
+  g.absmax = t->down_absmax;
+  g.N = H;
+  g.K = I;
+  g.epilogue = E4B_EPI_NONE;
+  g.out = x.down_rows;
+  g.out_dtype = E4B_F16;  // fp16 rows: one bf16 rounding (the final output) instead of two
+  g.Nout = H;
+  g.lora_xa = d.lora_rank > 0 ? x.xa_dn : nullptr;
+  g.lora_B = t->down_lora_B;
+  g.tiles_per_expert = H / 16;
+  g.max_tasks = max_active * g.tiles_per_expert;
+  if (x.use_umma) {
+    UmmaArgs u = umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R);
+    st = launch_umma(u, d.act_dtype, s);
+  } else {
+    st = launch_gemv_auto(g, R, x.max_rows_per_expert, s);
+  }
+  if (st != E4B_OK) return st;
+  mark_stage(t, 5, s);
+  return E4B_OK;
 }
 
 static bool desc_ok(const e4b_moe_desc& d) {
@@ -213,19 +333,8 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   char* ws = static_cast<char*>(workspace);
   int* err = reinterpret_cast<int*>(ws);
   const int R = T * k;
-  const int n1 = d.has_gate ? 2 * I : I;
 
-  auto mark = [&](int i) {
-    if (!t->stage_events || !t->stage_events[i]) return;
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    cudaStreamIsCapturing(s, &cs);
-    cudaEvent_t ev = (cudaEvent_t)t->stage_events[i];
-    if (cs == cudaStreamCaptureStatusActive)
-      cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal);
-    else
-      cudaEventRecord(ev, s);
-  };
-  mark(0);
+  mark_stage(t, 0, s);
   PermuteArgs pa{};
   pa.topk_idx = t->topk_idx;
   pa.T = T;
@@ -266,110 +375,30 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     gather_convert_kernel<<<conv_ctas_for(R, 8), 256, 0, s>>>(cv, pa.sorted_token);
     if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
   }
-  mark(1);
+  mark_stage(t, 1, s);
 
-  void* h = ws + L.h;
-  void* down_rows = ws + L.down_rows;
-  float* xa_gu = reinterpret_cast<float*>(ws + L.xa_gu);
-  float* xa_dn = reinterpret_cast<float*>(ws + L.xa_dn);
-  const int max_active = R < E ? R : E;
-  const int lora_tiles = R / kLoraRows + max_active;
+  ExpertRows x{};
+  x.x16 = x16;
+  x.x_scale = x_scale;
+  x.a_rows = use_umma ? nullptr : pa.sorted_token;
+  x.x_rows = use_umma ? R : T;
+  x.R = R;
+  x.max_rows_per_expert = T;
+  x.offsets = pa.offsets;
+  x.active = pa.active;
+  x.num_active = pa.num_active;
+  x.tile_a = pa.tile_start_a;
+  x.tile_b = pa.tile_start_b;
+  x.use_umma = use_umma;
+  x.h = ws + L.h;
+  x.down_rows = ws + L.down_rows;
+  x.xa_gu = reinterpret_cast<float*>(ws + L.xa_gu);
+  x.xa_dn = reinterpret_cast<float*>(ws + L.xa_dn);
+  x.umma_scratch = ws + L.umma;
+  x.err = err;
+  if ((st = run_expert_stages(d, t, x, s)) != E4B_OK) return st;
 
-  if (d.lora_rank > 0) {
-    LoraAArgs la{};
-    la.a = x16;
-    la.a_scale = x_scale;
-    la.a_rows = use_umma ? nullptr : pa.sorted_token;
-    la.loraA = t->gate_up_lora_A;
-    la.offsets = pa.offsets;
-    la.tile_start = pa.tile_start_a;
-    la.E = E;
-    la.K = H;
-    la.rank = d.lora_rank;
-    la.lora_dtype = d.lora_dtype;
-    la.scaling = d.lora_scaling;
-    la.xa = xa_gu;
-    la.max_tiles = lora_tiles;
-    if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
-  }
-  mark(2);
-
-  GemvArgs g{};
-  g.a = x16;
-  g.a_scale = x_scale;
-  g.a_rows = use_umma ? nullptr : pa.sorted_token;
-  g.packed = t->gate_up_packed;
-  g.absmax = t->gate_up_absmax;
-  g.offsets = pa.offsets;
-  g.active = pa.active;
-  g.num_active = pa.num_active;
-  g.E = E;
-  g.N = n1;
-  g.K = H;
-  g.epilogue = d.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
-  g.out = h;
-  g.out_dtype = E4B_F16;
-  g.Nout = I;
-  g.lora_xa = d.lora_rank > 0 ? xa_gu : nullptr;
-  g.lora_B = t->gate_up_lora_B;
-  g.lora_dtype = d.lora_dtype;
-  g.rank = d.lora_rank;
-  g.tiles_per_expert = n1 / 16;
-  g.max_tasks = max_active * g.tiles_per_expert;
-  g.err = err;
-  if (use_umma) {
-    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k, R);
-    st = launch_umma(u, d.act_dtype, s);
-  } else {
-    st = launch_gemv_auto(g, T, T, s);
-  }
-  if (st != E4B_OK) return st;
-  mark(3);
-
-  if (d.lora_rank > 0) {
-    LoraAArgs la{};
-    la.a = reinterpret_cast<const __half*>(h);
-    la.a_scale = nullptr;
-    la.a_rows = nullptr;
-    la.loraA = t->down_lora_A;
-    la.offsets = pa.offsets;
-    la.tile_start = pa.tile_start_a;
-    la.E = E;
-    la.K = I;
-    la.rank = d.lora_rank;
-    la.lora_dtype = d.lora_dtype;
-    la.scaling = d.lora_scaling;
-    la.xa = xa_dn;
-    la.max_tiles = lora_tiles;
-    if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
-  }
-  mark(4);
-
-  g.a = h;
-  g.a_scale = nullptr;
-  g.a_rows = nullptr;
-  g.packed = t->down_packed;
-  g.absmax = t->down_absmax;
-  g.N = H;
-  g.K = I;
-  g.epilogue = E4B_EPI_NONE;
-  g.out = down_rows;
-  g.out_dtype = E4B_F16;  // fp16 rows: one bf16 rounding (the final output) instead of two
-  g.Nout = H;
-  g.lora_xa = d.lora_rank > 0 ? xa_dn : nullptr;
-  g.lora_B = t->down_lora_B;
-  g.tiles_per_expert = H / 16;
-  g.max_tasks = max_active * g.tiles_per_expert;
-  if (use_umma) {
-    UmmaArgs u = umma_args_from(g, ws + L.umma, pa.tile_start_b, T, k, R);
-    st = launch_umma(u, d.act_dtype, s);
-  } else {
-    st = launch_gemv_auto(g, R, T, s);
-  }
-  if (st != E4B_OK) return st;
-  mark(5);
-
-  st = e4b_combine(down_rows, E4B_F16, pa.inv, t->topk_w, d.weight_dtype, T, k, H, t->out, d.out_dtype, stream);
-  mark(6);
+  st = e4b_combine(x.down_rows, E4B_F16, pa.inv, t->topk_w, d.weight_dtype, T, k, H, t->out, d.out_dtype, stream);
+  mark_stage(t, 6, s);
   return st;
 }

@@ -195,6 +195,30 @@ E4B_API e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tenso
 #define E4B_STATIC_SCRATCH_BYTES (16u << 20)
 E4B_API e4b_status e4b_moe_forward_static(const e4b_moe_desc* desc, const e4b_moe_tensors* t, void* stream);
 
+/* ---- Expert parallelism (experts sharded over P ranks) ---------
+ * No counterpart in the reference (it has no distributed code); the split
+ * follows its per-expert loop (_vendor/experts.py:486-513). Rank p owns the
+ * experts [p*E/P, (p+1)*E/P). One layer on every rank:
+ *   1. e4b_ep_dispatch on the rank's token shard: stable permutation by global
+ *      expert (as fast.py:125-135), rows gathered into send_rows [T*k, H] in that
+ *      order, per-expert row counts [E] and the inverse permutation [T*k].
+ *   2. caller: all-to-all of the counts (E/P per peer) and of the rows (the rows
+ *      for peer q are send_rows[offsets[q*E/P] .. offsets[(q+1)*E/P])).
+ *   3. e4b_ep_experts on the received rows (source-major): `local` describes the
+ *      rank's experts (num_experts = E/P, top_k = 1, tokens = received rows,
+ *      out_dtype = E4B_F16), `recv_counts` [P, E/P] (device), t->hidden = received
+ *      rows, t->out = unweighted fp16 down rows [tokens, H] in the received order;
+ *      t's weight/adapter pointers are the rank's expert slices. topk_* unused.
+ *   4. caller: reverse all-to-all of those rows; they land in send_rows' order.
+ *   5. e4b_combine(rows, E4B_F16, inv, topk_w, ...) on the shard. */
+E4B_API size_t e4b_ep_dispatch_workspace_bytes(int T, int k, int E);
+E4B_API e4b_status e4b_ep_dispatch(const void* hidden, int act_dtype, const int64_t* topk_idx, int T, int k, int E,
+                           int H, void* send_rows, int32_t* expert_counts, int32_t* inv, void* workspace,
+                           size_t workspace_bytes, void* stream);
+E4B_API size_t e4b_ep_experts_workspace_bytes(const e4b_moe_desc* local, int world);
+E4B_API e4b_status e4b_ep_experts(const e4b_moe_desc* local, int world, const int32_t* recv_counts,
+                          const e4b_moe_tensors* t, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Reads (and clears) the device error word of a workspace used by the calls
  * above. Synchronises `stream`; for debugging and tests, not the hot path. */
 E4B_API e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out);
