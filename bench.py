@@ -57,7 +57,7 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks/throttle reasons sampled every 50 ms while running."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -72,7 +72,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
         except (OSError, FileNotFoundError):
@@ -390,6 +390,42 @@ def run_ep(args, wl, world, rank, local):
         ms = float(t_.item())
     value = args.steps * wl["T"] / (ms / 1e3)
 
+    # phase breakdown of one layer on every rank (events between phases; outside the timed region)
+    def phases(s):
+        li = s % Lc
+        x = X[s % pool]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        lay = layers[li]
+        ev[0].record()
+        w, idx = pkg.route(x, routers[li], k, norm_topk_prob=wl["norm"])
+        ev[1].record()
+        send, counts, inv = lay.stages.dispatch(x, idx)
+        ev[2].record()
+        rc, ss, rs = lay.exchange_counts(counts)
+        ev[3].record()
+        rows = torch.empty(sum(rs), H, dtype=send.dtype, device=dev)
+        if world > 1:
+            torch.distributed.all_to_all_single(rows, send, rs, ss)
+        else:
+            rows.copy_(send)
+        ev[4].record()
+        back = lay.stages.experts(rows, rc)
+        ev[5].record()
+        ret = torch.empty(T * k, H, dtype=back.dtype, device=dev)
+        if world > 1:
+            torch.distributed.all_to_all_single(ret, back, ss, rs)
+        else:
+            ret.copy_(back)
+        ev[6].record()
+        lay.stages.combine(ret, inv, w, T, k, x.dtype)
+        ev[7].record()
+        torch.cuda.synchronize()
+        return [ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(7)]
+
+    ph = [phases(s) for s in range(6)][2:]
+    phase_names = ["router", "dispatch", "count_exchange_sync", "rows_a2a", "experts", "return_a2a", "combine"]
+    phase_us = {n: round(statistics.mean(v[i] for v in ph), 1) for i, n in enumerate(phase_names)}
+
     # per-stage device times of this rank's expert side, from the library's stage events
     cudart = _cudart()
     nst = N.MOE_STAGE_EVENTS
@@ -426,7 +462,8 @@ def run_ep(args, wl, world, rank, local):
                 "down_kernel_us": round(st_us["down"], 1),
                 "down_achieved_tflops": round(2.0 * Rr * H * I / (st_us["down"] * 1e-6) / 1e12, 1),
                 "rows_received": int(Rr), "stage_us": {n: round(v, 1) for n, v in st_us.items()},
-                "nvlink_bytes_per_layer_per_rank": int(2 * T * k * H * 2 * (world - 1) / world)}
+                "nvlink_bytes_per_layer_per_rank": int(2 * T * k * H * 2 * (world - 1) / world),
+                "phase_us_rank%d" % rank: phase_us}
 
     # e2e through the public API: pinned host tokens in, route + layer, output back to the host
     host_in = torch.empty(pool, T, H, dtype=torch.bfloat16, pin_memory=True)

@@ -78,6 +78,23 @@ def test_router_topk_bit_exact_on_same_logits(ops, T, E, k, H, kind, norm):
     torch.testing.assert_close(w.cpu(), rw, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("wdt,xdt", [(torch.float32, torch.float16), (torch.float16, torch.bfloat16),
+                                     (torch.float32, torch.bfloat16)])
+def test_router_mixed_dtypes_split_k(ops, wdt, xdt):
+    """Weights of another type than the activations, on the K-split tensor-core path."""
+    T, E, k, H = 100, 16, 4, 1024
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(T, H, generator=g).to(xdt)
+    wr = (torch.randn(E, H, generator=g) * 0.02).to(wdt)
+    w, idx, logits = ops.router_topk(x.to(DEV), wr.to(DEV), k, 0, False, return_logits=True)
+    logits = logits.cpu()
+    # the kernel rounds the weights to the activation type; the oracle sees the same values
+    ref_logits = M.router_logits_f32(x, wr.to(xdt))
+    assert torch.allclose(logits, ref_logits, rtol=1e-4, atol=1e-4)
+    rw, ridx = M.route_on_host(logits, k, M.SOFTMAX_THEN_TOPK, False)
+    assert torch.equal(idx.cpu(), ridx)
+
+
 def test_router_tie_known_answer(ops):
     """engines/cpu_router.py tie rule: logits [1,3,3,.5,3,2], k=3 -> [1,2,4]."""
     logits = torch.tensor([[1.0, 3.0, 3.0, 0.5, 3.0, 2.0]])
