@@ -20,6 +20,8 @@ E4B_ERR_EXPERT_INDEX = 6
 BF16, F16, F32 = 0, 1, 2
 SOFTMAX_THEN_TOPK, TOPK_THEN_SOFTMAX = 0, 1
 EPI_NONE, EPI_SWIGLU, EPI_SILU = 0, 1, 2
+FMT_NF4, FMT_FP8_BLOCK128 = 0, 1
+ABI_VERSION = 2
 
 # Every symbol include/e4b.h exports, in declaration order.
 EXPORTED_SYMBOLS = (
@@ -27,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "e4b_nf4_quantize", "e4b_nf4_dequantize", "e4b_nf4_quantize_host", "e4b_nf4_dequantize_host",
     "e4b_router_workspace_bytes", "e4b_router_topk",
     "e4b_permute_workspace_bytes", "e4b_permute",
+    "e4b_fp8_block_dequantize",
     "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
     "e4b_combine",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
@@ -49,7 +52,8 @@ class E4BError(RuntimeError):
 class MoeDesc(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in (
         "num_experts", "hidden", "intermediate", "top_k", "tokens", "has_gate", "act_dtype",
-        "weight_dtype", "out_dtype", "lora_rank", "lora_dtype")] + [("lora_scaling", ctypes.c_float)]
+        "weight_dtype", "out_dtype", "lora_rank", "lora_dtype")] + [("lora_scaling", ctypes.c_float),
+                                                                     ("weight_format", ctypes.c_int)]
 
 
 class MoeTensors(ctypes.Structure):
@@ -77,6 +81,7 @@ def _declare(lib):
         "e4b_router_topk": (I, [P, I, P, I, I, I, I, I, I, I, P, P, P, P, SZ, P]),
         "e4b_permute_workspace_bytes": (SZ, [I, I, I]),
         "e4b_permute": (I, [P, I, I, I, P, P, P, P, SZ, P]),
+        "e4b_fp8_block_dequantize": (I, [P, P, I64, I64, P, I, P]),
         "e4b_grouped_gemm_workspace_bytes": (SZ, [I, I, I, I]),
         "e4b_grouped_nf4_gemm": (I, [P, I, P, P, P, P, I, I, I, I, I, P, P, SZ, P]),
         "e4b_combine": (I, [P, I, P, P, I, I, I, I, P, I, P]),
@@ -111,7 +116,7 @@ def lib():
                 except OSError as e:
                     raise NativeLibraryError(f"failed to load {LIB_PATH}: {e}") from e
                 _declare(l)
-                if l.e4b_abi_version() != 1:
+                if l.e4b_abi_version() != ABI_VERSION:
                     raise NativeLibraryError("libe4b.so ABI version mismatch; rebuild it")
                 _lib = l
     return _lib

@@ -228,6 +228,7 @@ extern "C" e4b_status e4b_ep_experts(const e4b_moe_desc* local, int world, const
   if (d.hidden % 64 || d.intermediate % 64) return E4B_ERR_UNSUPPORTED;
   if (d.lora_rank < 0 || d.lora_rank > kLoraMaxRank) return E4B_ERR_UNSUPPORTED;
   if (d.lora_rank > 0 && !is_any_dtype(d.lora_dtype)) return E4B_ERR_UNSUPPORTED;
+  if (e4b_status fs = check_weight_format(d)) return fs;
   const int R = d.tokens, El = d.num_experts, H = d.hidden, I = d.intermediate;
   if (!recv_counts || !t->gate_up_packed || !t->gate_up_absmax || !t->down_packed || !t->down_absmax)
     return E4B_ERR_INVALID_ARG;

@@ -36,6 +36,9 @@ e4b_status launch_gemv(const GemvArgs& g, int max_rows_per_expert, cudaStream_t 
 bool gemv_stream_eligible(const GemvArgs& g, int x_rows, int max_rows_per_expert);
 e4b_status launch_gemv_stream(const GemvArgs& g, int x_rows, int max_rows_per_expert, cudaStream_t s);
 
+// Block-scaled FP8 weights (fp8.cu): bf16 activations, `absmax` holds the fp32 tile scales.
+e4b_status launch_fp8_gemv(const GemvArgs& g, cudaStream_t s);
+
 // Picks the streaming kernel when eligible, else the general one.
 inline e4b_status launch_gemv_auto(const GemvArgs& g, int x_rows, int max_rows_per_expert, cudaStream_t s) {
   if (gemv_stream_eligible(g, x_rows, max_rows_per_expert)) return launch_gemv_stream(g, x_rows, max_rows_per_expert, s);

@@ -70,6 +70,35 @@ e4b_status launch_gather_convert(const ConvertArgs& c, const int32_t* rows_map, 
   return launch_status();
 }
 
+__global__ void __launch_bounds__(256) gather_rows16_kernel(const uint4* __restrict__ src,
+                                                            const int32_t* __restrict__ map, int rows, int vec,
+                                                            uint4* __restrict__ dst) {
+  const int lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += gridDim.x * 8) {
+    const uint4* a = src + (int64_t)map[r] * vec;
+    uint4* b = dst + (int64_t)r * vec;
+    for (int v = lane; v < vec; v += 32) b[v] = a[v];
+  }
+}
+
+e4b_status launch_gather_rows16(const void* src, const int32_t* rows_map, int rows, int K, void* dst, cudaStream_t s) {
+  if (rows <= 0) return E4B_OK;
+  int c = (rows + 7) / 8;
+  c = c > 148 * 8 ? 148 * 8 : c;
+  gather_rows16_kernel<<<c, 256, 0, s>>>(static_cast<const uint4*>(src), rows_map, rows, K / 8,
+                                         static_cast<uint4*>(dst));
+  return launch_status();
+}
+
+e4b_status check_weight_format(const e4b_moe_desc& d) {
+  if (d.weight_format == E4B_FMT_NF4) return E4B_OK;
+  if (d.weight_format != E4B_FMT_FP8_BLOCK128) return E4B_ERR_INVALID_ARG;
+  // FP8 experts: whole 128x128 scale tiles, no adapters
+  if (d.lora_rank != 0) return E4B_ERR_UNSUPPORTED;
+  if (d.hidden % 128 || d.intermediate % 128) return E4B_ERR_UNSUPPORTED;
+  return E4B_OK;
+}
+
 int conv_ctas_for(int rows, int warps_per_cta) {
   int c = (rows + warps_per_cta - 1) / warps_per_cta;
   return c < 1 ? 1 : (c > 148 * 4 ? 148 * 4 : c);
@@ -102,6 +131,55 @@ e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, co
   const int max_active = R < E ? R : E;
   const int lora_tiles = R / kLoraRows + max_active;
   e4b_status st = E4B_OK;
+  if (d.weight_format == E4B_FMT_FP8_BLOCK128) {
+    mark_stage(t, 2, s);
+    GemvArgs g{};
+    g.a = x.x16;
+    g.a_scale = x.x_scale;
+    g.a_rows = x.a_rows;
+    g.packed = t->gate_up_packed;
+    g.absmax = t->gate_up_absmax;  // fp32 tile scales
+    g.offsets = x.offsets;
+    g.active = x.active;
+    g.num_active = x.num_active;
+    g.E = E;
+    g.N = n1;
+    g.K = H;
+    g.epilogue = d.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
+    g.out = x.h;
+    g.out_dtype = E4B_F16;
+    g.Nout = I;
+    g.tiles_per_expert = I / 16;
+    g.max_tasks = max_active * g.tiles_per_expert;
+    g.err = x.err;
+    if (x.use_umma)
+      st = launch_umma(umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R), d.act_dtype, s, d.weight_format);
+    else
+      st = launch_fp8_gemv(g, s);
+    if (st != E4B_OK) return st;
+    mark_stage(t, 3, s);
+    mark_stage(t, 4, s);
+    g.a = x.h;
+    g.a_scale = nullptr;
+    g.a_rows = nullptr;
+    g.packed = t->down_packed;
+    g.absmax = t->down_absmax;
+    g.N = H;
+    g.K = I;
+    g.epilogue = E4B_EPI_NONE;
+    g.out = x.down_rows;
+    g.out_dtype = E4B_F16;
+    g.Nout = H;
+    g.tiles_per_expert = H / 16;
+    g.max_tasks = max_active * g.tiles_per_expert;
+    if (x.use_umma)
+      st = launch_umma(umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R), d.act_dtype, s, d.weight_format);
+    else
+      st = launch_fp8_gemv(g, s);
+    if (st != E4B_OK) return st;
+    mark_stage(t, 5, s);
+    return E4B_OK;
+  }
   if (d.lora_rank > 0) {
     LoraAArgs la{};
     la.a = x.x16;
@@ -226,7 +304,7 @@ extern "C" const char* e4b_status_string(e4b_status s) {
   return "unknown status";
 }
 
-extern "C" int e4b_abi_version(void) { return 1; }
+extern "C" int e4b_abi_version(void) { return 2; }
 
 extern "C" e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out) {
   if (!workspace || !error_out) return E4B_ERR_INVALID_ARG;
@@ -317,6 +395,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   if (d.hidden % 64 || d.intermediate % 64) return E4B_ERR_UNSUPPORTED;
   if (d.lora_rank < 0 || d.lora_rank > kLoraMaxRank) return E4B_ERR_UNSUPPORTED;
   if (d.lora_rank > 0 && !is_any_dtype(d.lora_dtype)) return E4B_ERR_UNSUPPORTED;
+  if (e4b_status fs = check_weight_format(d)) return fs;
   const int T = d.tokens, k = d.top_k, E = d.num_experts, H = d.hidden, I = d.intermediate;
   if (T == 0) return E4B_OK;
   if (!t->hidden || !t->topk_idx || !t->topk_w || !t->gate_up_packed || !t->gate_up_absmax || !t->down_packed ||

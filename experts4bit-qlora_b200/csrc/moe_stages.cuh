@@ -9,7 +9,7 @@ namespace e4b {
 // Rows already grouped by expert, with their segment tables, and the scratch the
 // stages write. `x16` holds fp16 activations with per-row power-of-two scales.
 struct ExpertRows {
-  const __half* x16;
+  const __half* x16;            // fp16 rows with per-row power-of-two scales
   const float* x_scale;
   const int32_t* a_rows;        // nullable: sorted row r reads x16[a_rows[r]] (streaming path only)
   int x_rows;                   // rows of x16
@@ -42,5 +42,9 @@ e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, co
 int conv_ctas_for(int rows, int warps_per_cta);
 // dst[r] = fp16(src[rows_map[r]]) with per-row power-of-two scales (convert.cuh).
 e4b_status launch_gather_convert(const ConvertArgs& c, const int32_t* rows_map, cudaStream_t s);
+// dst[r] = src[rows_map[r]] for rows of K 16-bit elements (K % 8 == 0), no conversion.
+e4b_status launch_gather_rows16(const void* src, const int32_t* rows_map, int rows, int K, void* dst, cudaStream_t s);
+// Validation shared by the fused layer entry points.
+e4b_status check_weight_format(const e4b_moe_desc& d);
 
 }  // namespace e4b

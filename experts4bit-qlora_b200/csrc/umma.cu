@@ -28,6 +28,7 @@
 // same time share the weight tile through L2. Every wait is bounded; a timeout
 // raises E4B_ERR_TIMEOUT and all roles run to the common exit (TMEM is freed).
 #include "async.cuh"
+#include "fp8.cuh"
 #include "umma.cuh"
 #include "tmap.cuh"
 
@@ -60,18 +61,22 @@ constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA N)
 constexpr int kRows = 128;          // weight rows per group (UMMA M)
 constexpr int kKc = 64;             // K per chunk
 constexpr int kThreads = 512;
-constexpr int kWBytes = kRows * kKc / 2;        // 4 KB packed per group
 constexpr int kABytes = kRows * kKc * 2;        // 16 KB fp16 per group
 constexpr int kBBytes = kTok * kKc * 2;         // 16 KB fp16
 constexpr int kLut = 256 * 128;
 constexpr int kEpiMaxRank = 16;  // LoRA ranks above this take the streaming path
 
-struct Smem {
+// Shared-memory plan per weight format: NF4 rows carry 32 packed bytes per 64-wide
+// chunk and need the 32 KB pair table; FP8 rows carry 64 bytes and no table.
+template <int FMT>
+struct SmemT {
+  static constexpr int wrow = FMT == E4B_FMT_NF4 ? kKc / 2 : kKc;  // weight bytes per row per chunk
+  static constexpr int wbytes = kRows * wrow;                      // per group per stage
   static constexpr int lut = 0;
-  static constexpr int a = kLut;                                  // [stage][group] 16 KB, 1024-aligned
+  static constexpr int a = FMT == E4B_FMT_NF4 ? kLut : 0;          // [stage][group] 16 KB, 1024-aligned
   static constexpr int b = a + kSA * 2 * kABytes;                 // [stage] 16 KB
-  static constexpr int w = b + kSB * kBBytes;                     // [stage][group] 4 KB
-  static constexpr int epi = w + kSW * 2 * kWBytes;                // epilogue staging
+  static constexpr int w = b + kSB * kBBytes;                     // [stage][group]
+  static constexpr int epi = w + kSW * 2 * wbytes;                // epilogue staging
   static constexpr int bars = epi + kTok * (1 + kEpiMaxRank) * 4;
   // full_w, w_empty [kSW]; full_b, b_empty [kSB]; a_ready, a_empty [kSA]; acc_full, acc_empty [2]
   static constexpr int nbars = 2 * kSW + 2 * kSB + 2 * kSA + 4;
@@ -114,9 +119,10 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: fp16 A and B, fp32 D, both K-major, M = 128, N = kTok.
-__device__ __forceinline__ uint32_t idesc_f16() {
-  return (1u << 4) | ((uint32_t)(kTok >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+// kind::f16 instruction descriptor: fp16 (or bf16) A and B, fp32 D, both K-major, M = 128, N = kTok.
+__device__ __forceinline__ uint32_t idesc_f16(bool bf16) {
+  const uint32_t ab = bf16 ? (1u << 7) | (1u << 10) : 0u;  // A and B formats
+  return (1u << 4) | ab | ((uint32_t)(kTok >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
@@ -167,9 +173,11 @@ __device__ __forceinline__ void tile_info(const int32_t* ts, const int32_t* offs
 
 }  // namespace
 
-template <typename OutT, int GROUPS>
+template <typename OutT, int GROUPS, int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
     nf4_umma_kernel(UmmaArgs u, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap) {
+  using Smem = SmemT<FMT>;
+  constexpr int kWBytes = Smem::wbytes;
   extern __shared__ __align__(1024) char smem[];
 #ifdef E4B_TRACE
   const long long t_start = clock64();
@@ -222,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  {  // pair table: entry e of lane l at (e << 7) | (l << 2)
+  if (FMT == E4B_FMT_NF4) {  // pair table: entry e of lane l at (e << 7) | (l << 2)
     const float code = c_nf4[lane & 15];
     for (int e = warp; e < 256; e += kThreads / 32) {
       const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
@@ -248,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int h = 0; h < GROUPS; ++h) {
             const int row = ti.e * g.N + (h == 0 ? ti.ft * kRows : (g.N / 2) + ti.ft * kRows);
-            tma_load_2d(smem + Smem::w + (s * 2 + h) * kWBytes, &wmap, c * (kKc / 2), row, &full_w[s]);
+            tma_load_2d(smem + Smem::w + (s * 2 + h) * kWBytes, &wmap, c * Smem::wrow, row, &full_w[s]);
           }
         }
       }
@@ -275,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 3) {
     // ---------------- MMA issuer -------------------------------------------------------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16();
+      const uint32_t idesc = idesc_f16(false);
       int n = 0, it = 0;
       for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
         const int buf = it & 1;
@@ -311,6 +319,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       TileInfo ti;
       tile_info(s_ts, s_offs, g.E, nft, t, ti);
       const int row = h == 0 ? ti.ft * kRows + r : (g.N / 2) + ti.ft * kRows + r;
+      if (FMT == E4B_FMT_FP8_BLOCK128) {
+        // e4m3 row -> fp16(fp32(w) * s_kb / s_ref): the tile's 128 rows share one scale per 128-wide
+        // K block; s_ref (the largest over K) goes back in the epilogue. For e8m0 scales the ratio
+        // is a power of two <= 1 and the operand is exact while it stays above fp16's 2^-24.
+        const float* sc = g.absmax + ((int64_t)ti.e * (g.N / kFp8Block) + row / kFp8Block) * (g.K / kFp8Block);
+        float inv_ref = 0.f;
+        if (h < GROUPS) {
+          float m = 0.f;
+          for (int kb = 0; kb < g.K / kFp8Block; ++kb) m = fmaxf(m, __ldg(sc + kb));
+          inv_ref = m > 0.f ? 1.f / m : 0.f;
+        }
+        for (int c = 0; c < kchunks; ++c, ++n) {
+          const int s = n % kSW, sa = n % kSA;
+          const float scale = h < GROUPS ? __ldg(sc + (c >> 1)) * inv_ref : 0.f;
+          if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (n / kSW) & 1)) : wt.wait(&full_w[s], (n / kSW) & 1))) break;
+          uint4 p[4];
+          const int rot = r & 3;  // rotated unit order spreads a quarter-warp over the banks
+          if (h < GROUPS) {
+            const uint4* wsrc = reinterpret_cast<const uint4*>(smem + Smem::w + (s * 2 + h) * kWBytes + r * 64);
+#pragma unroll
+            for (int u4 = 0; u4 < 4; ++u4) p[u4] = wsrc[(u4 + rot) & 3];
+          }
+          fence_proxy_async();
+          mbar_arrive(&w_empty[s]);
+          if (!wt.wait(&a_empty[sa], ((n / kSA) & 1) ^ 1)) break;
+          if (h < GROUPS) {
+            char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
+            const int swz = (smem_u32(adst) >> 7) & 7;
+#pragma unroll
+            for (int u4 = 0; u4 < 4; ++u4) {  // 16 weight bytes -> A units 2U, 2U+1 (8 fp16 each)
+              const int U = (u4 + rot) & 3;
+              const uint32_t wd[4] = {p[u4].x, p[u4].y, p[u4].z, p[u4].w};
+              uint32_t o[8];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                o[2 * j] = e4m3x2_to_f16x2_scaled(wd[j] & 0xffffu, scale);
+                o[2 * j + 1] = e4m3x2_to_f16x2_scaled(wd[j] >> 16, scale);
+              }
+              *reinterpret_cast<uint4*>(adst + (((2 * U) ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<uint4*>(adst + (((2 * U + 1) ^ swz) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+          }
+          fence_proxy_async();
+          mbar_arrive(&a_ready[sa]);
+        }
+        continue;
+      }
       const float* am = g.absmax + ((int64_t)ti.e * g.N + row) * (g.K / 64);
       float am_next = h < GROUPS ? __ldg(am) : 0.f;
       for (int c = 0; c < kchunks; ++c, ++n) {
@@ -366,6 +421,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int rowA = ti.ft * kRows + r;
       const int rowB = (g.N / 2) + ti.ft * kRows + r;
       const int feat = ti.ft * kRows + r;  // output column
+      float wsa = 1.f, wsb = 1.f;          // FP8: the tile's reference scales (gate, up)
+      if (FMT == E4B_FMT_FP8_BLOCK128) {
+        const int kbs = g.K / kFp8Block;
+        const float* sa_ = g.absmax + ((int64_t)ti.e * (g.N / kFp8Block) + rowA / kFp8Block) * kbs;
+        const float* sb_ = g.absmax + ((int64_t)ti.e * (g.N / kFp8Block) + rowB / kFp8Block) * kbs;
+        float ma = 0.f, mb = 0.f;
+        for (int kb = 0; kb < kbs; ++kb) {
+          ma = fmaxf(ma, __ldg(sa_ + kb));
+          if (GROUPS == 2) mb = fmaxf(mb, __ldg(sb_ + kb));
+        }
+        wsa = ma;
+        wsb = mb;
+      }
       {  // token r of the tile: scale and LoRA-A vector
         const int m = ti.tt * kTok + r;
         float sc = 1.f;
@@ -397,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (m >= ti.M) break;
           const int64_t srow = ti.row0 + m;
           const float sc = s_sc[c0 + i];
-          float xa = va[i] * sc, xb = GROUPS == 2 ? vb[i] * sc : 0.f;
+          float xa = va[i] * (sc * wsa), xb = GROUPS == 2 ? vb[i] * (sc * wsb) : 0.f;
           if (rank) {  // rank is a multiple of 4 here: 128-bit broadcast reads of the token's vector
             const float4* la = reinterpret_cast<const float4*>(s_xa + (c0 + i) * rank);
 #pragma unroll
@@ -458,15 +526,16 @@ UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_st
   return u;
 }
 
-template <typename OutT, int GROUPS>
+template <typename OutT, int GROUPS, int FMT>
 static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
+  using Smem = SmemT<FMT>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return E4B_ERR_CUDA;
   static unsigned long long configured = 0;
   static int sm_count[64] = {0};
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(configured & bit)) {
-    if (cudaFuncSetAttribute(nf4_umma_kernel<OutT, GROUPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(nf4_umma_kernel<OutT, GROUPS, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Smem::total) != cudaSuccess)
       return E4B_ERR_CUDA;
     cudaDeviceGetAttribute(&sm_count[dev & 63], cudaDevAttrMultiProcessorCount, dev);
@@ -478,10 +547,11 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   const int bound = u.max_tiles * nft;
   if (bound < grid) grid = bound;
   if (grid < 1) return E4B_OK;
-  CUtensorMap wmap;  // packed bytes [E*N rows][K/2 bytes], box {32 B, 128 rows}
-  const cuuint64_t dims[2] = {(cuuint64_t)(g.K / 2), (cuuint64_t)g.E * g.N};
-  const cuuint64_t str[1] = {(cuuint64_t)(g.K / 2)};
-  const cuuint32_t box[2] = {kKc / 2, kRows};
+  CUtensorMap wmap;  // weight bytes [E*N rows][K bytes per row (K/2 for NF4)], box {bytes of a chunk, 128 rows}
+  const cuuint64_t row_bytes = FMT == E4B_FMT_NF4 ? (cuuint64_t)(g.K / 2) : (cuuint64_t)g.K;
+  const cuuint64_t dims[2] = {row_bytes, (cuuint64_t)g.E * g.N};
+  const cuuint64_t str[1] = {row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)Smem::wrow, kRows};
   if (!encode_tiled(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, g.packed, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
     return E4B_ERR_CUDA;
   if (g.a_rows) return E4B_ERR_UNSUPPORTED;  // activations must be expert-sorted rows
@@ -491,16 +561,23 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   const cuuint32_t bbox[2] = {kKc, kTok};
   if (!encode_tiled(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.a, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B))
     return E4B_ERR_CUDA;
-  nf4_umma_kernel<OutT, GROUPS><<<grid, kThreads, Smem::total, s>>>(u, wmap, bmap);
+  nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kThreads, Smem::total, s>>>(u, wmap, bmap);
   return launch_status();
 }
 
-e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s) {
+e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s, int weight_format) {
   (void)act_dtype;
   const bool two = u.g.epilogue == E4B_EPI_SWIGLU;
+  if (weight_format == E4B_FMT_FP8_BLOCK128) {
+    if (u.g.K % kFp8Block || (two ? (u.g.N / 2) % kFp8Block : u.g.N % kFp8Block) || u.g.rank) return E4B_ERR_UNSUPPORTED;
+    if (u.g.out_dtype == E4B_BF16)
+      return two ? launch_groups<__nv_bfloat16, 2, E4B_FMT_FP8_BLOCK128>(u, s)
+                 : launch_groups<__nv_bfloat16, 1, E4B_FMT_FP8_BLOCK128>(u, s);
+    return two ? launch_groups<__half, 2, E4B_FMT_FP8_BLOCK128>(u, s) : launch_groups<__half, 1, E4B_FMT_FP8_BLOCK128>(u, s);
+  }
   if (u.g.out_dtype == E4B_BF16)
-    return two ? launch_groups<__nv_bfloat16, 2>(u, s) : launch_groups<__nv_bfloat16, 1>(u, s);
-  return two ? launch_groups<__half, 2>(u, s) : launch_groups<__half, 1>(u, s);
+    return two ? launch_groups<__nv_bfloat16, 2, E4B_FMT_NF4>(u, s) : launch_groups<__nv_bfloat16, 1, E4B_FMT_NF4>(u, s);
+  return two ? launch_groups<__half, 2, E4B_FMT_NF4>(u, s) : launch_groups<__half, 1, E4B_FMT_NF4>(u, s);
 }
 
 }  // namespace e4b

@@ -18,6 +18,6 @@ struct UmmaArgs {
 size_t umma_workspace_bytes(int T, int k, int E, int H, int I);
 bool umma_eligible(int T, int k, int E, int H, int I, int has_gate, int act_dtype, int lora_rank);
 UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k, int x_rows);
-e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s);
+e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s, int weight_format = E4B_FMT_NF4);
 
 }  // namespace e4b

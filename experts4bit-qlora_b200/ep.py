@@ -41,12 +41,22 @@ class ExpertShard:
     first: int
     count: int
     lora: tuple | None = None      # (A_gu, B_gu, A_dn, B_dn, scaling), expert-sliced
+    weight_format: int = N.FMT_NF4  # FMT_FP8_BLOCK128: *_packed = e4m3 bytes, *_absmax = fp32 tile scales
 
 
 def shard_experts(mod, rank: int, world: int) -> ExpertShard:
-    """Slice an ``ExpertsNbit`` (or ``ExpertsLoRA``) module's experts for ``rank``."""
+    """Slice an ``ExpertsNbit`` / ``ExpertsLoRA`` / ``ExpertsFp8Blocks`` module's experts for ``rank``."""
     base = mod.base if hasattr(mod, "base") else mod
     E = base.num_experts
+    if getattr(base, "quant_type", None) == "fp8_block128":
+        if E % world:
+            raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+        El = E // world
+        lo, hi = rank * El, (rank + 1) * El
+        gs, ds = base.scale_values()
+        return ExpertShard(base.gate_up_proj.data[lo:hi].contiguous(), gs[lo:hi].contiguous(),
+                           base.down_proj.data[lo:hi].contiguous(), ds[lo:hi].contiguous(), lo, El, None,
+                           N.FMT_FP8_BLOCK128)
     if E % world:
         raise ValueError(f"{E} experts do not split evenly over {world} ranks")
     El = E // world
@@ -87,7 +97,7 @@ class NativeStages:
         dev = rows.device
         out = torch.empty(Rr, self.H, dtype=torch.float16, device=dev)
         d = MoeDesc_from(sh.count, self.H, self.I, 1, Rr, self.has_gate, rows.dtype, torch.float32, torch.float16,
-                         sh.lora)
+                         sh.lora, sh.weight_format)
         t = N.MoeTensors()
         t.hidden = rows.data_ptr() if Rr else None
         t.gate_up_packed, t.gate_up_absmax = sh.gate_up_packed.data_ptr(), sh.gate_up_absmax.data_ptr()

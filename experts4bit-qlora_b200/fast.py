@@ -33,8 +33,25 @@ def fast_available() -> bool:
     return _native.available() and torch.cuda.is_available()
 
 
+def _eligible_fp8(mod) -> Optional[str]:
+    """Eligibility of an ``ExpertsFp8Blocks`` stack for the fused FP8 path."""
+    n1, k1 = mod._gate_up_shape
+    n2, k2 = mod._down_shape
+    if n1 % 128 or k1 % 128 or n2 % 128 or k2 % 128 or (mod.has_gate and (n1 // 2) % 128):
+        return "FP8 dims not multiples of the 128x128 scale tile"
+    if mod.num_experts > 1024:
+        return "more than 1024 experts"
+    if not mod.gate_up_proj.is_cuda:
+        return "storage not on CUDA"
+    if getattr(mod, "act_fn", None) is not torch.nn.functional.silu:
+        return "activation is not SiLU"
+    return None
+
+
 def _eligible(mod) -> Optional[str]:
     """None if ``mod`` can take the fused path, else the reason (``fast.py:75-97``)."""
+    if getattr(mod, "quant_type", None) == "fp8_block128":
+        return _eligible_fp8(mod)
     if getattr(mod, "_e4b_mxfp4_arena", False):
         return "storage is MXFP4 (arena), which the NF4 grouped kernel cannot read"
     if getattr(mod, "bits", None) != 4 or getattr(mod, "quant_type", None) != "nf4":
@@ -78,6 +95,21 @@ def fused_experts_forward(mod, hidden_states, top_k_index, top_k_weights):
     return _run(mod, hidden_states, top_k_index, top_k_weights, compute_dtype, hidden_states.dtype)
 
 
+def fused_fp8_experts_forward(mod, hidden_states, top_k_index, top_k_weights):
+    """Fused inference forward of an ``ExpertsFp8Blocks`` stack (bf16 or fp16 compute)."""
+    if _grad_needed(mod, hidden_states):
+        return mod._e4b_fast_ref(hidden_states, top_k_index, top_k_weights)
+    compute_dtype = mod.compute_dtype if mod.compute_dtype is not None else hidden_states.dtype
+    if compute_dtype not in (torch.bfloat16, torch.float16) or mod.gate_up_proj.numel() == 0:
+        return mod._e4b_fast_ref(hidden_states, top_k_index, top_k_weights)
+    hs = hidden_states if hidden_states.dtype == compute_dtype else hidden_states.to(compute_dtype)
+    gs, ds = mod.scale_values()
+    return ops.moe_forward(hs, top_k_index, top_k_weights, mod.gate_up_proj, gs, mod.down_proj, ds,
+                           mod.num_experts, mod.intermediate_dim, has_gate=mod.has_gate,
+                           out_dtype=hidden_states.dtype, check_errors=_CHECK,
+                           weight_format=_native.FMT_FP8_BLOCK128)
+
+
 def fused_experts_lora_forward(mod, hidden_states, top_k_index, top_k_weights):
     """Fused inference forward of an ``ExpertsLoRA`` wrapper (``fast.py:163-257``):
     the adapter deltas run inside the grouped GEMMs, before the activation."""
@@ -98,6 +130,7 @@ def fused_experts_lora_forward(mod, hidden_states, top_k_index, top_k_weights):
 def enable_fast(model, verbose: bool = False) -> int:
     """Patch every eligible module under ``model``; returns the patch count (``fast.py:281-411``)."""
     from .experts import Experts4bit, ExpertsNbit
+    from .fp8_experts import ExpertsFp8Blocks
     from .lora import ExpertsLoRA
 
     stock_forwards = {ExpertsNbit.forward, Experts4bit.forward}
@@ -124,6 +157,19 @@ def enable_fast(model, verbose: bool = False) -> int:
             continue
         mod._e4b_fast_ref = mod.forward
         mod.forward = fused_experts_lora_forward.__get__(mod)
+        patched += 1
+    for mod in mods:
+        if not isinstance(mod, ExpertsFp8Blocks) or type(mod).forward is not ExpertsFp8Blocks.forward:
+            continue
+        reason = _eligible(mod)
+        if reason is not None:
+            if verbose:
+                print(f"[e4b.fast] skip {type(mod).__name__}: {reason}")
+            continue
+        if hasattr(mod, "_e4b_fast_ref"):
+            continue
+        mod._e4b_fast_ref = mod.forward
+        mod.forward = fused_fp8_experts_forward.__get__(mod)
         patched += 1
     for mod in mods:
         if not isinstance(mod, ExpertsNbit):

@@ -62,6 +62,24 @@ def nf4_dequantize(packed: torch.Tensor, absmax: torch.Tensor, shape, dtype=torc
     return out.view(*shape)
 
 
+def fp8_block_dequantize(w_u8: torch.Tensor, scale: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    """``e4b_fp8_block_dequantize``: e4m3 bytes ``[out, in]`` with fp32 tile multipliers
+    ``[ceil(out/128), ceil(in/128)]`` -> ``dtype`` (formats/fp8_blocks.py:60-128)."""
+    _cuda(w_u8, "w")
+    w = w_u8.contiguous()
+    if w.dtype != torch.uint8:
+        w = w.view(torch.uint8)
+    rows, cols = w.shape
+    if tuple(scale.shape) != ((rows + 127) // 128, (cols + 127) // 128):
+        raise ValueError(f"scale {tuple(scale.shape)} does not tile a [{rows}, {cols}] weight at 128")
+    sc = scale.float().contiguous()
+    out = torch.empty(rows, cols, dtype=dtype, device=w.device)
+    N.check(N.lib().e4b_fp8_block_dequantize(w.data_ptr(), sc.data_ptr(), rows, cols, out.data_ptr(),
+                                             N.dtype_code(dtype), N.stream_handle(w.device)),
+            "e4b_fp8_block_dequantize")
+    return out
+
+
 # --------------------------------------------------------------------------- #
 # Router, permutation, grouped GEMM, combine
 # --------------------------------------------------------------------------- #
@@ -145,11 +163,13 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
                 gate_up_packed: torch.Tensor, gate_up_absmax: torch.Tensor, down_packed: torch.Tensor,
                 down_absmax: torch.Tensor, num_experts: int, intermediate: int, has_gate: bool = True,
                 out_dtype=None, lora=None, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-                check_errors: bool = False) -> torch.Tensor:
+                check_errors: bool = False, weight_format: int = N.FMT_NF4) -> torch.Tensor:
     """One fused expert layer through ``e4b_moe_forward``.
 
     ``hidden [T,H]`` must already be in the compute dtype (bf16/fp16).
     ``lora`` = ``(A_gu [E,r,H], B_gu [E,n1,r], A_dn [E,r,I], B_dn [E,H,r], scaling)`` or None.
+    ``weight_format`` = ``FMT_FP8_BLOCK128``: the ``*_packed`` stacks are e4m3 bytes and the
+    ``*_absmax`` stacks fp32 tile multipliers (bf16 activations, no adapters).
     """
     _cuda(hidden, "hidden_states")
     if hidden.dtype not in (torch.bfloat16, torch.float16):
@@ -166,7 +186,8 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     out_dtype = out_dtype or hidden.dtype
     if out is None:
         out = torch.empty(T, H, dtype=out_dtype, device=hidden.device)
-    d = MoeDesc_from(num_experts, H, intermediate, k, T, has_gate, hidden.dtype, w.dtype, out_dtype, lora)
+    d = MoeDesc_from(num_experts, H, intermediate, k, T, has_gate, hidden.dtype, w.dtype, out_dtype, lora,
+                     weight_format)
     t = N.MoeTensors()
     t.hidden, t.topk_idx, t.topk_w = hidden.data_ptr(), idx.data_ptr(), w.data_ptr()
     t.gate_up_packed, t.gate_up_absmax = gate_up_packed.data_ptr(), gate_up_absmax.data_ptr()
@@ -195,8 +216,9 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     return out
 
 
-def MoeDesc_from(E, H, I, k, T, has_gate, act_dtype, w_dtype, out_dtype, lora) -> N.MoeDesc:
+def MoeDesc_from(E, H, I, k, T, has_gate, act_dtype, w_dtype, out_dtype, lora, weight_format=N.FMT_NF4) -> N.MoeDesc:
     d = N.MoeDesc()
+    d.weight_format = int(weight_format)
     d.num_experts, d.hidden, d.intermediate, d.top_k, d.tokens = E, H, I, k, T
     d.has_gate = int(bool(has_gate))
     d.act_dtype = N.dtype_code(act_dtype)
@@ -210,8 +232,10 @@ def MoeDesc_from(E, H, I, k, T, has_gate, act_dtype, w_dtype, out_dtype, lora) -
     return d
 
 
-def moe_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16, lora_rank=0) -> int:
+def moe_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16, lora_rank=0,
+                        weight_format=N.FMT_NF4) -> int:
     d = N.MoeDesc()
+    d.weight_format = int(weight_format)
     d.num_experts, d.hidden, d.intermediate, d.top_k, d.tokens = E, H, I, k, T
     d.has_gate = int(bool(has_gate))
     d.act_dtype = N.dtype_code(act_dtype)

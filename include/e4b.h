@@ -59,6 +59,15 @@ typedef enum {
 
 typedef enum { E4B_EPI_NONE = 0, E4B_EPI_SWIGLU = 1, E4B_EPI_SILU = 2 } e4b_epilogue;
 
+/* Expert weight storage of the fused layer.
+ * E4B_FMT_NF4: blockwise NF4 (2 codes per byte, first element in the high nibble)
+ *   with one fp32 absmax per 64 consecutive elements (_vendor/experts.py:398-457).
+ * E4B_FMT_FP8_BLOCK128: float8_e4m3fn bytes [out, in] per expert with one fp32
+ *   multiplier per [128, 128] tile, [ceil(out/128), ceil(in/128)] per expert, the
+ *   storage of formats/fp8_blocks.py:60-128 (an e8m0 scale is passed as its value
+ *   2^(b-127)). The fused layer uses the weights at full precision, fp32(w) * scale. */
+typedef enum { E4B_FMT_NF4 = 0, E4B_FMT_FP8_BLOCK128 = 1 } e4b_weight_format;
+
 E4B_API const char* e4b_status_string(e4b_status s);
 /* ABI version: bumped when a signature or a struct below changes. */
 E4B_API int e4b_abi_version(void);
@@ -109,6 +118,13 @@ E4B_API size_t e4b_permute_workspace_bytes(int T, int k, int E);
 E4B_API e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, int32_t* order, int32_t* inv,
                        int32_t* offsets, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Block-scaled FP8 weights (R12) -------------------------------------
+ * dequantize_fp8_blocks (formats/fp8_blocks.py:60-128): out[o, i] =
+ * dtype(fp32(e4m3 w[o, i]) * scale[o / 128, i / 128]); `scale` holds fp32 values
+ * [ceil(rows/128), ceil(cols/128)]; ragged final tiles are allowed. */
+E4B_API e4b_status e4b_fp8_block_dequantize(const uint8_t* w, const float* scale, int64_t rows, int64_t cols,
+                                    void* out, int out_dtype, void* stream);
+
 /* ---- Grouped NF4 GEMM (R3, R4, R6) --------------------------------------- */
 
 /* Replaces nf4_grouped.gemm_4bit_grouped(a, packed.view(E,N,K/2),
@@ -150,6 +166,7 @@ typedef struct {
   int lora_rank;          /* 0 = no adapter */
   int lora_dtype;         /* adapter dtype: E4B_F32 or E4B_BF16 (or E4B_F16) */
   float lora_scaling;     /* alpha / r */
+  int weight_format;      /* e4b_weight_format; FP8 takes no adapters and needs H, I % 128 == 0 */
 } e4b_moe_desc;
 
 typedef struct {

@@ -124,12 +124,12 @@ def reference_forward(st, hidden_states, top_k_index, top_k_weights, compute_dty
         for e in hit.tolist():
             pos, tok = torch.where(mask[e])
             x = hs[tok]
-            w_gu = dequant_expert(st["gate_up_packed"], st["gate_up_absmax"], e, gu_shape, cdt)
+            w_gu = expert_weight(st, "gate_up", e, cdt)
             proj = F.linear(x, w_gu)
             if lora is not None:
                 proj = proj + _lora(x, lora["gate_up_A"][e], lora["gate_up_B"][e], lora["scaling"])
             h = _epilogue(proj, has_gate)
-            w_dn = dequant_expert(st["down_packed"], st["down_absmax"], e, dn_shape, cdt)
+            w_dn = expert_weight(st, "down", e, cdt)
             d = F.linear(h, w_dn)
             if lora is not None:
                 d = d + _lora(h, lora["down_A"][e], lora["down_B"][e], lora["scaling"])
@@ -149,6 +149,11 @@ def fp32_oracle(st, hidden_states, top_k_index, top_k_weights, lora=None, w_cach
     dn_shape = (H, I)
     if w_cache is not None and "gu" in w_cache:
         W_gu, W_dn = w_cache["gu"], w_cache["dn"]
+    elif st.get("format", "nf4") == "fp8":
+        W_gu = torch.stack([expert_weight(st, "gate_up", e, torch.float32) for e in range(E)])
+        W_dn = torch.stack([expert_weight(st, "down", e, torch.float32) for e in range(E)])
+        if w_cache is not None:
+            w_cache["gu"], w_cache["dn"] = W_gu, W_dn
     else:
         W_gu = dequant_stack_f32(st["gate_up_packed"], st["gate_up_absmax"], gu_shape)
         W_dn = dequant_stack_f32(st["down_packed"], st["down_absmax"], dn_shape)
@@ -208,14 +213,37 @@ def fused_driver_forward(st, hidden_states, top_k_index, top_k_weights, compute_
 # --------------------------------------------------------------------------- #
 # FP8 e4m3 with 128x128 block scales (formats/fp8_blocks.py:60-128)
 # --------------------------------------------------------------------------- #
+def fp8_scale_values(scale):
+    """e8m0 bytes -> fp32 multipliers ``2**(b-127)`` (``fp8_blocks.py:44-60``, ``_scale_values``);
+    a float tensor already holds the values."""
+    scale = torch.as_tensor(scale)
+    if scale.dtype in (torch.uint8, torch.int8):
+        return torch.exp2((scale.view(torch.uint8).to(torch.int32) - 127).float())
+    return scale.float()
+
+
 def fp8_block_dequant(weight_u8, scale, block=128, dtype=torch.bfloat16):
-    """``dequantize_fp8_blocks``: ``(fp32(e4m3) * scale_tile).to(dtype)``; an fp32 scale
-    per ``block x block`` tile (the general path, ``fp8_blocks.py:126-127``)."""
+    """``dequantize_fp8_blocks`` (``fp8_blocks.py:60-128``). Aligned shapes
+    (``:104-121``): ``bf16(e4m3) * bf16(scale)`` in ``dtype``, i.e. the scale rounded to
+    ``dtype`` and one rounding of the product; ragged shapes (``:126-127``):
+    ``(fp32(e4m3) * scale).to(dtype)``."""
     w = torch.as_tensor(weight_u8).view(torch.float8_e4m3fn).float()
     out, inn = w.shape
-    s = torch.as_tensor(scale).float()
+    s = fp8_scale_values(scale)
+    if out % block == 0 and inn % block == 0:
+        s = s.to(dtype).float()
     s = s.repeat_interleave(block, 0)[:out].repeat_interleave(block, 1)[:, :inn]
     return (w * s).to(dtype)
+
+
+def expert_weight(st, which, e, dtype):
+    """Dequantized ``[out, in]`` weight of expert ``e`` (``which`` = "gate_up" | "down") of a
+    stack dict: NF4 (``format`` absent or "nf4") or FP8 blocks (``format`` == "fp8")."""
+    E, H, I, has_gate = st["E"], st["H"], st["I"], st.get("has_gate", True)
+    shape = ((2 * I if has_gate else I), H) if which == "gate_up" else (H, I)
+    if st.get("format", "nf4") == "fp8":
+        return fp8_block_dequant(st[which + "_w"][e].reshape(shape), st[which + "_scale"][e], dtype=dtype)
+    return dequant_expert(st[which + "_packed"], st[which + "_absmax"], e, shape, dtype)
 
 
 def rel_errors(got, ref):
