@@ -44,6 +44,16 @@ WORKLOADS = {
     "mixtral-ep": dict(E=8, H=4096, I=14336, k=2, T=8192, layers=32, norm=True, lora=0, ep=True,
                        desc="Mixtral-8x7B geometry (config 4): 32 MoE layers, E=8, H=4096, I=14336, top-2, "
                             "T=8192 tokens per layer sharded over the ranks, experts sharded over the ranks"),
+    # config 5: FP8 e4m3 experts with 128x128 e8m0 scales, Zipf(1.1) expert popularity; routes are
+    # sampled from that popularity (DeepSeek's sigmoid group-limited router is not this path's)
+    "deepseek-fp8-decode": dict(E=256, H=7168, I=2048, k=8, T=64, layers=4, norm=True, lora=0, ep=True, fmt="fp8",
+                                routing="zipf", bound="hbm",
+                                desc="DeepSeek-V3 geometry (config 5): E=256, H=7168, I=2048, top-8, FP8 e4m3 "
+                                     "128x128 blocks, Zipf(1.1) routing, decode bs=64 (global)"),
+    "deepseek-fp8-prefill": dict(E=256, H=7168, I=2048, k=8, T=16384, layers=4, norm=True, lora=0, ep=True,
+                                 fmt="fp8", routing="zipf", bound="tensor",
+                                 desc="DeepSeek-V3 geometry (config 5): E=256, H=7168, I=2048, top-8, FP8 e4m3 "
+                                      "128x128 blocks, Zipf(1.1) routing, prefill T=16384 (global)"),
 }
 
 
@@ -267,7 +277,15 @@ def run_ours(args, wl, world, rank, local):
     gu_bytes = mean_uniq * per_expert_gu + T * H * 2 + T * k * I * 2
     dn_bytes = mean_uniq * per_expert_dn + T * k * I * 2 + T * k * H * 2
     peaks, peak_kind = load_peaks()
-    if wl["T"] <= 16:
+    path = ops.moe_path(wl["E"], H, wl["I"], wl["k"], T, lora_rank=wl["lora"])
+    one_launch = path == N.PATH_DECODE_LAYER
+    if one_launch:
+        # the whole layer is one kernel (stage marks 1..6 follow it): its interval is mark 0 -> 1
+        layer_us = stage_avg_us["permute"]
+        bound, unit = "hbm", "GB/s"
+        achieved = (gu_bytes + dn_bytes) / (layer_us * 1e-6) / 1e9
+        peak = peaks["hbm_gbs"]
+    elif wl["T"] <= 16:
         bound, unit = "hbm", "GB/s"
         achieved = gu_bytes / (stage_avg_us["gate_up"] * 1e-6) / 1e9
         peak = peaks["hbm_gbs"]
@@ -276,12 +294,17 @@ def run_ours(args, wl, world, rank, local):
         flops = 2.0 * T * k * H * n1
         achieved = flops / (stage_avg_us["gate_up"] * 1e-6) / 1e12
         peak = peaks["bf16_tflops"]
-    roofline = {"bound": bound, "kernel": "nf4 grouped gate_up (SwiGLU fused)", "achieved": round(achieved, 1),
+    roofline = {"bound": bound,
+                "kernel": ("nf4 decode layer, one launch: permute + gate_up GEMV (SwiGLU) + down GEMV + combine"
+                           if one_launch else "nf4 grouped gate_up (SwiGLU fused)"),
+                "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": peak_kind, "unit": unit, "frac": round(achieved / peak, 4),
-                "traffic": None, "algorithmic_bytes_per_launch": int(gu_bytes),
-                "kernel_us": round(stage_avg_us["gate_up"], 3),
+                "traffic": None,
+                "algorithmic_bytes_per_launch": int(gu_bytes + dn_bytes) if one_launch else int(gu_bytes),
+                "kernel_us": round(stage_avg_us["permute"] if one_launch else stage_avg_us["gate_up"], 3),
                 "down_kernel_us": round(stage_avg_us["down"], 3),
-                "down_achieved": round(dn_bytes / (stage_avg_us["down"] * 1e-6) / 1e9, 1) if bound == "hbm" else None,
+                "down_achieved": (round(dn_bytes / (stage_avg_us["down"] * 1e-6) / 1e9, 1)
+                                  if bound == "hbm" and not one_launch else None),
                 "layer_bytes": int(gu_bytes + dn_bytes + wl["E"] * H * 2),
                 "stage_us": {k_: round(v, 3) for k_, v in stage_avg_us.items()},
                 "event_node_us_subtracted": round(node_us, 3)}
@@ -294,7 +317,8 @@ def run_ours(args, wl, world, rank, local):
         e2e["ms"] = float(t_.item())
     e2e_value = args.steps * T * Lc * world / (e2e["ms"] / 1e3)
 
-    launches_per_layer = 2 + (5 if wl["lora"] else 3) + 1  # router 2; permute, [lora], gate_up, down, combine
+    # router 2; then one layer kernel, or permute, [lora x2], gate_up, down, combine
+    launches_per_layer = 2 + (1 if one_launch else (5 if wl["lora"] else 3) + 1)
     result = {
         "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
@@ -323,8 +347,10 @@ def build_ep_layers(pkg, wl, dev, rank, world):
     """The rank's expert slice of every layer. Expert e of layer l is drawn from its own
     seed, so a slice holds the same weights whatever the world size."""
     ep = pkg.ep
+    f8 = pkg.fp8_experts
     E, H, I = wl["E"], wl["H"], wl["I"]
     El = E // world
+    fp8 = wl.get("fmt") == "fp8"
     shards, routers = [], []
     for li in range(wl["layers"]):
         parts = {"gu": [], "gua": [], "dn": [], "dna": []}
@@ -332,12 +358,17 @@ def build_ep_layers(pkg, wl, dev, rank, world):
             g = torch.Generator(device=dev).manual_seed(1_000_003 * li + e)
             for key, shape in (("gu", (2 * I, H)), ("dn", (H, I))):
                 w = (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-                packed, absmax = pkg.ops.nf4_quantize(w)
+                if fp8:
+                    q, sc = f8.quantize_fp8_blocks(w, "e8m0")
+                    packed, absmax = q, f8.scale_values(sc)
+                else:
+                    packed, absmax = pkg.ops.nf4_quantize(w)
                 parts[key].append(packed)
                 parts[key + "a"].append(absmax)
                 del w
         shards.append(ep.ExpertShard(torch.stack(parts["gu"]), torch.stack(parts["gua"]), torch.stack(parts["dn"]),
-                                     torch.stack(parts["dna"]), rank * El, El))
+                                     torch.stack(parts["dna"]), rank * El, El, None,
+                                     pkg._native.FMT_FP8_BLOCK128 if fp8 else pkg._native.FMT_NF4))
         g = torch.Generator(device=dev).manual_seed(7_000_001 + li)
         routers.append((torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16))
     torch.cuda.synchronize()
@@ -363,11 +394,28 @@ def run_ep(args, wl, world, rank, local):
     pool = 4
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     X = torch.randn(pool, T, H, generator=g, device=dev).to(torch.bfloat16)
+    zipf = wl.get("routing") == "zipf"
+    routes = None
+    if zipf:  # Zipf(1.1) popularity over a seeded permutation of the experts, the same on every rank
+        gp = torch.Generator(device=dev).manual_seed(4242)
+        perm = torch.randperm(E, generator=gp, device=dev)
+        pop = torch.empty(E, device=dev)
+        pop[perm] = 1.0 / torch.arange(1, E + 1, device=dev, dtype=torch.float32) ** 1.1
+        routes = []
+        for _ in range(pool):
+            idx = torch.multinomial(pop.expand(T, E), k, replacement=False, generator=g)
+            w = torch.softmax(torch.randn(T, k, generator=g, device=dev), -1)
+            routes.append((w, idx))
+
+    def route(s, x):
+        if zipf:
+            return routes[s % pool]
+        return pkg.route(x, routers[s % Lc], k, norm_topk_prob=wl["norm"])
 
     def step(s, x=None):
         li = s % Lc
         x = X[s % pool] if x is None else x
-        w, idx = pkg.route(x, routers[li], k, norm_topk_prob=wl["norm"])
+        w, idx = route(s, x)
         return layers[li](x, idx, w)
 
     for s in range(max(args.warmup, 3)):
@@ -397,7 +445,7 @@ def run_ep(args, wl, world, rank, local):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
         lay = layers[li]
         ev[0].record()
-        w, idx = pkg.route(x, routers[li], k, norm_topk_prob=wl["norm"])
+        w, idx = route(s, x)
         ev[1].record()
         send, counts, inv = lay.stages.dispatch(x, idx)
         ev[2].record()
@@ -430,11 +478,11 @@ def run_ep(args, wl, world, rank, local):
     cudart = _cudart()
     nst = N.MOE_STAGE_EVENTS
     stage_ms = [[] for _ in range(nst - 1)]
-    recv_rows = []
+    recv_rows, uniq = [], []
     for rep in range(4):
         li = rep % Lc
         x = X[rep % pool]
-        w, idx = pkg.route(x, routers[li], k, norm_topk_prob=wl["norm"])
+        w, idx = route(rep, x)
         lay = layers[li]
         send, counts, inv = lay.stages.dispatch(x, idx)
         rc, ss, rs = lay.exchange_counts(counts)
@@ -449,18 +497,28 @@ def run_ep(args, wl, world, rank, local):
         for si in range(nst - 1):
             stage_ms[si].append(ev[si].elapsed_ms(ev[si + 1]))
         recv_rows.append(rows.shape[0])
+        uniq.append(int((rc.sum(0) > 0).sum().item()))
     names = ["plan", "convert", "gate_up", "lora_a_h", "down", "scatter"]
     st_us = {n: 1e3 * statistics.mean(v) for n, v in zip(names, stage_ms)}
     Rr = statistics.mean(recv_rows)
-    gu_flops = 2.0 * Rr * H * 2 * I
     peaks, peak_kind = load_peaks()
-    peak = peaks["bf16_tflops"]
-    achieved = gu_flops / (st_us["gate_up"] * 1e-6) / 1e12
-    roofline = {"bound": "tensor", "kernel": "nf4 grouped gate_up (SwiGLU fused), tcgen05, rank 0 expert side",
-                "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind, "unit": "TFLOP/s",
+    wfmt = "fp8 e4m3 128x128" if wl.get("fmt") == "fp8" else "nf4"
+    if wl.get("bound", "tensor") == "hbm":
+        per_el = 1.0 if wl.get("fmt") == "fp8" else 0.5 + 4 / 64
+        gu_bytes = statistics.mean(uniq) * 2 * I * H * per_el
+        dn_bytes = statistics.mean(uniq) * H * I * per_el
+        achieved = gu_bytes / (st_us["gate_up"] * 1e-6) / 1e9
+        peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+        down_ach = dn_bytes / (st_us["down"] * 1e-6) / 1e9
+    else:
+        achieved = 2.0 * Rr * H * 2 * I / (st_us["gate_up"] * 1e-6) / 1e12
+        peak, unit, bound = peaks["bf16_tflops"], "TFLOP/s", "tensor"
+        down_ach = 2.0 * Rr * H * I / (st_us["down"] * 1e-6) / 1e12
+    roofline = {"bound": bound, "kernel": f"{wfmt} grouped gate_up (SwiGLU fused), rank 0 expert side",
+                "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind, "unit": unit,
                 "frac": round(achieved / peak, 4), "traffic": None, "kernel_us": round(st_us["gate_up"], 1),
-                "down_kernel_us": round(st_us["down"], 1),
-                "down_achieved_tflops": round(2.0 * Rr * H * I / (st_us["down"] * 1e-6) / 1e12, 1),
+                "down_kernel_us": round(st_us["down"], 1), "down_achieved": round(down_ach, 1),
+                "unique_local_experts": round(statistics.mean(uniq), 2),
                 "rows_received": int(Rr), "stage_us": {n: round(v, 1) for n, v in st_us.items()},
                 "nvlink_bytes_per_layer_per_rank": int(2 * T * k * H * 2 * (world - 1) / world),
                 "phase_us_rank%d" % rank: phase_us}
@@ -493,12 +551,14 @@ def run_ep(args, wl, world, rank, local):
         t_ = torch.tensor([e2e_ms], device=dev)
         torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(t_.item())
-    layer_gb = wl["E"] * (2 * I * H + H * I) * (0.5 + 4 / 64) / 1e9
+    layer_gb = wl["E"] * (2 * I * H + H * I) * (1.0 if wl.get("fmt") == "fp8" else 0.5 + 4 / 64) / 1e9
     result = {
         "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (random-init N(0,0.02) weights quantized to NF4; N(0,1) tokens; random router)",
+        "data": "synthetic (random-init N(0,0.02) weights quantized to %s; N(0,1) tokens; %s)" % (
+            "FP8 e4m3 with e8m0 128x128 scales" if wl.get("fmt") == "fp8" else "NF4",
+            "routes sampled from Zipf(1.1) expert popularity" if wl.get("routing") == "zipf" else "random router"),
         "config": {"workload": args.workload, "desc": wl["desc"], "tokens_per_layer": wl["T"],
                    "tokens_per_rank": T, "layers_cycled": Lc, "experts": E, "hidden": H, "intermediate": I,
                    "top_k": k, "parallelism": f"ep{world}" if world > 1 else "single-gpu",
@@ -601,14 +661,25 @@ def cpu_baseline(wl, seconds=15.0, threads=None):
     E, H, I, k = wl["E"], wl["H"], wl["I"], wl["k"]
     big = H * I > 16 * 2**20
     T = min(wl["T"], 16 if big else 128)
+    if wl.get("fmt") == "fp8":
+        T = min(T, 8)  # one call dequantizes every hit expert of a 256-expert layer
     # quantize a handful of distinct experts and reuse them (quantization is not timed)
     ne = 1 if big else min(E, 8)
-    gp, ga = quantize_stack((torch.randn(ne, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16))
-    dp, da = quantize_stack((torch.randn(ne, H, I, generator=g) * 0.02).to(torch.bfloat16))
-    rep = (E + ne - 1) // ne
-    st = {"gate_up_packed": gp.repeat(rep, 1)[:E], "gate_up_absmax": ga.repeat(rep, 1)[:E],
-          "down_packed": dp.repeat(rep, 1)[:E], "down_absmax": da.repeat(rep, 1)[:E],
-          "E": E, "H": H, "I": I, "has_gate": True}
+    if wl.get("fmt") == "fp8":
+        import importlib
+        f8 = importlib.import_module("experts4bit-qlora_b200.fp8_experts")
+        gq, gs = f8.quantize_fp8_blocks((torch.randn(1, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16))
+        dq, ds = f8.quantize_fp8_blocks((torch.randn(1, H, I, generator=g) * 0.02).to(torch.bfloat16))
+        st = {"format": "fp8", "gate_up_w": gq.expand(E, -1, -1), "gate_up_scale": gs.expand(E, -1, -1),
+              "down_w": dq.expand(E, -1, -1), "down_scale": ds.expand(E, -1, -1), "E": E, "H": H, "I": I,
+              "has_gate": True}
+    else:
+        gp, ga = quantize_stack((torch.randn(ne, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16))
+        dp, da = quantize_stack((torch.randn(ne, H, I, generator=g) * 0.02).to(torch.bfloat16))
+        rep = (E + ne - 1) // ne
+        st = {"gate_up_packed": gp.repeat(rep, 1)[:E], "gate_up_absmax": ga.repeat(rep, 1)[:E],
+              "down_packed": dp.repeat(rep, 1)[:E], "down_absmax": da.repeat(rep, 1)[:E],
+              "E": E, "H": H, "I": I, "has_gate": True}
     router = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
     n_tok = 0
     t0 = time.perf_counter()

@@ -21,6 +21,7 @@ BF16, F16, F32 = 0, 1, 2
 SOFTMAX_THEN_TOPK, TOPK_THEN_SOFTMAX = 0, 1
 EPI_NONE, EPI_SWIGLU, EPI_SILU = 0, 1, 2
 FMT_NF4, FMT_FP8_BLOCK128 = 0, 1
+PATH_STREAMING, PATH_TENSOR_CORE, PATH_DECODE_LAYER = 0, 1, 2
 ABI_VERSION = 2
 
 # Every symbol include/e4b.h exports, in declaration order.
@@ -33,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
     "e4b_combine",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
+    "e4b_moe_path", "e4b_set_decode_kernel",
     "e4b_moe_forward_static",
     "e4b_ep_dispatch_workspace_bytes", "e4b_ep_dispatch", "e4b_ep_experts_workspace_bytes", "e4b_ep_experts",
     "e4b_read_device_error",
@@ -88,6 +90,8 @@ def _declare(lib):
         "e4b_moe_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
         "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
         "e4b_moe_forward_static": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P]),
+        "e4b_moe_path": (I, [ctypes.POINTER(MoeDesc)]),
+        "e4b_set_decode_kernel": (I, [I]),
         "e4b_ep_dispatch_workspace_bytes": (SZ, [I, I, I]),
         "e4b_ep_dispatch": (I, [P, I, P, I, I, I, I, P, P, P, P, SZ, P]),
         "e4b_ep_experts_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc), I]),

@@ -1,0 +1,769 @@
+// Whole expert layer in one persistent launch for the decode regime (NF4, at
+// most 128 picks, no adapters): the per-layer kernel chain of fast.py:100-160 --
+// permute, grouped gate_up GEMM + SwiGLU, grouped down GEMM, weighted combine --
+// as phases of one cooperative kernel with one CTA per SM:
+//   phase 0  every CTA rebuilds the (at most 128-pick) stable expert-major
+//            permutation in shared memory from top_k_index and starts its first
+//            weight copies at once; meanwhile it converts the token rows (loaded
+//            into registers at entry) to fp16 with a per-row power-of-two scale and
+//            builds the NF4 pair table;
+//   phase A  gate_up tiles: a warp pair owns 16 weight rows (8 gate + the 8
+//            matching up rows) and streams them in items of up to 2048 K elements,
+//            one 8 KB TMA box per 8 rows and one absmax box; fragments go to
+//            mma.sync m16n8k16 with the tokens as the n8 operand; h rows (fp16) to
+//            the workspace; then the CTA asks L2 to prefetch its share of the
+//            active experts' down weights;                       grid barrier;
+//   phase B  down tiles, activations (h) staged from L2;        grid barrier;
+//   phase C  fixed-slot-order combine into the output.
+// The arithmetic is the streaming GEMV's (gemv_stream.cu) and the combine
+// kernel's, so the result equals the multi-kernel path bit for bit. Copy waits
+// are bounded (a timeout raises E4B_ERR_TIMEOUT and the kernel runs to its end);
+// the grid barriers are cooperative-launch grid syncs that every CTA reaches.
+// Errors are collected per CTA and folded into the workspace's error word by
+// CTA 0 after the last barrier, so each call reports its own errors.
+#include <cooperative_groups.h>
+
+#include "convert.cuh"
+#include "decode_layer.cuh"
+#include "stream_core.cuh"
+#include "tmap.cuh"
+
+// Profiling instrumentation, compiled only with -DE4B_TRACE: per-CTA %globaltimer
+// stamps at phase boundaries, read back with e4b_decode_trace_read.
+#ifdef E4B_TRACE
+__device__ unsigned long long g_dl_trace[1024 * 16];
+extern "C" __attribute__((visibility("default"))) int e4b_decode_trace_read(unsigned long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, g_dl_trace, n * sizeof(unsigned long long));
+}
+__device__ unsigned long long g_dl_pair[1024 * 8 * 4];  // per pair: phase A item0 ready, A done, B item0, B done
+extern "C" __attribute__((visibility("default"))) int e4b_decode_pair_read(unsigned long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, g_dl_pair, n * sizeof(unsigned long long));
+}
+#define DTRACE(i)                                                  \
+  if (threadIdx.x == 0) {                                          \
+    unsigned long long t_;                                         \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));        \
+    g_dl_trace[blockIdx.x * 16 + (i)] = t_;                        \
+  }
+#define PTRACE(i)                                                  \
+  if (lane == 0 && member == 0) {                                  \
+    unsigned long long t_;                                         \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));        \
+    g_dl_pair[(blockIdx.x * 8 + pair) * 4 + (i)] = t_;             \
+  }
+#else
+#define DTRACE(i)
+#define PTRACE(i)
+#endif
+
+namespace e4b {
+
+namespace {
+
+using stream::kLut;
+using stream::kPairs;
+using stream::kThreads;
+using stream::kWarps;
+using stream::lut2;
+using stream::mma16816;
+using stream::mma16816_zero;
+using stream::named_barrier;
+
+constexpr int kMaxPicks = 128;
+constexpr int kDChunk = 2048;             // K elements per item
+constexpr int kWBoxCap = 8 * 1024;        // one 8-row group, up to 8 lines of 128 B
+constexpr int kABoxCap = 32 * 8 * 4;      // one 8-row group, up to 32 absmax floats
+constexpr int kDSlotBytes = 2 * kWBoxCap + 2 * kABoxCap;  // 18 KB, a multiple of 1024
+constexpr int kDXBudget = 20 * 1024;      // token rows (then h rows) staged in shared memory
+
+__host__ __device__ constexpr int box_lines(int K) { return K / 256 < 8 ? K / 256 : 8; }
+__host__ __device__ constexpr int abox_floats(int K) { return K / 64 < 32 ? K / 64 : 32; }
+
+// Byte offset of (row r, block b) in an absmax box whose rows are S = abox_floats * 4 bytes
+// (16..128), stored with the S-byte swizzle (none for 16): the 16-byte unit of block b is XORed
+// with address bits 7.. of the row, which spreads the 8 rows over distinct banks.
+__device__ __forceinline__ int aofs(int r, int b, int S) {
+  return r * S + ((((b >> 2) ^ ((r * S) >> 7)) & (S / 16 - 1)) << 4) + ((b & 3) << 2);
+}
+
+struct DSmem {
+  static constexpr int lut = 0;
+  static constexpr int x = kLut;
+  static constexpr int slots = x + kDXBudget;
+  static constexpr int red = slots + kPairs * kDSlotBytes;
+  static constexpr int bars = red + kPairs * 32 * 8 * 4;
+  static constexpr int tables = bars + kPairs * 8;
+  // int tables of kMaxPicks: pick expert, sorted expert, sorted token, inverse, active expert/row0/count;
+  // 16 token scales, 16 misc words, kMaxPicks top-k weights, 16 row maxima
+  static constexpr int total = tables + 7 * kMaxPicks * 4 + 16 * 4 + 16 * 4 + kMaxPicks * 4 + 16 * 4;
+};
+static_assert(DSmem::slots % 1024 == 0 && kDSlotBytes % 1024 == 0, "swizzled boxes need 1024-byte alignment");
+static_assert(DSmem::total <= 232448, "shared memory budget");
+
+struct DecodeArgs {
+  const void* hidden;
+  int act_dtype;
+  const int64_t* topk_idx;
+  const void* topk_w;
+  int w_dtype;
+  const uint8_t* gu_packed;
+  const float* gu_absmax;
+  const uint8_t* dn_packed;
+  const float* dn_absmax;
+  int T, k, E, H, I, has_gate;
+  void* out;
+  int out_dtype;
+  __half* h;                   // [R, I]
+  __half* down_rows;           // [R, H]
+  int* cta_err;                // [gridDim.x]
+  int* err;
+};
+
+struct Tables {
+  int* pick_e;     // expert of flat pick i
+  int* sorted_e;   // expert of sorted row r
+  int* sorted_tok; // token of sorted row r
+  int* inv;        // sorted row of flat pick i
+  int* act_e;
+  int* act_row0;
+  int* act_cnt;
+  float* xscale;   // per token row
+  float* w;        // top-k weight of flat pick i (fp32)
+  unsigned* rowmax;// per token row: max |x| as float bits
+  int* misc;       // [0] active experts, [1] CTA error, [2..5] warp start counts, [7] error fold
+};
+
+__device__ __forceinline__ void cta_raise(int* cta_err, int code) { atomicCAS(cta_err, 0, code); }
+
+template <typename T> __device__ __forceinline__ T store_cast_out(float v, int*) { return from_f32<T>(v); }
+template <> __device__ __forceinline__ __half store_cast_out<__half>(float v, int* err) {
+  return store_cast<__half>(v, err);
+}
+
+// Eight 16-bit activations (bf16 or fp16) -> fp32.
+__device__ __forceinline__ void unpack8(const uint4& r, int dtype, float (&v)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (dtype == E4B_BF16) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
+struct Phase {
+  const CUtensorMap* wmap;
+  const CUtensorMap* amap;
+  int N, K, epilogue, tiles_per_expert;
+  const __half* x;     // token rows: shared memory (phase A) or global (phase B)
+  int xpitch;          // halves
+  bool x_mapped;       // sorted row -> token row through sorted_tok, and per-token scales
+  __half* out;
+  int Nout;
+};
+
+__device__ __forceinline__ int phase_chunks(const Phase& p) { return (p.K + kDChunk - 1) / kDChunk; }
+
+// The pair's items: tiles gp, gp + npairs, ... below nact * tiles_per_expert, chunks each.
+__device__ __forceinline__ int phase_items(const Phase& p, int nact, int gp) {
+  const int npairs = gridDim.x * kPairs;
+  const int limit = nact * p.tiles_per_expert;
+  return (limit > gp ? (limit - gp + npairs - 1) / npairs : 0) * phase_chunks(p);
+}
+
+__device__ __forceinline__ int group_row(const Phase& p, int tile, int h) {
+  if (p.epilogue == E4B_EPI_SWIGLU) return h == 0 ? tile * 8 : (p.N >> 1) + tile * 8;
+  return tile * 16 + 8 * h;
+}
+
+// Copies of the pair's item n into its slot (pair leader only).
+__device__ __forceinline__ void issue_item(const Phase& p, const Tables& tb, char* slot, uint64_t* bar, int gp,
+                                           int n) {
+  const int npairs = gridDim.x * kPairs;
+  const int chunks = phase_chunks(p);
+  const int t = gp + (n / chunks) * npairs;
+  const int j = t / p.tiles_per_expert;
+  const int tile = t - j * p.tiles_per_expert;
+  const int rowbase = tb.act_e[j] * p.N;
+  const int c = n % chunks;
+  const uint32_t wbytes = box_lines(p.K) * 1024, abytes = abox_floats(p.K) * 32;
+  mbar_arrive_expect_tx(bar, 2 * (wbytes + abytes));
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r0 = rowbase + group_row(p, tile, h);
+    tma_load_3d(slot + h * kWBoxCap, p.wmap, 0, r0, c * (kDChunk / 256), bar);
+    tma_load_2d(slot + 2 * kWBoxCap + h * kABoxCap, p.amap, c * (kDChunk / 64), r0, bar);
+  }
+}
+
+// Byte offset of lane (row r, quad lane q)'s 8-byte piece of block bc (of the chunk) in a weight
+// box whose shared address is 1024-aligned: line bc / 4 holds blocks 4 (bc / 4) .. +3.
+__device__ __forceinline__ int wofs(int r, int q, int bc) {
+  const int unit = (((bc & 3) << 1) | (q >> 1)) ^ r;
+  return (bc >> 2) * 1024 + r * 128 + (unit << 4) + ((q & 1) << 3);
+}
+
+// One phase of streamed tiles for this pair; its items run through one slot and one mbarrier
+// whose phase parity `n_run` keeps across phases.
+template <int NT>
+__device__ void stream_phase(const Phase& p, const Tables& tb, int nact, char* smem, int& n_run, bool& dead,
+                             int* cta_err, bool head_issued, int trace_slot) {
+  char* lut = smem + DSmem::lut;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int pair = warp >> 1, member = warp & 1;
+  const int gq = lane >> 2, q = lane & 3;
+  const uint32_t lane4 = (uint32_t)lane << 2;
+  char* slot = smem + DSmem::slots + pair * kDSlotBytes;
+  float* red = reinterpret_cast<float*>(smem + DSmem::red) + pair * 32 * 8;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DSmem::bars) + pair;
+  const bool leader = member == 0 && lane == 0;
+  const int npairs = gridDim.x * kPairs;
+  const int chunks = phase_chunks(p);
+  const int gp = blockIdx.x * kPairs + pair;
+  const int total_items = phase_items(p, nact, gp);
+  const int n0 = n_run;
+  const bool swiglu = p.epilogue == E4B_EPI_SWIGLU;
+  const int arow = abox_floats(p.K) * 4;  // bytes per absmax box row
+  (void)trace_slot;
+  if (leader && !dead && !head_issued && total_items > 0) issue_item(p, tb, slot, bar, gp, 0);
+
+  int row0 = 0, M = 0, tile = 0;
+  float acc[NT][4];
+  for (int n = 0; n < total_items; ++n) {
+    const int c = n % chunks;
+    if (c == 0) {
+      const int t = gp + (n / chunks) * npairs;
+      const int j = t / p.tiles_per_expert;
+      tile = t - j * p.tiles_per_expert;
+      row0 = tb.act_row0[j];
+      M = tb.act_cnt[j];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
+    }
+    if (!dead && !mbar_wait(bar, (n0 + n) & 1)) {
+      cta_raise(cta_err, E4B_ERR_TIMEOUT);
+      dead = true;
+    }
+    if (n == 0) PTRACE(trace_slot);
+    if (!dead) {
+      // blocks of this chunk; the members take alternate groups of four (the streaming GEMV's split,
+      // so both kernels accumulate in the same order)
+      const int nb = min(kDChunk, p.K - c * kDChunk) / 64;
+      const __half* xrow[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int m = nt * 8 + gq;
+        const int sr = row0 + (m < M ? m : 0);
+        const int src = p.x_mapped ? tb.sorted_tok[sr] : sr;
+        xrow[nt] = p.x + src * p.xpitch + c * kDChunk + q * 16;
+      }
+      const char* wA = slot;
+      const char* wB = slot + kWBoxCap;
+      const char* aA = slot + 2 * kWBoxCap;
+      const char* aB = slot + 2 * kWBoxCap + kABoxCap;
+      for (int b0 = 4 * member; b0 < nb; b0 += 8) {
+        uint2 wa[4], wb[4];
+        float sa[4], sb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int b = b0 + i < nb ? b0 + i : b0;
+          wa[i] = *reinterpret_cast<const uint2*>(wA + wofs(gq, q, b));
+          wb[i] = *reinterpret_cast<const uint2*>(wB + wofs(gq, q, b));
+          sa[i] = *reinterpret_cast<const float*>(aA + aofs(gq, b, arow));
+          sb[i] = *reinterpret_cast<const float*>(aB + aofs(gq, b, arow));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int b = b0 + i;
+          if (b >= nb) break;
+          uint4 xf[NT][2];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            xf[nt][0] = *reinterpret_cast<const uint4*>(xrow[nt] + b * 64);
+            xf[nt][1] = *reinterpret_cast<const uint4*>(xrow[nt] + b * 64 + 8);
+          }
+          float pp[NT][4];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const uint32_t w0 = jj < 2 ? wa[i].x : wa[i].y, w1 = jj < 2 ? wb[i].x : wb[i].y;
+            uint32_t a0, a1, a2, a3;
+            if (jj & 1) {
+              a0 = lut2<2>(lut, w0, lane4); a2 = lut2<3>(lut, w0, lane4);
+              a1 = lut2<2>(lut, w1, lane4); a3 = lut2<3>(lut, w1, lane4);
+            } else {
+              a0 = lut2<0>(lut, w0, lane4); a2 = lut2<1>(lut, w0, lane4);
+              a1 = lut2<0>(lut, w1, lane4); a3 = lut2<1>(lut, w1, lane4);
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xf[nt][jj >> 1]);
+              if (jj == 0)
+                mma16816_zero(pp[nt], a0, a1, a2, a3, xw[0], xw[1]);
+              else
+                mma16816(pp[nt], a0, a1, a2, a3, xw[(jj & 1) * 2], xw[(jj & 1) * 2 + 1]);
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] = fmaf(pp[nt][0], sa[i], acc[nt][0]);
+            acc[nt][1] = fmaf(pp[nt][1], sa[i], acc[nt][1]);
+            acc[nt][2] = fmaf(pp[nt][2], sb[i], acc[nt][2]);
+            acc[nt][3] = fmaf(pp[nt][3], sb[i], acc[nt][3]);
+          }
+        }
+      }
+    }
+    const bool last = c == chunks - 1;
+    if (last && member == 1) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) red[(nt * 4 + r) * 32 + lane] = acc[nt][r];
+    }
+    // both members are done reading the slot; the proxy fence orders those generic reads before
+    // the slot's refill by the async proxy
+    fence_proxy_async();
+    named_barrier(1 + pair, 64);
+    if (leader && !dead && n + 1 < total_items) issue_item(p, tb, slot, bar, gp, n + 1);
+    if (last && member == 0 && !dead) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[nt][r] += red[(nt * 4 + r) * 32 + lane];
+      const int rA = group_row(p, tile, 0) + gq, rB = group_row(p, tile, 1) + gq;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int m = nt * 8 + 2 * q + h;
+          if (m >= M) continue;
+          const int srow = row0 + m;
+          float va = acc[nt][h], vb = acc[nt][2 + h];
+          if (p.x_mapped) {
+            const float sc = tb.xscale[tb.sorted_tok[srow]];
+            va *= sc;
+            vb *= sc;
+          }
+          __half* o = p.out + (int64_t)srow * p.Nout;
+          if (swiglu) {
+            o[tile * 8 + gq] = store_cast<__half>(silu_f32(va) * vb, cta_err);
+          } else if (p.epilogue == E4B_EPI_SILU) {
+            o[rA] = store_cast<__half>(silu_f32(va), cta_err);
+            o[rB] = store_cast<__half>(silu_f32(vb), cta_err);
+          } else {
+            o[rA] = store_cast<__half>(va, cta_err);
+            o[rB] = store_cast<__half>(vb, cta_err);
+          }
+        }
+    }
+  }
+  if (dead && leader && total_items > 0) (void)mbar_wait(bar, (n0 + total_items - 1) & 1);  // drain, bounded
+  if (total_items > 0) PTRACE(trace_slot + 1);
+  n_run = n0 + total_items;
+}
+
+template <typename OutT, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_decode_layer_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap wmap_gu,
+                            const __grid_constant__ CUtensorMap amap_gu, const __grid_constant__ CUtensorMap wmap_dn,
+                            const __grid_constant__ CUtensorMap amap_dn) {
+  extern __shared__ __align__(1024) char smem[];
+  namespace cg = cooperative_groups;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = a.T * a.k;
+  DTRACE(0);
+  if (tid < 4) {  // descriptors into the TMA unit's cache before the first copies
+    const CUtensorMap* m = tid == 0 ? &wmap_gu : tid == 1 ? &amap_gu : tid == 2 ? &wmap_dn : &amap_dn;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+  }
+  // token rows into registers first: their latency overlaps the permutation below
+  const int xvec = a.T * (a.H / 8);
+  uint4 xr[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int v = tid + i * kThreads;
+    if (v < xvec) xr[i] = reinterpret_cast<const uint4*>(a.hidden)[v];
+  }
+  Tables tb;
+  int* ti = reinterpret_cast<int*>(smem + DSmem::tables);
+  tb.pick_e = ti;
+  tb.sorted_e = ti + kMaxPicks;
+  tb.sorted_tok = ti + 2 * kMaxPicks;
+  tb.inv = ti + 3 * kMaxPicks;
+  tb.act_e = ti + 4 * kMaxPicks;
+  tb.act_row0 = ti + 5 * kMaxPicks;
+  tb.act_cnt = ti + 6 * kMaxPicks;
+  tb.xscale = reinterpret_cast<float*>(ti + 7 * kMaxPicks);
+  tb.misc = ti + 7 * kMaxPicks + 16;
+  tb.w = reinterpret_cast<float*>(ti + 7 * kMaxPicks + 32);
+  tb.rowmax = reinterpret_cast<unsigned*>(ti + 8 * kMaxPicks + 32);
+  int* cta_err = &tb.misc[1];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DSmem::bars);
+  __half* xs = reinterpret_cast<__half*>(smem + DSmem::x);
+  const int xpitch = a.H + 8;
+
+  Phase pa{};
+  pa.wmap = &wmap_gu;
+  pa.amap = &amap_gu;
+  pa.N = a.has_gate ? 2 * a.I : a.I;
+  pa.K = a.H;
+  pa.epilogue = a.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
+  pa.tiles_per_expert = pa.N / 16;
+  pa.x = xs;
+  pa.xpitch = xpitch;
+  pa.x_mapped = true;
+  pa.out = a.h;
+  pa.Nout = a.I;
+
+  // ---- phase 0: the permutation first, so the weight stream starts early ------------------
+  if (tid == 0) {
+    tb.misc[1] = 0;
+    for (int s = 0; s < kPairs; ++s) mbar_init(&bars[s], 1);
+    fence_proxy_async();
+  }
+  if (tid < 16) tb.rowmax[tid] = 0u;
+  if (tid < R) {
+    int64_t e = a.topk_idx[tid];
+    if (e < 0 || e >= a.E) {
+      if (blockIdx.x == 0) atomicCAS(&tb.misc[1], 0, E4B_ERR_EXPERT_INDEX);
+      e = e < 0 ? 0 : a.E - 1;
+    }
+    tb.pick_e[tid] = (int)e;
+    tb.w[tid] = load_as_f32(a.topk_w, a.w_dtype, tid);
+  }
+  __syncthreads();
+  if (tid < R) {  // stable rank by (expert, flat index): the permutation of fast.py:126-133
+    const int e = tb.pick_e[tid];
+    int rank = 0;
+    for (int j = 0; j < R; ++j) {
+      const int ej = tb.pick_e[j];
+      rank += (ej < e) | ((ej == e) & (j < tid));
+    }
+    tb.sorted_e[rank] = e;
+    tb.sorted_tok[rank] = tid / a.k;
+    tb.inv[tid] = rank;
+  }
+  __syncthreads();
+  bool start = false;
+  unsigned ball = 0;
+  if (warp < kMaxPicks / 32) {
+    start = tid < R && (tid == 0 || tb.sorted_e[tid - 1] != tb.sorted_e[tid]);
+    ball = __ballot_sync(0xffffffffu, start);
+    if (lane == 0) tb.misc[2 + warp] = __popc(ball);
+  }
+  __syncthreads();
+  if (warp < kMaxPicks / 32) {
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += tb.misc[2 + w];
+    const int idx = before + __popc(ball & ((1u << lane) - 1u));
+    if (start) {
+      tb.act_e[idx] = tb.sorted_e[tid];
+      tb.act_row0[idx] = tid;
+    }
+    if (tid == 0) tb.misc[0] = tb.misc[2] + tb.misc[3] + tb.misc[4] + tb.misc[5];
+  }
+  __syncthreads();
+  const int nact = tb.misc[0];
+  DTRACE(1);
+  if ((warp & 1) == 0 && lane == 0) {  // pair leaders: the first gate_up item
+    const int gp = blockIdx.x * kPairs + (warp >> 1);
+    if (phase_items(pa, nact, gp) > 0)
+      issue_item(pa, tb, smem + DSmem::slots + (warp >> 1) * kDSlotBytes, &bars[warp >> 1], gp, 0);
+  }
+  if (tid < nact) tb.act_cnt[tid] = (tid + 1 < nact ? tb.act_row0[tid + 1] : R) - tb.act_row0[tid];
+  DTRACE(10);
+  {  // pair table
+    char* lut = smem + DSmem::lut;
+    const float code = c_nf4[lane & 15];
+#pragma unroll 4
+    for (int e = warp; e < 256; e += kWarps) {
+      const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
+      reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
+    }
+  }
+  DTRACE(11);
+  {  // token rows -> fp16 with the per-row power-of-two scale of convert.cuh
+    float v[2][8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int vi = tid + i * kThreads;
+      if (vi < xvec) {
+        unpack8(xr[i], a.act_dtype, v[i]);
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
+        atomicMax(&tb.rowmax[vi / (a.H / 8)], __float_as_uint(m));
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int vi = tid + i * kThreads;
+      if (vi < xvec) {
+        const int r = vi / (a.H / 8), c8 = vi - r * (a.H / 8);
+        const float m = __uint_as_float(tb.rowmax[r]);
+        int sh = 0;
+        if (m > 32768.f) {
+          int ex;
+          frexpf(m / 32768.f, &ex);
+          sh = ex;
+        }
+        const float inv = ldexpf(1.f, -sh);
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ow[j] = pack2<__half>(v[i][2 * j] * inv, v[i][2 * j + 1] * inv);
+        *reinterpret_cast<uint4*>(xs + r * xpitch + c8 * 8) = o;
+        if (c8 == 0) tb.xscale[r] = ldexpf(1.f, sh);
+      }
+    }
+  }
+  DTRACE(12);
+  __syncthreads();
+  DTRACE(13);
+
+  // ---- phase A: gate_up --------------------------------------------------------------------
+  int n_run = 0;
+  bool dead = false;
+  DTRACE(2);
+  stream_phase<NT>(pa, tb, nact, smem, n_run, dead, cta_err, true, 0);
+  {  // L2 prefetch of this CTA's share of the active experts' down weights and absmax
+    auto prefetch = [&](const char* base, int64_t per) {
+      const int64_t total = per * nact;
+      const int64_t share = ((total + gridDim.x - 1) / gridDim.x + 4095) & ~4095ll;
+      const int64_t end = min(total, (blockIdx.x + 1) * share);
+      for (int64_t off = blockIdx.x * share + (int64_t)tid * 4096; off < end; off += kThreads * 4096) {
+        const int j = (int)(off / per);
+        const int64_t in = off - j * per;
+        int64_t nbytes = per - in < 4096 ? per - in : 4096;
+        if (end - off < nbytes) nbytes = end - off;
+        const char* src = base + (int64_t)tb.act_e[j] * per + in;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"((uint32_t)nbytes & ~15u)
+                     : "memory");
+      }
+    };
+    prefetch(reinterpret_cast<const char*>(a.dn_packed), (int64_t)a.H * a.I / 2);
+    prefetch(reinterpret_cast<const char*>(a.dn_absmax), (int64_t)a.H * (a.I / 64) * 4);
+  }
+  DTRACE(3);
+  cg::this_grid().sync();
+  DTRACE(4);
+
+  // ---- phase B: down -----------------------------------------------------------------------
+  Phase pb{};
+  pb.wmap = &wmap_dn;
+  pb.amap = &amap_dn;
+  pb.N = a.H;
+  pb.K = a.I;
+  pb.epilogue = E4B_EPI_NONE;
+  pb.tiles_per_expert = a.H / 16;
+  pb.x = a.h;
+  pb.xpitch = a.I;
+  pb.x_mapped = false;
+  pb.out = a.down_rows;
+  pb.Nout = a.H;
+  if ((warp & 1) == 0 && lane == 0 && !dead) {
+    const int gp = blockIdx.x * kPairs + (warp >> 1);
+    if (phase_items(pb, nact, gp) > 0)
+      issue_item(pb, tb, smem + DSmem::slots + (warp >> 1) * kDSlotBytes, &bars[warp >> 1], gp, 0);
+  }
+  if ((int64_t)R * (a.I + 8) * 2 <= kDXBudget) {  // all of h fits where the token rows were: stage it
+    const int hp = a.I + 8, vec = a.I / 8;
+    for (int v = tid; v < R * vec; v += kThreads) {
+      const int r = v / vec, c = v - r * vec;
+      *reinterpret_cast<uint4*>(xs + r * hp + c * 8) = *reinterpret_cast<const uint4*>(a.h + (int64_t)r * a.I + c * 8);
+    }
+    __syncthreads();
+    pb.x = xs;
+    pb.xpitch = hp;
+  }
+  DTRACE(5);
+  stream_phase<NT>(pb, tb, nact, smem, n_run, dead, cta_err, true, 2);
+  DTRACE(6);
+  __syncthreads();
+  if (tid == 0) a.cta_err[blockIdx.x] = tb.misc[1];
+  cg::this_grid().sync();
+  DTRACE(7);
+
+  // errors of phases 0-B: the first failing CTA's code (CTA 0, parallel reads)
+  auto fold_errors = [&]() {
+    if (blockIdx.x != 0) return;
+    if (tid == 0) tb.misc[7] = 0x7fffffff;
+    __syncthreads();
+    for (int b = tid; b < (int)gridDim.x; b += kThreads)
+      if (a.cta_err[b]) atomicMin(&tb.misc[7], b);
+    __syncthreads();
+    if (tid == 0) *a.err = tb.misc[7] == 0x7fffffff ? 0 : a.cta_err[tb.misc[7]];
+  };
+  fold_errors();
+
+  // ---- phase C: out[t] = sum over slots, in order, of fp32(down[inv[t*k+s]]) * w[t,s] ----------
+  const int vecs = a.T * (a.H / 8);
+  for (int v = blockIdx.x * kThreads + tid; v < vecs; v += gridDim.x * kThreads) {
+    const int t = v / (a.H / 8), h8 = (v - t * (a.H / 8)) * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int s0 = 0; s0 < a.k; s0 += 8) {
+      uint4 d[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < a.k)
+          d[u] = *reinterpret_cast<const uint4*>(a.down_rows + (int64_t)tb.inv[t * a.k + s0 + u] * a.H + h8);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + u >= a.k) break;
+        const __half* dv = reinterpret_cast<const __half*>(&d[u]);
+        const float ws = tb.w[t * a.k + s0 + u];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(__half2float(dv[i]), ws, acc[i]);  // slot order
+      }
+    }
+    OutT* o = reinterpret_cast<OutT*>(a.out) + (int64_t)t * a.H + h8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = store_cast_out<OutT>(acc[i], cta_err);
+  }
+  DTRACE(8);
+  if (a.out_dtype == E4B_F16) {  // fp16 outputs can saturate in phase C: fold once more
+    __syncthreads();
+    if (tid == 0) a.cta_err[blockIdx.x] = tb.misc[1];
+    cg::this_grid().sync();
+    fold_errors();
+  }
+  DTRACE(9);
+}
+
+int g_decode_enabled = -1;  // -1: not yet read from E4B_DECODE_KERNEL
+
+}  // namespace
+
+size_t decode_layer_sync_bytes(int grid) { return (size_t)grid * sizeof(int); }
+
+static int sm_count_cached() {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (!sms[dev & 63]) cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+  return sms[dev & 63];
+}
+
+int decode_layer_grid() { return sm_count_cached(); }
+
+bool decode_layer_eligible(const e4b_moe_desc& d) {
+  if (g_decode_enabled < 0) {
+    const char* v = getenv("E4B_DECODE_KERNEL");
+    g_decode_enabled = (v && v[0] == '0') ? 0 : 1;
+  }
+  if (!g_decode_enabled) return false;
+  if (d.weight_format != E4B_FMT_NF4 || d.lora_rank != 0) return false;
+  if (d.tokens < 1 || d.tokens > 16 || (int64_t)d.tokens * d.top_k > kMaxPicks) return false;
+  if (d.hidden % 256 || d.intermediate % 256) return false;
+  if ((int64_t)d.tokens * (d.hidden + 8) * 2 > kDXBudget) return false;
+  if ((int64_t)d.tokens * d.hidden > 2 * kThreads * 8) return false;  // two 16-byte vectors of rows per thread
+  if (d.tokens > 16) return false;
+  if ((int64_t)d.num_experts * (d.has_gate ? 2 * d.intermediate : d.intermediate) >= (1ll << 31)) return false;
+  if ((int64_t)d.num_experts * d.hidden >= (1ll << 31)) return false;
+  if (!is_act_dtype(d.act_dtype)) return false;
+  return encode_tiled_fn() != nullptr && decode_layer_grid() > 0;
+}
+
+template <typename OutT, int NT>
+static e4b_status launch_decode(const DecodeArgs& a, cudaStream_t s) {
+  static unsigned long long configured = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return E4B_ERR_CUDA;
+  const unsigned long long bit = 1ull << (dev & 63);
+  auto kern = nf4_decode_layer_kernel<OutT, NT>;
+  if (!(configured & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DSmem::total) != cudaSuccess)
+      return E4B_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, DSmem::total) != cudaSuccess ||
+        per_sm < 1)
+      return E4B_ERR_UNSUPPORTED;
+    configured |= bit;
+  }
+  const int n1 = a.has_gate ? 2 * a.I : a.I;
+  CUtensorMap wgu, agu, wdn, adn;
+  auto maps = [&](CUtensorMap& w, CUtensorMap& am, const uint8_t* packed, const float* absmax, int rows_per_e,
+                  int K) {
+    const cuuint64_t rows = (cuuint64_t)a.E * rows_per_e;
+    // packed bytes as [lines (K/256)][rows][128 B]: a box of 8 rows x up to 8 lines lands row-major
+    // per line, so the 128-byte swizzle XORs row r's units with r (conflict-free fragment reads)
+    const cuuint64_t wdims[3] = {128, rows, (cuuint64_t)(K / 256)};
+    const cuuint64_t wstr[2] = {(cuuint64_t)(K / 2), 128};
+    const cuuint32_t wbox[3] = {128, 8, (cuuint32_t)box_lines(K)};
+    const cuuint64_t adims[2] = {(cuuint64_t)(K / 64), rows};
+    const cuuint64_t astr[1] = {(cuuint64_t)(K / 64) * 4};
+    const cuuint32_t abox[2] = {(cuuint32_t)abox_floats(K), 8};
+    const int S = abox_floats(K) * 4;
+    const CUtensorMapSwizzle asw = S == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : S == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                   : S == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                             : CU_TENSOR_MAP_SWIZZLE_NONE;
+    return encode_tiled(&w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, packed, wdims, wstr, wbox,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_tiled(&am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, absmax, adims, astr, abox, asw);
+  };
+  if (!maps(wgu, agu, a.gu_packed, a.gu_absmax, n1, a.H) || !maps(wdn, adn, a.dn_packed, a.dn_absmax, a.H, a.I))
+    return E4B_ERR_CUDA;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(decode_layer_grid());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = DSmem::total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, wgu, agu, wdn, adn) != cudaSuccess) return E4B_ERR_CUDA;
+  return launch_status();
+}
+
+e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,
+                               void* sync, int* err, cudaStream_t s) {
+  DecodeArgs a{};
+  a.hidden = t->hidden;
+  a.act_dtype = d.act_dtype;
+  a.topk_idx = t->topk_idx;
+  a.topk_w = t->topk_w;
+  a.w_dtype = d.weight_dtype;
+  a.gu_packed = static_cast<const uint8_t*>(t->gate_up_packed);
+  a.gu_absmax = static_cast<const float*>(t->gate_up_absmax);
+  a.dn_packed = static_cast<const uint8_t*>(t->down_packed);
+  a.dn_absmax = static_cast<const float*>(t->down_absmax);
+  a.T = d.tokens;
+  a.k = d.top_k;
+  a.E = d.num_experts;
+  a.H = d.hidden;
+  a.I = d.intermediate;
+  a.has_gate = d.has_gate;
+  a.out = t->out;
+  a.out_dtype = d.out_dtype;
+  a.h = static_cast<__half*>(h);
+  a.down_rows = static_cast<__half*>(down_rows);
+  a.cta_err = static_cast<int*>(sync);
+  a.err = err;
+  const bool two = d.tokens > 8;
+  switch (d.out_dtype) {
+    case E4B_BF16: return two ? launch_decode<__nv_bfloat16, 2>(a, s) : launch_decode<__nv_bfloat16, 1>(a, s);
+    case E4B_F16: return two ? launch_decode<__half, 2>(a, s) : launch_decode<__half, 1>(a, s);
+    default: return two ? launch_decode<float, 2>(a, s) : launch_decode<float, 1>(a, s);
+  }
+}
+
+}  // namespace e4b
+
+extern "C" E4B_API int e4b_set_decode_kernel(int enabled) {
+  const int prev = e4b::g_decode_enabled;
+  e4b::g_decode_enabled = enabled ? 1 : 0;
+  return prev;
+}

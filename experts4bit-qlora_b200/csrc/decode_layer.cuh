@@ -1,0 +1,17 @@
+// Internal interface of the one-launch decode layer kernel (decode_layer.cu).
+#pragma once
+#include "common.cuh"
+
+namespace e4b {
+
+// Whether the fused decode-layer kernel takes this layer (NF4, <= 128 picks, no
+// adapters, H and I multiples of 256, token rows within 20 KB of shared memory).
+bool decode_layer_eligible(const e4b_moe_desc& d);
+// Workspace bytes of its per-CTA error slots.
+size_t decode_layer_sync_bytes(int grid);
+// h [R, I] and down_rows [R, H] are fp16 scratch; `sync` holds
+// decode_layer_sync_bytes(grid) bytes (rewritten by every launch).
+e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,
+                               void* sync, int* err, cudaStream_t s);
+
+}  // namespace e4b

@@ -72,55 +72,116 @@ struct PlanArgs {
 // One CTA: segment tables of the received rows and the expert-major -> source-major
 // row map. Received rows are source-major, and within a source expert-major (the
 // order the source's permutation produced); the expert stages want expert-major,
-// and within an expert source-major.
-__global__ void __launch_bounds__(1024) ep_plan_kernel(PlanArgs a) {
-  __shared__ int s_total;
-  const int tid = threadIdx.x;
-  // per source: running start over its experts
-  for (int p = tid; p < a.P; p += blockDim.x) {
-    int acc = 0;
-    for (int q = 0; q < p; ++q)
-      for (int e = 0; e < a.El; ++e) acc += a.recv_counts[q * a.El + e];
-    for (int e = 0; e < a.El; ++e) {
-      a.src_start[p * a.El + e] = acc;
-      acc += a.recv_counts[p * a.El + e];
-    }
+// and within an expert source-major. Block starts come from two exclusive scans
+// over the P x El count matrix (source-major and expert-major), done with a
+// shared-memory scan over chunks of 1024 blocks.
+__device__ __forceinline__ int block_scan_exclusive(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
   }
-  if (tid == 0) {
-    int off = 0, ta = 0, tb = 0, n = 0;
-    for (int e = 0; e < a.El; ++e) {
-      int c = 0;
-      for (int p = 0; p < a.P; ++p) {
-        const int v = a.recv_counts[p * a.El + e];
-        a.dst_start[p * a.El + e] = off + c;
-        c += v < 0 ? 0 : v;
-      }
-      a.offsets[e] = off;
-      a.tile_a[e] = ta;
-      a.tile_b[e] = tb;
-      if (c > 0) a.active[n++] = e;
-      off += c;
-      ta += (c + a.tile_a_rows - 1) / a.tile_a_rows;
-      tb += (c + a.tile_b_rows - 1) / a.tile_b_rows;
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
     }
-    a.offsets[a.El] = off;
-    a.tile_a[a.El] = ta;
-    a.tile_b[a.El] = tb;
-    *a.num_active = n;
-    s_total = off;
-    if (off != a.R) raise_error(a.err, E4B_ERR_INVALID_ARG);
+    if (lane < nw) s_warp[lane] = w;
   }
   __syncthreads();
+  const int excl = x - v + (warp ? s_warp[warp - 1] : 0);
+  total = s_warp[nw - 1];
+  __syncthreads();
+  return excl;
+}
+
+__global__ void __launch_bounds__(1024) ep_plan_kernel(PlanArgs a) {
+  __shared__ int s_warp[32];
+  __shared__ int s_n;
+  const int tid = threadIdx.x;
+  const int nb = a.P * a.El;
+  // source-major starts: block b = p * El + e in storage order
+  int carry = 0;
+  for (int b0 = 0; b0 < nb; b0 += blockDim.x) {
+    const int b = b0 + tid;
+    const int v = b < nb ? max(a.recv_counts[b], 0) : 0;
+    int tot;
+    const int ex = block_scan_exclusive(v, s_warp, tot);
+    if (b < nb) a.src_start[b] = carry + ex;
+    carry += tot;
+  }
+  // expert-major starts: position j = e * P + p
+  carry = 0;
+  for (int j0 = 0; j0 < nb; j0 += blockDim.x) {
+    const int j = j0 + tid;
+    const int e = j / a.P, p = j - e * a.P;
+    const int v = j < nb ? max(a.recv_counts[p * a.El + e], 0) : 0;
+    int tot;
+    const int ex = block_scan_exclusive(v, s_warp, tot);
+    if (j < nb) a.dst_start[p * a.El + e] = carry + ex;
+    carry += tot;
+  }
+  const int total = carry;
+  __syncthreads();  // starts visible to the whole block
+  // per-expert segment tables and tile prefixes (scan over experts)
+  if (tid == 0) s_n = 0;
+  carry = 0;
+  int ta_carry = 0, tb_carry = 0;
+  for (int e0 = 0; e0 < a.El; e0 += blockDim.x) {
+    const int e = e0 + tid;
+    int c = 0;
+    if (e < a.El)
+      for (int p = 0; p < a.P; ++p) c += max(a.recv_counts[p * a.El + e], 0);
+    int tot, tta, ttb;
+    const int ex = block_scan_exclusive(c, s_warp, tot);
+    const int exa = block_scan_exclusive((c + a.tile_a_rows - 1) / a.tile_a_rows, s_warp, tta);
+    const int exb = block_scan_exclusive((c + a.tile_b_rows - 1) / a.tile_b_rows, s_warp, ttb);
+    if (e < a.El) {
+      a.offsets[e] = carry + ex;
+      a.tile_a[e] = ta_carry + exa;
+      a.tile_b[e] = tb_carry + exb;
+    }
+    carry += tot;
+    ta_carry += tta;
+    tb_carry += ttb;
+  }
+  // active list in ascending order
+  for (int e0 = 0; e0 < a.El; e0 += blockDim.x) {
+    const int e = e0 + tid;
+    int c = 0;
+    if (e < a.El)
+      for (int p = 0; p < a.P; ++p) c += max(a.recv_counts[p * a.El + e], 0);
+    int tot;
+    const int ex = block_scan_exclusive(c > 0 ? 1 : 0, s_warp, tot);
+    if (e < a.El && c > 0) a.active[s_n + ex] = e;
+    __syncthreads();
+    if (tid == 0) s_n += tot;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    a.offsets[a.El] = total;
+    a.tile_a[a.El] = ta_carry;
+    a.tile_b[a.El] = tb_carry;
+    *a.num_active = s_n;
+    if (total != a.R) raise_error(a.err, E4B_ERR_INVALID_ARG);
+  }
+  __syncthreads();
+  // map fill: one warp per (source, expert) block
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-  for (int b = warp; b < a.P * a.El; b += nwarps) {
+  for (int b = warp; b < nb; b += nwarps) {
     const int c = a.recv_counts[b];
     const int s0 = a.src_start[b], d0 = a.dst_start[b];
     for (int i = lane; i < c; i += 32)
       if (d0 + i < a.R && s0 + i < a.R) a.map[d0 + i] = s0 + i;
   }
   // rows no block covers (only when the counts disagree with R) map to row 0
-  if (s_total < a.R)
-    for (int i = s_total + tid; i < a.R; i += blockDim.x) a.map[i] = 0;
+  for (int i = total + tid; i < a.R; i += blockDim.x) a.map[i] = 0;
 }
 
 int rows_ctas(int rows) {
@@ -292,8 +353,8 @@ extern "C" e4b_status e4b_ep_experts(const e4b_moe_desc* local, int world, const
   x.num_active = pl.num_active;
   x.tile_a = pl.tile_a;
   x.tile_b = pl.tile_b;
-  // The same regime rule as the single-GPU layer (rows here play the role of tokens there).
-  x.use_umma = umma_eligible(R, 1, El, H, I, d.has_gate, d.act_dtype, d.lora_rank);
+  // The same regime rule as the single-GPU layer: average rows per local expert.
+  x.use_umma = umma_worthwhile(R, El) && umma_eligible(R, 1, El, H, I, d.has_gate, d.act_dtype, d.lora_rank);
   x.h = ws + L.h;
   x.down_rows = ws + L.down_rows;
   x.xa_gu = reinterpret_cast<float*>(ws + L.xa_gu);

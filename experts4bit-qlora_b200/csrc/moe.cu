@@ -13,12 +13,13 @@
 #include "permute.cuh"
 #include "umma.cuh"
 #include "moe_stages.cuh"
+#include "decode_layer.cuh"
 
 namespace e4b {
 
 struct MoeLayout {
   size_t offsets, active, num_active, tile_a, tile_b, inv, sorted_token, x16, x_scale, h, down_rows, xa_gu, xa_dn,
-      umma, total;
+      umma, sync, total;
 };
 
 static MoeLayout moe_layout(const e4b_moe_desc& d) {
@@ -46,6 +47,7 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   L.xa_gu = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
   L.xa_dn = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
   L.umma = take(umma_workspace_bytes(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate));
+  L.sync = take(decode_layer_sync_bytes(1024));
   L.total = o;
   return L;
 }
@@ -381,6 +383,17 @@ extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int
   return launch_gemv_auto(g, R, R, s);
 }
 
+extern "C" int e4b_moe_path(const e4b_moe_desc* desc) {
+  if (!desc || !desc_ok(*desc)) return -1;
+  const e4b_moe_desc& d = *desc;
+  if (decode_layer_eligible(d)) return E4B_PATH_DECODE_LAYER;
+  const int64_t R = (int64_t)d.tokens * d.top_k;
+  if (umma_worthwhile(R, d.num_experts) &&
+      umma_eligible(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate, d.has_gate, d.act_dtype, d.lora_rank))
+    return E4B_PATH_TENSOR_CORE;
+  return E4B_PATH_STREAMING;
+}
+
 extern "C" size_t e4b_moe_workspace_bytes(const e4b_moe_desc* desc) {
   if (!desc || !desc_ok(*desc)) return 0;
   return moe_layout(*desc).total;
@@ -414,6 +427,11 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   const int R = T * k;
 
   mark_stage(t, 0, s);
+  if (decode_layer_eligible(d)) {  // one launch: permute, both GEMVs and the combine
+    e4b_status st = launch_decode_layer(d, t, ws + L.h, ws + L.down_rows, ws + L.sync, err, s);
+    for (int i = 1; i < E4B_MOE_STAGE_EVENTS; ++i) mark_stage(t, i, s);
+    return st;
+  }
   PermuteArgs pa{};
   pa.topk_idx = t->topk_idx;
   pa.T = T;
@@ -439,7 +457,8 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   pa.conv.rows = T;
   pa.conv.K = H;
   pa.conv_ctas = conv_ctas_for(T, 32);
-  const bool use_umma = umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype, d.lora_rank);
+  const bool use_umma =
+      umma_worthwhile((int64_t)T * k, E) && umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype, d.lora_rank);
   if (use_umma) pa.conv.src = nullptr;  // converted below, in expert-sorted order
   e4b_status st = launch_permute(pa, s);
   if (st != E4B_OK) return st;

@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u4 = 0; u4 < 4; ++u4) p[u4] = wsrc[(u4 + rot) & 3];
           }
-          fence_proxy_async();
+          fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
           mbar_arrive(&w_empty[s]);
           if (!wt.wait(&a_empty[sa], ((n / kSA) & 1) ^ 1)) break;
           if (h < GROUPS) {
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           p0 = reinterpret_cast<const uint4*>(wsrc)[0];
           p1 = reinterpret_cast<const uint4*>(wsrc)[1];
         }
-        fence_proxy_async();
+        fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
         mbar_arrive(&w_empty[s]);  // packed bytes are in registers: the slot can be refilled
         if (!wt.wait(&a_empty[sa], ((n / kSA) & 1) ^ 1)) break;
         if (h < GROUPS) {

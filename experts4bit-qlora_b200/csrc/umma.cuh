@@ -15,6 +15,11 @@ struct UmmaArgs {
   void* scratch;
 };
 
+// Rows per expert (on average) from which the tensor-core path beats the GEMV, which
+// re-reads an expert's weights for every 16 of its rows.
+constexpr int kUmmaMinRowsPerExpert = 16;
+inline bool umma_worthwhile(int64_t rows, int experts) { return rows >= (int64_t)kUmmaMinRowsPerExpert * experts; }
+
 size_t umma_workspace_bytes(int T, int k, int E, int H, int I);
 bool umma_eligible(int T, int k, int E, int H, int I, int has_gate, int act_dtype, int lora_rank);
 UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k, int x_rows);

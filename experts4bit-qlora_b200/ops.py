@@ -232,6 +232,25 @@ def MoeDesc_from(E, H, I, k, T, has_gate, act_dtype, w_dtype, out_dtype, lora, w
     return d
 
 
+def moe_path(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16, lora_rank=0, weight_format=N.FMT_NF4) -> int:
+    """Which kernel sequence ``e4b_moe_forward`` runs (``_native.PATH_*``)."""
+    d = N.MoeDesc()
+    d.num_experts, d.hidden, d.intermediate, d.top_k, d.tokens = E, H, I, k, T
+    d.has_gate = int(bool(has_gate))
+    d.act_dtype = N.dtype_code(act_dtype)
+    d.weight_dtype = N.F32
+    d.out_dtype = N.dtype_code(act_dtype)
+    d.lora_rank = lora_rank
+    d.lora_dtype = N.F32
+    d.weight_format = int(weight_format)
+    return N.lib().e4b_moe_path(ctypes.byref(d))
+
+
+def set_decode_kernel(enabled: bool) -> int:
+    """Turn the one-launch decode-layer kernel on or off for the process; returns the old setting."""
+    return N.lib().e4b_set_decode_kernel(int(bool(enabled)))
+
+
 def moe_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16, lora_rank=0,
                         weight_format=N.FMT_NF4) -> int:
     d = N.MoeDesc()

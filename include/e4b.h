@@ -200,6 +200,19 @@ E4B_API size_t e4b_moe_workspace_bytes(const e4b_moe_desc* desc);
 E4B_API e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tensors* t, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Which kernel sequence e4b_moe_forward runs for `desc` (no counterpart in the
+ * reference): E4B_PATH_DECODE_LAYER = one persistent launch for the whole layer
+ * (decode regime, NF4, no adapters), E4B_PATH_STREAMING = permute + grouped GEMV
+ * kernels, E4B_PATH_TENSOR_CORE = permute + tcgen05 grouped GEMMs; -1 for an
+ * invalid descriptor. e4b_set_decode_kernel(0) turns the one-launch path off for
+ * the process (also E4B_DECODE_KERNEL=0 in the environment); returns the
+ * previous setting (-1 = not yet read). */
+#define E4B_PATH_STREAMING 0
+#define E4B_PATH_TENSOR_CORE 1
+#define E4B_PATH_DECODE_LAYER 2
+E4B_API int e4b_moe_path(const e4b_moe_desc* desc);
+E4B_API int e4b_set_decode_kernel(int enabled);
+
 /* No counterpart in the reference. Same layer as e4b_moe_forward for callers
  * that cannot allocate device memory (a host framework that owns all device
  * allocations, a plugin host that forbids cudaMalloc after start-up): the

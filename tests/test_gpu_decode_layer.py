@@ -1,0 +1,109 @@
+"""GPU: the one-launch decode-layer kernel (permute, both grouped GEMVs and the
+combine as phases of one persistent cooperative kernel). It must equal the
+multi-kernel path bit for bit, meet the layer tolerance against the fp32
+oracle, capture into a CUDA graph, and report errors per call."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import moe as M
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _layer(e4b, E, H, I, has_gate=True, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    n1 = 2 * I if has_gate else I
+    gu = (torch.randn(E, n1, H, generator=g) * 0.02).to(torch.bfloat16)
+    dn = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    mod = e4b.Experts4bit.from_float(gu.to(DEV), dn.to(DEV), has_gate=has_gate)
+    st = {"gate_up_packed": mod.gate_up_proj.data.cpu(), "gate_up_absmax": mod.gate_up_absmax.cpu(),
+          "down_packed": mod.down_proj.data.cpu(), "down_absmax": mod.down_absmax.cpu(), "E": E, "H": H, "I": I,
+          "has_gate": has_gate}
+    return mod, st
+
+
+def _inputs(E, H, T, k, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w, idx = M.route_on_host(torch.randn(T, E, generator=g), k)
+    return x, idx, w
+
+
+def _fwd(e4b, mod, x, idx, w, E, I, has_gate=True, out_dtype=None, check=True):
+    return e4b.ops.moe_forward(x.to(DEV), idx.to(DEV), w.to(DEV), mod.gate_up_proj, mod.gate_up_absmax,
+                               mod.down_proj, mod.down_absmax, E, I, has_gate=has_gate, out_dtype=out_dtype,
+                               check_errors=check)
+
+
+@pytest.mark.parametrize("E,H,I,k,T", [(64, 2048, 1024, 8, 1), (64, 2048, 1024, 8, 2), (64, 2048, 1024, 8, 3),
+                                       (64, 2048, 1024, 8, 4), (32, 512, 256, 8, 12), (128, 1024, 512, 4, 8)])
+def test_decode_layer_bitexact_vs_multikernel_and_oracle(e4b, E, H, I, k, T):
+    mod, st = _layer(e4b, E, H, I)
+    x, idx, w = _inputs(E, H, T, k, seed=T)
+    assert e4b.ops.moe_path(E, H, I, k, T) == e4b._native.PATH_DECODE_LAYER
+    fused = _fwd(e4b, mod, x, idx, w, E, I)
+    old = e4b.ops.set_decode_kernel(False)
+    try:
+        assert e4b.ops.moe_path(E, H, I, k, T) == e4b._native.PATH_STREAMING
+        multi = _fwd(e4b, mod, x, idx, w, E, I)
+    finally:
+        e4b.ops.set_decode_kernel(True)
+    # the multi-kernel path runs the same streaming arithmetic while its token (and h) rows fit the
+    # streaming kernel's 64 KB of shared memory; beyond that it takes the general GEMV (other order)
+    if T * k * (I + 8) * 2 <= 64 * 1024:
+        assert torch.equal(fused, multi)
+    else:
+        assert M.rel_errors(fused.float(), multi.float())[0] <= 2e-3
+    mx, mean = M.rel_errors(fused.float().cpu(), M.fp32_oracle(st, x, idx, w))
+    assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
+
+
+def test_decode_layer_silu_only_and_fp32_out(e4b):
+    E, H, I, k, T = 16, 512, 256, 4, 3
+    mod, st = _layer(e4b, E, H, I, has_gate=False, seed=2)
+    x, idx, w = _inputs(E, H, T, k, seed=3)
+    assert e4b.ops.moe_path(E, H, I, k, T, has_gate=False) == e4b._native.PATH_DECODE_LAYER
+    got = _fwd(e4b, mod, x, idx, w, E, I, has_gate=False, out_dtype=torch.float32)
+    assert got.dtype == torch.float32
+    mx, mean = M.rel_errors(got.cpu(), M.fp32_oracle(st, x, idx, w))
+    assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
+
+
+def test_decode_layer_graph_capture_and_repeat(e4b):
+    E, H, I, k, T = 64, 2048, 1024, 8, 1
+    mod, _ = _layer(e4b, E, H, I, seed=4)
+    x, idx, w = _inputs(E, H, T, k, seed=5)
+    xc, ic, wc = x.to(DEV), idx.to(DEV), w.to(DEV)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    call = lambda: e4b.ops.moe_forward(xc, ic, wc, mod.gate_up_proj, mod.gate_up_absmax, mod.down_proj,  # noqa
+                                       mod.down_absmax, E, I, out=out)
+    call()
+    ref = out.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        call()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        call()
+    for _ in range(20):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+
+
+def test_decode_layer_reports_errors_per_call(e4b):
+    E, H, I, k, T = 16, 512, 256, 2, 2
+    mod, _ = _layer(e4b, E, H, I, seed=6)
+    x, idx, w = _inputs(E, H, T, k, seed=7)
+    bad = idx.clone()
+    bad[0, 0] = E + 3
+    with pytest.raises(e4b._native.E4BError) as ei:
+        _fwd(e4b, mod, x, bad, w, E, I)
+    assert ei.value.status == e4b._native.E4B_ERR_EXPERT_INDEX
+    _fwd(e4b, mod, x, idx, w, E, I)  # a valid call afterwards reports nothing
