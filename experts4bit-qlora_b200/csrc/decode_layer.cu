@@ -11,8 +11,8 @@
 //            matching up rows) and streams them in items of up to 2048 K elements,
 //            one 8 KB TMA box per 8 rows and one absmax box; fragments go to
 //            mma.sync m16n8k16 with the tokens as the n8 operand; h rows (fp16) to
-//            the workspace; then the CTA asks L2 to prefetch its share of the
-//            active experts' down weights;                       grid barrier;
+//            the workspace; each pair then starts its first down-weight copy,
+//            which overlaps the barrier;                         grid barrier;
 //   phase B  down tiles, activations (h) staged from L2;        grid barrier;
 //   phase C  fixed-slot-order combine into the output.
 // The arithmetic is the streaming GEMV's (gemv_stream.cu) and the combine
@@ -70,7 +70,10 @@ using stream::mma16816_zero;
 using stream::named_barrier;
 
 constexpr int kMaxPicks = 128;
+// One item per tile up to K = 2048: the pair-table lookups, not the copies, bound an item, so
+// splitting tiles into smaller items in flight together does not pay here.
 constexpr int kDChunk = 2048;             // K elements per item
+constexpr int kDSlots = 1;                // items in flight per pair
 constexpr int kWBoxCap = 8 * 1024;        // one 8-row group, up to 8 lines of 128 B
 constexpr int kABoxCap = 32 * 8 * 4;      // one 8-row group, up to 32 absmax floats
 constexpr int kDSlotBytes = 2 * kWBoxCap + 2 * kABoxCap;  // 18 KB, a multiple of 1024
@@ -90,9 +93,9 @@ struct DSmem {
   static constexpr int lut = 0;
   static constexpr int x = kLut;
   static constexpr int slots = x + kDXBudget;
-  static constexpr int red = slots + kPairs * kDSlotBytes;
+  static constexpr int red = slots + kPairs * kDSlots * kDSlotBytes;
   static constexpr int bars = red + kPairs * 32 * 8 * 4;
-  static constexpr int tables = bars + kPairs * 8;
+  static constexpr int tables = bars + kPairs * kDSlots * 8;
   // int tables of kMaxPicks: pick expert, sorted expert, sorted token, inverse, active expert/row0/count;
   // 16 token scales, 16 misc words, kMaxPicks top-k weights, 16 row maxima
   static constexpr int total = tables + 7 * kMaxPicks * 4 + 16 * 4 + 16 * 4 + kMaxPicks * 4 + 16 * 4;
@@ -181,9 +184,12 @@ __device__ __forceinline__ int group_row(const Phase& p, int tile, int h) {
   return tile * 16 + 8 * h;
 }
 
-// Copies of the pair's item n into its slot (pair leader only).
-__device__ __forceinline__ void issue_item(const Phase& p, const Tables& tb, char* slot, uint64_t* bar, int gp,
-                                           int n) {
+// Copies of the pair's item n (of this phase; n0 items before it) into ring slot (n0 + n) % kDSlots
+// (pair leader only).
+__device__ __forceinline__ void issue_item(const Phase& p, const Tables& tb, char* smem, int gp, int n, int n0) {
+  const int pair = gp - blockIdx.x * kPairs;
+  char* slot = smem + DSmem::slots + (pair * kDSlots + (n0 + n) % kDSlots) * kDSlotBytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DSmem::bars) + pair * kDSlots + (n0 + n) % kDSlots;
   const int npairs = gridDim.x * kPairs;
   const int chunks = phase_chunks(p);
   const int t = gp + (n / chunks) * npairs;
@@ -199,6 +205,12 @@ __device__ __forceinline__ void issue_item(const Phase& p, const Tables& tb, cha
     tma_load_3d(slot + h * kWBoxCap, p.wmap, 0, r0, c * (kDChunk / 256), bar);
     tma_load_2d(slot + 2 * kWBoxCap + h * kABoxCap, p.amap, c * (kDChunk / 64), r0, bar);
   }
+}
+
+// The first kDSlots items of the pair's phase (pair leader only).
+__device__ __forceinline__ void issue_head(const Phase& p, const Tables& tb, char* smem, int nact, int gp, int n0) {
+  const int total = phase_items(p, nact, gp);
+  for (int n = 0; n < kDSlots && n < total; ++n) issue_item(p, tb, smem, gp, n, n0);
 }
 
 // Byte offset of lane (row r, quad lane q)'s 8-byte piece of block bc (of the chunk) in a weight
@@ -218,9 +230,9 @@ __device__ void stream_phase(const Phase& p, const Tables& tb, int nact, char* s
   const int pair = warp >> 1, member = warp & 1;
   const int gq = lane >> 2, q = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
-  char* slot = smem + DSmem::slots + pair * kDSlotBytes;
+  char* slots = smem + DSmem::slots + pair * kDSlots * kDSlotBytes;
   float* red = reinterpret_cast<float*>(smem + DSmem::red) + pair * 32 * 8;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DSmem::bars) + pair;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DSmem::bars) + pair * kDSlots;
   const bool leader = member == 0 && lane == 0;
   const int npairs = gridDim.x * kPairs;
   const int chunks = phase_chunks(p);
@@ -230,7 +242,7 @@ __device__ void stream_phase(const Phase& p, const Tables& tb, int nact, char* s
   const bool swiglu = p.epilogue == E4B_EPI_SWIGLU;
   const int arow = abox_floats(p.K) * 4;  // bytes per absmax box row
   (void)trace_slot;
-  if (leader && !dead && !head_issued && total_items > 0) issue_item(p, tb, slot, bar, gp, 0);
+  if (leader && !dead && !head_issued) issue_head(p, tb, smem, nact, gp, n0);
 
   int row0 = 0, M = 0, tile = 0;
   float acc[NT][4];
@@ -247,7 +259,9 @@ __device__ void stream_phase(const Phase& p, const Tables& tb, int nact, char* s
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
     }
-    if (!dead && !mbar_wait(bar, (n0 + n) & 1)) {
+    const int gn = n0 + n;
+    char* slot = slots + (gn % kDSlots) * kDSlotBytes;
+    if (!dead && !mbar_wait(&bars[gn % kDSlots], (gn / kDSlots) & 1)) {
       cta_raise(cta_err, E4B_ERR_TIMEOUT);
       dead = true;
     }
@@ -331,7 +345,7 @@ __device__ void stream_phase(const Phase& p, const Tables& tb, int nact, char* s
     // the slot's refill by the async proxy
     fence_proxy_async();
     named_barrier(1 + pair, 64);
-    if (leader && !dead && n + 1 < total_items) issue_item(p, tb, slot, bar, gp, n + 1);
+    if (leader && !dead && n + kDSlots < total_items) issue_item(p, tb, smem, gp, n + kDSlots, n0);
     if (last && member == 0 && !dead) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -364,7 +378,9 @@ __device__ void stream_phase(const Phase& p, const Tables& tb, int nact, char* s
         }
     }
   }
-  if (dead && leader && total_items > 0) (void)mbar_wait(bar, (n0 + total_items - 1) & 1);  // drain, bounded
+  if (dead && leader)  // drain what may still be in flight, bounded
+    for (int m = total_items - kDSlots; m < total_items; ++m)
+      if (m >= 0) (void)mbar_wait(&bars[(n0 + m) % kDSlots], ((n0 + m) / kDSlots) & 1);
   if (total_items > 0) PTRACE(trace_slot + 1);
   n_run = n0 + total_items;
 }
@@ -425,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- phase 0: the permutation first, so the weight stream starts early ------------------
   if (tid == 0) {
     tb.misc[1] = 0;
-    for (int s = 0; s < kPairs; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kPairs * kDSlots; ++s) mbar_init(&bars[s], 1);
     fence_proxy_async();
   }
   if (tid < 16) tb.rowmax[tid] = 0u;
@@ -472,11 +488,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   const int nact = tb.misc[0];
   DTRACE(1);
-  if ((warp & 1) == 0 && lane == 0) {  // pair leaders: the first gate_up item
-    const int gp = blockIdx.x * kPairs + (warp >> 1);
-    if (phase_items(pa, nact, gp) > 0)
-      issue_item(pa, tb, smem + DSmem::slots + (warp >> 1) * kDSlotBytes, &bars[warp >> 1], gp, 0);
-  }
+  if ((warp & 1) == 0 && lane == 0)  // pair leaders: the first gate_up items
+    issue_head(pa, tb, smem, nact, blockIdx.x * kPairs + (warp >> 1), 0);
   if (tid < nact) tb.act_cnt[tid] = (tid + 1 < nact ? tb.act_row0[tid + 1] : R) - tb.act_row0[tid];
   DTRACE(10);
   {  // pair table
@@ -534,29 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool dead = false;
   DTRACE(2);
   stream_phase<NT>(pa, tb, nact, smem, n_run, dead, cta_err, true, 0);
-  {  // L2 prefetch of this CTA's share of the active experts' down weights and absmax
-    auto prefetch = [&](const char* base, int64_t per) {
-      const int64_t total = per * nact;
-      const int64_t share = ((total + gridDim.x - 1) / gridDim.x + 4095) & ~4095ll;
-      const int64_t end = min(total, (blockIdx.x + 1) * share);
-      for (int64_t off = blockIdx.x * share + (int64_t)tid * 4096; off < end; off += kThreads * 4096) {
-        const int j = (int)(off / per);
-        const int64_t in = off - j * per;
-        int64_t nbytes = per - in < 4096 ? per - in : 4096;
-        if (end - off < nbytes) nbytes = end - off;
-        const char* src = base + (int64_t)tb.act_e[j] * per + in;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"((uint32_t)nbytes & ~15u)
-                     : "memory");
-      }
-    };
-    prefetch(reinterpret_cast<const char*>(a.dn_packed), (int64_t)a.H * a.I / 2);
-    prefetch(reinterpret_cast<const char*>(a.dn_absmax), (int64_t)a.H * (a.I / 64) * 4);
-  }
-  DTRACE(3);
-  cg::this_grid().sync();
-  DTRACE(4);
-
-  // ---- phase B: down -----------------------------------------------------------------------
+  // phase B's weights do not depend on phase A: each pair starts its first down item now, so the
+  // copy overlaps the grid barrier
   Phase pb{};
   pb.wmap = &wmap_dn;
   pb.amap = &amap_dn;
@@ -569,11 +561,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   pb.x_mapped = false;
   pb.out = a.down_rows;
   pb.Nout = a.H;
-  if ((warp & 1) == 0 && lane == 0 && !dead) {
-    const int gp = blockIdx.x * kPairs + (warp >> 1);
-    if (phase_items(pb, nact, gp) > 0)
-      issue_item(pb, tb, smem + DSmem::slots + (warp >> 1) * kDSlotBytes, &bars[warp >> 1], gp, 0);
-  }
+  if ((warp & 1) == 0 && lane == 0 && !dead) issue_head(pb, tb, smem, nact, blockIdx.x * kPairs + (warp >> 1), n_run);
+  DTRACE(3);
+  cg::this_grid().sync();
+  DTRACE(4);
+
+  // ---- phase B: down -----------------------------------------------------------------------
   if ((int64_t)R * (a.I + 8) * 2 <= kDXBudget) {  // all of h fits where the token rows were: stage it
     const int hp = a.I + 8, vec = a.I / 8;
     for (int v = tid; v < R * vec; v += kThreads) {
