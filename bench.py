@@ -173,7 +173,8 @@ def run_ours(args, wl, world, rank, local):
     outs = torch.empty(Lc, T, H, dtype=torch.bfloat16, device=dev)
     base = lambda m: m.base if hasattr(m, "base") else m  # noqa: E731
     ws = N.workspaces.get(dev, max(ops.moe_workspace_bytes(wl["E"], H, wl["I"], wl["k"], T, lora_rank=wl["lora"]),
-                                   1 << 20), "bench")
+                                   ops.moe_decode_step_workspace_bytes(wl["E"], H, wl["I"], wl["k"], T), 1 << 20),
+                          "bench")
     rws = N.workspaces.get(dev, N.lib().e4b_router_workspace_bytes(T, wl["E"]), "bench_router")
     topw = torch.empty(Lc, T, wl["k"], dtype=torch.float32, device=dev)
     topi = torch.empty(Lc, T, wl["k"], dtype=torch.int64, device=dev)
@@ -183,6 +184,12 @@ def run_ours(args, wl, world, rank, local):
     def layer_call(li, x, events=None):
         mod, router, lora = layers[li]
         b = base(mod)
+        if lora is None:  # router + layer in one call (one launch in the decode regime)
+            ev = [e.cuda_event for e in events] if events is not None else None
+            ops.moe_decode_step(x, router, wl["k"], b.gate_up_proj, b.gate_up_absmax, b.down_proj, b.down_absmax,
+                                wl["E"], wl["I"], norm_topk_prob=wl["norm"], out=outs[li], topk_idx=topi[li],
+                                topk_w=topw[li], workspace=ws, stage_events=ev)
+            return
         N.check(L.e4b_router_topk(x.data_ptr(), N.BF16, router.data_ptr(), N.BF16, T, H, wl["E"], wl["k"],
                                   N.SOFTMAX_THEN_TOPK, int(wl["norm"]), None, topi[li].data_ptr(), topw[li].data_ptr(),
                                   rws.data_ptr(), rws.numel(), torch.cuda.current_stream().cuda_stream), "router")
@@ -280,9 +287,10 @@ def run_ours(args, wl, world, rank, local):
     path = ops.moe_path(wl["E"], H, wl["I"], wl["k"], T, lora_rank=wl["lora"])
     one_launch = path == N.PATH_DECODE_LAYER
     if one_launch:
-        # the whole layer is one kernel (stage marks 1..6 follow it): its interval is mark 0 -> 1
+        # router + whole layer in one kernel (stage marks 1..6 follow it): its interval is mark 0 -> 1
         layer_us = stage_avg_us["permute"]
         bound, unit = "hbm", "GB/s"
+        gu_bytes += wl["E"] * H * 2  # the router weights the same launch reads
         achieved = (gu_bytes + dn_bytes) / (layer_us * 1e-6) / 1e9
         peak = peaks["hbm_gbs"]
     elif wl["T"] <= 16:
@@ -295,7 +303,7 @@ def run_ours(args, wl, world, rank, local):
         achieved = flops / (stage_avg_us["gate_up"] * 1e-6) / 1e12
         peak = peaks["bf16_tflops"]
     roofline = {"bound": bound,
-                "kernel": ("nf4 decode layer, one launch: permute + gate_up GEMV (SwiGLU) + down GEMV + combine"
+                "kernel": ("nf4 decode step, one launch: router + permute + gate_up GEMV (SwiGLU) + down GEMV + combine"
                            if one_launch else "nf4 grouped gate_up (SwiGLU fused)"),
                 "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": peak_kind, "unit": unit, "frac": round(achieved / peak, 4),
@@ -318,7 +326,7 @@ def run_ours(args, wl, world, rank, local):
     e2e_value = args.steps * T * Lc * world / (e2e["ms"] / 1e3)
 
     # router 2; then one layer kernel, or permute, [lora x2], gate_up, down, combine
-    launches_per_layer = 2 + (1 if one_launch else (5 if wl["lora"] else 3) + 1)
+    launches_per_layer = 1 if one_launch else 2 + (5 if wl["lora"] else 3) + 1
     result = {
         "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),

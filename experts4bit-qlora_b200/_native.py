@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
     "e4b_combine",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
+    "e4b_moe_decode_step_workspace_bytes", "e4b_moe_decode_step",
     "e4b_moe_path", "e4b_set_decode_kernel",
     "e4b_moe_forward_static",
     "e4b_ep_dispatch_workspace_bytes", "e4b_ep_dispatch", "e4b_ep_experts_workspace_bytes", "e4b_ep_experts",
@@ -91,6 +92,8 @@ def _declare(lib):
         "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
         "e4b_moe_forward_static": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P]),
         "e4b_moe_path": (I, [ctypes.POINTER(MoeDesc)]),
+        "e4b_moe_decode_step_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
+        "e4b_moe_decode_step": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, I, I, I, P, P, P, SZ, P]),
         "e4b_set_decode_kernel": (I, [I]),
         "e4b_ep_dispatch_workspace_bytes": (SZ, [I, I, I]),
         "e4b_ep_dispatch": (I, [P, I, P, I, I, I, I, P, P, P, P, SZ, P]),

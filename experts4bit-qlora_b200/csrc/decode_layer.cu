@@ -25,13 +25,14 @@
 
 #include "convert.cuh"
 #include "decode_layer.cuh"
+#include "router.cuh"
 #include "stream_core.cuh"
 #include "tmap.cuh"
 
 // Profiling instrumentation, compiled only with -DE4B_TRACE: per-CTA %globaltimer
 // stamps at phase boundaries, read back with e4b_decode_trace_read.
 #ifdef E4B_TRACE
-__device__ unsigned long long g_dl_trace[1024 * 16];
+__device__ unsigned long long g_dl_trace[1024 * 24];
 extern "C" __attribute__((visibility("default"))) int e4b_decode_trace_read(unsigned long long* host, int n) {
   return (int)cudaMemcpyFromSymbol(host, g_dl_trace, n * sizeof(unsigned long long));
 }
@@ -43,7 +44,7 @@ extern "C" __attribute__((visibility("default"))) int e4b_decode_pair_read(unsig
   if (threadIdx.x == 0) {                                          \
     unsigned long long t_;                                         \
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));        \
-    g_dl_trace[blockIdx.x * 16 + (i)] = t_;                        \
+    g_dl_trace[blockIdx.x * 24 + (i)] = t_;                        \
   }
 #define PTRACE(i)                                                  \
   if (lane == 0 && member == 0) {                                  \
@@ -70,6 +71,7 @@ using stream::mma16816_zero;
 using stream::named_barrier;
 
 constexpr int kMaxPicks = 128;
+constexpr int kMaxLogits = 4096;          // T x E of the fused router, in shared memory
 // One item per tile up to K = 2048: the pair-table lookups, not the copies, bound an item, so
 // splitting tiles into smaller items in flight together does not pay here.
 constexpr int kDChunk = 2048;             // K elements per item
@@ -98,7 +100,8 @@ struct DSmem {
   static constexpr int tables = bars + kPairs * kDSlots * 8;
   // int tables of kMaxPicks: pick expert, sorted expert, sorted token, inverse, active expert/row0/count;
   // 16 token scales, 16 misc words, kMaxPicks top-k weights, 16 row maxima
-  static constexpr int total = tables + 7 * kMaxPicks * 4 + 16 * 4 + 16 * 4 + kMaxPicks * 4 + 16 * 4;
+  static constexpr int logits = tables + 7 * kMaxPicks * 4 + 16 * 4 + 16 * 4 + kMaxPicks * 4 + 16 * 4;
+  static constexpr int total = logits + kMaxLogits * 4;  // fused router: [T, E] fp32
 };
 static_assert(DSmem::slots % 1024 == 0 && kDSlotBytes % 1024 == 0, "swizzled boxes need 1024-byte alignment");
 static_assert(DSmem::total <= 232448, "shared memory budget");
@@ -120,6 +123,11 @@ struct DecodeArgs {
   __half* down_rows;           // [R, H]
   int* cta_err;                // [gridDim.x]
   int* err;
+  // fused router (router_w != null): logits of x . W_r^T and the top-k replace topk_idx / topk_w
+  const void* router_w;
+  int router_w_dtype, route_kind, renorm;
+  int64_t* topk_idx_out;       // [T, k] (written by CTA 0)
+  float* topk_w_out;           // [T, k]
 };
 
 struct Tables {
@@ -445,7 +453,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async();
   }
   if (tid < 16) tb.rowmax[tid] = 0u;
-  if (tid < R) {
+  if (a.router_w) {
+    // ---- fused router: every CTA computes all logits into its shared memory (the weights are
+    // L2 resident after the first CTA touches them) and the same top-k: no grid barrier ----
+    float* logits = reinterpret_cast<float*>(smem + DSmem::logits);
+    const int ttiles = (a.T + kRouterTT - 1) / kRouterTT, tasks = a.E * ttiles;
+    for (int task = warp; task < tasks; task += kWarps)
+      router_logits_warp(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
+                         (task / a.E) * kRouterTT, logits);
+    DTRACE(14);
+    __syncthreads();
+    DTRACE(15);
+    if (warp < a.T) {
+      int se = 0;
+      float sw = 0.f;
+      if (a.E <= 32) router_topk_warp<1>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
+      else if (a.E <= 64) router_topk_warp<2>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
+      else if (a.E <= 128) router_topk_warp<4>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
+      else if (a.E <= 256) router_topk_warp<8>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
+      else router_topk_warp<32>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
+      if (lane < a.k) {
+        tb.pick_e[warp * a.k + lane] = se;
+        tb.w[warp * a.k + lane] = sw;
+        if (blockIdx.x == 0) {
+          a.topk_idx_out[warp * a.k + lane] = se;
+          a.topk_w_out[warp * a.k + lane] = sw;
+        }
+      }
+    }
+    DTRACE(16);
+  } else if (tid < R) {
     int64_t e = a.topk_idx[tid];
     if (e < 0 || e >= a.E) {
       if (blockIdx.x == 0) atomicCAS(&tb.misc[1], 0, E4B_ERR_EXPERT_INDEX);
@@ -455,6 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tb.w[tid] = load_as_f32(a.topk_w, a.w_dtype, tid);
   }
   __syncthreads();
+  DTRACE(17);
   if (tid < R) {  // stable rank by (expert, flat index): the permutation of fast.py:126-133
     const int e = tb.pick_e[tid];
     int rank = 0;
@@ -467,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tb.inv[tid] = rank;
   }
   __syncthreads();
+  DTRACE(18);
   bool start = false;
   unsigned ball = 0;
   if (warp < kMaxPicks / 32) {
@@ -649,6 +688,8 @@ static int sm_count_cached() {
 
 int decode_layer_grid() { return sm_count_cached(); }
 
+bool decode_router_fusable(const e4b_moe_desc& d) { return (int64_t)d.tokens * d.num_experts <= kMaxLogits; }
+
 bool decode_layer_eligible(const e4b_moe_desc& d) {
   if (g_decode_enabled < 0) {
     const char* v = getenv("E4B_DECODE_KERNEL");
@@ -722,13 +763,21 @@ static e4b_status launch_decode(const DecodeArgs& a, cudaStream_t s) {
 }
 
 e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,
-                               void* sync, int* err, cudaStream_t s) {
+                               void* sync, int* err, cudaStream_t s, const DecodeRouter* router) {
   DecodeArgs a{};
+  if (router) {
+    a.router_w = router->weight;
+    a.router_w_dtype = router->weight_dtype;
+    a.route_kind = router->kind;
+    a.renorm = router->norm_topk_prob;
+    a.topk_idx_out = router->topk_idx;
+    a.topk_w_out = router->topk_w;
+  }
   a.hidden = t->hidden;
   a.act_dtype = d.act_dtype;
   a.topk_idx = t->topk_idx;
   a.topk_w = t->topk_w;
-  a.w_dtype = d.weight_dtype;
+  a.w_dtype = router ? E4B_F32 : d.weight_dtype;
   a.gu_packed = static_cast<const uint8_t*>(t->gate_up_packed);
   a.gu_absmax = static_cast<const float*>(t->gate_up_absmax);
   a.dn_packed = static_cast<const uint8_t*>(t->down_packed);

@@ -11,7 +11,17 @@ bool decode_layer_eligible(const e4b_moe_desc& d);
 size_t decode_layer_sync_bytes(int grid);
 // h [R, I] and down_rows [R, H] are fp16 scratch; `sync` holds
 // decode_layer_sync_bytes(grid) bytes (rewritten by every launch).
+// Optional router fused in front of the layer (instead of the two router kernels): every CTA
+// computes the T x E logits of x . W_r^T (T * E <= 4096) and the top-k, written to
+// topk_idx / topk_w [T, k] by CTA 0.
+struct DecodeRouter {
+  const void* weight;
+  int weight_dtype, kind, norm_topk_prob;
+  int64_t* topk_idx;
+  float* topk_w;
+};
+bool decode_router_fusable(const e4b_moe_desc& d);
 e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,
-                               void* sync, int* err, cudaStream_t s);
+                               void* sync, int* err, cudaStream_t s, const DecodeRouter* router = nullptr);
 
 }  // namespace e4b

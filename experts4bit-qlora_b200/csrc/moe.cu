@@ -383,6 +383,48 @@ extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int
   return launch_gemv_auto(g, R, R, s);
 }
 
+extern "C" size_t e4b_moe_decode_step_workspace_bytes(const e4b_moe_desc* desc) {
+  if (!desc || !desc_ok(*desc)) return 0;
+  return align_up(moe_layout(*desc).total, 256) + e4b_router_workspace_bytes(desc->tokens, desc->num_experts);
+}
+
+extern "C" e4b_status e4b_moe_decode_step(const e4b_moe_desc* desc, const e4b_moe_tensors* t, const void* router_w,
+                                          int router_w_dtype, int kind, int norm_topk_prob, int64_t* topk_idx,
+                                          float* topk_w, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!desc || !t || !desc_ok(*desc)) return E4B_ERR_INVALID_ARG;
+  if (!router_w || !topk_idx || !topk_w) return E4B_ERR_INVALID_ARG;
+  if (!is_any_dtype(router_w_dtype)) return E4B_ERR_UNSUPPORTED;
+  if (kind != E4B_SOFTMAX_THEN_TOPK && kind != E4B_TOPK_THEN_SOFTMAX) return E4B_ERR_INVALID_ARG;
+  const size_t need = e4b_moe_decode_step_workspace_bytes(desc);
+  if (!workspace || workspace_bytes < need) return E4B_ERR_WORKSPACE;
+  if (!aligned16(workspace) || !aligned16(router_w)) return E4B_ERR_ALIGNMENT;
+  e4b_moe_desc d = *desc;
+  d.weight_dtype = E4B_F32;  // the router's weights
+  e4b_moe_tensors tt = *t;
+  tt.topk_idx = topk_idx;
+  tt.topk_w = topk_w;
+  char* ws = static_cast<char*>(workspace);
+  const size_t layer_bytes = align_up(moe_layout(d).total, 256);
+  char* rws = ws + layer_bytes;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (d.tokens > 0 && decode_layer_eligible(d) && decode_router_fusable(d) && t->hidden && t->out && t->gate_up_packed && t->gate_up_absmax &&
+      t->down_packed && t->down_absmax && aligned16(t->hidden) && aligned16(t->out) && aligned16(t->gate_up_packed) &&
+      aligned16(t->down_packed) && is_act_dtype(d.act_dtype) && is_any_dtype(d.out_dtype)) {
+    const MoeLayout L = moe_layout(d);
+    DecodeRouter r{router_w, router_w_dtype, kind, norm_topk_prob, topk_idx, topk_w};
+    mark_stage(&tt, 0, s);
+    e4b_status st = launch_decode_layer(d, &tt, ws + L.h, ws + L.down_rows, ws + L.sync, reinterpret_cast<int*>(ws), s,
+                                        &r);
+    for (int i = 1; i < E4B_MOE_STAGE_EVENTS; ++i) mark_stage(&tt, i, s);
+    return st;
+  }
+  e4b_status st = e4b_router_topk(t->hidden, d.act_dtype, router_w, router_w_dtype, d.tokens, d.hidden, d.num_experts,
+                                  d.top_k, kind, norm_topk_prob, nullptr, topk_idx, topk_w, rws,
+                                  e4b_router_workspace_bytes(d.tokens, d.num_experts), stream);
+  if (st != E4B_OK) return st;
+  return e4b_moe_forward(&d, &tt, workspace, layer_bytes, stream);
+}
+
 extern "C" int e4b_moe_path(const e4b_moe_desc* desc) {
   if (!desc || !desc_ok(*desc)) return -1;
   const e4b_moe_desc& d = *desc;

@@ -216,6 +216,52 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     return out
 
 
+def moe_decode_step(hidden: torch.Tensor, router_weight: torch.Tensor, top_k: int, gate_up_packed: torch.Tensor,
+                    gate_up_absmax: torch.Tensor, down_packed: torch.Tensor, down_absmax: torch.Tensor,
+                    num_experts: int, intermediate: int, has_gate: bool = True, kind: int = N.SOFTMAX_THEN_TOPK,
+                    norm_topk_prob: bool = False, out_dtype=None, out: torch.Tensor | None = None,
+                    topk_idx: torch.Tensor | None = None, topk_w: torch.Tensor | None = None,
+                    workspace: torch.Tensor | None = None, check_errors: bool = False, stage_events=None):
+    """Router and expert layer in one call (``e4b_moe_decode_step``): top-k of the fp32 logits
+    ``hidden . router_weight^T``, then the fused layer with those picks. In the decode regime
+    both run in a single launch. Returns ``(out [T,H], top_k_weights f32 [T,k], top_k_index i64 [T,k])``."""
+    _cuda(hidden, "hidden_states")
+    hidden = hidden.contiguous()
+    T, H = hidden.shape
+    dev = hidden.device
+    out_dtype = out_dtype or hidden.dtype
+    out = out if out is not None else torch.empty(T, H, dtype=out_dtype, device=dev)
+    topk_idx = topk_idx if topk_idx is not None else torch.empty(T, top_k, dtype=torch.int64, device=dev)
+    topk_w = topk_w if topk_w is not None else torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    wr = router_weight.contiguous()
+    d = MoeDesc_from(num_experts, H, intermediate, top_k, T, has_gate, hidden.dtype, torch.float32, out_dtype, None)
+    t = N.MoeTensors()
+    t.hidden = hidden.data_ptr()
+    t.gate_up_packed, t.gate_up_absmax = gate_up_packed.data_ptr(), gate_up_absmax.data_ptr()
+    t.down_packed, t.down_absmax = down_packed.data_ptr(), down_absmax.data_ptr()
+    t.out = out.data_ptr()
+    keep = None
+    if stage_events is not None:
+        keep = (ctypes.c_void_p * N.MOE_STAGE_EVENTS)(*stage_events)
+        t.stage_events = ctypes.cast(keep, ctypes.c_void_p)
+    L = N.lib()
+    nbytes = L.e4b_moe_decode_step_workspace_bytes(ctypes.byref(d))
+    if nbytes == 0:
+        raise ValueError("invalid expert-layer geometry for the fused kernel")
+    ws = workspace if workspace is not None else N.workspaces.get(dev, nbytes, "moe_step")
+    if ws.numel() < nbytes:
+        raise ValueError(f"workspace of {ws.numel()} bytes < required {nbytes}")
+    N.check(L.e4b_moe_decode_step(ctypes.byref(d), ctypes.byref(t), wr.data_ptr(), N.dtype_code(wr.dtype), kind,
+                                  int(norm_topk_prob), topk_idx.data_ptr(), topk_w.data_ptr(), ws.data_ptr(),
+                                  ws.numel(), N.stream_handle(dev)), "e4b_moe_decode_step")
+    del keep
+    if check_errors:
+        err = N.read_device_error(ws)
+        if err:
+            raise N.E4BError(err, "e4b_moe_decode_step (device)")
+    return out, topk_w, topk_idx
+
+
 def MoeDesc_from(E, H, I, k, T, has_gate, act_dtype, w_dtype, out_dtype, lora, weight_format=N.FMT_NF4) -> N.MoeDesc:
     d = N.MoeDesc()
     d.weight_format = int(weight_format)
@@ -244,6 +290,11 @@ def moe_path(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16, lora_rank=0
     d.lora_dtype = N.F32
     d.weight_format = int(weight_format)
     return N.lib().e4b_moe_path(ctypes.byref(d))
+
+
+def moe_decode_step_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16) -> int:
+    d = MoeDesc_from(E, H, I, k, T, has_gate, act_dtype, torch.float32, act_dtype, None)
+    return N.lib().e4b_moe_decode_step_workspace_bytes(ctypes.byref(d))
 
 
 def set_decode_kernel(enabled: bool) -> int:

@@ -213,6 +213,18 @@ E4B_API e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tenso
 E4B_API int e4b_moe_path(const e4b_moe_desc* desc);
 E4B_API int e4b_set_decode_kernel(int enabled);
 
+/* No counterpart in the reference (its router is the model's own module): router
+ * and expert layer in one call. Top-k of fp32 logits x . W_r^T (router_w [E, H],
+ * rules as e4b_router_topk) into topk_idx / topk_w (fp32), then the layer of
+ * e4b_moe_forward with those picks (t->topk_idx / t->topk_w are ignored). In the
+ * decode regime (E4B_PATH_DECODE_LAYER) both run in one launch; otherwise it
+ * runs e4b_router_topk then e4b_moe_forward. Workspace:
+ * e4b_moe_decode_step_workspace_bytes. */
+E4B_API size_t e4b_moe_decode_step_workspace_bytes(const e4b_moe_desc* desc);
+E4B_API e4b_status e4b_moe_decode_step(const e4b_moe_desc* desc, const e4b_moe_tensors* t, const void* router_w,
+                               int router_w_dtype, int kind, int norm_topk_prob, int64_t* topk_idx, float* topk_w,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* No counterpart in the reference. Same layer as e4b_moe_forward for callers
  * that cannot allocate device memory (a host framework that owns all device
  * allocations, a plugin host that forbids cudaMalloc after start-up): the

@@ -107,3 +107,23 @@ def test_decode_layer_reports_errors_per_call(e4b):
         _fwd(e4b, mod, x, bad, w, E, I)
     assert ei.value.status == e4b._native.E4B_ERR_EXPERT_INDEX
     _fwd(e4b, mod, x, idx, w, E, I)  # a valid call afterwards reports nothing
+
+
+@pytest.mark.parametrize("E,H,I,k,T,kind,norm", [(64, 2048, 1024, 8, 1, 0, False), (64, 2048, 1024, 8, 3, 0, True),
+                                                 (128, 1024, 512, 4, 8, 1, False), (64, 2048, 1024, 8, 24, 0, False)])
+def test_decode_step_router_fused_equals_two_calls(e4b, E, H, I, k, T, kind, norm):
+    """Router + layer in one launch equals e4b_router_topk followed by e4b_moe_forward bit for bit
+    (T=24 is past the one-launch regime: the call falls back to those two)."""
+    mod, st = _layer(e4b, E, H, I, seed=T)
+    g = torch.Generator().manual_seed(100 + T)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    wr = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    out, w, idx = e4b.ops.moe_decode_step(x, wr, k, mod.gate_up_proj, mod.gate_up_absmax, mod.down_proj,
+                                          mod.down_absmax, E, I, kind=kind, norm_topk_prob=norm, check_errors=True)
+    w2, idx2 = e4b.ops.router_topk(x, wr, k, kind, norm)
+    assert torch.equal(idx, idx2) and torch.equal(w, w2)
+    ref = e4b.ops.moe_forward(x, idx2, w2, mod.gate_up_proj, mod.gate_up_absmax, mod.down_proj, mod.down_absmax, E, I,
+                              check_errors=True)
+    assert torch.equal(out, ref)
+    mx, mean = M.rel_errors(out.float().cpu(), M.fp32_oracle(st, x.cpu(), idx.cpu(), w.cpu()))
+    assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
