@@ -57,6 +57,16 @@ WORKLOADS = {
 }
 
 
+# DRAM bytes (read + write) per launch of the dominant kernel, from the ncu captures summarised
+# under profiles/ (same kernels and shapes); workloads without a capture report null.
+MEASURED_TRAFFIC = {
+    "olmoe-decode": {"bytes": 28697088 + 3328, "kernel": "nf4_decode_layer_kernel",
+                     "source": "profiles/nf4_decode_step__olmoe_decode.md"},
+    "qwen3-prefill-base": {"bytes": 364481536 + 40394240, "kernel": "nf4_umma_kernel<__half, 2> (gate_up)",
+                           "source": "profiles/nf4_umma__qwen3_prefill.md"},
+}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -307,7 +317,9 @@ def run_ours(args, wl, world, rank, local):
                            if one_launch else "nf4 grouped gate_up (SwiGLU fused)"),
                 "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": peak_kind, "unit": unit, "frac": round(achieved / peak, 4),
-                "traffic": None,
+                "traffic": (MEASURED_TRAFFIC[args.workload]["bytes"] if args.workload in MEASURED_TRAFFIC else None),
+                "traffic_source": (MEASURED_TRAFFIC[args.workload]["source"] if args.workload in MEASURED_TRAFFIC
+                                   else None),
                 "algorithmic_bytes_per_launch": int(gu_bytes + dn_bytes) if one_launch else int(gu_bytes),
                 "kernel_us": round(stage_avg_us["permute"] if one_launch else stage_avg_us["gate_up"], 3),
                 "down_kernel_us": round(stage_avg_us["down"], 3),
