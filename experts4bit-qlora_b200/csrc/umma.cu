@@ -4,26 +4,26 @@
 // (experts4bit_qlora/engines/fast.py:137-156) with the gate_up epilogue
 // (lora._epilogue, lora.py:102-128) and the LoRA delta (lora.py:251-256) fused.
 //
-// D[feature, token] = W_e[feature, :] . X[token, :] on the 5th-generation tensor
-// cores: the NF4 weight tile is the M = 128 operand, a tile of 128 tokens of
-// the same expert the N = 128 operand, fp32 accumulators live in tensor memory.
-// For SwiGLU the CTA tile is 128 output features: 128 gate rows and the 128
-// matching up rows accumulate into two TMEM accumulators, so silu(gate) * up
-// happens in registers in the epilogue.
+// D[token, feature] = X[token, :] . W_e[feature, :] on the 5th-generation tensor
+// cores: a tile of 128 tokens of one expert is the M = 128 operand, the tile's
+// decoded weight rows the N operand, fp32 accumulators live in tensor memory.
+// For SwiGLU the CTA tile is 128 output features: its 128 gate rows and the 128
+// matching up rows form one N = 256 operand, so one MMA per k-step covers both
+// and silu(gate) * up happens in the thread that owns the token.
 //
 // One persistent CTA per SM, 16 warps with fixed roles, 64-wide K chunks (one
 // quantization block per row per chunk) through three rings of their own depth --
-// packed weights 4 deep, activation tiles 5 deep, decoded A tiles 2 deep:
+// packed weights 4 deep, activation tiles 4 deep, decoded weight tiles 2 deep:
 //   warp 0      TMA: packed NF4 bytes of the tile's rows (2-D boxes {32 B, 128 rows});
 //   warp 1      TMA of the 128 token rows (fp16, expert-sorted), one box per chunk,
 //               landing in the 128-byte-swizzled K-major operand layout;
 //   warp 3      allocates TMEM, issues tcgen05.mma (one thread), commits;
 //   warps 4-11  NF4 -> fp16 decode: one thread per weight row, 32 pair-table
 //               lookups per chunk, scaled by the block's absmax, stored into the
-//               swizzled A operand;
+//               swizzled, K-major weight operand;
 //   warps 12-15 epilogue: tcgen05.ld of the finished accumulators (double
-//               buffered, so it overlaps the next tile's MMAs), activation
-//               scale, LoRA delta, activation, fp16 / bf16 stores.
+//               buffered, so it overlaps the next tile's MMAs), one token row per
+//               thread: activation scale, LoRA delta, activation, 16-byte stores.
 // Tiles are ordered (expert, feature tile, token tile) so CTAs that run at the
 // same time share the weight tile through L2. Every wait is bounded; a timeout
 // raises E4B_ERR_TIMEOUT and all roles run to the common exit (TMEM is freed).
@@ -55,9 +55,9 @@ namespace e4b {
 namespace {
 
 constexpr int kSW = 4;  // packed-weight ring depth (HBM latency)
-constexpr int kSB = 5;  // activation ring depth (L2 latency of the gathers)
+constexpr int kSB = 4;  // activation ring depth
 constexpr int kSA = 2;  // decoded-A ring depth (produced on chip)
-constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA N)
+constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA M)
 constexpr int kRows = 128;          // weight rows per group (UMMA M)
 constexpr int kKc = 64;             // K per chunk
 constexpr int kThreads = 512;
@@ -77,7 +77,7 @@ struct SmemT {
   static constexpr int b = a + kSA * 2 * kABytes;                 // [stage] 16 KB
   static constexpr int w = b + kSB * kBBytes;                     // [stage][group]
   static constexpr int epi = w + kSW * 2 * wbytes;                // epilogue staging
-  static constexpr int bars = epi + kTok * (1 + kEpiMaxRank) * 4;
+  static constexpr int bars = epi + 2 * kRows * kEpiMaxRank * 4;  // LoRA-B of the tile's features, fp32
   // full_w, w_empty [kSW]; full_b, b_empty [kSB]; a_ready, a_empty [kSA]; acc_full, acc_empty [2]
   static constexpr int nbars = 2 * kSW + 2 * kSB + 2 * kSA + 4;
   static constexpr int tmem_slot = bars + nbars * 8;
@@ -119,10 +119,9 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: fp16 (or bf16) A and B, fp32 D, both K-major, M = 128, N = kTok.
-__device__ __forceinline__ uint32_t idesc_f16(bool bf16) {
-  const uint32_t ab = bf16 ? (1u << 7) | (1u << 10) : 0u;  // A and B formats
-  return (1u << 4) | ab | ((uint32_t)(kTok >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+// kind::f16 instruction descriptor: fp16 A and B, fp32 D, both K-major, M = 128 tokens, N = n features.
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTok >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
@@ -283,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 3) {
     // ---------------- MMA issuer -------------------------------------------------------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(false);
+      const uint32_t idesc = idesc_f16(GROUPS * kRows);  // N = the tile's gate (+ up) rows
       int n = 0, it = 0;
       for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
         const int buf = it & 1;
@@ -294,15 +293,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!STAT_WAIT(2, wt.wait(&full_b[s], (n / kSB) & 1))) break;
           if (!STAT_WAIT(3, wt.wait(&a_ready[sa], (n / kSA) & 1))) break;
           tc_fence_after();
-          const uint32_t bsm = smem_u32(smem + Smem::b + s * kBBytes);
+          // D[token][feature] += X[token][k] . W[feature][k]: the 128 tokens are the M operand, the
+          // tile's decoded gate and up rows (adjacent 16 KB groups) one N = 256 operand
+          const uint32_t xsm = smem_u32(smem + Smem::b + s * kBBytes);
+          const uint32_t wsm = smem_u32(smem + Smem::a + (sa * 2) * kABytes);
 #pragma unroll
-          for (int h = 0; h < GROUPS; ++h) {
-            const uint32_t asm_ = smem_u32(smem + Smem::a + (sa * 2 + h) * kABytes);
-            const uint32_t d = tmem + buf * 256 + h * 128;
-#pragma unroll
-            for (int kk = 0; kk < kKc / 16; ++kk)
-              umma_f16(d, sw128_desc(asm_ + kk * 32), sw128_desc(bsm + kk * 32), idesc, (c | kk) != 0);
-          }
+          for (int kk = 0; kk < kKc / 16; ++kk)
+            umma_f16(tmem + buf * 256, sw128_desc(xsm + kk * 32), sw128_desc(wsm + kk * 32), idesc, (c | kk) != 0);
           umma_commit(&b_empty[s]);
           umma_commit(&a_empty[sa]);
         }
@@ -406,24 +403,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> global ---------------------------------
-    // Per tile, the 128 tokens' activation scales and LoRA-A vectors are staged once in shared
-    // memory (read back as broadcasts); each thread keeps its feature's LoRA-B rows in registers.
+    // TMEM lane = token, column = feature: a thread owns one token row of the tile. Its scale and
+    // LoRA-A vector live in registers; the tile's LoRA-B rows are staged once in shared memory
+    // (read back as broadcasts). Gate column j and up column 128 + j meet in one thread, and the
+    // row's 16-feature pieces leave as 16-byte stores.
     const int ew = warp - 12;          // TMEM lanes 32*ew .. 32*ew+31
-    const int r = ew * 32 + lane;      // row within the tile
-    float* s_sc = reinterpret_cast<float*>(smem + Smem::epi);
-    float* s_xa = s_sc + kTok;         // [kTok][rank]
+    const int r = ew * 32 + lane;      // token within the tile
+    float* s_lb = reinterpret_cast<float*>(smem + Smem::epi);  // [GROUPS * 128 features][rank]
     const int rank = g.rank;
     int it = 0;
     for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
       TileInfo ti;
       tile_info(s_ts, s_offs, g.E, nft, t, ti);
       const int buf = it & 1;
-      const int rowA = ti.ft * kRows + r;
-      const int rowB = (g.N / 2) + ti.ft * kRows + r;
-      const int feat = ti.ft * kRows + r;  // output column
-      float wsa = 1.f, wsb = 1.f;          // FP8: the tile's reference scales (gate, up)
+      float wsa = 1.f, wsb = 1.f;  // FP8: the tile's reference scales (gate rows, up rows)
       if (FMT == E4B_FMT_FP8_BLOCK128) {
         const int kbs = g.K / kFp8Block;
+        const int rowA = ti.ft * kRows, rowB = (g.N / 2) + ti.ft * kRows;
         const float* sa_ = g.absmax + ((int64_t)ti.e * (g.N / kFp8Block) + rowA / kFp8Block) * kbs;
         const float* sb_ = g.absmax + ((int64_t)ti.e * (g.N / kFp8Block) + rowB / kFp8Block) * kbs;
         float ma = 0.f, mb = 0.f;
@@ -434,61 +430,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         wsa = ma;
         wsb = mb;
       }
-      {  // token r of the tile: scale and LoRA-A vector
-        const int m = ti.tt * kTok + r;
-        float sc = 1.f;
-        if (m < ti.M) {
-          const int64_t srow = ti.row0 + m;
-          if (g.a_scale) sc = g.a_scale[g.a_rows ? g.a_rows[srow] : srow];
-          for (int j = 0; j < rank; ++j) s_xa[r * rank + j] = g.lora_xa[srow * rank + j];
-        }
-        s_sc[r] = sc;
-      }
-      float lb_a[kEpiMaxRank], lb_b[kEpiMaxRank];
+      const int m = ti.tt * kTok + r;
+      const bool valid = m < ti.M;
+      const int64_t srow = ti.row0 + (valid ? m : 0);
+      float sc = 1.f;
+      if (g.a_scale) sc = g.a_scale[g.a_rows ? g.a_rows[srow] : srow];
+      float xa[kEpiMaxRank];
 #pragma unroll
-      for (int j = 0; j < kEpiMaxRank; ++j) {
-        lb_a[j] = j < rank ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + rowA) * rank + j) : 0.f;
-        lb_b[j] = (GROUPS == 2 && j < rank) ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + rowB) * rank + j)
-                                            : 0.f;
+      for (int j = 0; j < kEpiMaxRank; ++j) xa[j] = (j < rank && valid) ? g.lora_xa[srow * rank + j] : 0.f;
+      if (rank) {  // LoRA-B rows of the tile's features: gate rows, then up rows
+        for (int i = r; i < GROUPS * kRows * rank; i += 128) {
+          const int f = i / rank, j = i - f * rank;
+          const int row = f < kRows ? ti.ft * kRows + f : (g.N / 2) + ti.ft * kRows + (f - kRows);
+          s_lb[i] = load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + row) * rank + j);
+        }
       }
       named_bar(1, 128);
       if (!(r == 0 ? STAT_WAIT(6, wt.wait(&acc_full[buf], (it >> 1) & 1)) : wt.wait(&acc_full[buf], (it >> 1) & 1))) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + buf * 256;
-      for (int c0 = 0; c0 < kTok; c0 += 16) {
+      OutT* orow = reinterpret_cast<OutT*>(g.out) + srow * g.Nout + ti.ft * kRows;
+      for (int c0 = 0; c0 < kRows; c0 += 16) {
         float va[16], vb[16];
         tmem_ld16(tbase + c0, va);
-        if (GROUPS == 2) tmem_ld16(tbase + 128 + c0, vb);
+        if (GROUPS == 2) tmem_ld16(tbase + kRows + c0, vb);
+        float o[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int m = ti.tt * kTok + c0 + i;
-          if (m >= ti.M) break;
-          const int64_t srow = ti.row0 + m;
-          const float sc = s_sc[c0 + i];
-          float xa = va[i] * (sc * wsa), xb = GROUPS == 2 ? vb[i] * (sc * wsb) : 0.f;
-          if (rank) {  // rank is a multiple of 4 here: 128-bit broadcast reads of the token's vector
-            const float4* la = reinterpret_cast<const float4*>(s_xa + (c0 + i) * rank);
+          const int f = c0 + i;
+          float ya = va[i] * (sc * wsa), yb = GROUPS == 2 ? vb[i] * (sc * wsb) : 0.f;
+          if (rank) {  // rank is a multiple of 4 here: 128-bit broadcast reads of the feature's row
+            const float4* la = reinterpret_cast<const float4*>(s_lb + f * rank);
+            const float4* lb = reinterpret_cast<const float4*>(s_lb + (kRows + f) * rank);
 #pragma unroll
             for (int j4 = 0; j4 < kEpiMaxRank / 4; ++j4) {
               if (4 * j4 >= rank) break;
               const float4 l = la[j4];
-              xa = fmaf(l.x, lb_a[4 * j4], fmaf(l.y, lb_a[4 * j4 + 1], fmaf(l.z, lb_a[4 * j4 + 2], fmaf(l.w, lb_a[4 * j4 + 3], xa))));
-              if (GROUPS == 2)
-                xb = fmaf(l.x, lb_b[4 * j4], fmaf(l.y, lb_b[4 * j4 + 1], fmaf(l.z, lb_b[4 * j4 + 2], fmaf(l.w, lb_b[4 * j4 + 3], xb))));
+              ya = fmaf(xa[4 * j4], l.x, fmaf(xa[4 * j4 + 1], l.y, fmaf(xa[4 * j4 + 2], l.z, fmaf(xa[4 * j4 + 3], l.w, ya))));
+              if (GROUPS == 2) {
+                const float4 u = lb[j4];
+                yb = fmaf(xa[4 * j4], u.x, fmaf(xa[4 * j4 + 1], u.y, fmaf(xa[4 * j4 + 2], u.z, fmaf(xa[4 * j4 + 3], u.w, yb))));
+              }
             }
           }
-          OutT* o = reinterpret_cast<OutT*>(g.out) + srow * g.Nout;
           if (g.epilogue == E4B_EPI_SWIGLU)
-            o[feat] = store_cast<OutT>(silu_f32(xa) * xb, g.err);
+            o[i] = silu_f32(ya) * yb;
           else if (g.epilogue == E4B_EPI_SILU)
-            o[feat] = store_cast<OutT>(silu_f32(xa), g.err);
+            o[i] = silu_f32(ya);
           else
-            o[feat] = store_cast<OutT>(xa, g.err);
+            o[i] = ya;
+        }
+        if (valid) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const OutT lo = store_cast<OutT>(o[2 * j], g.err), hi = store_cast<OutT>(o[2 * j + 1], g.err);
+            pk[j] = (uint32_t)(*reinterpret_cast<const uint16_t*>(&lo)) |
+                    ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
-      named_bar(1, 128);  // staging of the next tile may overwrite s_sc / s_xa
+      named_bar(1, 128);  // staging of the next tile may overwrite s_lb
     }
   }
 
