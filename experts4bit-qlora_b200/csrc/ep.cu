@@ -216,8 +216,10 @@ EpLayout ep_layout(const e4b_moe_desc& d, int P) {
   L.x_scale = take(R * 4);
   L.h = take(R * d.intermediate * 2);
   L.down_rows = take(R * d.hidden * 2);
-  L.xa_gu = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
-  L.xa_dn = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
+  // LoRA-A products: fp32 [R, rank] for the GEMV path, fp16 [R, 64] for the tensor-core path
+  const size_t xa_bytes = d.lora_rank > 0 ? (R * d.lora_rank * 4 > R * 128 ? R * d.lora_rank * 4 : R * 128) : 0;
+  L.xa_gu = take(xa_bytes);
+  L.xa_dn = take(xa_bytes);
   L.umma = take(umma_workspace_bytes((int)R, 1, d.num_experts, d.hidden, d.intermediate));
   L.total = o;
   return L;

@@ -80,6 +80,20 @@ __global__ void __launch_bounds__(128) lora_a_kernel(LoraAArgs g) {
   for (int h = 0; h < 2; ++h) {
     const int r = r0 + warp * 16 + gq + 8 * h;
     if (r >= rend) continue;
+    if (g.xa16) {  // fp16, no activation scale: the GEMM's epilogue applies it to the whole accumulator
+#pragma unroll
+      for (int n = 0; n < NR; ++n) {
+        const int j = n * 8 + 2 * q;
+        if (j < 16)
+          *reinterpret_cast<__half2*>(g.xa16 + (int64_t)r * 64 + j) =
+              __floats2half2_rn(j < g.rank ? g.scaling * acc[n][2 * h] : 0.f,
+                                j + 1 < g.rank ? g.scaling * acc[n][2 * h + 1] : 0.f);
+      }
+      if (NR == 1) {  // ranks <= 8: the second 8 of the 16 columns are zero
+        *reinterpret_cast<__half2*>(g.xa16 + (int64_t)r * 64 + 8 + 2 * q) = __floats2half2_rn(0.f, 0.f);
+      }
+      continue;
+    }
     float sc = g.scaling;
     if (g.a_scale) sc *= g.a_scale[g.a_rows ? g.a_rows[r] : r];
 #pragma unroll

@@ -13,7 +13,9 @@ struct LoraAArgs {
   const int32_t* tile_start; // [E+1] prefix of ceil(count / kLoraRows)
   int E, K, rank, lora_dtype;
   float scaling;
-  float* xa;                 // [R, rank] fp32 = scaling * (a_row . A[e]^T)
+  float* xa;                 // [R, rank] fp32 = scaling * (a_row . A[e]^T) (a_scale applied)
+  __half* xa16;              // instead of xa when set: [R, 64] fp16 = scaling * (a_row . A[e]^T) without
+                             // a_scale, ranks zero padded to 16 (the tensor-core GEMM's extra K step)
   int max_tiles;
 };
 constexpr int kLoraRows = 64;

@@ -44,8 +44,10 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   L.x_scale = take(R * 4);
   L.h = take(R * d.intermediate * 2);
   L.down_rows = take(R * d.hidden * 2);
-  L.xa_gu = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
-  L.xa_dn = take(d.lora_rank > 0 ? R * d.lora_rank * 4 : 0);
+  // LoRA-A products: fp32 [R, rank] for the GEMV path, fp16 [R, 64] for the tensor-core path
+  const size_t xa_bytes = d.lora_rank > 0 ? (R * d.lora_rank * 4 > R * 128 ? R * d.lora_rank * 4 : R * 128) : 0;
+  L.xa_gu = take(xa_bytes);
+  L.xa_dn = take(xa_bytes);
   L.umma = take(umma_workspace_bytes(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate));
   L.sync = take(decode_layer_sync_bytes(1024));
   L.total = o;
@@ -196,6 +198,7 @@ e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, co
     la.lora_dtype = d.lora_dtype;
     la.scaling = d.lora_scaling;
     la.xa = x.xa_gu;
+    if (x.use_umma) la.xa16 = reinterpret_cast<__half*>(x.xa_gu);
     la.max_tiles = lora_tiles;
     if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
   }
@@ -226,6 +229,7 @@ e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, co
   g.err = x.err;
   if (x.use_umma) {
     UmmaArgs u = umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R);
+    u.lora_xa16 = reinterpret_cast<const __half*>(g.lora_xa);  // fp16 [R, 64] in the tensor-core path
     st = launch_umma(u, d.act_dtype, s);
   } else {
     st = launch_gemv_auto(g, x.x_rows, x.max_rows_per_expert, s);
@@ -247,6 +251,7 @@ e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, co
     la.lora_dtype = d.lora_dtype;
     la.scaling = d.lora_scaling;
     la.xa = x.xa_dn;
+    if (x.use_umma) la.xa16 = reinterpret_cast<__half*>(x.xa_dn);
     la.max_tiles = lora_tiles;
     if ((st = launch_lora_a(la, s)) != E4B_OK) return st;
   }
@@ -269,6 +274,7 @@ e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, co
   g.max_tasks = max_active * g.tiles_per_expert;
   if (x.use_umma) {
     UmmaArgs u = umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R);
+    u.lora_xa16 = reinterpret_cast<const __half*>(g.lora_xa);  // fp16 [R, 64] in the tensor-core path
     st = launch_umma(u, d.act_dtype, s);
   } else {
     st = launch_gemv_auto(g, R, x.max_rows_per_expert, s);

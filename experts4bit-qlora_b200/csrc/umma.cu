@@ -23,7 +23,12 @@
 //               swizzled, K-major weight operand;
 //   warps 12-15 epilogue: tcgen05.ld of the finished accumulators (double
 //               buffered, so it overlaps the next tile's MMAs), one token row per
-//               thread: activation scale, LoRA delta, activation, 16-byte stores.
+//               thread: activation scale, activation, 16-byte stores.
+// With an adapter, each tile takes one more chunk: the activation warp loads the
+// tile's LoRA-A products (fp16, from the LoRA-A pre-pass), the decode warps write
+// the LoRA-B rows of the tile's features, and the MMA adds a K = 16 step, so the
+// delta enters the accumulator on the tensor cores (before the activation, as
+// lora.py:102-128 adds it).
 // Tiles are ordered (expert, feature tile, token tile) so CTAs that run at the
 // same time share the weight tile through L2. Every wait is bounded; a timeout
 // raises E4B_ERR_TIMEOUT and all roles run to the common exit (TMEM is freed).
@@ -55,7 +60,7 @@ namespace e4b {
 namespace {
 
 constexpr int kSW = 4;  // packed-weight ring depth (HBM latency)
-constexpr int kSB = 4;  // activation ring depth
+constexpr int kSB = 5;  // activation ring depth
 constexpr int kSA = 2;  // decoded-A ring depth (produced on chip)
 constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA M)
 constexpr int kRows = 128;          // weight rows per group (UMMA M)
@@ -77,7 +82,7 @@ struct SmemT {
   static constexpr int b = a + kSA * 2 * kABytes;                 // [stage] 16 KB
   static constexpr int w = b + kSB * kBBytes;                     // [stage][group]
   static constexpr int epi = w + kSW * 2 * wbytes;                // epilogue staging
-  static constexpr int bars = epi + 2 * kRows * kEpiMaxRank * 4;  // LoRA-B of the tile's features, fp32
+  static constexpr int bars = epi;
   // full_w, w_empty [kSW]; full_b, b_empty [kSB]; a_ready, a_empty [kSA]; acc_full, acc_empty [2]
   static constexpr int nbars = 2 * kSW + 2 * kSB + 2 * kSA + 4;
   static constexpr int tmem_slot = bars + nbars * 8;
@@ -174,7 +179,8 @@ __device__ __forceinline__ void tile_info(const int32_t* ts, const int32_t* offs
 
 template <typename OutT, int GROUPS, int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
-    nf4_umma_kernel(UmmaArgs u, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap) {
+    nf4_umma_kernel(UmmaArgs u, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap,
+                    const __grid_constant__ CUtensorMap lmap) {
   using Smem = SmemT<FMT>;
   constexpr int kWBytes = Smem::wbytes;
   extern __shared__ __align__(1024) char smem[];
@@ -269,11 +275,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
         TileInfo ti;
         tile_info(s_ts, s_offs, g.E, nft, t, ti);
-        for (int c = 0; c < kchunks; ++c, ++n) {
+        for (int c = 0; c < kchunks + (g.rank ? 1 : 0); ++c, ++n) {  // + the tile's LoRA-A chunk
           const int s = n % kSB;
           if (!STAT_WAIT(1, wt.wait(&b_empty[s], ((n / kSB) & 1) ^ 1))) break;
           mbar_arrive_expect_tx(&full_b[s], kBBytes);
-          tma_load_2d(smem + Smem::b + s * kBBytes, &bmap, c * kKc, ti.row0 + ti.tt * kTok, &full_b[s]);
+          if (c < kchunks)
+            tma_load_2d(smem + Smem::b + s * kBBytes, &bmap, c * kKc, ti.row0 + ti.tt * kTok, &full_b[s]);
+          else  // scaling * (x . A^T) of the tile's tokens, fp16 rows padded to 64 columns
+            tma_load_2d(smem + Smem::b + s * kBBytes, &lmap, 0, ti.row0 + ti.tt * kTok, &full_b[s]);
         }
       }
     }
@@ -288,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = it & 1;
         if (!STAT_WAIT(4, wt.wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1))) break;
         tc_fence_after();
-        for (int c = 0; c < kchunks; ++c, ++n) {
+        for (int c = 0; c < kchunks + (g.rank ? 1 : 0); ++c, ++n) {  // + the LoRA chunk (one K = 16 step)
           const int s = n % kSB, sa = n % kSA;
           if (!STAT_WAIT(2, wt.wait(&full_b[s], (n / kSB) & 1))) break;
           if (!STAT_WAIT(3, wt.wait(&a_ready[sa], (n / kSA) & 1))) break;
@@ -297,8 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // tile's decoded gate and up rows (adjacent 16 KB groups) one N = 256 operand
           const uint32_t xsm = smem_u32(smem + Smem::b + s * kBBytes);
           const uint32_t wsm = smem_u32(smem + Smem::a + (sa * 2) * kABytes);
-#pragma unroll
-          for (int kk = 0; kk < kKc / 16; ++kk)
+          const int ksteps = c < kchunks ? kKc / 16 : 1;
+          for (int kk = 0; kk < ksteps; ++kk)
             umma_f16(tmem + buf * 256, sw128_desc(xsm + kk * 32), sw128_desc(wsm + kk * 32), idesc, (c | kk) != 0);
           umma_commit(&b_empty[s]);
           umma_commit(&a_empty[sa]);
@@ -311,7 +320,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int d = tid - 128;          // 0..255
     const int h = d >> 7, r = d & 127;  // group, row within the tile
     const uint32_t lane4 = (uint32_t)lane << 2;
-    int n = 0;
+    int nw = 0, na = 0;  // packed-weight ring items, decoded-weight ring items (the LoRA chunk has no packed weights)
+    // LoRA chunk of a tile: this row's LoRA-B values (rank <= 16, fp16) as K elements 0..15 of the
+    // weight operand; the MMA issues a single K = 16 step for it, so the rest of the row is unused.
+    auto lora_chunk = [&](const TileInfo& ti, int row) -> bool {
+      const int sa = na % kSA;
+      if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) return false;
+      if (h < GROUPS) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          v[j] = j < g.rank ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + row) * g.rank + j) : 0.f;
+        char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
+        const int swz = (smem_u32(adst) >> 7) & 7;
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          *reinterpret_cast<uint4*>(adst + ((u ^ swz) << 4)) =
+              make_uint4(pack2<__half>(v[8 * u], v[8 * u + 1]), pack2<__half>(v[8 * u + 2], v[8 * u + 3]),
+                         pack2<__half>(v[8 * u + 4], v[8 * u + 5]), pack2<__half>(v[8 * u + 6], v[8 * u + 7]));
+      }
+      fence_proxy_async();
+      mbar_arrive(&a_ready[sa]);
+      ++na;
+      return true;
+    };
     for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
       TileInfo ti;
       tile_info(s_ts, s_offs, g.E, nft, t, ti);
@@ -327,10 +359,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kb = 0; kb < g.K / kFp8Block; ++kb) m = fmaxf(m, __ldg(sc + kb));
           inv_ref = m > 0.f ? 1.f / m : 0.f;
         }
-        for (int c = 0; c < kchunks; ++c, ++n) {
-          const int s = n % kSW, sa = n % kSA;
+        for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
+          const int s = nw % kSW, sa = na % kSA;
           const float scale = h < GROUPS ? __ldg(sc + (c >> 1)) * inv_ref : 0.f;
-          if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (n / kSW) & 1)) : wt.wait(&full_w[s], (n / kSW) & 1))) break;
+          if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
           uint4 p[4];
           const int rot = r & 3;  // rotated unit order spreads a quarter-warp over the banks
           if (h < GROUPS) {
@@ -340,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
           mbar_arrive(&w_empty[s]);
-          if (!wt.wait(&a_empty[sa], ((n / kSA) & 1) ^ 1)) break;
+          if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) break;
           if (h < GROUPS) {
             char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
             const int swz = (smem_u32(adst) >> 7) & 7;
@@ -361,15 +393,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async();
           mbar_arrive(&a_ready[sa]);
         }
+        if (g.rank && !wt.dead) lora_chunk(ti, row);
         continue;
       }
       const float* am = g.absmax + ((int64_t)ti.e * g.N + row) * (g.K / 64);
       float am_next = h < GROUPS ? __ldg(am) : 0.f;
-      for (int c = 0; c < kchunks; ++c, ++n) {
-        const int s = n % kSW, sa = n % kSA;
+      for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
+        const int s = nw % kSW, sa = na % kSA;
         const float a = am_next;
         if (h < GROUPS && c + 1 < kchunks) am_next = __ldg(am + c + 1);
-        if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (n / kSW) & 1)) : wt.wait(&full_w[s], (n / kSW) & 1))) break;
+        if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
         uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
         if (h < GROUPS) {
           const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
@@ -378,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
         mbar_arrive(&w_empty[s]);  // packed bytes are in registers: the slot can be refilled
-        if (!wt.wait(&a_empty[sa], ((n / kSA) & 1) ^ 1)) break;
+        if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) break;
         if (h < GROUPS) {
           const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
           const __half2 sc = __float2half2_rn(a);
@@ -400,17 +433,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async();
         mbar_arrive(&a_ready[sa]);
       }
+      if (g.rank && !wt.dead) lora_chunk(ti, row);
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> global ---------------------------------
-    // TMEM lane = token, column = feature: a thread owns one token row of the tile. Its scale and
-    // LoRA-A vector live in registers; the tile's LoRA-B rows are staged once in shared memory
-    // (read back as broadcasts). Gate column j and up column 128 + j meet in one thread, and the
-    // row's 16-feature pieces leave as 16-byte stores.
+    // TMEM lane = token, column = feature: a thread owns one token row of the tile (the LoRA
+    // delta is already in the accumulator: the MMA's extra K step). Gate column j and up column
+    // 128 + j meet in one thread, and the row's 16-feature pieces leave as 16-byte stores.
     const int ew = warp - 12;          // TMEM lanes 32*ew .. 32*ew+31
     const int r = ew * 32 + lane;      // token within the tile
-    float* s_lb = reinterpret_cast<float*>(smem + Smem::epi);  // [GROUPS * 128 features][rank]
-    const int rank = g.rank;
     int it = 0;
     for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
       TileInfo ti;
@@ -435,17 +466,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t srow = ti.row0 + (valid ? m : 0);
       float sc = 1.f;
       if (g.a_scale) sc = g.a_scale[g.a_rows ? g.a_rows[srow] : srow];
-      float xa[kEpiMaxRank];
-#pragma unroll
-      for (int j = 0; j < kEpiMaxRank; ++j) xa[j] = (j < rank && valid) ? g.lora_xa[srow * rank + j] : 0.f;
-      if (rank) {  // LoRA-B rows of the tile's features: gate rows, then up rows
-        for (int i = r; i < GROUPS * kRows * rank; i += 128) {
-          const int f = i / rank, j = i - f * rank;
-          const int row = f < kRows ? ti.ft * kRows + f : (g.N / 2) + ti.ft * kRows + (f - kRows);
-          s_lb[i] = load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + row) * rank + j);
-        }
-      }
-      named_bar(1, 128);
       if (!(r == 0 ? STAT_WAIT(6, wt.wait(&acc_full[buf], (it >> 1) & 1)) : wt.wait(&acc_full[buf], (it >> 1) & 1))) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + buf * 256;
@@ -457,22 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float o[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int f = c0 + i;
-          float ya = va[i] * (sc * wsa), yb = GROUPS == 2 ? vb[i] * (sc * wsb) : 0.f;
-          if (rank) {  // rank is a multiple of 4 here: 128-bit broadcast reads of the feature's row
-            const float4* la = reinterpret_cast<const float4*>(s_lb + f * rank);
-            const float4* lb = reinterpret_cast<const float4*>(s_lb + (kRows + f) * rank);
-#pragma unroll
-            for (int j4 = 0; j4 < kEpiMaxRank / 4; ++j4) {
-              if (4 * j4 >= rank) break;
-              const float4 l = la[j4];
-              ya = fmaf(xa[4 * j4], l.x, fmaf(xa[4 * j4 + 1], l.y, fmaf(xa[4 * j4 + 2], l.z, fmaf(xa[4 * j4 + 3], l.w, ya))));
-              if (GROUPS == 2) {
-                const float4 u = lb[j4];
-                yb = fmaf(xa[4 * j4], u.x, fmaf(xa[4 * j4 + 1], u.y, fmaf(xa[4 * j4 + 2], u.z, fmaf(xa[4 * j4 + 3], u.w, yb))));
-              }
-            }
-          }
+          const float ya = va[i] * (sc * wsa), yb = GROUPS == 2 ? vb[i] * (sc * wsb) : 0.f;
           if (g.epilogue == E4B_EPI_SWIGLU)
             o[i] = silu_f32(ya) * yb;
           else if (g.epilogue == E4B_EPI_SILU)
@@ -495,7 +500,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
-      named_bar(1, 128);  // staging of the next tile may overwrite s_lb
     }
   }
 
@@ -568,7 +572,16 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   const cuuint32_t bbox[2] = {kKc, kTok};
   if (!encode_tiled(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.a, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B))
     return E4B_ERR_CUDA;
-  nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kThreads, Smem::total, s>>>(u, wmap, bmap);
+  CUtensorMap lmap = bmap;  // LoRA-A products: fp16 rows of 64 (rank values, zero padded), same boxes
+  if (g.rank) {
+    if (!u.lora_xa16) return E4B_ERR_INVALID_ARG;
+    const cuuint64_t ldims[2] = {64, (cuuint64_t)u.x_rows};
+    const cuuint64_t lstr[1] = {128};
+    if (!encode_tiled(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, u.lora_xa16, ldims, lstr, bbox,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+      return E4B_ERR_CUDA;
+  }
+  nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kThreads, Smem::total, s>>>(u, wmap, bmap, lmap);
   return launch_status();
 }
 

@@ -13,6 +13,7 @@ struct UmmaArgs {
   int max_tiles;
   int x_rows;                      // rows of the activation matrix g.a
   void* scratch;
+  const __half* lora_xa16;         // [x_rows, 64] fp16: scaling * (x16_row . A^T), zero padded (rank > 0)
 };
 
 // Rows per expert (on average) from which the tensor-core path beats the GEMV, which
