@@ -153,6 +153,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// First weight row of group h of feature tile ft. SwiGLU: the tile's 128 gate rows and the
+// matching 128 up rows; otherwise (GROUPS == 2) 256 consecutive rows, (GROUPS == 1) 128.
+__device__ __forceinline__ int group_row0(const GemvArgs& g, int ft, int h, int groups) {
+  if (g.epilogue == E4B_EPI_SWIGLU) return h == 0 ? ft * 128 : (g.N / 2) + ft * 128;
+  return ft * 128 * groups + h * 128;
+}
+
 struct TileInfo {
   int e, row0, M, ft, tt;
 };
@@ -207,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_offs[i] = u.g.offsets[i];
   }
 
-  const int nft = GROUPS == 2 ? (g.N / 2) / kRows : g.N / kRows;  // feature tiles per expert
+  const int nft = g.N / (GROUPS * kRows);  // feature tiles per expert (SwiGLU: gate+up rows per tile)
   const int kchunks = g.K / kKc;
   const int total_tiles = u.tile_start[g.E] * nft;
   Waiter wt{false, g.err};
@@ -260,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full_w[s], GROUPS * kWBytes);
 #pragma unroll
           for (int h = 0; h < GROUPS; ++h) {
-            const int row = ti.e * g.N + (h == 0 ? ti.ft * kRows : (g.N / 2) + ti.ft * kRows);
+            const int row = ti.e * g.N + group_row0(g, ti.ft, h, GROUPS);
             tma_load_2d(smem + Smem::w + (s * 2 + h) * kWBytes, &wmap, c * Smem::wrow, row, &full_w[s]);
           }
         }
@@ -347,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
       TileInfo ti;
       tile_info(s_ts, s_offs, g.E, nft, t, ti);
-      const int row = h == 0 ? ti.ft * kRows + r : (g.N / 2) + ti.ft * kRows + r;
+      const int row = group_row0(g, ti.ft, h, GROUPS) + r;
       if (FMT == E4B_FMT_FP8_BLOCK128) {
         // e4m3 row -> fp16(fp32(w) * s_kb / s_ref): the tile's 128 rows share one scale per 128-wide
         // K block; s_ref (the largest over K) goes back in the epilogue. For e8m0 scales the ratio
@@ -450,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float wsa = 1.f, wsb = 1.f;  // FP8: the tile's reference scales (gate rows, up rows)
       if (FMT == E4B_FMT_FP8_BLOCK128) {
         const int kbs = g.K / kFp8Block;
-        const int rowA = ti.ft * kRows, rowB = (g.N / 2) + ti.ft * kRows;
+        const int rowA = group_row0(g, ti.ft, 0, GROUPS), rowB = group_row0(g, ti.ft, 1, GROUPS);
         const float* sa_ = g.absmax + ((int64_t)ti.e * (g.N / kFp8Block) + rowA / kFp8Block) * kbs;
         const float* sb_ = g.absmax + ((int64_t)ti.e * (g.N / kFp8Block) + rowB / kFp8Block) * kbs;
         float ma = 0.f, mb = 0.f;
@@ -469,33 +476,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(r == 0 ? STAT_WAIT(6, wt.wait(&acc_full[buf], (it >> 1) & 1)) : wt.wait(&acc_full[buf], (it >> 1) & 1))) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + buf * 256;
-      OutT* orow = reinterpret_cast<OutT*>(g.out) + srow * g.Nout + ti.ft * kRows;
-      for (int c0 = 0; c0 < kRows; c0 += 16) {
-        float va[16], vb[16];
-        tmem_ld16(tbase + c0, va);
-        if (GROUPS == 2) tmem_ld16(tbase + kRows + c0, vb);
-        float o[16];
+      const bool swiglu = g.epilogue == E4B_EPI_SWIGLU;
+      // SwiGLU: 128 outputs from gate (columns 0..127) and up (128..255); otherwise GROUPS x 128
+      // consecutive outputs, column c -> feature ft * GROUPS * 128 + c
+      const int halves = (GROUPS == 2 && !swiglu) ? 2 : 1;
+      OutT* orow = reinterpret_cast<OutT*>(g.out) + srow * g.Nout + ti.ft * kRows * (swiglu ? 1 : GROUPS);
+      for (int hh = 0; hh < halves; ++hh) {
+        const float sh = sc * (hh == 0 ? wsa : wsb);
+        for (int c0 = 0; c0 < kRows; c0 += 16) {
+          float va[16], vb[16];
+          tmem_ld16(tbase + hh * kRows + c0, va);
+          if (GROUPS == 2 && swiglu) tmem_ld16(tbase + kRows + c0, vb);
+          float o[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float ya = va[i] * (sc * wsa), yb = GROUPS == 2 ? vb[i] * (sc * wsb) : 0.f;
-          if (g.epilogue == E4B_EPI_SWIGLU)
-            o[i] = silu_f32(ya) * yb;
-          else if (g.epilogue == E4B_EPI_SILU)
-            o[i] = silu_f32(ya);
-          else
-            o[i] = ya;
-        }
-        if (valid) {
-          uint32_t pk[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const OutT lo = store_cast<OutT>(o[2 * j], g.err), hi = store_cast<OutT>(o[2 * j + 1], g.err);
-            pk[j] = (uint32_t)(*reinterpret_cast<const uint16_t*>(&lo)) |
-                    ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+          for (int i = 0; i < 16; ++i) {
+            const float ya = va[i] * sh;
+            if (GROUPS == 2 && swiglu)
+              o[i] = silu_f32(ya) * (vb[i] * (sc * wsb));
+            else if (g.epilogue == E4B_EPI_SILU)
+              o[i] = silu_f32(ya);
+            else
+              o[i] = ya;
           }
-          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          if (valid) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const OutT lo = store_cast<OutT>(o[2 * j], g.err), hi = store_cast<OutT>(o[2 * j + 1], g.err);
+              pk[j] = (uint32_t)(*reinterpret_cast<const uint16_t*>(&lo)) |
+                      ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(orow + hh * kRows + c0);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
         }
       }
       tc_fence_before();
@@ -553,7 +567,7 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
     configured |= bit;
   }
   const GemvArgs& g = u.g;
-  const int nft = GROUPS == 2 ? (g.N / 2) / kRows : g.N / kRows;
+  const int nft = g.N / (GROUPS * kRows);
   int grid = sm_count[dev & 63];
   const int bound = u.max_tiles * nft;
   if (bound < grid) grid = bound;
@@ -587,9 +601,12 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
 
 e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s, int weight_format) {
   (void)act_dtype;
-  const bool two = u.g.epilogue == E4B_EPI_SWIGLU;
+  // two 128-row groups per tile: gate + up for SwiGLU, else 256 consecutive features when they divide N
+  const bool two = u.g.epilogue == E4B_EPI_SWIGLU || u.g.N % (2 * kRows) == 0;
   if (weight_format == E4B_FMT_FP8_BLOCK128) {
-    if (u.g.K % kFp8Block || (two ? (u.g.N / 2) % kFp8Block : u.g.N % kFp8Block) || u.g.rank) return E4B_ERR_UNSUPPORTED;
+    if (u.g.K % kFp8Block || u.g.N % kFp8Block || (u.g.epilogue == E4B_EPI_SWIGLU && (u.g.N / 2) % kFp8Block) ||
+        u.g.rank)
+      return E4B_ERR_UNSUPPORTED;
     if (u.g.out_dtype == E4B_BF16)
       return two ? launch_groups<__nv_bfloat16, 2, E4B_FMT_FP8_BLOCK128>(u, s)
                  : launch_groups<__nv_bfloat16, 1, E4B_FMT_FP8_BLOCK128>(u, s);
