@@ -95,6 +95,9 @@ class ClockSampler:
                  "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            t0 = time.time()  # the timed region starts once the sampler reports (it takes a moment to start)
+            while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -102,6 +105,10 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def mark(self):
+        """Index of the next sample: summary(since=mark()) keeps only samples taken after it."""
+        return len(self.lines)
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -111,10 +118,10 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, since=0):
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in self.lines[since:]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -246,6 +253,7 @@ def run_ours(args, wl, world, rank, local):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if world == 1 else local) as clocks:
         torch.cuda.synchronize()
+        clock_mark = max(0, clocks.mark() - 1)  # the sample just before the region, and those during it
         start.record()
         for s in range(args.steps):
             graphs[s % pool].replay()
@@ -355,7 +363,7 @@ def run_ours(args, wl, world, rank, local):
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "path": "public API (route + enable_fast module call), eager"},
         "gpu_launches": launches_per_layer * Lc * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clocks.summary(since=clock_mark),
         "unique_experts_per_layer": round(mean_uniq, 2),
     }
     if rank == 0 and args.cpu_seconds > 0:
@@ -446,6 +454,7 @@ def run_ep(args, wl, world, rank, local):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
+        clock_mark = max(0, clocks.mark() - 1)  # the sample just before the region, and those during it
         start.record()
         for s in range(args.steps):
             step(s)
@@ -590,7 +599,7 @@ def run_ep(args, wl, world, rank, local):
                 "h2d_bytes_per_step": T * H * 2 * world, "d2h_bytes_per_step": T * H * 2 * world,
                 "path": "public API (route + ExpertParallelMoE), pinned host tokens in, outputs out"},
         "gpu_launches": 10 * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clocks.summary(since=clock_mark),
     }
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         result["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)

@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libe4b.so")
 
 E4B_OK = 0
 E4B_ERR_EXPERT_INDEX = 6
+E4B_ERR_TIMEOUT = 8
 BF16, F16, F32 = 0, 1, 2
 SOFTMAX_THEN_TOPK, TOPK_THEN_SOFTMAX = 0, 1
 EPI_NONE, EPI_SWIGLU, EPI_SILU = 0, 1, 2
@@ -38,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "e4b_moe_path", "e4b_set_decode_kernel",
     "e4b_moe_forward_static",
     "e4b_ep_dispatch_workspace_bytes", "e4b_ep_dispatch", "e4b_ep_experts_workspace_bytes", "e4b_ep_experts",
+    "e4b_selftest_wait_timeout",
     "e4b_read_device_error",
 )
 
@@ -99,6 +101,7 @@ def _declare(lib):
         "e4b_ep_dispatch": (I, [P, I, P, I, I, I, I, P, P, P, P, SZ, P]),
         "e4b_ep_experts_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc), I]),
         "e4b_ep_experts": (I, [ctypes.POINTER(MoeDesc), I, P, ctypes.POINTER(MoeTensors), P, SZ, P]),
+        "e4b_selftest_wait_timeout": (I, [P, SZ, P]),
         "e4b_read_device_error": (I, [P, P, ctypes.POINTER(I)]),
     }
     for name, (res, args) in sig.items():

@@ -11,8 +11,10 @@
 namespace e4b {
 
 namespace {
-constexpr int kKc = 64;
-constexpr int kPitch = kKc + 8;  // halves; 144-byte rows keep fragment reads conflict free
+// K chunk per shared-memory round: 256 for ranks <= 16 (fewer barriers and more loads in flight),
+// 64 above (the A tile grows with the rank); rows padded by 8 halves keep fragment reads
+// conflict free.
+template <int NR> struct LoraChunk { static constexpr int kc = NR <= 2 ? 256 : 64; };
 
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
@@ -25,6 +27,8 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
 
 template <int NR>  // n8 tiles of ranks: rank <= 8 * NR
 __global__ void __launch_bounds__(128) lora_a_kernel(LoraAArgs g) {
+  constexpr int kKc = LoraChunk<NR>::kc;
+  constexpr int kPitch = kKc + 8;
   __shared__ __align__(16) __half xs[kLoraRows][kPitch];
   __shared__ __align__(16) __half as[8 * NR][kPitch];
   const int t = blockIdx.x;
@@ -48,7 +52,7 @@ __global__ void __launch_bounds__(128) lora_a_kernel(LoraAArgs g) {
       const int rr = i / (kKc / 8), v = i % (kKc / 8);
       const int r = r0 + rr;
       uint4 val = make_uint4(0, 0, 0, 0);
-      if (r < rend) {
+      if (r < rend && k0 + v * 8 < g.K) {  // zero past K: a chunk may overrun a K that is a multiple of 64
         const int64_t src = g.a_rows ? (int64_t)g.a_rows[r] : (int64_t)r;
         val = *reinterpret_cast<const uint4*>(g.a + src * g.K + k0 + v * 8);
       }
@@ -56,7 +60,9 @@ __global__ void __launch_bounds__(128) lora_a_kernel(LoraAArgs g) {
     }
     for (int i = threadIdx.x; i < 8 * NR * kKc; i += blockDim.x) {
       const int j = i / kKc, kk = i % kKc;
-      const float v = j < g.rank ? load_as_f32(g.loraA, g.lora_dtype, ((int64_t)e * g.rank + j) * g.K + k0 + kk) : 0.f;
+      const float v = (j < g.rank && k0 + kk < g.K)
+                          ? load_as_f32(g.loraA, g.lora_dtype, ((int64_t)e * g.rank + j) * g.K + k0 + kk)
+                          : 0.f;
       as[j][kk] = __float2half_rn(v);
     }
     __syncthreads();
@@ -108,7 +114,7 @@ __global__ void __launch_bounds__(128) lora_a_kernel(LoraAArgs g) {
 
 e4b_status launch_lora_a(const LoraAArgs& g, cudaStream_t s) {
   if (g.max_tiles <= 0) return E4B_OK;
-  if (g.K % kKc) return E4B_ERR_UNSUPPORTED;
+  if (g.K % 64) return E4B_ERR_UNSUPPORTED;
   const int nr = (g.rank + 7) / 8;
   if (nr <= 1)
     lora_a_kernel<1><<<g.max_tiles, 128, 0, s>>>(g);

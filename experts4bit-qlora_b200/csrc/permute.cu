@@ -119,24 +119,36 @@ permute_kernel(PermuteArgs a) {
   const int seg = (n + 31) / 32;
   const int s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
   const unsigned lt = (1u << lane) - 1u;
-  // pass 1: per-warp counts
-  for (int base = s0; base < s1; base += 32) {
-    const int i = base + lane;
-    const bool valid = i < s1;
-    int e = 0;
-    if (valid) {
-      const int64_t raw = a.topk_idx[i];
-      e = (int)raw;
-      if (raw < 0 || raw >= E) {
-        raise_error(a.err, E4B_ERR_EXPERT_INDEX);
-        e = raw < 0 ? 0 : E - 1;
-      }
+  // The segment's first kCache x 32 entries are loaded once, all in flight, and kept in registers
+  // (fully unrolled steps, so the indices are static) for pass 3; longer segments reload the rest.
+  constexpr int kCache = 24;
+  int ec[kCache];
+  auto load_entry = [&](int i, bool flag) -> int {
+    const int64_t raw = a.topk_idx[i];
+    if (raw < 0 || raw >= E) {
+      if (flag) raise_error(a.err, E4B_ERR_EXPERT_INDEX);
+      return raw < 0 ? 0 : E - 1;
     }
+    return (int)raw;
+  };
+#pragma unroll
+  for (int it = 0; it < kCache; ++it) {
+    const int i = s0 + it * 32 + lane;
+    ec[it] = i < s1 ? load_entry(i, true) : 0;
+  }
+  auto count_step = [&](int base, int e) {  // pass 1 on the 32 entries at base
+    const bool valid = base + lane < s1;
     const unsigned act = __ballot_sync(0xffffffffu, valid);
     const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1) & act;
     if (valid && (peers & lt) == 0) wc[warp * E + e] += __popc(peers);
     __syncwarp();
-  }
+  };
+  // pass 1: per-warp counts
+#pragma unroll
+  for (int it = 0; it < kCache; ++it)
+    if (s0 + it * 32 < s1) count_step(s0 + it * 32, ec[it]);
+  for (int base = s0 + kCache * 32; base < s1; base += 32)
+    count_step(base, base + lane < s1 ? load_entry(base + lane, true) : 0);
   __syncthreads();
   // pass 2: counts, offsets, per-warp bases (one expert per thread, E <= 1024)
   {
@@ -172,14 +184,9 @@ permute_kernel(PermuteArgs a) {
   }
   __syncthreads();
   // pass 3: place every entry (stable)
-  for (int base = s0; base < s1; base += 32) {
+  auto place_step = [&](int base, int e) {
     const int i = base + lane;
     const bool valid = i < s1;
-    int e = 0;
-    if (valid) {
-      const int64_t raw = a.topk_idx[i];
-      e = raw < 0 ? 0 : (raw >= E ? E - 1 : (int)raw);
-    }
     const unsigned act = __ballot_sync(0xffffffffu, valid);
     const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1) & act;
     int pos = 0;
@@ -192,7 +199,12 @@ permute_kernel(PermuteArgs a) {
       if (a.inv) a.inv[i] = pos;
       if (a.sorted_token) a.sorted_token[pos] = i / a.k;
     }
-  }
+  };
+#pragma unroll
+  for (int it = 0; it < kCache; ++it)
+    if (s0 + it * 32 < s1) place_step(s0 + it * 32, ec[it]);
+  for (int base = s0 + kCache * 32; base < s1; base += 32)
+    place_step(base, base + lane < s1 ? load_entry(base + lane, false) : 0);
 }
 
 size_t permute_smem_bytes(int E) { return (size_t)32 * E * sizeof(int); }

@@ -261,6 +261,13 @@ E4B_API size_t e4b_ep_experts_workspace_bytes(const e4b_moe_desc* local, int wor
 E4B_API e4b_status e4b_ep_experts(const e4b_moe_desc* local, int world, const int32_t* recv_counts,
                           const e4b_moe_tensors* t, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Self-test of the failure path (no counterpart in the reference): one kernel
+ * waits, with the library's bounded wait, on an asynchronous copy that is never
+ * issued; the wait runs out, the kernel records E4B_ERR_TIMEOUT in the
+ * workspace's error word (read it with e4b_read_device_error) and returns. The
+ * second word of the workspace is 0 (timed out) or 1. Takes a few milliseconds. */
+E4B_API e4b_status e4b_selftest_wait_timeout(void* workspace, size_t workspace_bytes, void* stream);
+
 /* Reads (and clears) the device error word of a workspace used by the calls
  * above. Synchronises `stream`; for debugging and tests, not the hot path. */
 E4B_API e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out);

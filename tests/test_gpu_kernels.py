@@ -205,3 +205,22 @@ def test_gemv_rows_beyond_fp16_range_are_scaled_exactly(ops):
     for r in range(3):
         mx, mean = M.rel_errors(out[r], ref[r])
         assert mx <= 1e-2 and mean <= 2e-3, (r, mx, mean)
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(ops):
+    """A wait on a copy that never comes runs out after its iteration cap, reports
+    E4B_ERR_TIMEOUT through the error word, and the context keeps working."""
+    import importlib
+    import time
+    N = importlib.import_module("experts4bit-qlora_b200._native")
+    ws = torch.zeros(1024, dtype=torch.uint8, device=DEV)
+    t0 = time.perf_counter()
+    N.check(N.lib().e4b_selftest_wait_timeout(ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream),
+            "e4b_selftest_wait_timeout")
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 30.0
+    assert ws[4:8].view(torch.int32).item() == 0          # the wait did not complete
+    assert N.read_device_error(ws) == N.E4B_ERR_TIMEOUT
+    # the context is still usable
+    x = torch.randn(64, device=DEV)
+    assert torch.isfinite(x.sum()).item()
