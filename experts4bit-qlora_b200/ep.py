@@ -160,34 +160,112 @@ class ExpertParallelMoE:
 
     def exchange_counts(self, counts: torch.Tensor):
         """Counts all-to-all; returns (recv_counts [P, El] on the device, send splits, recv splits)."""
-        P, El = self.world, self.E // self.world
+        recv, splits = self._exchange_counts_mb([counts])
+        return recv[0], splits[0][0], splits[0][1]
+
+    def _exchange_counts_mb(self, counts_list):
+        """One all-to-all of the per-expert counts of every micro-batch and one host sync for all of
+        their row splits. Returns per micro-batch recv_counts [P, El] and (send, recv) splits."""
+        P, El, M = self.world, self.E // self.world, len(counts_list)
+        # [P, M, El]: the block for peer q holds each micro-batch's counts of q's experts
+        send = torch.stack([c.view(P, El) for c in counts_list], 1).contiguous()
         if P == 1:
-            recv = counts
+            recv = send
         else:
-            recv = torch.empty_like(counts)
-            dist.all_to_all_single(recv, counts, group=self.group)
-        host = torch.cat([counts, recv]).cpu()  # the one host sync: NCCL needs the row splits
-        send_splits = host[:self.E].view(P, El).sum(1).tolist()
-        recv_splits = host[self.E:].view(P, El).sum(1).tolist()
-        return recv.view(P, El), send_splits, recv_splits
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+        host = torch.cat([send.view(-1), recv.view(-1)]).cpu()  # the one host sync: NCCL needs the row splits
+        hs, hr = host[:P * M * El].view(P, M, El), host[P * M * El:].view(P, M, El)
+        out_counts = [recv[:, m] for m in range(M)]
+        splits = [(hs[:, m].sum(1).tolist(), hr[:, m].sum(1).tolist()) for m in range(M)]
+        return out_counts, splits
 
     def forward(self, hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor,
-                out_dtype=None) -> torch.Tensor:
+                out_dtype=None, micro_batches: int | None = None) -> torch.Tensor:
+        """The rank's [T, H] output. With P > 1 the shard runs as micro-batches (two when it has at
+        least 256 tokens): the row exchanges of one run on a communication stream while the experts
+        of the other compute, and all micro-batches share one count exchange and host sync."""
         T, k = top_k_index.shape
         idx = top_k_index.contiguous().long()
         w = top_k_weights.contiguous()
         if w.dtype not in (torch.bfloat16, torch.float16, torch.float32):
             w = w.float()
         hidden = hidden.contiguous()
-        send, counts, inv = self.stages.dispatch(hidden, idx)
-        recv_counts, send_splits, recv_splits = self.exchange_counts(counts)
+        od = out_dtype or hidden.dtype
+        M = micro_batches if micro_batches is not None else (2 if self.world > 1 and T >= 256 else 1)
+        M = max(1, min(M, T)) if T > 0 else 1
+        bounds = [T * m // M for m in range(M + 1)]
+        parts = [self.stages.dispatch(hidden[bounds[m]:bounds[m + 1]], idx[bounds[m]:bounds[m + 1]])
+                 for m in range(M)]
+        recv_counts, splits = self._exchange_counts_mb([p[1] for p in parts])
         if self.world == 1:  # one rank: the exchanges are identities
-            return self.stages.combine(self.stages.experts(send, recv_counts), inv, w, T, k, out_dtype or hidden.dtype)
-        rows = torch.empty(sum(recv_splits), self.H, dtype=send.dtype, device=send.device)
-        dist.all_to_all_single(rows, send, recv_splits, send_splits, group=self.group)
-        back = self.stages.experts(rows, recv_counts)
-        ret = torch.empty(T * k, self.H, dtype=back.dtype, device=back.device)
-        dist.all_to_all_single(ret, back, send_splits, recv_splits, group=self.group)
-        return self.stages.combine(ret, inv, w, T, k, out_dtype or hidden.dtype)
+            outs = [self.stages.combine(self.stages.experts(p[0], rc), p[2], w[bounds[m]:bounds[m + 1]],
+                                        bounds[m + 1] - bounds[m], k, od)
+                    for m, (p, rc) in enumerate(zip(parts, recv_counts))]
+            return outs[0] if M == 1 else torch.cat(outs)
+        cuda = hidden.is_cuda
+        main = torch.cuda.current_stream(hidden.device) if cuda else None
+        comm = self._comm_stream(hidden.device) if cuda else None
+
+        def on_comm(fn, *wait):
+            if not cuda:
+                return fn(), None
+            for ev in wait:
+                comm.wait_event(ev)
+            with torch.cuda.stream(comm):
+                r = fn()
+            done = torch.cuda.Event()
+            done.record(comm)
+            return r, done
+
+        def event_main():
+            if not cuda:
+                return None
+            ev = torch.cuda.Event()
+            ev.record(main)
+            return ev
+
+        ready = event_main()
+        rows, rows_done = [], []
+        for m, (send, _, _) in enumerate(parts):  # every micro-batch's rows go out at once
+            ss, rs = splits[m]
+            buf = torch.empty(sum(rs), self.H, dtype=send.dtype, device=send.device)
+            _, ev = on_comm(lambda buf=buf, send=send, ss=ss, rs=rs: dist.all_to_all_single(
+                buf, send, rs, ss, group=self.group), *([ready] if ready is not None else []))
+            if cuda:
+                send.record_stream(comm)
+                buf.record_stream(comm)
+            rows.append(buf)
+            rows_done.append(ev)
+        rets, rets_done = [], []
+        for m in range(M):
+            if cuda:
+                main.wait_event(rows_done[m])
+            back = self.stages.experts(rows[m], recv_counts[m])
+            ss, rs = splits[m]
+            n = bounds[m + 1] - bounds[m]
+            ret = torch.empty(n * k, self.H, dtype=back.dtype, device=back.device)
+            computed = event_main()
+            _, ev = on_comm(lambda ret=ret, back=back, ss=ss, rs=rs: dist.all_to_all_single(
+                ret, back, ss, rs, group=self.group), *([computed] if computed is not None else []))
+            if cuda:
+                back.record_stream(comm)
+                ret.record_stream(comm)
+            rets.append(ret)
+            rets_done.append(ev)
+        outs = []
+        for m in range(M):
+            if cuda:
+                main.wait_event(rets_done[m])
+            outs.append(self.stages.combine(rets[m], parts[m][2], w[bounds[m]:bounds[m + 1]],
+                                            bounds[m + 1] - bounds[m], k, od))
+        return outs[0] if M == 1 else torch.cat(outs)
+
+    def _comm_stream(self, device):
+        st = getattr(self, "_comm", None)
+        if st is None or st.device != device:
+            st = torch.cuda.Stream(device=device)
+            self._comm = st
+        return st
 
     __call__ = forward

@@ -36,9 +36,10 @@ def main():
     t1 = t0 + sizes[rank]
     layer = e4b.ExpertParallelMoE.from_module(mod)
     got = layer(x[t0:t1], idx[t0:t1], w[t0:t1])
+    got2 = layer(x[t0:t1], idx[t0:t1], w[t0:t1], micro_batches=3)  # comm stream overlapping compute
     ref = e4b.ops.moe_forward(x[t0:t1].contiguous(), idx[t0:t1].contiguous(), w[t0:t1].contiguous(),
                               mod.gate_up_proj.data, mod.gate_up_absmax, mod.down_proj.data, mod.down_absmax, E, I)
-    ok = torch.tensor([1 if torch.equal(got, ref) else 0], device="cuda")
+    ok = torch.tensor([1 if torch.equal(got, ref) and torch.equal(got2, ref) else 0], device="cuda")
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     if rank == 0 and int(ok.item()) == 1:
         print("EP_OK", flush=True)

@@ -81,7 +81,7 @@ def _case(E=8, H=128, I=64, k=2, T=24, seed=0):
     return st, x, idx, w
 
 
-def _worker(rank, world, port, shard_sizes, skew, q):
+def _worker(rank, world, port, shard_sizes, skew, q, micro_batches=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -100,7 +100,7 @@ def _worker(rank, world, port, shard_sizes, skew, q):
         layer = ep.ExpertParallelMoE(shard, E, st["H"], st["I"], True, stages=OracleStages(st_local, E, world))
         t0 = sum(shard_sizes[:rank])
         t1 = t0 + shard_sizes[rank]
-        out = layer(x[t0:t1], idx[t0:t1], w[t0:t1])
+        out = layer(x[t0:t1], idx[t0:t1], w[t0:t1], micro_batches=micro_batches)
         ref = M.fp32_oracle(st, x[t0:t1], idx[t0:t1], w[t0:t1])
         if t1 > t0:
             mx, mean = M.rel_errors(out.float(), ref)
@@ -111,12 +111,13 @@ def _worker(rank, world, port, shard_sizes, skew, q):
         dist.destroy_process_group()
 
 
-def _run(shard_sizes, skew=False):
+def _run(shard_sizes, skew=False, micro_batches=None):
     world = len(shard_sizes)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shard_sizes, skew, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shard_sizes, skew, q, micro_batches))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -135,4 +136,11 @@ def test_ep_world2_matches_oracle(shard_sizes):
 
 def test_ep_world2_all_picks_on_one_rank():
     for rank, shape, mx, mean in _run((12, 12), skew=True):
+        assert mx <= 1e-2 and mean <= 2e-3, (rank, mx, mean)
+
+
+def test_ep_world2_micro_batches():
+    """Three micro-batches per shard (one count exchange, per-micro-batch row exchanges)."""
+    for rank, shape, mx, mean in _run((9, 15), micro_batches=3):
+        assert shape == ((9, 15)[rank], 128)
         assert mx <= 1e-2 and mean <= 2e-3, (rank, mx, mean)
