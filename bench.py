@@ -418,7 +418,7 @@ def run_ep(args, wl, world, rank, local):
     E, H, I, k, Lc = wl["E"], wl["H"], wl["I"], wl["k"], wl["layers"]
     T = wl["T"] // world
     shards, routers = build_ep_layers(pkg, wl, dev, rank, world)
-    layers = [pkg.ExpertParallelMoE(sh, E, H, I, True) for sh in shards]
+    layers = [pkg.ExpertParallelMoE(sh, E, H, I, True, exchange=args.exchange, max_tokens=T) for sh in shards]
     pool = 4
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     X = torch.randn(pool, T, H, generator=g, device=dev).to(torch.bfloat16)
@@ -444,7 +444,7 @@ def run_ep(args, wl, world, rank, local):
         li = s % Lc
         x = X[s % pool] if x is None else x
         w, idx = route(s, x)
-        return layers[li](x, idx, w)
+        return layers[li](x, idx, w, micro_batches=args.micro_batches)
 
     for s in range(max(args.warmup, 3)):
         step(s)
@@ -499,8 +499,23 @@ def run_ep(args, wl, world, rank, local):
         torch.cuda.synchronize()
         return [ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(7)]
 
-    ph = [phases(s) for s in range(6)][2:]
-    phase_names = ["router", "dispatch", "count_exchange_sync", "rows_a2a", "experts", "return_a2a", "combine"]
+    def phases_peer(s):
+        li = s % Lc
+        x = X[s % pool]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[0].record()
+        w, idx = route(s, x)
+        layers[li]._forward_peer(x, idx.long(), w, x.dtype, phase_events=ev[1:])
+        torch.cuda.synchronize()
+        return [ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(4)]
+
+    peer = world > 1 and layers[0]._use_peer(X[0])
+    if peer:
+        ph = [phases_peer(s) for s in range(6)][2:]
+        phase_names = ["router", "dispatch_peer", "experts_peer", "combine_peer"]
+    else:
+        ph = [phases(s) for s in range(6)][2:]
+        phase_names = ["router", "dispatch", "count_exchange_sync", "rows_a2a", "experts", "return_a2a", "combine"]
     phase_us = {n: round(statistics.mean(v[i] for v in ph), 1) for i, n in enumerate(phase_names)}
 
     # per-stage device times of this rank's expert side, from the library's stage events
@@ -513,6 +528,18 @@ def run_ep(args, wl, world, rank, local):
         x = X[rep % pool]
         w, idx = route(rep, x)
         lay = layers[li]
+        ev = [_RawEvent(cudart) for _ in range(nst)]
+        if peer:
+            lay._forward_peer(x, idx.long(), w, x.dtype, stage_events=[e.cuda_event for e in ev])
+            torch.cuda.synchronize()
+            for si in range(nst - 1):
+                stage_ms[si].append(ev[si].elapsed_ms(ev[si + 1]))
+            cnt = torch.bincount(idx.reshape(-1).long(), minlength=E)  # rows each expert gets, all ranks
+            torch.distributed.all_reduce(cnt)
+            mine = cnt[rank * (E // world):(rank + 1) * (E // world)]
+            recv_rows.append(int(mine.sum().item()))
+            uniq.append(int((mine > 0).sum().item()))
+            continue
         send, counts, inv = lay.stages.dispatch(x, idx)
         rc, ss, rs = lay.exchange_counts(counts)
         rows = torch.empty(sum(rs), H, dtype=send.dtype, device=dev)
@@ -520,7 +547,6 @@ def run_ep(args, wl, world, rank, local):
             torch.distributed.all_to_all_single(rows, send, rs, ss)
         else:
             rows.copy_(send)
-        ev = [_RawEvent(cudart) for _ in range(nst)]
         lay.stages.experts(rows, rc, events=[e.cuda_event for e in ev])
         torch.cuda.synchronize()
         for si in range(nst - 1):
@@ -591,6 +617,9 @@ def run_ep(args, wl, world, rank, local):
         "config": {"workload": args.workload, "desc": wl["desc"], "tokens_per_layer": wl["T"],
                    "tokens_per_rank": T, "layers_cycled": Lc, "experts": E, "hidden": H, "intermediate": I,
                    "top_k": k, "parallelism": f"ep{world}" if world > 1 else "single-gpu",
+                   "micro_batches": args.micro_batches or "default",
+                   "exchange": ("peer-memory stores (CUDA IPC over NVLink)" if peer else
+                                "NCCL all-to-all" if world > 1 else "none (one rank)"),
                    "l2": "inputs larger than L2: each step reads a %.0f MB layer slice per rank" %
                          (layer_gb * 1e3 / world),
                    "timing": "CUDA events around K eager steps, max over ranks"},
@@ -745,6 +774,10 @@ def main():
                     help="auto: olmoe-decode on one GPU, mixtral-ep (expert parallel) on several")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="0 skips the CPU baseline")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling)")
+    ap.add_argument("--micro-batches", type=int, default=None,
+                    help="expert-parallel micro-batches per layer (default: the layer's own choice)")
+    ap.add_argument("--exchange", choices=["auto", "peer", "nccl"], default="auto",
+                    help="expert-parallel exchange: peer-memory stores or NCCL all-to-alls")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the public-API e2e leg (profiling)")
     args = ap.parse_args()
     if args.workload == "auto":

@@ -16,7 +16,7 @@ from . import _native, ep, ops  # noqa: F401
 from .experts import Experts4bit, ExpertsNbit, normalize_quant_type
 from .fast import disable_fast, enable_fast, fast_available
 from .fp8_experts import ExpertsFp8Blocks
-from .ep import ExpertParallelMoE, shard_experts
+from .ep import ExpertParallelMoE, PeerExchange, shard_experts
 from .lora import ExpertsLoRA
 from .router import route, TopKRouter
 
@@ -24,7 +24,7 @@ __version__ = "0.1.0"
 
 __all__ = [
     "Experts4bit", "ExpertsNbit", "ExpertsLoRA", "enable_fast", "disable_fast", "fast_available",
-    "normalize_quant_type", "route", "TopKRouter", "ops", "ExpertParallelMoE", "shard_experts", "ExpertsFp8Blocks",
+    "normalize_quant_type", "route", "TopKRouter", "ops", "ExpertParallelMoE", "PeerExchange", "shard_experts", "ExpertsFp8Blocks",
 ]
 
 _sys.modules.setdefault("experts4bit_qlora_b200", _sys.modules[__name__])

@@ -23,7 +23,7 @@ SOFTMAX_THEN_TOPK, TOPK_THEN_SOFTMAX = 0, 1
 EPI_NONE, EPI_SWIGLU, EPI_SILU = 0, 1, 2
 FMT_NF4, FMT_FP8_BLOCK128 = 0, 1
 PATH_STREAMING, PATH_TENSOR_CORE, PATH_DECODE_LAYER = 0, 1, 2
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # Every symbol include/e4b.h exports, in declaration order.
 EXPORTED_SYMBOLS = (
@@ -39,6 +39,9 @@ EXPORTED_SYMBOLS = (
     "e4b_moe_path", "e4b_set_decode_kernel",
     "e4b_moe_forward_static",
     "e4b_ep_dispatch_workspace_bytes", "e4b_ep_dispatch", "e4b_ep_experts_workspace_bytes", "e4b_ep_experts",
+    "e4b_ep_comm_bytes", "e4b_ipc_export", "e4b_ipc_open", "e4b_ipc_close",
+    "e4b_ep_dispatch_peer_workspace_bytes", "e4b_ep_dispatch_peer",
+    "e4b_ep_experts_peer_workspace_bytes", "e4b_ep_experts_peer", "e4b_ep_combine_peer",
     "e4b_selftest_wait_timeout",
     "e4b_read_device_error",
 )
@@ -67,6 +70,13 @@ class MoeTensors(ctypes.Structure):
         "gate_up_lora_A", "gate_up_lora_B", "down_lora_A", "down_lora_B", "out", "stage_events")]
 
 MOE_STAGE_EVENTS = 7
+IPC_HANDLE_BYTES = 64
+EP_MAX_PEERS = 16
+
+
+class EpPeerDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("world", "rank", "local_experts", "rows_per_rank", "hidden",
+                                            "act_dtype")] + [("epoch", ctypes.c_uint32), ("peers", ctypes.c_void_p)]
 
 
 _lib = None
@@ -101,6 +111,16 @@ def _declare(lib):
         "e4b_ep_dispatch": (I, [P, I, P, I, I, I, I, P, P, P, P, SZ, P]),
         "e4b_ep_experts_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc), I]),
         "e4b_ep_experts": (I, [ctypes.POINTER(MoeDesc), I, P, ctypes.POINTER(MoeTensors), P, SZ, P]),
+        "e4b_ep_comm_bytes": (SZ, [I, I, I, I]),
+        "e4b_ipc_export": (I, [P, P, ctypes.POINTER(SZ)]),
+        "e4b_ipc_open": (I, [P, SZ, ctypes.POINTER(P)]),
+        "e4b_ipc_close": (I, [P, SZ]),
+        "e4b_ep_dispatch_peer_workspace_bytes": (SZ, [I, I, I]),
+        "e4b_ep_dispatch_peer": (I, [ctypes.POINTER(EpPeerDesc), P, P, I, I, P, P, SZ, P]),
+        "e4b_ep_experts_peer_workspace_bytes": (SZ, [ctypes.POINTER(EpPeerDesc), ctypes.POINTER(MoeDesc)]),
+        "e4b_ep_experts_peer": (I, [ctypes.POINTER(EpPeerDesc), ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors),
+                                    P, SZ, P]),
+        "e4b_ep_combine_peer": (I, [ctypes.POINTER(EpPeerDesc), P, P, I, I, I, P, I, P]),
         "e4b_selftest_wait_timeout": (I, [P, SZ, P]),
         "e4b_read_device_error": (I, [P, P, ctypes.POINTER(I)]),
     }

@@ -312,7 +312,7 @@ extern "C" const char* e4b_status_string(e4b_status s) {
   return "unknown status";
 }
 
-extern "C" int e4b_abi_version(void) { return 2; }
+extern "C" int e4b_abi_version(void) { return 3; }
 
 extern "C" e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out) {
   if (!workspace || !error_out) return E4B_ERR_INVALID_ARG;

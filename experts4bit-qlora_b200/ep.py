@@ -16,12 +16,19 @@ tokens; the router runs on each rank's own tokens. One layer:
 5. ``e4b_combine``: weighted fixed-order k-sum. Every row sees the same kernels
    as on one GPU, so the output does not depend on P.
 
-The exchanges use ``torch.distributed`` (NCCL over NVLink on GPUs; gloo for the
-CPU tests, which swap the kernel stages for the oracle through ``stages``).
+On GPUs of one node the exchanges are the library's own peer-memory stores
+(``exchange="peer"``, the default there): every rank maps every other rank's
+exchange region (``PeerExchange``, CUDA IPC) once, dispatch stores rows and
+counts straight into the owners' regions, the expert side stores its down rows
+straight into the sources' regions, and flags order the steps -- no host sync,
+no all-to-all. Otherwise (``exchange="nccl"``, or gloo for the CPU tests, which
+swap the kernel stages for the oracle through ``stages``) the exchanges are
+``torch.distributed`` all-to-alls.
 """
 from __future__ import annotations
 
 import ctypes
+import socket
 from dataclasses import dataclass
 
 import torch
@@ -120,6 +127,31 @@ class NativeStages:
         del keep
         return out
 
+    def experts_peer(self, ex: "PeerExchange", expected_rows: int, events=None):
+        """The expert side over peer memory: waits for every source, runs the stages, returns the
+        down rows into the sources' regions (``e4b_ep_experts_peer``)."""
+        sh = self.shard
+        dev = ex.region.device
+        d = MoeDesc_from(sh.count, self.H, self.I, 1, expected_rows, self.has_gate, ex.act_dtype, torch.float32,
+                         torch.float16, sh.lora, sh.weight_format)
+        t = N.MoeTensors()
+        t.gate_up_packed, t.gate_up_absmax = sh.gate_up_packed.data_ptr(), sh.gate_up_absmax.data_ptr()
+        t.down_packed, t.down_absmax = sh.down_packed.data_ptr(), sh.down_absmax.data_ptr()
+        if sh.lora is not None:
+            t.gate_up_lora_A, t.gate_up_lora_B, t.down_lora_A, t.down_lora_B = (m.data_ptr() for m in sh.lora[:4])
+        keep = None
+        if events is not None:
+            keep = (ctypes.c_void_p * N.MOE_STAGE_EVENTS)(*events)
+            t.stage_events = ctypes.cast(keep, ctypes.c_void_p)
+        L = N.lib()
+        nbytes = L.e4b_ep_experts_peer_workspace_bytes(ctypes.byref(ex.desc), ctypes.byref(d))
+        if nbytes == 0:
+            raise ValueError("invalid expert-parallel geometry")
+        ws = N.workspaces.get(dev, nbytes, "ep_experts_peer")
+        N.check(L.e4b_ep_experts_peer(ctypes.byref(ex.desc), ctypes.byref(d), ctypes.byref(t), ws.data_ptr(),
+                                      ws.numel(), N.stream_handle(dev)), "e4b_ep_experts_peer")
+        del keep
+
     def combine(self, rows: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, T: int, k: int, out_dtype):
         out = torch.empty(T, self.H, dtype=out_dtype, device=rows.device)
         N.check(N.lib().e4b_combine(rows.data_ptr(), N.F16, inv.data_ptr(), w.data_ptr(), N.dtype_code(w.dtype), T, k,
@@ -128,15 +160,97 @@ class NativeStages:
         return out
 
 
+class PeerExchange:
+    """This rank's exchange region and every peer's, mapped here (include/e4b.h, peer section).
+
+    Built collectively once per (group, geometry): each rank allocates its region (zeroed),
+    exports a CUDA IPC handle, gathers everyone's, and opens the others. One exchange serves
+    every layer that all ranks call in the same order; ``next_epoch`` numbers the calls."""
+
+    def __init__(self, world: int, rank: int, local_experts: int, rows_per_rank: int, hidden: int,
+                 act_dtype: torch.dtype, device: torch.device, group=None, _regions=None):
+        L = N.lib()
+        nbytes = L.e4b_ep_comm_bytes(world, local_experts, rows_per_rank, hidden)
+        if nbytes == 0:
+            raise ValueError("invalid peer-exchange geometry (world <= %d, E <= 1024)" % N.EP_MAX_PEERS)
+        self.world, self.rank, self.act_dtype = world, rank, act_dtype
+        self.rows_per_rank = rows_per_rank
+        self._opened = []
+        if _regions is not None:  # one process holding every rank's region (single-GPU emulation)
+            self.region = _regions[rank]
+            ptrs = [r.data_ptr() for r in _regions]
+        else:
+            self.region = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+            torch.cuda.synchronize(device)
+            handle = (ctypes.c_char * N.IPC_HANDLE_BYTES)()
+            off = ctypes.c_size_t()
+            N.check(L.e4b_ipc_export(self.region.data_ptr(), handle, ctypes.byref(off)), "e4b_ipc_export")
+            info = [None] * world
+            dist.all_gather_object(info, (handle.raw, off.value), group=group)
+            ptrs = []
+            for q, (h, o) in enumerate(info):
+                if q == rank:
+                    ptrs.append(self.region.data_ptr())
+                    continue
+                p = ctypes.c_void_p()
+                N.check(L.e4b_ipc_open(h, o, ctypes.byref(p)), "e4b_ipc_open")
+                self._opened.append((p.value, o))
+                ptrs.append(p.value)
+            dist.barrier(group=group)  # every region mapped everywhere before the first store
+        self._ptrs = (ctypes.c_void_p * world)(*ptrs)
+        self.desc = N.EpPeerDesc(world, rank, local_experts, rows_per_rank, hidden, N.dtype_code(act_dtype), 0,
+                                 ctypes.cast(self._ptrs, ctypes.c_void_p))
+
+    @classmethod
+    def emulated(cls, world, local_experts, rows_per_rank, hidden, act_dtype, device):
+        """``world`` exchanges whose regions all live on one device (tests; launches in rank order)."""
+        nbytes = N.lib().e4b_ep_comm_bytes(world, local_experts, rows_per_rank, hidden)
+        regions = [torch.zeros(nbytes, dtype=torch.uint8, device=device) for _ in range(world)]
+        return [cls(world, r, local_experts, rows_per_rank, hidden, act_dtype, device, _regions=regions)
+                for r in range(world)]
+
+    def next_epoch(self):
+        e = self.desc.epoch + 1
+        self.desc.epoch = e if e < 2 ** 32 else 1
+        return self.desc
+
+    def close(self):
+        L = N.lib()
+        for p, o in self._opened:
+            L.e4b_ipc_close(p, o)
+        self._opened = []
+
+
+_exchanges = {}
+
+
+def _peer_exchange(group, world, rank, El, cap, H, dtype, device):
+    key = (id(group), world, rank, El, cap, H, dtype, device.index)
+    ex = _exchanges.get(key)
+    if ex is None:
+        ex = _exchanges[key] = PeerExchange(world, rank, El, cap, H, dtype, device, group)
+    return ex
+
+
 class ExpertParallelMoE:
     """One expert layer whose experts are sharded over ``group`` (default: WORLD).
 
     ``forward(hidden [T,H], top_k_index [T,k], top_k_weights [T,k])`` takes the
     rank's own token shard (global expert ids) and returns its ``[T,H]`` output,
-    equal to the single-GPU layer on those tokens."""
+    equal to the single-GPU layer on those tokens.
+
+    ``exchange``: "peer" (library stores into the other ranks' memory; GPUs of one node),
+    "nccl" (torch.distributed all-to-alls), or "auto" (peer when every rank is a GPU process on
+    this host, else nccl). ``max_tokens``: the most tokens any rank passes in one call, which
+    sizes the peer regions; by default the largest shard of the first call (a collective)."""
 
     def __init__(self, shard: ExpertShard, num_experts: int, hidden: int, intermediate: int, has_gate: bool = True,
-                 group=None, stages=None):
+                 group=None, stages=None, exchange: str = "auto", max_tokens: int | None = None):
+        if exchange not in ("auto", "peer", "nccl"):
+            raise ValueError("exchange must be 'auto', 'peer' or 'nccl'")
+        self.exchange = exchange
+        self.max_tokens = max_tokens
+        self._peer_ok = None
         self.group = group
         single = not (dist.is_available() and dist.is_initialized())
         self.world = 1 if single else dist.get_world_size(group)
@@ -150,13 +264,13 @@ class ExpertParallelMoE:
         self.stages = stages or NativeStages(shard, num_experts, hidden, intermediate, has_gate, self.world)
 
     @classmethod
-    def from_module(cls, mod, group=None, stages=None):
+    def from_module(cls, mod, group=None, stages=None, **kw):
         single = not (dist.is_available() and dist.is_initialized())
         world = 1 if single else dist.get_world_size(group)
         rank = 0 if single else dist.get_rank(group)
         base = mod.base if hasattr(mod, "base") else mod
         return cls(shard_experts(mod, rank, world), base.num_experts, base.hidden_dim, base.intermediate_dim,
-                   base.has_gate, group, stages)
+                   base.has_gate, group, stages, **kw)
 
     def exchange_counts(self, counts: torch.Tensor):
         """Counts all-to-all; returns (recv_counts [P, El] on the device, send splits, recv splits)."""
@@ -182,9 +296,10 @@ class ExpertParallelMoE:
 
     def forward(self, hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor,
                 out_dtype=None, micro_batches: int | None = None) -> torch.Tensor:
-        """The rank's [T, H] output. With P > 1 the shard runs as micro-batches (two when it has at
-        least 256 tokens): the row exchanges of one run on a communication stream while the experts
-        of the other compute, and all micro-batches share one count exchange and host sync."""
+        """The rank's [T, H] output. Over NCCL, ``micro_batches`` > 1 splits the shard: the row
+        exchanges of one micro-batch run on a communication stream while the experts of the other
+        compute, and all share one count exchange and host sync (default 1: on B200 the NCCL kernels
+        beside the persistent GEMM cost more than the overlap gains)."""
         T, k = top_k_index.shape
         idx = top_k_index.contiguous().long()
         w = top_k_weights.contiguous()
@@ -192,7 +307,9 @@ class ExpertParallelMoE:
             w = w.float()
         hidden = hidden.contiguous()
         od = out_dtype or hidden.dtype
-        M = micro_batches if micro_batches is not None else (2 if self.world > 1 and T >= 256 else 1)
+        if self._use_peer(hidden):
+            return self._forward_peer(hidden, idx, w, od)
+        M = micro_batches if micro_batches is not None else 1
         M = max(1, min(M, T)) if T > 0 else 1
         bounds = [T * m // M for m in range(M + 1)]
         parts = [self.stages.dispatch(hidden[bounds[m]:bounds[m + 1]], idx[bounds[m]:bounds[m + 1]])
@@ -260,6 +377,55 @@ class ExpertParallelMoE:
             outs.append(self.stages.combine(rets[m], parts[m][2], w[bounds[m]:bounds[m + 1]],
                                             bounds[m + 1] - bounds[m], k, od))
         return outs[0] if M == 1 else torch.cat(outs)
+
+    def _use_peer(self, hidden):
+        if self._peer_ok is None:
+            ok = (self.world > 1 and hidden.is_cuda and isinstance(self.stages, NativeStages)
+                  and self.exchange != "nccl")
+            if ok and self.exchange == "auto":  # every rank on this host (a collective, first call only)
+                names = [None] * self.world
+                dist.all_gather_object(names, socket.gethostname(), group=self.group)
+                ok = len(set(names)) == 1
+            if self.exchange == "peer" and not ok:
+                raise ValueError("exchange='peer' needs CUDA tensors, native stages and world > 1 on one host")
+            self._peer_ok = ok
+        return self._peer_ok
+
+    def _exchange_for(self, T, k, hidden):
+        if self.max_tokens is None:  # the largest shard of the first call, agreed by all ranks
+            t = torch.tensor([T], dtype=torch.int64, device=hidden.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            self.max_tokens = max(1, int(t.item()))
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the peer exchange")
+        return _peer_exchange(self.group, self.world, self.rank, self.E // self.world, self.max_tokens * k, self.H,
+                              hidden.dtype, hidden.device)
+
+    def _forward_peer(self, hidden, idx, w, od, ex=None, phase_events=None, stage_events=None):
+        """Peer-memory layer. ``phase_events``: 4 CUDA events recorded before dispatch, after dispatch,
+        after the expert side and after combine; ``stage_events``: passed to the expert side."""
+        T, k = idx.shape
+        rec = (lambda i: phase_events[i].record()) if phase_events else (lambda i: None)
+        ex = ex or self._exchange_for(T, k, hidden)
+        if hidden.dtype != ex.act_dtype:
+            raise ValueError("the peer exchange carries %s rows" % ex.act_dtype)
+        desc = ex.next_epoch()
+        dev = hidden.device
+        L = N.lib()
+        stream = N.stream_handle(dev)
+        inv = torch.empty(T * k, dtype=torch.int32, device=dev)
+        ws = N.workspaces.get(dev, L.e4b_ep_dispatch_peer_workspace_bytes(T, k, self.E), "ep_dispatch")
+        rec(0)
+        N.check(L.e4b_ep_dispatch_peer(ctypes.byref(desc), hidden.data_ptr(), idx.data_ptr(), T, k, inv.data_ptr(),
+                                       ws.data_ptr(), ws.numel(), stream), "e4b_ep_dispatch_peer")
+        rec(1)
+        self.stages.experts_peer(ex, T * k, events=stage_events)
+        rec(2)
+        out = torch.empty(T, self.H, dtype=od, device=dev)
+        N.check(L.e4b_ep_combine_peer(ctypes.byref(desc), inv.data_ptr(), w.data_ptr(), N.dtype_code(w.dtype), T, k,
+                                      out.data_ptr(), N.dtype_code(od), stream), "e4b_ep_combine_peer")
+        rec(3)
+        return out
 
     def _comm_stream(self, device):
         st = getattr(self, "_comm", None)

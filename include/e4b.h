@@ -261,6 +261,61 @@ E4B_API size_t e4b_ep_experts_workspace_bytes(const e4b_moe_desc* local, int wor
 E4B_API e4b_status e4b_ep_experts(const e4b_moe_desc* local, int world, const int32_t* recv_counts,
                           const e4b_moe_tensors* t, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Expert parallelism over peer memory (one node, NVLink) -------
+ * No counterpart in the reference (it has no distributed code). The same layer
+ * as the section above, with both exchanges done by the library's own kernels
+ * as stores into the other ranks' memory instead of the caller's all-to-alls,
+ * so nothing waits on the host: no count exchange, no host sync, fixed shapes.
+ *
+ * Every rank owns one exchange region of e4b_ep_comm_bytes() bytes, zeroed
+ * before first use, and maps every other rank's region (CUDA IPC:
+ * e4b_ipc_export on the owner, e4b_ipc_open on the others). The region holds
+ * an error word, arrival flags, the counts and rows each source sends
+ * (rows_per_rank rows per source, in the source's expert-major order) and the
+ * returned down rows of the rank's own picks. One layer, on every rank:
+ *   1. e4b_ep_dispatch_peer: permutation + row gather; rows, per-expert counts
+ *      and the send offset go straight into each owner's region, then the
+ *      arrival flag (release at system scope).
+ *   2. e4b_ep_experts_peer: waits (bounded) for every source's flag, plans the
+ *      received rows, runs the expert stages, and stores the fp16 down rows
+ *      into each source's region at that source's sorted position, then a flag.
+ *   3. e4b_ep_combine_peer: waits (bounded) for every owner's flag and combines.
+ * `epoch` numbers the layer calls on a region: 1, 2, ... in the same sequence on
+ * every rank; one region serves any number of layers called in the same order on
+ * every rank. Waits give up after a few seconds with E4B_ERR_TIMEOUT in the
+ * region's error word (read with e4b_read_device_error(region, ...)); the
+ * dispatch of each layer clears that word. */
+#define E4B_IPC_HANDLE_BYTES 64
+#define E4B_EP_MAX_PEERS 16
+typedef struct {
+  int world;            /* ranks in the group, 1..E4B_EP_MAX_PEERS */
+  int rank;             /* this rank */
+  int local_experts;    /* E / world */
+  int rows_per_rank;    /* capacity: the most T*k rows any rank dispatches in one layer */
+  int hidden;           /* H, a multiple of 64 */
+  int act_dtype;        /* dtype of the exchanged activation rows (E4B_BF16 or E4B_F16) */
+  uint32_t epoch;       /* this layer call's number on the region (>= 1) */
+  void* const* peers;   /* HOST array [world]: each rank's region as mapped here (peers[rank] = own) */
+} e4b_ep_peer_desc;
+
+E4B_API size_t e4b_ep_comm_bytes(int world, int local_experts, int rows_per_rank, int hidden);
+/* Device memory <-> IPC handle (E4B_IPC_HANDLE_BYTES bytes) plus the offset of ptr in its allocation. */
+E4B_API e4b_status e4b_ipc_export(const void* ptr, void* handle_host, size_t* offset_host);
+E4B_API e4b_status e4b_ipc_open(const void* handle_host, size_t offset, void** ptr_host);
+E4B_API e4b_status e4b_ipc_close(void* ptr, size_t offset);
+E4B_API size_t e4b_ep_dispatch_peer_workspace_bytes(int T, int k, int E);
+E4B_API e4b_status e4b_ep_dispatch_peer(const e4b_ep_peer_desc* pd, const void* hidden, const int64_t* topk_idx, int T,
+                                int k, int32_t* inv, void* workspace, size_t workspace_bytes, void* stream);
+/* local: the rank's experts as for e4b_ep_experts (top_k = 1, out_dtype = E4B_F16);
+ * local->tokens = the rows this rank expects to receive (T*k of its own shard is
+ * the usual figure), used only to choose the GEMM regime; t->hidden, t->out and
+ * topk_* are unused. */
+E4B_API size_t e4b_ep_experts_peer_workspace_bytes(const e4b_ep_peer_desc* pd, const e4b_moe_desc* local);
+E4B_API e4b_status e4b_ep_experts_peer(const e4b_ep_peer_desc* pd, const e4b_moe_desc* local,
+                               const e4b_moe_tensors* t, void* workspace, size_t workspace_bytes, void* stream);
+E4B_API e4b_status e4b_ep_combine_peer(const e4b_ep_peer_desc* pd, const int32_t* inv, const void* topk_w,
+                               int w_dtype, int T, int k, void* out, int out_dtype, void* stream);
+
 /* Self-test of the failure path (no counterpart in the reference): one kernel
  * waits, with the library's bounded wait, on an asynchronous copy that is never
  * issued; the wait runs out, the kernel records E4B_ERR_TIMEOUT in the

@@ -34,12 +34,40 @@ def main():
     sizes = [T // world + (1 if r < T % world else 0) for r in range(world)]
     t0 = sum(sizes[:rank])
     t1 = t0 + sizes[rank]
-    layer = e4b.ExpertParallelMoE.from_module(mod)
-    got = layer(x[t0:t1], idx[t0:t1], w[t0:t1])
-    got2 = layer(x[t0:t1], idx[t0:t1], w[t0:t1], micro_batches=3)  # comm stream overlapping compute
     ref = e4b.ops.moe_forward(x[t0:t1].contiguous(), idx[t0:t1].contiguous(), w[t0:t1].contiguous(),
                               mod.gate_up_proj.data, mod.gate_up_absmax, mod.down_proj.data, mod.down_absmax, E, I)
-    ok = torch.tensor([1 if torch.equal(got, ref) and torch.equal(got2, ref) else 0], device="cuda")
+    nccl = e4b.ExpertParallelMoE.from_module(mod, exchange="nccl")
+    got = nccl(x[t0:t1], idx[t0:t1], w[t0:t1])
+    got2 = nccl(x[t0:t1], idx[t0:t1], w[t0:t1], micro_batches=3)  # comm stream overlapping compute
+    good = torch.equal(got, ref) and torch.equal(got2, ref)
+    # peer-memory exchange (the default on one node): repeated calls on the same regions, then a
+    # ragged split (rank 0 with fewer tokens than max_tokens, the last rank with none)
+    peer = e4b.ExpertParallelMoE.from_module(mod, exchange="auto", max_tokens=T)
+    for _ in range(3):
+        good = good and torch.equal(peer(x[t0:t1], idx[t0:t1], w[t0:t1]), ref)
+    r0 = 0 if rank == 0 else T // 3 + (rank - 1) * (T - T // 3) // max(world - 1, 1)
+    r1 = T // 3 if rank == 0 else (T if rank == world - 1 else T // 3 + rank * (T - T // 3) // max(world - 1, 1))
+    if world > 1 and rank == world - 1:
+        r0 = r1 = T
+    if world > 1 and rank == world - 2:
+        r1 = T
+    ref2 = e4b.ops.moe_forward(x[r0:r1].contiguous(), idx[r0:r1].contiguous(), w[r0:r1].contiguous(),
+                               mod.gate_up_proj.data, mod.gate_up_absmax, mod.down_proj.data, mod.down_absmax, E, I) \
+        if r1 > r0 else torch.empty(0, H, dtype=x.dtype, device=x.device)
+    got3 = peer(x[r0:r1], idx[r0:r1], w[r0:r1])
+    if r1 > r0:
+        # each rank picks the GEMM regime from its own shard (T*k), so with ragged shards a
+        # rank may run the other regime than the single-GPU layer: layer tolerance, not bit-exact
+        d = (got3.float() - ref2.float()).abs()
+        rel_max = float(d.max() / ref2.float().abs().max().clamp_min(1e-6))
+        rel_mean = float(d.mean() / ref2.float().abs().mean().clamp_min(1e-6))
+        good = good and rel_max <= 1e-2 and rel_mean <= 2e-3
+    else:
+        good = good and got3.shape == (0, H)
+    if not good:
+        print(f"rank {rank}: mismatch", flush=True)
+    torch.cuda.synchronize()
+    ok = torch.tensor([1 if good else 0], device="cuda")
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     if rank == 0 and int(ok.item()) == 1:
         print("EP_OK", flush=True)

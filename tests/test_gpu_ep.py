@@ -165,3 +165,98 @@ def test_ep_nccl_two_ranks():
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "EP_OK" in r.stdout
+
+
+def emulate_ep_peer(e4b, mod, x, idx, w, P, shard_sizes=None, layers=1, exchanges=None):
+    """The peer-memory layer over P emulated ranks whose exchange regions all live on this GPU.
+
+    Launch order is rank by rank for each step (every dispatch, then every expert side, then every
+    combine), so each flag a kernel waits for was set by a kernel that already finished."""
+    import ctypes
+    from importlib import import_module
+    ep = import_module("experts4bit-qlora_b200.ep")
+    N = e4b._native
+    b = mod.base if hasattr(mod, "base") else mod
+    E, H, I = b.num_experts, b.hidden_dim, b.intermediate_dim
+    El, k, T = E // P, idx.shape[1], x.shape[0]
+    if shard_sizes is None:
+        shard_sizes = [T // P + (1 if r < T % P else 0) for r in range(P)]
+    bounds = [sum(shard_sizes[:r]) for r in range(P + 1)]
+    cap = max(max(shard_sizes), 1) * k
+    exs = exchanges or ep.PeerExchange.emulated(P, El, cap, H, x.dtype, x.device)
+    stages = [ep.NativeStages(ep.shard_experts(mod, r, P), E, H, I, True, P) for r in range(P)]
+    L = N.lib()
+    stream = N.stream_handle(x.device)
+    outs_all = []
+    for _ in range(layers):
+        descs = [ex.next_epoch() for ex in exs]
+        invs, dws = [], []
+        for r in range(P):
+            t0, t1 = bounds[r], bounds[r + 1]
+            inv = torch.empty((t1 - t0) * k, dtype=torch.int32, device=x.device)
+            ws = torch.empty(L.e4b_ep_dispatch_peer_workspace_bytes(t1 - t0, k, E), dtype=torch.uint8,
+                             device=x.device)
+            N.check(L.e4b_ep_dispatch_peer(ctypes.byref(descs[r]), x[t0:t1].data_ptr(), idx[t0:t1].data_ptr(),
+                                           t1 - t0, k, inv.data_ptr(), ws.data_ptr(), ws.numel(), stream),
+                    "dispatch_peer")
+            invs.append(inv)
+            dws.append(ws)
+        for r in range(P):
+            stages[r].experts_peer(exs[r], (bounds[r + 1] - bounds[r]) * k)
+        outs = []
+        for r in range(P):
+            t0, t1 = bounds[r], bounds[r + 1]
+            out = torch.empty(t1 - t0, H, dtype=x.dtype, device=x.device)
+            wr = w[t0:t1].contiguous()
+            N.check(L.e4b_ep_combine_peer(ctypes.byref(descs[r]), invs[r].data_ptr(), wr.data_ptr(),
+                                          N.dtype_code(wr.dtype), t1 - t0, k, out.data_ptr(),
+                                          N.dtype_code(x.dtype), stream), "combine_peer")
+            outs.append(out)
+        outs_all.append(torch.cat(outs))
+    torch.cuda.synchronize()
+    for ex in exs:
+        err = ctypes.c_int(-1)
+        N.check(L.e4b_read_device_error(ex.region.data_ptr(), stream, ctypes.byref(err)), "read_device_error")
+        assert err.value == 0, N.status_string(err.value)
+    return outs_all if layers > 1 else outs_all[0]
+
+
+@pytest.mark.parametrize("P", [1, 2, 4, 8])
+def test_ep_peer_prefill_bitexact_vs_single_gpu(e4b, P):
+    E, H, I, k, T = 8, 256, 256, 2, 384
+    mod = _layer(e4b, E, H, I)
+    x, idx, w = _inputs(E, H, T, k)
+    xc, ic, wc = x.cuda(), idx.cuda(), w.cuda()
+    single = e4b.ops.moe_forward(xc, ic, wc, mod.gate_up_proj.data, mod.gate_up_absmax, mod.down_proj.data,
+                                 mod.down_absmax, E, I, check_errors=True)
+    got = emulate_ep_peer(e4b, mod, xc, ic, wc, P)
+    assert torch.equal(got, single)
+
+
+def test_ep_peer_lora_ragged_and_repeated_layers(e4b):
+    """Ragged shards (one empty), LoRA, three layer calls on the same regions (epochs 1..3)."""
+    E, H, I, k, T = 8, 256, 128, 2, 200
+    mod = _layer(e4b, E, H, I, seed=3, lora_rank=16)
+    x, idx, w = _inputs(E, H, T, k, seed=4)
+    outs = emulate_ep_peer(e4b, mod, x.cuda(), idx.cuda(), w.cuda(), 4, shard_sizes=[0, 17, 150, 33], layers=3)
+    ref = M.fp32_oracle(_st(mod), x, idx, w, lora=_lora_dict(mod))
+    for got in outs:
+        assert torch.equal(got, outs[0])
+        mx, mean = M.rel_errors(got.float().cpu(), ref)
+        assert mx <= 1e-2 and mean <= 2e-3
+
+
+def test_ep_peer_matches_nccl_layout_path(e4b):
+    """Decode-sized shards and all picks on one rank's experts: same result as the all-to-all path's
+    kernels within the layer tolerance, and the fp32 oracle."""
+    E, H, I, k, T = 16, 512, 256, 4, 6
+    mod = _layer(e4b, E, H, I, seed=5)
+    x, idx, w = _inputs(E, H, T, k, seed=6)
+    for P in (2, 4):
+        got = emulate_ep_peer(e4b, mod, x.cuda(), idx.cuda(), w.cuda(), P)
+        mx, mean = M.rel_errors(got.float().cpu(), M.fp32_oracle(_st(mod), x, idx, w))
+        assert mx <= 1e-2 and mean <= 2e-3, (P, mx, mean)
+    idx2 = torch.stack([torch.full((T,), 14), torch.full((T,), 15), torch.full((T,), 13), torch.full((T,), 12)], 1)
+    got = emulate_ep_peer(e4b, mod, x.cuda(), idx2.cuda(), w.cuda(), 4)
+    mx, mean = M.rel_errors(got.float().cpu(), M.fp32_oracle(_st(mod), x, idx2, w))
+    assert mx <= 1e-2 and mean <= 2e-3
