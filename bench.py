@@ -248,10 +248,10 @@ def run_ours(args, wl, world, rank, local):
     for w in range(max(args.warmup, 3)):
         graphs[w % pool].replay()
     torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if world == 1 else local) as clocks:
+        if world > 1:  # after every rank's sampler is up, so all ranks enter the region together
+            torch.distributed.barrier()
         torch.cuda.synchronize()
         clock_mark = max(0, clocks.mark() - 1)  # the sample just before the region, and those during it
         start.record()
@@ -449,16 +449,44 @@ def run_ep(args, wl, world, rank, local):
     for s in range(max(args.warmup, 3)):
         step(s)
     torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    # Peer exchange (or one rank): nothing waits on the host, so each layer's step (route + layer)
+    # is captured once as a CUDA graph and replayed; the NCCL path needs a host sync per layer.
+    peer = world > 1 and layers[0]._use_peer(X[0])
+    graphs = None
+    if (peer or world == 1) and not args.eager:
+        for li in range(Lc):  # first calls (one-time set-up) outside the capture
+            step(li)
+        torch.cuda.synchronize()
+        graphs, mempool = [], None
+        for li in range(Lc):
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_, pool=mempool):
+                step(li)
+            mempool = g_.pool()
+            graphs.append(g_)
+        for li in range(Lc):
+            graphs[li].replay()
+        torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        if world > 1:  # after every rank's sampler is up, so all ranks enter the region together
+            torch.distributed.barrier()
         torch.cuda.synchronize()
         clock_mark = max(0, clocks.mark() - 1)  # the sample just before the region, and those during it
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)] if args.trace else None
+        host_t0 = time.perf_counter()
         start.record()
         for s in range(args.steps):
-            step(s)
+            if marks:
+                marks[s].record()
+            if graphs is not None:
+                graphs[s % Lc].replay()
+            else:
+                step(s)
+        if marks:
+            marks[-1].record()
         end.record()
+        host_ms = (time.perf_counter() - host_t0) * 1e3
         torch.cuda.synchronize()
     ms = start.elapsed_time(end)
     if world > 1:
@@ -466,6 +494,16 @@ def run_ep(args, wl, world, rank, local):
         torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
         ms = float(t_.item())
     value = args.steps * wl["T"] / (ms / 1e3)
+    trace = None
+    if marks:
+        per = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
+        by_layer = {}
+        for i, v in enumerate(per):
+            by_layer.setdefault(i % Lc, []).append(v)
+        trace = {"host_enqueue_ms_per_step": round(host_ms / args.steps, 4),
+                 "step_ms": {"min": round(min(per), 4), "median": round(statistics.median(per), 4),
+                             "max": round(max(per), 4)},
+                 "layer_ms": [round(statistics.mean(by_layer[li]), 3) for li in sorted(by_layer)]}
 
     # phase breakdown of one layer on every rank (events between phases; outside the timed region)
     def phases(s):
@@ -509,7 +547,6 @@ def run_ep(args, wl, world, rank, local):
         torch.cuda.synchronize()
         return [ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(4)]
 
-    peer = world > 1 and layers[0]._use_peer(X[0])
     if peer:
         ph = [phases_peer(s) for s in range(6)][2:]
         phase_names = ["router", "dispatch_peer", "experts_peer", "combine_peer"]
@@ -577,6 +614,8 @@ def run_ep(args, wl, world, rank, local):
                 "rows_received": int(Rr), "stage_us": {n: round(v, 1) for n, v in st_us.items()},
                 "nvlink_bytes_per_layer_per_rank": int(2 * T * k * H * 2 * (world - 1) / world),
                 "phase_us_rank%d" % rank: phase_us}
+    if trace:
+        roofline["trace_rank%d" % rank] = trace
 
     # e2e through the public API: pinned host tokens in, route + layer, output back to the host
     host_in = torch.empty(pool, T, H, dtype=torch.bfloat16, pin_memory=True)
@@ -618,6 +657,7 @@ def run_ep(args, wl, world, rank, local):
                    "tokens_per_rank": T, "layers_cycled": Lc, "experts": E, "hidden": H, "intermediate": I,
                    "top_k": k, "parallelism": f"ep{world}" if world > 1 else "single-gpu",
                    "micro_batches": args.micro_batches or "default",
+                   "launch": "one CUDA graph per layer step, replayed" if graphs is not None else "eager",
                    "exchange": ("peer-memory stores (CUDA IPC over NVLink)" if peer else
                                 "NCCL all-to-all" if world > 1 else "none (one rank)"),
                    "l2": "inputs larger than L2: each step reads a %.0f MB layer slice per rank" %
@@ -776,6 +816,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling)")
     ap.add_argument("--micro-batches", type=int, default=None,
                     help="expert-parallel micro-batches per layer (default: the layer's own choice)")
+    ap.add_argument("--trace", action="store_true", help="per-step device times inside the timed region")
+    ap.add_argument("--eager", action="store_true", help="expert-parallel steps without CUDA graphs")
     ap.add_argument("--exchange", choices=["auto", "peer", "nccl"], default="auto",
                     help="expert-parallel exchange: peer-memory stores or NCCL all-to-alls")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the public-API e2e leg (profiling)")

@@ -76,7 +76,7 @@ EP_MAX_PEERS = 16
 
 class EpPeerDesc(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("world", "rank", "local_experts", "rows_per_rank", "hidden",
-                                            "act_dtype")] + [("epoch", ctypes.c_uint32), ("peers", ctypes.c_void_p)]
+                                            "act_dtype")] + [("peers", ctypes.c_void_p)]
 
 
 _lib = None

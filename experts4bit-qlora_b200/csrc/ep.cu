@@ -314,7 +314,7 @@ constexpr int kPeerWaitPolls = 1 << 24;
 
 // Offsets inside one rank's exchange region (identical on every rank of a group).
 struct PeerLayout {
-  size_t recv_flag, ret_flag, done, counts, recv_off, recv_rows, ret_rows, total;
+  size_t recv_flag, ret_flag, done, calls, counts, recv_off, recv_rows, ret_rows, total;
 };
 
 PeerLayout peer_layout(int P, int El, int cap, int H) {
@@ -325,9 +325,10 @@ PeerLayout peer_layout(int P, int El, int cap, int H) {
     o = align_up(o + bytes, 256);
     return at;
   };
-  L.recv_flag = take((size_t)P * 4);            // [P] u32: epoch of source p's rows + counts
-  L.ret_flag = take((size_t)P * 4);             // [P] u32: epoch of owner q's returned rows
+  L.recv_flag = take((size_t)P * 4);            // [P] u32: call number of source p's latest rows + counts
+  L.ret_flag = take((size_t)P * 4);             // [P] u32: call number of owner q's latest returned rows
   L.done = take(2 * 4);                         // CTA-completion counters (dispatch, return)
+  L.calls = take(4);                            // layer calls completed on this region (combine advances it)
   L.counts = take((size_t)P * El * 4);          // [P, El] rows source p sent for each local expert
   L.recv_off = take((size_t)P * 4);             // [P] source p's sorted position of its first row here
   L.recv_rows = take((size_t)P * cap * H * 2);  // [P, cap, H] 16-bit activation rows, per source
@@ -339,7 +340,7 @@ PeerLayout peer_layout(int P, int El, int cap, int H) {
 bool peer_desc_ok(const e4b_ep_peer_desc& p) {
   if (p.world < 1 || p.world > kMaxPeers || p.rank < 0 || p.rank >= p.world) return false;
   if (p.local_experts <= 0 || (int64_t)p.local_experts * p.world > 1024) return false;
-  if (p.rows_per_rank <= 0 || p.hidden <= 0 || p.hidden % 64 || p.epoch == 0) return false;
+  if (p.rows_per_rank <= 0 || p.hidden <= 0 || p.hidden % 64) return false;
   if ((int64_t)p.rows_per_rank * p.world > (1 << 30)) return false;
   if (!is_act_dtype(p.act_dtype) || !p.peers) return false;
   for (int q = 0; q < p.world; ++q)
@@ -368,7 +369,7 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
 }
 
 // Called by every thread of every CTA after its peer stores: the last CTA to finish
-// publishes `epoch` in flag slot `slot` of every peer region (flags at `flag_off`).
+// publishes the call number `epoch` in flag slot `slot` of every peer region (flags at `flag_off`).
 __device__ void publish_when_last(unsigned* done, const PeerPtrs& peers, int P, size_t flag_off, int slot,
                                   unsigned epoch) {
   __shared__ int s_last;
@@ -402,7 +403,7 @@ struct PushArgs {
   PeerPtrs peers;
   PeerLayout L;
   int P, rank, El, cap, vec;  // vec = H / 8 (16-byte units per row)
-  unsigned epoch;
+  const unsigned* calls;      // this call publishes *calls + 1
   const uint4* hidden;
   const int32_t* sorted_token;
   const int32_t* offsets;     // [E+1] global expert segments of this rank's sorted picks
@@ -434,16 +435,18 @@ __global__ void __launch_bounds__(256) ep_push_rows_kernel(PushArgs a) {
     uint4* dst = reinterpret_cast<uint4*>(a.peers.base[q] + a.L.recv_rows) + ((int64_t)a.rank * a.cap + j) * a.vec;
     copy_row_warp(src, dst, a.vec, lane);
   }
-  publish_when_last(a.done, a.peers, a.P, a.L.recv_flag, a.rank, a.epoch);
+  publish_when_last(a.done, a.peers, a.P, a.L.recv_flag, a.rank, *a.calls + 1);
 }
 
-// One CTA: bounded wait until every source's flag reaches `epoch`, then copy n words
-// of the region (counts, offsets) into local storage; sources that never arrived count 0.
-__global__ void __launch_bounds__(256) ep_peer_wait_kernel(const unsigned* flags, int P, unsigned epoch,
+// One CTA: bounded wait until every source's flag reaches this call's number (*calls + 1),
+// then copy the region's counts and offsets into local storage; sources that never arrived
+// count 0. With `advance` (the last step of a call), thread 0 records the call as complete.
+__global__ void __launch_bounds__(256) ep_peer_wait_kernel(const unsigned* flags, int P, unsigned* calls, int advance,
                                                            const int* src, int El, int* dst, const int* off_src,
                                                            int* off_dst, int* err) {
   __shared__ int s_dead[kMaxPeers];
   const int tid = threadIdx.x;
+  const unsigned epoch = *calls + 1;
   if (tid < P) {
     int dead = 1;
     for (int i = 0; i < kPeerWaitPolls; ++i) {
@@ -457,6 +460,7 @@ __global__ void __launch_bounds__(256) ep_peer_wait_kernel(const unsigned* flags
     s_dead[tid] = dead;
   }
   __syncthreads();
+  if (advance && tid == 0) *calls = epoch;
   if (!dst) return;
   for (int i = tid; i < P * El; i += blockDim.x) {
     const int p = i / El;
@@ -480,7 +484,7 @@ struct ReturnArgs {
   PeerPtrs peers;
   PeerLayout L;
   int P, rank, cap, vec;
-  unsigned epoch;
+  const unsigned* calls;
   const uint4* down_rows;     // [R] expert-major fp16 rows
   const int32_t* map;         // expert-major row -> p * cap + j
   const int32_t* total;       // rows received
@@ -500,7 +504,7 @@ __global__ void __launch_bounds__(256) ep_return_rows_kernel(ReturnArgs a) {
     uint4* dst = reinterpret_cast<uint4*>(a.peers.base[p] + a.L.ret_rows) + (int64_t)(a.recv_off[p] + j) * a.vec;
     copy_row_warp(src, dst, a.vec, lane);
   }
-  publish_when_last(a.done, a.peers, a.P, a.L.ret_flag, a.rank, a.epoch);
+  publish_when_last(a.done, a.peers, a.P, a.L.ret_flag, a.rank, *a.calls + 1);
 }
 
 // What the expert side needs to read from and write to peer regions.
@@ -527,7 +531,8 @@ e4b_status ep_experts_run(const e4b_moe_desc& d, int world, const int32_t* recv_
   if (peer) {
     const char* own = peer->peers.base[peer->pd->rank];
     ep_peer_wait_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const unsigned*>(own + peer->L.recv_flag), world,
-                                          peer->pd->epoch, reinterpret_cast<const int*>(own + peer->L.counts), El,
+                                          reinterpret_cast<unsigned*>(const_cast<char*>(own) + peer->L.calls), 0,
+                                          reinterpret_cast<const int*>(own + peer->L.counts), El,
                                           peer->counts_local, reinterpret_cast<const int*>(own + peer->L.recv_off),
                                           peer->off_local, reinterpret_cast<int*>(peer->peers.base[peer->pd->rank]));
     if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
@@ -608,7 +613,7 @@ e4b_status ep_experts_run(const e4b_moe_desc& d, int world, const int32_t* recv_
     ra.rank = peer->pd->rank;
     ra.cap = peer->pd->rows_per_rank;
     ra.vec = H / 8;
-    ra.epoch = peer->pd->epoch;
+    ra.calls = reinterpret_cast<const unsigned*>(peer->peers.base[peer->pd->rank] + peer->L.calls);
     ra.down_rows = static_cast<const uint4*>(x.down_rows);
     ra.map = pl.map;
     ra.total = pl.offsets + El;
@@ -764,7 +769,7 @@ extern "C" e4b_status e4b_ep_dispatch_peer(const e4b_ep_peer_desc* pd, const voi
   a.El = El;
   a.cap = pd->rows_per_rank;
   a.vec = H / 8;
-  a.epoch = pd->epoch;
+  a.calls = reinterpret_cast<const unsigned*>(own + L.calls);
   a.hidden = static_cast<const uint4*>(hidden);
   a.sorted_token = sorted_token;
   a.offsets = offsets;
@@ -811,8 +816,8 @@ extern "C" e4b_status e4b_ep_combine_peer(const e4b_ep_peer_desc* pd, const int3
   cudaStream_t s = (cudaStream_t)stream;
   char* own = static_cast<char*>(pd->peers[pd->rank]);
   const PeerLayout L = peer_layout(pd->world, pd->local_experts, pd->rows_per_rank, pd->hidden);
-  ep_peer_wait_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const unsigned*>(own + L.ret_flag), pd->world, pd->epoch,
-                                        nullptr, pd->local_experts, nullptr, nullptr, nullptr,
+  ep_peer_wait_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const unsigned*>(own + L.ret_flag), pd->world,
+                                        reinterpret_cast<unsigned*>(own + L.calls), 1, nullptr, pd->local_experts, nullptr, nullptr, nullptr,
                                         reinterpret_cast<int*>(own));
   if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
   return e4b_combine(own + L.ret_rows, E4B_F16, inv, topk_w, w_dtype, T, k, pd->hidden, out, out_dtype, stream);

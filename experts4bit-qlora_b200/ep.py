@@ -165,7 +165,8 @@ class PeerExchange:
 
     Built collectively once per (group, geometry): each rank allocates its region (zeroed),
     exports a CUDA IPC handle, gathers everyone's, and opens the others. One exchange serves
-    every layer that all ranks call in the same order; ``next_epoch`` numbers the calls."""
+    every layer that all ranks call in the same order; the region counts the calls on the
+    device, so a layer call can be captured in a CUDA graph and replayed."""
 
     def __init__(self, world: int, rank: int, local_experts: int, rows_per_rank: int, hidden: int,
                  act_dtype: torch.dtype, device: torch.device, group=None, _regions=None):
@@ -198,7 +199,7 @@ class PeerExchange:
                 ptrs.append(p.value)
             dist.barrier(group=group)  # every region mapped everywhere before the first store
         self._ptrs = (ctypes.c_void_p * world)(*ptrs)
-        self.desc = N.EpPeerDesc(world, rank, local_experts, rows_per_rank, hidden, N.dtype_code(act_dtype), 0,
+        self.desc = N.EpPeerDesc(world, rank, local_experts, rows_per_rank, hidden, N.dtype_code(act_dtype),
                                  ctypes.cast(self._ptrs, ctypes.c_void_p))
 
     @classmethod
@@ -209,11 +210,6 @@ class PeerExchange:
         return [cls(world, r, local_experts, rows_per_rank, hidden, act_dtype, device, _regions=regions)
                 for r in range(world)]
 
-    def next_epoch(self):
-        e = self.desc.epoch + 1
-        self.desc.epoch = e if e < 2 ** 32 else 1
-        return self.desc
-
     def close(self):
         L = N.lib()
         for p, o in self._opened:
@@ -222,6 +218,7 @@ class PeerExchange:
 
 
 _exchanges = {}
+_one_host = {}
 
 
 def _peer_exchange(group, world, rank, El, cap, H, dtype, device):
@@ -307,6 +304,13 @@ class ExpertParallelMoE:
             w = w.float()
         hidden = hidden.contiguous()
         od = out_dtype or hidden.dtype
+        if self.world == 1 and hidden.is_cuda and isinstance(self.stages, NativeStages):
+            # one rank holds every expert: the single-GPU fused layer (the same kernels on the
+            # same rows, so the same result), with no exchange and no host sync
+            sh = self.shard
+            from .ops import moe_forward
+            return moe_forward(hidden, idx, w, sh.gate_up_packed, sh.gate_up_absmax, sh.down_packed, sh.down_absmax,
+                               self.E, self.I, self.stages.has_gate, od, sh.lora, weight_format=sh.weight_format)
         if self._use_peer(hidden):
             return self._forward_peer(hidden, idx, w, od)
         M = micro_batches if micro_batches is not None else 1
@@ -382,10 +386,13 @@ class ExpertParallelMoE:
         if self._peer_ok is None:
             ok = (self.world > 1 and hidden.is_cuda and isinstance(self.stages, NativeStages)
                   and self.exchange != "nccl")
-            if ok and self.exchange == "auto":  # every rank on this host (a collective, first call only)
-                names = [None] * self.world
-                dist.all_gather_object(names, socket.gethostname(), group=self.group)
-                ok = len(set(names)) == 1
+            if ok and self.exchange == "auto":  # every rank on this host (a collective, once per group)
+                key = id(self.group)
+                if key not in _one_host:
+                    names = [None] * self.world
+                    dist.all_gather_object(names, socket.gethostname(), group=self.group)
+                    _one_host[key] = len(set(names)) == 1
+                ok = _one_host[key]
             if self.exchange == "peer" and not ok:
                 raise ValueError("exchange='peer' needs CUDA tensors, native stages and world > 1 on one host")
             self._peer_ok = ok
@@ -409,7 +416,7 @@ class ExpertParallelMoE:
         ex = ex or self._exchange_for(T, k, hidden)
         if hidden.dtype != ex.act_dtype:
             raise ValueError("the peer exchange carries %s rows" % ex.act_dtype)
-        desc = ex.next_epoch()
+        desc = ex.desc
         dev = hidden.device
         L = N.lib()
         stream = N.stream_handle(dev)

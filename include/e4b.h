@@ -280,11 +280,13 @@ E4B_API e4b_status e4b_ep_experts(const e4b_moe_desc* local, int world, const in
  *      received rows, runs the expert stages, and stores the fp16 down rows
  *      into each source's region at that source's sorted position, then a flag.
  *   3. e4b_ep_combine_peer: waits (bounded) for every owner's flag and combines.
- * `epoch` numbers the layer calls on a region: 1, 2, ... in the same sequence on
- * every rank; one region serves any number of layers called in the same order on
- * every rank. Waits give up after a few seconds with E4B_ERR_TIMEOUT in the
- * region's error word (read with e4b_read_device_error(region, ...)); the
- * dispatch of each layer clears that word. */
+ * The region counts the layer calls it has completed (advanced on the device by
+ * e4b_ep_combine_peer), and each step waits for its peers' flags to reach the
+ * current call's number, so nothing changes on the host between calls and a
+ * layer call can be captured in a CUDA graph and replayed. One region serves any
+ * number of layers called in the same order on every rank. Waits give up after a
+ * few seconds with E4B_ERR_TIMEOUT in the region's error word (read with
+ * e4b_read_device_error(region, ...)); the dispatch of each layer clears that word. */
 #define E4B_IPC_HANDLE_BYTES 64
 #define E4B_EP_MAX_PEERS 16
 typedef struct {
@@ -294,7 +296,6 @@ typedef struct {
   int rows_per_rank;    /* capacity: the most T*k rows any rank dispatches in one layer */
   int hidden;           /* H, a multiple of 64 */
   int act_dtype;        /* dtype of the exchanged activation rows (E4B_BF16 or E4B_F16) */
-  uint32_t epoch;       /* this layer call's number on the region (>= 1) */
   void* const* peers;   /* HOST array [world]: each rank's region as mapped here (peers[rank] = own) */
 } e4b_ep_peer_desc;
 

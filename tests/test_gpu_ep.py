@@ -189,7 +189,7 @@ def emulate_ep_peer(e4b, mod, x, idx, w, P, shard_sizes=None, layers=1, exchange
     stream = N.stream_handle(x.device)
     outs_all = []
     for _ in range(layers):
-        descs = [ex.next_epoch() for ex in exs]
+        descs = [ex.desc for ex in exs]
         invs, dws = [], []
         for r in range(P):
             t0, t1 = bounds[r], bounds[r + 1]
@@ -234,7 +234,7 @@ def test_ep_peer_prefill_bitexact_vs_single_gpu(e4b, P):
 
 
 def test_ep_peer_lora_ragged_and_repeated_layers(e4b):
-    """Ragged shards (one empty), LoRA, three layer calls on the same regions (epochs 1..3)."""
+    """Ragged shards (one empty), LoRA, three layer calls on the same regions (call numbers 1..3)."""
     E, H, I, k, T = 8, 256, 128, 2, 200
     mod = _layer(e4b, E, H, I, seed=3, lora_rank=16)
     x, idx, w = _inputs(E, H, T, k, seed=4)
