@@ -3,7 +3,7 @@
 Drop-in names (same constructors, state_dict layout and patch semantics as the
 reference's ``experts4bit_qlora`` package): ``ExpertsNbit``, ``Experts4bit``,
 ``ExpertsLoRA``, ``enable_fast``, ``disable_fast``, ``fast_available``,
-``normalize_quant_type``. The hot path is libe4b.so (hand-written sm_100a CUDA
+``enable_fast_train``, ``disable_fast_train``, ``normalize_quant_type``. The hot path is libe4b.so (hand-written sm_100a CUDA
 behind the C ABI in include/e4b.h), reached through ctypes.
 
 The package directory is named ``experts4bit-qlora_b200``; import it with
@@ -18,13 +18,14 @@ from .fast import disable_fast, enable_fast, fast_available
 from .fp8_experts import ExpertsFp8Blocks
 from .ep import ExpertParallelMoE, PeerExchange, shard_experts
 from .lora import ExpertsLoRA
+from .train import disable_fast_train, enable_fast_train
 from .router import route, TopKRouter
 
 __version__ = "0.1.0"
 
 __all__ = [
     "Experts4bit", "ExpertsNbit", "ExpertsLoRA", "enable_fast", "disable_fast", "fast_available",
-    "normalize_quant_type", "route", "TopKRouter", "ops", "ExpertParallelMoE", "PeerExchange", "shard_experts", "ExpertsFp8Blocks",
+    "normalize_quant_type", "enable_fast_train", "disable_fast_train", "route", "TopKRouter", "ops", "ExpertParallelMoE", "PeerExchange", "shard_experts", "ExpertsFp8Blocks",
 ]
 
 _sys.modules.setdefault("experts4bit_qlora_b200", _sys.modules[__name__])

@@ -6,6 +6,8 @@
 //   LoRA delta and SwiGLU fused -> [LoRA-A of h] -> grouped down GEMM with its
 //   LoRA delta -> weighted fixed-order combine.
 // All launches are stream-ordered on the caller's stream; nothing is allocated.
+#include <cub/block/block_scan.cuh>
+
 #include "common.cuh"
 #include "convert.cuh"
 #include "gemv.cuh"
@@ -106,6 +108,19 @@ e4b_status check_weight_format(const e4b_moe_desc& d) {
 int conv_ctas_for(int rows, int warps_per_cta) {
   int c = (rows + warps_per_cta - 1) / warps_per_cta;
   return c < 1 ? 1 : (c > 148 * 4 ? 148 * 4 : c);
+}
+
+// tile_start[e] = sum over e' < e of ceil(count(e') / tile_rows), one block of 1024 threads.
+__global__ void __launch_bounds__(1024) tiles_from_offsets_kernel(const int32_t* __restrict__ offsets, int E,
+                                                                  int tile_rows, int32_t* __restrict__ tile_start) {
+  using Scan = cub::BlockScan<int, 1024>;
+  __shared__ typename Scan::TempStorage tmp;
+  const int e = threadIdx.x;
+  const int c = e < E ? offsets[e + 1] - offsets[e] : 0;
+  int ex, total;
+  Scan(tmp).ExclusiveSum(c > 0 ? (c + tile_rows - 1) / tile_rows : 0, ex, total);
+  if (e < E) tile_start[e] = ex;
+  if (e == 0) tile_start[E] = total;
 }
 
 __global__ void active_from_offsets_kernel(const int32_t* __restrict__ offsets, int E, int32_t* __restrict__ active,
@@ -329,7 +344,7 @@ extern "C" size_t e4b_grouped_gemm_workspace_bytes(int R, int E, int N, int K) {
   (void)N;
   if (E <= 0 || R < 0 || K <= 0) return 0;
   return kErrBytes + align_up((size_t)(E + 1) * 4, 256) + align_up((size_t)R * K * 2, 256) +
-         align_up((size_t)R * 4, 256);
+         align_up((size_t)R * 4, 256) + align_up((size_t)(E + 1) * 4, 256);
 }
 
 extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int32_t* a_rows, const uint8_t* packed,
@@ -386,6 +401,15 @@ extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int
   g.tiles_per_expert = epilogue == E4B_EPI_SWIGLU ? N / 16 : N / 16;
   g.max_tasks = (R < E ? R : E) * g.tiles_per_expert;
   g.err = reinterpret_cast<int*>(ws);
+  // Prefill-sized groups take the tcgen05 kernel (the same rule as the fused layer: at
+  // least 16 rows per expert on average), with its 128-row token tiles counted here.
+  const int n_out = epilogue == E4B_EPI_SWIGLU ? N / 2 : N;
+  if (umma_worthwhile(R, E) && R > 16 && n_out % 128 == 0 && umma_eligible(R, 1, E, K, n_out, 1, a_dtype, 0)) {
+    int32_t* tile_start = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(a_scale) + align_up((size_t)R * 4, 256));
+    tiles_from_offsets_kernel<<<1, 1024, 0, s>>>(offsets, E, kUmmaTokens, tile_start);
+    if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
+    return launch_umma(umma_args_from(g, nullptr, tile_start, R, 1, R), a_dtype, s);
+  }
   return launch_gemv_auto(g, R, R, s);
 }
 

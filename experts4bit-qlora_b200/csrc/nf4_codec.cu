@@ -49,26 +49,41 @@ __global__ void nf4_quantize_kernel(const T* __restrict__ w, int64_t nblocks, ui
   }
 }
 
-// Each thread decodes 16 packed bytes (32 elements).
+// Each thread decodes 4 packed bytes (8 elements) into one 16-byte store (two for fp32), so a
+// warp reads 128 contiguous bytes and writes a contiguous run; the codebook is read from
+// shared memory (lanes index it independently). out must be 16-byte aligned.
+template <typename T> __device__ __forceinline__ uint32_t bits16(T v);
+template <> __device__ __forceinline__ uint32_t bits16<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat16_as_ushort(v); }
+template <> __device__ __forceinline__ uint32_t bits16<__half>(__half v) { return __half_as_ushort(v); }
+
 template <typename T>
-__global__ void nf4_dequantize_kernel(const uint8_t* __restrict__ packed, const float* __restrict__ absmax,
-                                      int64_t nchunks, T* __restrict__ out) {
-  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks; c += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(packed + c * 16);
-    const float a = absmax[c >> 1];  // 16 bytes = 32 elements = half a block
-    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-    T vals[32];
+__global__ void __launch_bounds__(256) nf4_dequantize_kernel(const uint8_t* __restrict__ packed,
+                                                             const float* __restrict__ absmax, int64_t ngroups,
+                                                             T* __restrict__ out) {
+  __shared__ float s_code[16];
+  if (threadIdx.x < 16) s_code[threadIdx.x] = c_nf4[threadIdx.x];
+  __syncthreads();
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < ngroups; c += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(packed + c * 4);
+    const float a = absmax[c >> 3];  // 4 bytes = 8 elements = an eighth of a block
+    float v[8];
 #pragma unroll
-    for (int wi = 0; wi < 4; ++wi)
+    for (int bi = 0; bi < 4; ++bi) {
+      const uint32_t byte = (word >> (8 * bi)) & 0xffu;
+      v[2 * bi] = __fmul_rn(s_code[byte >> 4], a);
+      v[2 * bi + 1] = __fmul_rn(s_code[byte & 15], a);
+    }
+    if constexpr (sizeof(T) == 4) {
+      float4* o = reinterpret_cast<float4*>(out + c * 8);
+      o[0] = make_float4(v[0], v[1], v[2], v[3]);
+      o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      uint32_t w[4];
 #pragma unroll
-      for (int bi = 0; bi < 4; ++bi) {
-        const uint32_t byte = (words[wi] >> (8 * bi)) & 0xffu;
-        vals[wi * 8 + bi * 2] = from_f32<T>(__fmul_rn(c_nf4[byte >> 4], a));
-        vals[wi * 8 + bi * 2 + 1] = from_f32<T>(__fmul_rn(c_nf4[byte & 15], a));
-      }
-    T* o = out + c * 32;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = vals[i];
+      for (int j = 0; j < 4; ++j)
+        w[j] = bits16<T>(from_f32<T>(v[2 * j])) | (bits16<T>(from_f32<T>(v[2 * j + 1])) << 16);
+      *reinterpret_cast<uint4*>(out + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   }
 }
 
@@ -124,16 +139,16 @@ extern "C" e4b_status e4b_nf4_dequantize(const uint8_t* packed, const float* abs
   if (n < 0 || n % 64 || (n && (!packed || !absmax || !out))) return E4B_ERR_INVALID_ARG;
   if (!is_any_dtype(out_dtype)) return E4B_ERR_UNSUPPORTED;
   if (n == 0) return E4B_OK;
-  if (!aligned16(packed)) return E4B_ERR_ALIGNMENT;
+  if (!aligned16(packed) || !aligned16(out)) return E4B_ERR_ALIGNMENT;
   cudaStream_t s = (cudaStream_t)stream;
-  const int64_t nchunks = n / 32;
-  const int grid = grid_for(nchunks, 256);
+  const int64_t ngroups = n / 8;
+  const int grid = grid_for(ngroups, 256);
   if (out_dtype == E4B_BF16)
-    nf4_dequantize_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(packed, absmax, nchunks, (__nv_bfloat16*)out);
+    nf4_dequantize_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(packed, absmax, ngroups, (__nv_bfloat16*)out);
   else if (out_dtype == E4B_F16)
-    nf4_dequantize_kernel<__half><<<grid, 256, 0, s>>>(packed, absmax, nchunks, (__half*)out);
+    nf4_dequantize_kernel<__half><<<grid, 256, 0, s>>>(packed, absmax, ngroups, (__half*)out);
   else
-    nf4_dequantize_kernel<float><<<grid, 256, 0, s>>>(packed, absmax, nchunks, (float*)out);
+    nf4_dequantize_kernel<float><<<grid, 256, 0, s>>>(packed, absmax, ngroups, (float*)out);
   return launch_status();
 }
 

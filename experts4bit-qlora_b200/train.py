@@ -1,0 +1,264 @@
+"""``enable_fast_train`` / ``disable_fast_train``: the differentiable expert path of an
+``ExpertsLoRA`` layer, drop-in for ``experts4bit_qlora.engines.fast.enable_fast_train``
+(experts4bit_qlora/engines/fast.py:453-675).
+
+``enable_fast`` is inference-only (it falls back whenever a gradient is needed); this
+patches the ``ExpertsLoRA`` wrapper itself so a training step reaches the library with
+gradients on. The composition is the reference's (fast.py:453-552): the frozen NF4
+projection and the trainable ``scaling * B(Ax)`` delta are added to the same
+pre-activation, then SiLU(gate)*up, then the down projection with its own delta, then
+the top-k-weighted scatter in fp32.
+
+Forward: the device permutation (``e4b_permute``) and the grouped NF4 GEMMs
+(``e4b_grouped_nf4_gemm``: tcgen05 tiles at prefill sizes) for both frozen
+projections; the adapter products per expert.
+
+Backward (recompute-decode, as the reference's per-expert decode loop): the frozen
+stacks are dequantised once per backward (``e4b_nf4_dequantize``, one launch per
+stack, bf16, freed after the step; B200's memory holds a whole stack), and every
+per-expert product -- ``dL/dh = dD . W_down``, ``dL/dx = dP . W_gate_up``, the adapter
+products and the four adapter gradients -- runs as one batched GEMM over the experts'
+row segments padded to the longest. ``dL/d top_k_weights`` is the row dot product of
+the incoming gradient with the unweighted down rows. Nothing is saved that depends
+on the frozen weights, so the decoded stacks never live past one backward.
+
+Numerics: bf16 compute with fp32 adapter math, as ``ExpertsLoRA.forward``; the
+frozen projections accumulate in fp32 on fp16 operands (the NF4 value is exact in
+fp16), and experts are summed in group-sorted order, so the path matches the
+reference loop within the bf16 noise floor, not bit for bit (the reference's
+parity contract, tests/test_fused_train_parity.py:46-80).
+"""
+from __future__ import annotations
+
+import types
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _native as N
+from . import ops
+
+
+class _Segments:
+    """Expert-sorted rows as a padded batch ``[Ea, L, C]``: active expert i's rows at [i, 0:count)."""
+
+    def __init__(self, offsets_host, R, device):
+        counts = [offsets_host[e + 1] - offsets_host[e] for e in range(len(offsets_host) - 1)]
+        self.experts = [e for e, c in enumerate(counts) if c > 0]
+        self.counts = [counts[e] for e in self.experts]
+        self.L = max(self.counts) if self.counts else 0
+        self.Ea = len(self.experts)
+        # flat padded position of sorted row j: i * L + (j - start_i)
+        pos = []
+        for i, e in enumerate(self.experts):
+            pos.append((i * self.L - offsets_host[e], offsets_host[e], offsets_host[e + 1]))
+        shift = torch.zeros(R, dtype=torch.int64)
+        for d, a, b in pos:
+            shift[a:b] = d
+        self.pos = (torch.arange(R, dtype=torch.int64) + shift).to(device, non_blocking=True)
+        self.eid = torch.tensor(self.experts, dtype=torch.int64).to(device, non_blocking=True)
+
+    def pad(self, x):
+        """``[R, C]`` -> ``[Ea, L, C]`` (padding rows are zero)."""
+        out = torch.zeros(self.Ea * self.L, x.shape[1], dtype=x.dtype, device=x.device)
+        out.index_copy_(0, self.pos, x)
+        return out.view(self.Ea, self.L, -1)
+
+    def unpad(self, xp):
+        """``[Ea, L, C]`` -> ``[R, C]`` in row order."""
+        return xp.reshape(self.Ea * self.L, -1).index_select(0, self.pos)
+
+
+def _swiglu(proj, has_gate, act):
+    if has_gate:
+        g, u = proj.chunk(2, dim=-1)
+        return act(g) * u
+    return act(proj)
+
+
+class _FusedExpertsLoRATrain(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, hidden, top_k_weights, A_gu, B_gu, A_dn, B_dn, lora_mod, top_k_index):
+        base = lora_mod.base
+        E, H, I = base.num_experts, base.hidden_dim, base.intermediate_dim
+        n1 = 2 * I if base.has_gate else I
+        s = float(lora_mod.scaling)
+        T, k = top_k_index.shape
+        dev = hidden.device
+        order, inv, offsets = ops.permute(top_k_index, E)
+        order = order.long()
+        token_rows = order // k
+        offs_host = offsets.tolist()  # one host sync, as the reference's sizes .tolist()
+        R = T * k
+        seg = _Segments(offs_host, R, dev)
+        gu_p = base.gate_up_proj.view(E, n1, H // 2)
+        gu_a = base.gate_up_absmax.view(E, n1, H // 64)
+        dn_p = base.down_proj.view(E, H, I // 2)
+        dn_a = base.down_absmax.view(E, H, I // 64)
+        x = hidden.index_select(0, token_rows)                       # [R, H] compute dtype
+        proj = ops.grouped_nf4_gemm(hidden, gu_p, gu_a, offsets, a_rows=token_rows.to(torch.int32))
+        eid = seg.eid
+        # adapter delta of gate_up, in the adapter dtype, added to the bf16 base projection
+        xp = seg.pad(x).to(A_gu.dtype)                                # [Ea, L, H]
+        xa_gu = torch.bmm(xp, A_gu[eid].transpose(1, 2))              # [Ea, L, r]
+        d_gu = s * torch.bmm(xa_gu, B_gu[eid].transpose(1, 2))        # [Ea, L, n1]
+        proj = proj + seg.unpad(d_gu).to(proj.dtype)
+        h = _swiglu(proj, base.has_gate, base.act_fn)                 # [R, I]
+        down = ops.grouped_nf4_gemm(h.contiguous(), dn_p, dn_a, offsets)
+        hp = seg.pad(h).to(A_dn.dtype)
+        xa_dn = torch.bmm(hp, A_dn[eid].transpose(1, 2))              # [Ea, L, r]
+        d_dn = s * torch.bmm(xa_dn, B_dn[eid].transpose(1, 2))        # [Ea, L, H]
+        down = down + seg.unpad(d_dn).to(down.dtype)                  # [R, H] compute dtype
+        w_rows = top_k_weights.reshape(-1)[order]
+        inv = inv.long()
+        # weighted rows summed per token over its k slots in slot order (no atomics)
+        out = (down * w_rows.view(-1, 1))[inv].view(T, k, H).float().sum(1)
+        ctx.lora_mod = lora_mod
+        ctx.seg = seg
+        ctx.meta = (T, k, E, H, I, n1, s)
+        ctx.save_for_backward(token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn = ctx.saved_tensors
+        lora_mod, seg = ctx.lora_mod, ctx.seg
+        base = lora_mod.base
+        T, k, E, H, I, n1, s = ctx.meta
+        cdt = proj.dtype
+        eid = seg.eid
+        g_rows = grad_out.float().index_select(0, token_rows)          # [R, H]
+        d_w = (g_rows * down.float()).sum(-1)                           # dL/d w_rows
+        grad_w = torch.zeros(T * k, dtype=torch.float32, device=grad_out.device)
+        grad_w[order] = d_w
+        dd = (g_rows * w_rows.float().view(-1, 1)).to(cdt)             # dL/d down rows
+        # frozen stacks decoded once for this backward (bf16, freed on return)
+        W_dn = ops.nf4_dequantize(base.down_proj, base.down_absmax, (E, H, I), cdt)
+        ddp = seg.pad(dd)                                               # [Ea, L, H]
+        dh = torch.bmm(ddp, W_dn if seg.Ea == E else W_dn[eid])        # [Ea, L, I]
+        del W_dn
+        ddp32 = ddp.to(B_dn.dtype)
+        t_dn = torch.bmm(ddp32, B_dn[eid])                              # [Ea, L, r]
+        gB_dn = s * torch.bmm(ddp32.transpose(1, 2), xa_dn)             # [Ea, H, r]
+        hp = seg.pad(h).to(A_dn.dtype)
+        gA_dn = s * torch.bmm(t_dn.transpose(1, 2), hp)                 # [Ea, r, I]
+        dh = seg.unpad(dh.float() + s * torch.bmm(t_dn, A_dn[eid]))     # [R, I] fp32
+        # SiLU(gate) * up
+        pf = proj.float()
+        if base.has_gate:
+            g, u = pf.chunk(2, dim=-1)
+            sg = torch.sigmoid(g)
+            dproj = torch.cat([dh * u * (sg * (1 + g * (1 - sg))), dh * (g * sg)], dim=-1)
+        else:
+            sg = torch.sigmoid(pf)
+            dproj = dh * (sg * (1 + pf * (1 - sg)))
+        dproj = dproj.to(cdt)
+        W_gu = ops.nf4_dequantize(base.gate_up_proj, base.gate_up_absmax, (E, n1, H), cdt)
+        dpp = seg.pad(dproj)                                            # [Ea, L, n1]
+        dx = torch.bmm(dpp, W_gu if seg.Ea == E else W_gu[eid])        # [Ea, L, H]
+        del W_gu
+        dpp32 = dpp.to(B_gu.dtype)
+        t_gu = torch.bmm(dpp32, B_gu[eid])                              # [Ea, L, r]
+        gB_gu = s * torch.bmm(dpp32.transpose(1, 2), xa_gu)             # [Ea, n1, r]
+        xp = seg.pad(x).to(A_gu.dtype)
+        gA_gu = s * torch.bmm(t_gu.transpose(1, 2), xp)                 # [Ea, r, H]
+        dx = seg.unpad(dx.float() + s * torch.bmm(t_gu, A_gu[eid]))     # [R, H] fp32
+        grad_hidden = dx[inv].view(T, k, H).sum(1)                      # slot order, no atomics
+
+        def scatter(g_act, like):
+            full = torch.zeros_like(like)
+            full[eid] = g_act.to(like.dtype)
+            return full
+
+        return (grad_hidden.to(cdt), grad_w.view(T, k),
+                scatter(gA_gu, A_gu), scatter(gB_gu, B_gu), scatter(gA_dn, A_dn), scatter(gB_dn, B_dn),
+                None, None)
+
+
+def fused_experts_train_forward(lora_mod, hidden_states, top_k_index, top_k_weights):
+    """Training-capable fused forward of an ``ExpertsLoRA`` (``fast.py:453-552``)."""
+    base = lora_mod.base
+    input_dtype = hidden_states.dtype
+    compute_dtype = base.compute_dtype if base.compute_dtype is not None else input_dtype
+    if compute_dtype not in (torch.bfloat16, torch.float16) or not hidden_states.is_cuda:
+        return lora_mod._e4b_train_ref(hidden_states, top_k_index, top_k_weights)
+    hs = hidden_states.to(compute_dtype).contiguous()
+    idx = top_k_index.contiguous().long()
+    out = _FusedExpertsLoRATrain.apply(hs, top_k_weights, lora_mod.gate_up_lora_A, lora_mod.gate_up_lora_B,
+                                       lora_mod.down_lora_A, lora_mod.down_lora_B, lora_mod, idx)
+    return out.to(input_dtype)
+
+
+def _train_ineligible(mod) -> Optional[str]:
+    from .fast import _eligible
+    reason = _eligible(mod.base)
+    if reason is not None:
+        return reason
+    if getattr(mod.base, "quant_type", None) == "fp8_block128":
+        return "FP8 block storage has no training path"
+    H, I = mod.base.hidden_dim, mod.base.intermediate_dim
+    if H % 64 or I % 64:
+        return "hidden and intermediate sizes must be multiples of 64"
+    return None
+
+
+def enable_fast_train(model, verbose: bool = False, dgrad: bool = False) -> int:
+    """Route ``ExpertsLoRA`` training through the fused path; returns the patch count
+    (``fast.py:555-660``). ``dgrad`` is accepted for the reference's signature and recorded
+    on the module: this backward always decodes each frozen stack once and runs the
+    input-gradient products as batched GEMMs, which is what the reference's single-launch
+    dgrad kernel option selects."""
+    from .experts import Experts4bit, ExpertsNbit
+    from .lora import ExpertsLoRA
+
+    if not N.available():
+        if verbose:
+            print("[e4b.fast] libe4b.so is not built: no fused training path")
+        return 0
+    stock = {ExpertsNbit.forward, Experts4bit.forward}
+    mods = list(model.modules()) if hasattr(model, "modules") else [model]
+    patched = 0
+    for mod in mods:
+        if not isinstance(mod, ExpertsLoRA):
+            continue
+        if hasattr(mod, "_e4b_train_ref"):
+            if getattr(mod, "_e4b_dgrad", False) != dgrad:
+                import warnings
+                warnings.warn(
+                    f"[e4b.fast] enable_fast_train(dgrad={dgrad}) on a module already patched with "
+                    f"dgrad={getattr(mod, '_e4b_dgrad', False)}: the existing patch is kept. Call "
+                    "disable_fast_train first to change it.", RuntimeWarning, stacklevel=2)
+            continue
+        if type(mod.base).forward not in stock and not hasattr(mod.base, "_apply_gate"):
+            if verbose:
+                print(f"[e4b.fast] skip {type(mod).__name__}: base {type(mod.base).__name__} has a custom forward")
+            continue
+        reason = _train_ineligible(mod)
+        if reason is not None:
+            if verbose:
+                print(f"[e4b.fast] skip {type(mod).__name__}: {reason}")
+            continue
+        mod._e4b_train_ref = mod.forward
+        mod._e4b_dgrad = dgrad
+        mod.forward = types.MethodType(
+            lambda self, hs, tki, tkw: fused_experts_train_forward(self, hs, tki, tkw), mod)
+        patched += 1
+    if verbose:
+        print(f"[e4b.fast] fused TRAINING path on {patched} ExpertsLoRA module(s)")
+    return patched
+
+
+def disable_fast_train(model) -> int:
+    """Undo ``enable_fast_train`` (``fast.py:663-675``); returns the number restored."""
+    n = 0
+    mods = model.modules() if hasattr(model, "modules") else [model]
+    for mod in mods:
+        ref = getattr(mod, "_e4b_train_ref", None)
+        if ref is not None:
+            mod.forward = ref
+            del mod._e4b_train_ref
+            if hasattr(mod, "_e4b_dgrad"):
+                del mod._e4b_dgrad
+            n += 1
+    return n

@@ -83,7 +83,8 @@ E4B_API e4b_status e4b_nf4_quantize(const void* w, int w_dtype, int64_t n, uint8
 
 /* Replaces bitsandbytes.functional.dequantize_4bit as called by
  * ExpertsNbit._dequantize_expert (_vendor/experts.py:447-457):
- * out[i] = out_dtype(code[q_i] * absmax[i/64]) with one round-to-nearest-even. */
+ * out[i] = out_dtype(code[q_i] * absmax[i/64]) with one round-to-nearest-even.
+ * packed and out 16-byte aligned. */
 E4B_API e4b_status e4b_nf4_dequantize(const uint8_t* packed, const float* absmax, int64_t n, void* out, int out_dtype,
                               void* stream);
 

@@ -125,7 +125,9 @@ def test_permute_bit_exact(ops, T, k, E):
 
 
 @pytest.mark.parametrize("E,NN,K,m,epi", [(4, 256, 128, 1, 0), (8, 512, 1024, 3, 1), (3, 128, 2048, 8, 2),
-                                           (5, 256, 768, 13, 1), (4, 128, 128, 40, 0), (2, 4096, 1024, 1, 0)])
+                                           (5, 256, 768, 13, 1), (4, 128, 128, 40, 0), (2, 4096, 1024, 1, 0),
+                                           # prefill-sized groups: the tcgen05 kernel
+                                           (4, 512, 256, 300, 1), (3, 256, 512, 200, 0), (6, 384, 768, 150, 2)])
 def test_grouped_gemm_vs_fp32(ops, E, NN, K, m, epi):
     g = torch.Generator().manual_seed(E * NN + K + m)
     w = torch.randn(E, NN, K, generator=g) * 0.05
