@@ -105,6 +105,7 @@ struct DSmem {
 };
 static_assert(DSmem::slots % 1024 == 0 && kDSlotBytes % 1024 == 0, "swizzled boxes need 1024-byte alignment");
 static_assert(DSmem::total <= 232448, "shared memory budget");
+static_assert(16 * 64 * 4 <= kPairs * 32 * 8 * 4, "top-k selection slots of 16 token warps fit the reduction area");
 
 struct DecodeArgs {
   const void* hidden;
@@ -128,6 +129,7 @@ struct DecodeArgs {
   int router_w_dtype, route_kind, renorm;
   int64_t* topk_idx_out;       // [T, k] (written by CTA 0)
   float* topk_w_out;           // [T, k]
+  float* router_logits;        // [T, E] global scratch: logits spread over the grid, then a grid sync
 };
 
 struct Tables {
@@ -458,20 +460,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     // L2 resident after the first CTA touches them) and the same top-k: no grid barrier ----
     float* logits = reinterpret_cast<float*>(smem + DSmem::logits);
     const int ttiles = (a.T + kRouterTT - 1) / kRouterTT, tasks = a.E * ttiles;
-    for (int task = warp; task < tasks; task += kWarps)
-      router_logits_warp(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
-                         (task / a.E) * kRouterTT, logits);
+    const bool w16 = a.router_w_dtype != E4B_F32;  // 16-bit weights: all strips of a lane in flight
+    // With global scratch the (expert, token tile) tasks are spread one warp per SM across the
+    // grid and shared through a grid barrier; otherwise every CTA computes all of them.
+    float* dst = a.router_logits ? a.router_logits : logits;
+    const int w0 = a.router_logits ? warp * (int)gridDim.x + blockIdx.x : warp;
+    const int wstep = a.router_logits ? kWarps * (int)gridDim.x : kWarps;
+    for (int task = w0; task < tasks; task += wstep) {
+      if (w16)
+        router_logits_warp16<8>(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
+                                (task / a.E) * kRouterTT, dst);
+      else
+        router_logits_warp(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
+                           (task / a.E) * kRouterTT, dst);
+    }
+    if (a.router_logits) {
+      cg::this_grid().sync();
+      for (int i = tid; i < a.T * a.E; i += kThreads) logits[i] = __ldcg(a.router_logits + i);
+    }
     DTRACE(14);
     __syncthreads();
     DTRACE(15);
     if (warp < a.T) {
       int se = 0;
       float sw = 0.f;
-      if (a.E <= 32) router_topk_warp<1>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
-      else if (a.E <= 64) router_topk_warp<2>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
-      else if (a.E <= 128) router_topk_warp<4>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
-      else if (a.E <= 256) router_topk_warp<8>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
-      else router_topk_warp<32>(logits, 1, nullptr, a.T, a.E, a.k, a.route_kind, a.renorm, warp, se, sw);
+      // selection slots per token warp in the (not yet used) reduction area: 32 values + 32 ids
+      float* sv = reinterpret_cast<float*>(smem + DSmem::red) + warp * 64;
+      int* si = reinterpret_cast<int*>(sv + 32);
+#define E4B_DTOPK(EPL) \
+  router_topk_warp_ranked<EPL>(logits, a.T, a.E, a.k, a.route_kind, a.renorm, warp, sv, si, se, sw)
+      if (a.E <= 32) E4B_DTOPK(1);
+      else if (a.E <= 64) E4B_DTOPK(2);
+      else if (a.E <= 128) E4B_DTOPK(4);
+      else if (a.E <= 256) E4B_DTOPK(8);
+      else E4B_DTOPK(32);
+#undef E4B_DTOPK
       if (lane < a.k) {
         tb.pick_e[warp * a.k + lane] = se;
         tb.w[warp * a.k + lane] = sw;
@@ -772,6 +795,7 @@ e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, 
     a.renorm = router->norm_topk_prob;
     a.topk_idx_out = router->topk_idx;
     a.topk_w_out = router->topk_w;
+    a.router_logits = router->logits;
   }
   a.hidden = t->hidden;
   a.act_dtype = d.act_dtype;

@@ -19,6 +19,7 @@ struct DecodeRouter {
   int weight_dtype, kind, norm_topk_prob;
   int64_t* topk_idx;
   float* topk_w;
+  float* logits;  // [T, E] fp32 scratch in global memory: logits computed across the grid (null: per CTA)
 };
 bool decode_router_fusable(const e4b_moe_desc& d);
 e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,

@@ -441,7 +441,8 @@ extern "C" e4b_status e4b_moe_decode_step(const e4b_moe_desc* desc, const e4b_mo
       t->down_packed && t->down_absmax && aligned16(t->hidden) && aligned16(t->out) && aligned16(t->gate_up_packed) &&
       aligned16(t->down_packed) && is_act_dtype(d.act_dtype) && is_any_dtype(d.out_dtype)) {
     const MoeLayout L = moe_layout(d);
-    DecodeRouter r{router_w, router_w_dtype, kind, norm_topk_prob, topk_idx, topk_w};
+    DecodeRouter r{router_w, router_w_dtype, kind, norm_topk_prob, topk_idx, topk_w,
+                   reinterpret_cast<float*>(rws + kErrBytes)};
     mark_stage(&tt, 0, s);
     e4b_status st = launch_decode_layer(d, &tt, ws + L.h, ws + L.down_rows, ws + L.sync, reinterpret_cast<int*>(ws), s,
                                         &r);
