@@ -456,8 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (tid < 16) tb.rowmax[tid] = 0u;
   if (a.router_w) {
-    // ---- fused router: every CTA computes all logits into its shared memory (the weights are
-    // L2 resident after the first CTA touches them) and the same top-k: no grid barrier ----
+    // ---- fused router: logits into shared memory (spread over the grid through global
+    // scratch and a grid barrier, or computed by every CTA), then the same top-k everywhere ----
     float* logits = reinterpret_cast<float*>(smem + DSmem::logits);
     const int ttiles = (a.T + kRouterTT - 1) / kRouterTT, tasks = a.E * ttiles;
     const bool w16 = a.router_w_dtype != E4B_F32;  // 16-bit weights: all strips of a lane in flight
@@ -569,12 +569,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int vi = tid + i * kThreads;
-      if (vi < xvec) {
-        unpack8(xr[i], a.act_dtype, v[i]);
+      // a warp's 32 vectors lie in one row (H / 8 is a multiple of 32): reduce, then one atomic
+      if (i * kThreads + warp * 32 < xvec) {
         float m = 0.f;
+        if (vi < xvec) {
+          unpack8(xr[i], a.act_dtype, v[i]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
-        atomicMax(&tb.rowmax[vi / (a.H / 8)], __float_as_uint(m));
+          for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) atomicMax(&tb.rowmax[vi / (a.H / 8)], __float_as_uint(m));
       }
     }
     __syncthreads();

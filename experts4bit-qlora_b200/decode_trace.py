@@ -25,7 +25,7 @@ ROOT = os.path.dirname(HERE)
 # stamp index -> phase boundary (decode_layer.cu, DTRACE calls)
 PHASES = [(0, "start"), (14, "router logits (+ grid sync)"), (15, "logits in shared memory"), (16, "top-k"),
           (17, "permutation count"), (18, "permutation place"), (1, "permutation done"),
-          (10, "first weight copies issued"), (11, "token rows converted"), (12, "pair table built"),
+          (10, "first weight copies issued"), (11, "pair table built"), (12, "token rows converted"),
           (13, "block barrier"), (2, "phase A start"), (3, "gate_up done, down copies issued"),
           (4, "grid barrier 1"), (5, "h staged"), (6, "down done"), (7, "grid barrier 2"), (8, "combine"),
           (9, "error fold")]
