@@ -46,7 +46,7 @@ typedef enum {
   E4B_ERR_CUDA = 5,           /* a CUDA launch or query failed */
   E4B_ERR_EXPERT_INDEX = 6,   /* device-reported: a top-k index outside [0, E) */
   E4B_ERR_RANGE = 7,          /* device-reported: an intermediate activation beyond +-65504 saturated */
-  E4B_ERR_TIMEOUT = 8,        /* device-reported: a bounded wait on an async copy gave up */
+  E4B_ERR_TIMEOUT = 8,        /* device-reported: a bounded wait (async copy, peer flag) gave up */
   E4B_ERR_STATIC_SCRATCH = 9  /* layer needs more scratch than e4b_moe_forward_static's fixed array */
 } e4b_status;
 

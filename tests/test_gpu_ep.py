@@ -260,3 +260,29 @@ def test_ep_peer_matches_nccl_layout_path(e4b):
     got = emulate_ep_peer(e4b, mod, x.cuda(), idx2.cuda(), w.cuda(), 4)
     mx, mean = M.rel_errors(got.float().cpu(), M.fp32_oracle(_st(mod), x, idx2, w))
     assert mx <= 1e-2 and mean <= 2e-3
+
+
+def test_ep_peer_wait_times_out_and_context_survives(e4b):
+    """A source that never dispatches: the expert side's bounded wait gives up (a few seconds),
+    reports E4B_ERR_TIMEOUT in the region's error word, treats that source as empty, and the
+    context keeps working. Nothing else waits on this kernel."""
+    import ctypes
+    import time
+    from importlib import import_module
+    ep = import_module("experts4bit-qlora_b200.ep")
+    N = e4b._native
+    E, H, I = 8, 256, 128
+    mod = _layer(e4b, E, H, I, seed=9)
+    exs = ep.PeerExchange.emulated(2, E // 2, 32, H, torch.bfloat16, torch.device("cuda"))
+    stage = ep.NativeStages(ep.shard_experts(mod, 0, 2), E, H, I, True, 2)
+    t0 = time.time()
+    stage.experts_peer(exs[0], 32)        # rank 0's expert side; no rank ever dispatched
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    err = ctypes.c_int(-1)
+    N.check(N.lib().e4b_read_device_error(exs[0].region.data_ptr(), N.stream_handle(torch.device("cuda")),
+                                          ctypes.byref(err)), "read_device_error")
+    assert err.value == N.E4B_ERR_TIMEOUT, N.status_string(err.value)
+    assert waited > 0.5
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum()) == 8.0    # the context is usable
