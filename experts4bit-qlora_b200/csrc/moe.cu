@@ -320,7 +320,7 @@ extern "C" const char* e4b_status_string(e4b_status s) {
     case E4B_ERR_CUDA: return "CUDA launch or query failed";
     case E4B_ERR_EXPERT_INDEX: return "top-k expert index outside [0, num_experts)";
     case E4B_ERR_RANGE: return "an intermediate activation exceeded the fp16 range (+-65504) and was saturated";
-    case E4B_ERR_TIMEOUT: return "a bounded device wait on an asynchronous copy timed out";
+    case E4B_ERR_TIMEOUT: return "a bounded device wait (asynchronous copy or peer arrival flag) timed out";
     case E4B_ERR_STATIC_SCRATCH:
       return "layer needs more scratch than the static array of e4b_moe_forward_static (E4B_STATIC_SCRATCH_BYTES)";
   }
