@@ -12,7 +12,7 @@ it is also registered as ``experts4bit_qlora_b200``.
 """
 import sys as _sys
 
-from . import _native, ep, ops  # noqa: F401
+from . import _native, ep, mxfp4, ops  # noqa: F401
 from .experts import Experts4bit, ExpertsNbit, normalize_quant_type
 from .fast import disable_fast, enable_fast, fast_available
 from .fp8_experts import ExpertsFp8Blocks

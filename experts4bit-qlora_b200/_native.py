@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "e4b_router_workspace_bytes", "e4b_router_topk",
     "e4b_permute_workspace_bytes", "e4b_permute",
     "e4b_fp8_block_dequantize",
+    "e4b_mxfp4_dequantize", "e4b_mxfp4_dequantize_host",
     "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
     "e4b_combine",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
@@ -97,6 +98,8 @@ def _declare(lib):
         "e4b_permute_workspace_bytes": (SZ, [I, I, I]),
         "e4b_permute": (I, [P, I, I, I, P, P, P, P, SZ, P]),
         "e4b_fp8_block_dequantize": (I, [P, P, I64, I64, P, I, P]),
+        "e4b_mxfp4_dequantize": (I, [P, P, I64, I64, I64, I64, P, I, P]),
+        "e4b_mxfp4_dequantize_host": (I, [P, P, I64, I64, I64, I64, P, I]),
         "e4b_grouped_gemm_workspace_bytes": (SZ, [I, I, I, I]),
         "e4b_grouped_nf4_gemm": (I, [P, I, P, P, P, P, I, I, I, I, I, P, P, SZ, P]),
         "e4b_combine": (I, [P, I, P, P, I, I, I, I, P, I, P]),

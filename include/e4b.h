@@ -126,6 +126,19 @@ E4B_API e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, int
 E4B_API e4b_status e4b_fp8_block_dequantize(const uint8_t* w, const float* scale, int64_t rows, int64_t cols,
                                     void* out, int out_dtype, void* stream);
 
+/* ---- MXFP4 weights (the storage format) ----------------
+ * Replaces formats/mxfp4.py:35-105 (dequantize_mxfp4): blocks uint8 [P, rows, G, B]
+ * (two e2m1 codes per byte, low nibble first), scales uint8 [P, rows, G] (e8m0,
+ * bias 127, one per block of 2B values); out [P, G*2B, rows] in out_dtype -- the
+ * trailing (rows, K) pair transposed, as the reference returns it -- with
+ * out = out_dtype(fp32(e2m1) * 2^(s-127)), one rounding. P = the product of the
+ * leading dimensions (1 for a single projection). The _host variant takes host
+ * pointers and produces the same bits. */
+E4B_API e4b_status e4b_mxfp4_dequantize(const uint8_t* blocks, const uint8_t* scales, int64_t P, int64_t rows,
+                                int64_t G, int64_t B, void* out, int out_dtype, void* stream);
+E4B_API e4b_status e4b_mxfp4_dequantize_host(const uint8_t* blocks_host, const uint8_t* scales_host, int64_t P,
+                                     int64_t rows, int64_t G, int64_t B, void* out_host, int out_dtype);
+
 /* ---- Grouped NF4 GEMM (R3, R4, R6) --------------------------------------- */
 
 /* Replaces nf4_grouped.gemm_4bit_grouped(a, packed.view(E,N,K/2),
