@@ -144,3 +144,10 @@ def test_ep_world2_micro_batches():
     for rank, shape, mx, mean in _run((9, 15), micro_batches=3):
         assert shape == ((9, 15)[rank], 128)
         assert mx <= 1e-2 and mean <= 2e-3, (rank, mx, mean)
+
+
+def test_ep_world4_ragged_with_an_empty_rank():
+    """Four ranks (two experts each), shards of 0, 3, 14 and 7 tokens."""
+    for rank, shape, mx, mean in _run((0, 3, 14, 7)):
+        assert shape == ((0, 3, 14, 7)[rank], 128)
+        assert mx <= 1e-2 and mean <= 2e-3, (rank, mx, mean)

@@ -1,0 +1,89 @@
+"""CPU: the training path's autograd math (train.py) with its three device calls --
+permutation, grouped NF4 GEMM, stack dequantization -- replaced by CPU stand-ins built on
+the oracle and the host codec. Forward and every gradient of the fused autograd function
+must match autograd through the ``ExpertsLoRA`` loop on the same NF4 bytes (the GPU test,
+test_gpu_train.py, checks the real kernels under the same contract)."""
+import importlib
+import types
+
+import pytest
+import torch
+
+from oracle import moe as M
+
+
+def _rel(got, want):
+    return float((got.float() - want.float()).norm() / want.float().norm().clamp_min(1e-12))
+
+
+def _cpu_ops(e4b):
+    real = e4b.ops
+
+    def permute(idx, E):
+        order, _, _, _, offsets = M.permute(idx.cpu(), E)
+        inv = torch.empty_like(order)
+        inv[order] = torch.arange(order.numel())
+        return order.to(torch.int32), inv.to(torch.int32), offsets.to(torch.int32)
+
+    def grouped_nf4_gemm(a, packed, absmax, offsets, a_rows=None, epilogue=0):
+        E, Nn, Kh = packed.shape
+        W = real.nf4_dequantize(packed, absmax, (E, Nn, Kh * 2), a.dtype)   # host codec
+        x = a[a_rows.long()] if a_rows is not None else a
+        out = torch.empty(x.shape[0], Nn, dtype=a.dtype)
+        for e in range(E):
+            lo, hi = int(offsets[e]), int(offsets[e + 1])
+            out[lo:hi] = (x[lo:hi].float() @ W[e].float().t()).to(a.dtype)
+        return out
+
+    return types.SimpleNamespace(permute=permute, grouped_nf4_gemm=grouped_nf4_gemm,
+                                 nf4_dequantize=real.nf4_dequantize)
+
+
+@pytest.mark.parametrize("has_gate", [True, False])
+def test_fused_train_autograd_matches_loop_on_cpu(e4b, monkeypatch, has_gate):
+    train = importlib.import_module("experts4bit-qlora_b200.train")
+    monkeypatch.setattr(train, "ops", _cpu_ops(e4b))
+    E, H, I, k, T = 8, 128, 192, 2, 48
+    torch.manual_seed(0)
+    n1 = 2 * I if has_gate else I
+    base = e4b.Experts4bit.from_float(torch.randn(E, n1, H) * 0.1, torch.randn(E, H, I) * 0.1,
+                                      has_gate=has_gate, compute_dtype=torch.bfloat16)
+    lm = e4b.ExpertsLoRA(base, r=8, alpha=16, dtype=torch.float32)
+    with torch.no_grad():
+        lm.gate_up_lora_B.normal_(0, 0.02)
+        lm.down_lora_B.normal_(0, 0.02)
+    lm.train()
+    torch.manual_seed(1)
+    hs = torch.randn(T, H, dtype=torch.bfloat16)
+    idx = torch.randint(0, E, (T, k))
+    idx[:, 1] = (idx[:, 0] + 1 + torch.randint(0, E - 1, (T,))) % E        # distinct picks per token
+    idx[idx == 5] = 6                                                     # expert 5 never routed
+    idx[:, 1] = torch.where(idx[:, 1] == idx[:, 0], (idx[:, 0] + 2) % E, idx[:, 1])
+    wts = torch.rand(T, k, dtype=torch.bfloat16)
+    loss_w = torch.randn(T, H)
+
+    def run(fused):
+        x = hs.clone().requires_grad_(True)
+        w = wts.clone().requires_grad_(True)
+        for p in lm.parameters():
+            p.grad = None
+        if fused:
+            out = train._FusedExpertsLoRATrain.apply(x, w, lm.gate_up_lora_A, lm.gate_up_lora_B, lm.down_lora_A,
+                                                     lm.down_lora_B, lm, idx).to(x.dtype)
+        else:
+            out = lm(x, idx, w)
+        (out.float() * loss_w).sum().backward()
+        grads = {n: p.grad.clone() for n, p in lm.named_parameters() if p.grad is not None}
+        return out.detach(), x.grad.clone(), w.grad.clone(), grads
+
+    ref = run(False)
+    got = run(True)
+    print("\nfwd %.2e dx %.2e dw %.2e " % (_rel(got[0], ref[0]), _rel(got[1], ref[1]), _rel(got[2], ref[2])) + " ".join("%s %.2e" % (n, _rel(got[3][n], ref[3][n])) for n in ref[3]))
+    assert _rel(got[0], ref[0]) < 1e-2
+    assert _rel(got[1], ref[1]) < 1e-2
+    assert _rel(got[2], ref[2]) < 1e-2
+    assert set(got[3]) == set(ref[3])
+    for n in ref[3]:
+        assert _rel(got[3][n], ref[3][n]) < 1e-2, n
+        # the adapter rows of the expert nobody routed to get exactly zero gradient
+        assert got[3][n][5].abs().sum() == 0, n
