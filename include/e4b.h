@@ -5,8 +5,7 @@
  * Python call into grouped-nf4-gemm / bitsandbytes. Each entry point below
  * replaces one such call (or one stage of experts4bit_qlora/engines/fast.py)
  * and is cited to the reference line it stands in for. A maintainer binds them
- * with ctypes; the Python package in this repository does
- * exactly that.
+ * with ctypes; the Python package in this repository does exactly that.
  *
  * Conventions
  *   - Every pointer is a DEVICE pointer unless the name ends in _host.
@@ -126,7 +125,7 @@ E4B_API e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, int
 E4B_API e4b_status e4b_fp8_block_dequantize(const uint8_t* w, const float* scale, int64_t rows, int64_t cols,
                                     void* out, int out_dtype, void* stream);
 
-/* ---- MXFP4 weights (the storage format) ----------------
+/* ---- MXFP4 weights (the storage format) ------------------------------------
  * Replaces formats/mxfp4.py:35-105 (dequantize_mxfp4): blocks uint8 [P, rows, G, B]
  * (two e2m1 codes per byte, low nibble first), scales uint8 [P, rows, G] (e8m0,
  * bias 127, one per block of 2B values); out [P, G*2B, rows] in out_dtype -- the
