@@ -31,6 +31,25 @@ __host__ __device__ __forceinline__ float e8m0_value(uint32_t s) {
   return f;
 }
 
+// code * 2^(s-127) exactly as ldexp (the reference's torch.ldexp) gives it: one rounding of the
+// exact product. For s <= 254 the factor is a float and one multiply is exact or rounds once; for
+// s = 255 the factor 2^128 is not, so the product is formed as (code * 2^64) * 2^64: 0.5 * 2^128
+// stays finite, codes >= 1 overflow to inf, zero stays a signed zero (no 0 * inf = NaN).
+__device__ __forceinline__ float e8m0_scale_dev(float c, uint32_t s) {
+  if (s == 255u) return __fmul_rn(__fmul_rn(c, 18446744073709551616.0f), 18446744073709551616.0f);
+  return __fmul_rn(c, e8m0_value(s));
+}
+inline float e8m0_scale_host(float c, uint32_t s) {
+  volatile float v;
+  if (s == 255u) {
+    v = c * 18446744073709551616.0f;
+    v = v * 18446744073709551616.0f;
+  } else {
+    v = c * e8m0_value(s);
+  }
+  return v;
+}
+
 // One thread per output element (p, k, r), r fastest: the stores are coalesced; each
 // warp reads its rows' bytes of one 2-element column pair (served by L1/L2).
 template <typename T>
@@ -47,7 +66,7 @@ __global__ void __launch_bounds__(256) mxfp4_dequant_kernel(const uint8_t* __res
     const int64_t row = p * rows + r;
     const uint32_t byte = blocks[row * G * B + (k >> 1)];
     const uint32_t code = (k & 1) ? byte >> 4 : byte & 15u;
-    const float v = __fmul_rn(s_code[code], e8m0_value(scales[row * G + k / (2 * B)]));
+    const float v = e8m0_scale_dev(s_code[code], scales[row * G + k / (2 * B)]);
     out[i] = from_f32<T>(v);
   }
 }
@@ -75,7 +94,7 @@ void mxfp4_dequant_host(const uint8_t* blocks, const uint8_t* scales, int64_t P,
       for (int64_t k = 0; k < K; ++k) {
         const uint32_t byte = blocks[row * G * B + (k >> 1)];
         const uint32_t code = (k & 1) ? byte >> 4 : byte & 15u;
-        volatile float v = h_e2m1[code] * e8m0_value(scales[row * G + k / (2 * B)]);  // one fp32 product
+        const float v = e8m0_scale_host(h_e2m1[code], scales[row * G + k / (2 * B)]);
         out[(p * K + k) * rows + r] = host_cast<T>(v);
       }
     }

@@ -27,6 +27,8 @@ def dequantize_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, *, dtype: torch
     if blocks.ndim < 3:
         raise ValueError(
             f"blocks must be [..., rows, G, B] with at least one leading row axis; got {tuple(blocks.shape)}")
+    if scales.device != blocks.device:
+        raise ValueError(f"scales are on {scales.device} but blocks on {blocks.device}")
     if blocks.dtype != torch.uint8:
         blocks = blocks.view(torch.uint8)
     if scales.dtype != torch.uint8:

@@ -5,7 +5,8 @@ Follows formats/mxfp4.py:25-105 of the reference (itself a restatement of
 transformers' convert_moe_packed_tensors): blocks ``uint8 [..., rows, G, B]`` hold two
 e2m1 codes per byte, LOW nibble first; scales ``uint8 [..., rows, G]`` are e8m0
 exponents (bias 127), one per block of 2B values; the value is
-``FP4_VALUES[code] * 2**(s - 127)`` computed in fp32 and rounded once to the output
+``ldexp(FP4_VALUES[code], s - 127)`` in fp32 (the exact product, rounded once; 2**128 is not
+formed on its own, so zero codes stay signed zeros even for s = 255), rounded once to the output
 dtype, and the result has its trailing (rows, K) pair transposed to ``[..., K, rows]``.
 Pinned by tests/golden/mxfp4.npz, made by running the reference's function.
 """
@@ -25,8 +26,10 @@ def dequantize_mxfp4_f32(blocks: np.ndarray, scales: np.ndarray) -> np.ndarray:
     vals = np.empty((*prefix, rows, G, 2 * B), dtype=np.float32)
     vals[..., 0::2] = lo
     vals[..., 1::2] = hi
-    scale = np.ldexp(np.float32(1.0), scales.astype(np.int32) - 127).astype(np.float32)
-    with np.errstate(invalid="ignore", over="ignore"):
-        vals = vals * scale[..., None]
+    exp = (scales.astype(np.int32) - 127)[..., None]
+    with np.errstate(over="ignore"):
+        # ldexp, as the reference's torch.ldexp: one rounding of the exact product, so 0.5 * 2**128
+        # is finite and a zero code stays a signed zero under e8m0 255
+        vals = np.ldexp(vals, exp).astype(np.float32)
     vals = vals.reshape(*prefix, rows, G * 2 * B)
     return np.swapaxes(vals, -1, -2).copy()

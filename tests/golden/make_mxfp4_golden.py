@@ -5,7 +5,8 @@ reference from its source tree):
     python tests/golden/make_mxfp4_golden.py [/path/to/experts4bit-qlora]
 
 Cases: a gpt-oss-like rank-4 stack ``[E, rows, G, 16]`` and a single rank-3 projection,
-with random codes and e8m0 scales over 0..254 (the extremes included), dequantized to
+with random codes and e8m0 scales over 0..255 (the extremes included; 255 with zero codes,
+which the reference turns into NaN), dequantized to
 bf16, fp16 and fp32. The outputs are stored as raw bit patterns.
 """
 from __future__ import annotations
@@ -27,7 +28,9 @@ def inputs(name):
     blocks = g.integers(0, 256, size=shape, dtype=np.uint8)
     scales = g.integers(100, 140, size=shape[:-1], dtype=np.uint8)   # realistic weight scales
     flat = scales.reshape(-1)
-    flat[:4] = (0, 1, 253, 254)                                      # the extremes
+    flat[:5] = (0, 1, 253, 254, 255)                                 # the extremes; 255 gives 2**128 = inf
+    codes = blocks.reshape(-1, shape[-1])
+    codes[4, :2] = (0x00, 0x80)                                      # +0 and -0 codes under the inf scale
     return blocks, scales
 
 

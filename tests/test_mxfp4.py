@@ -54,3 +54,21 @@ def test_device_kernel_matches_reference(e4b, case, dt, tag, view):
     got = mx.dequantize_mxfp4(torch.from_numpy(G[f"{case}_blocks"]).cuda(),
                               torch.from_numpy(G[f"{case}_scales"]).cuda(), dtype=dt)
     assert np.array_equal(_bits(got, view), G[f"{case}_{tag}"])
+
+
+def test_scales_on_another_device_are_refused(e4b):
+    """Scales on another device than the blocks are refused before any pointer reaches a kernel."""
+    mx = importlib.import_module("experts4bit-qlora_b200.mxfp4")
+    b, s = torch.from_numpy(G["single_blocks"]), torch.from_numpy(G["single_scales"])
+    with pytest.raises(ValueError, match="blocks on"):
+        mx.dequantize_mxfp4(b, s.to("meta"))
+
+
+def test_scale_255_follows_ldexp():
+    """e8m0 255 is 2**128: 0.5 * 2**128 stays finite, codes >= 1 overflow, zero codes stay zeros."""
+    blocks = np.array([[[0x10, 0x8A]]], dtype=np.uint8)   # codes (lo, hi): 0, 0.5 | -1.0, -0.0
+    v = OM.dequantize_mxfp4_f32(blocks, np.array([[255]], dtype=np.uint8)).reshape(-1)
+    assert v[0] == 0 and not np.signbit(v[0])
+    assert v[1] == np.float32(2.0 ** 127)
+    assert v[2] == -np.inf
+    assert v[3] == 0 and np.signbit(v[3])
