@@ -1,6 +1,6 @@
 """MoE-layer throughput of the fused NF4 expert path on B200.
 
-Default workload (N=1): BASELINE config 2, OLMoE-1B-7B geometry bs=1 decode --
+Default workload (one GPU): OLMoE-1B-7B geometry bs=1 decode --
 16 MoE layers (E=64, H=2048, I=1024, top-8 softmax router), random-init NF4
 experts (N(0, 0.02) bf16 weights quantized on the device). One step = one
 decode token through all 16 MoE layers (router + fused expert layer each),
@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -140,6 +141,27 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def config_of(args, wl, world):
+    """The line's ``config``: the workload and its geometry only, so both arms print the same dict."""
+    E, H, I, k = wl["E"], wl["H"], wl["I"], wl["k"]
+    per_el = 1.0 if wl.get("fmt") == "fp8" else 0.5 + 4 / 64
+    c = {"workload": args.workload, "desc": wl["desc"], "tokens_per_layer": wl["T"], "layers": wl["layers"],
+         "experts": E, "hidden": H, "intermediate": I, "top_k": k, "lora_rank": wl["lora"],
+         "weights": "fp8 e4m3 128x128" if wl.get("fmt") == "fp8" else "nf4 blocksize 64"}
+    if wl.get("ep"):
+        c["tokens_per_rank"] = wl["T"] // world
+        c["parallelism"] = f"ep{world}" if world > 1 else "single-gpu"
+        c["l2"] = ("inputs larger than L2: each step reads a %.0f MB layer slice per rank"
+                   % (E * 3 * I * H * per_el / 1e6 / world))
+        c["timing"] = "CUDA events around K steps, max over ranks"
+    else:
+        c["parallelism"] = "replicas" if world > 1 else "single-gpu"
+        c["l2"] = ("inputs larger than L2: a step streams the weights of every expert its tokens pick, "
+                   "at least %.0f MB" % (wl["layers"] * min(E, k * wl["T"]) * 3 * I * H * per_el / 1e6))
+        c["timing"] = "CUDA-graph replay of the step, CUDA events, median of timed K-step blocks, max over ranks"
+    return c
+
+
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -251,26 +273,39 @@ def run_ours(args, wl, world, rank, local):
     for w in range(max(args.warmup, 3)):
         graphs[w % pool].replay()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The timed region: `blocks` repetitions of exactly K replayed steps, each bracketed by a barrier
+    # and a synchronize; the reported time is the median block (min / max beside it), so the clock
+    # sampler sees a long interval while every figure is still a K-step measurement.
+    block_ms = []
     with ClockSampler(dev.index if world == 1 else local) as clocks:
-        if world > 1:  # after every rank's sampler is up, so all ranks enter the region together
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
         clock_mark = max(0, clocks.mark() - 1)  # the sample just before the region, and those during it
-        start.record()
-        for s in range(args.steps):
-            graphs[s % pool].replay()
-        end.record()
-        torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
-    if world > 1:
-        t_ = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t_.item())
+        blocks = args.blocks if args.blocks > 0 else 1
+        b_ = 0
+        while b_ < blocks:
+            b_ += 1
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            for s_ in range(args.steps):
+                graphs[s_ % pool].replay()
+            end.record()
+            torch.cuda.synchronize()
+            ms_b = start.elapsed_time(end)
+            if world > 1:
+                t_ = torch.tensor([ms_b], device=dev)
+                torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
+                ms_b = float(t_.item())
+            block_ms.append(ms_b)
+            if args.blocks <= 0 and b_ == 1:  # auto: about one second of timed blocks, 5 to 200 of them
+                blocks = int(min(200, max(5, math.ceil(1000.0 / max(ms_b, 1e-3)))))
+    ms = statistics.median(block_ms)
     units = args.steps * T * Lc * world
     value = units / (ms / 1e3)
 
     # --- per-stage kernel times, live, from event nodes inside replayed graphs ----
+    # (multi-kernel paths only: the stage boundaries of the one-launch kernels are inside one launch)
     cudart = _cudart()
     ev = [[_RawEvent(cudart) for _ in range(nstage)] for _ in range(Lc)]
     gt = torch.cuda.CUDAGraph()
@@ -308,37 +343,49 @@ def run_ours(args, wl, world, rank, local):
     path = ops.moe_path(wl["E"], H, wl["I"], wl["k"], T, lora_rank=wl["lora"])
     one_launch = path == N.PATH_DECODE_LAYER
     if one_launch:
-        # router + whole layer in one kernel (stage marks 1..6 follow it): its interval is mark 0 -> 1
-        layer_us = stage_avg_us["permute"]
+        # router + whole layer in one kernel, the only launch of the step: its time per launch is
+        # the driver-timed step time over the layers (kernel time x launches <= ms_per_step)
+        layer_us = 1e3 * ms / args.steps / Lc
         bound, unit = "hbm", "GB/s"
         gu_bytes += wl["E"] * H * 2  # the router weights the same launch reads
         achieved = (gu_bytes + dn_bytes) / (layer_us * 1e-6) / 1e9
         peak = peaks["hbm_gbs"]
+        kernel_us = layer_us
+        stage_report = {"decode_layer": round(layer_us, 3)}
     elif wl["T"] <= 16:
         bound, unit = "hbm", "GB/s"
         achieved = gu_bytes / (stage_avg_us["gate_up"] * 1e-6) / 1e9
         peak = peaks["hbm_gbs"]
+        kernel_us = stage_avg_us["gate_up"]
+        stage_report = {k_: round(v, 3) for k_, v in stage_avg_us.items()}
     else:
         bound, unit = "tensor", "TFLOP/s"
         flops = 2.0 * T * k * H * n1
         achieved = flops / (stage_avg_us["gate_up"] * 1e-6) / 1e12
         peak = peaks["bf16_tflops"]
+        kernel_us = stage_avg_us["gate_up"]
+        stage_report = {k_: round(v, 3) for k_, v in stage_avg_us.items()}
+    kname = {"olmoe-decode": "nf4_decode_flow_kernel"}.get(args.workload, "nf4 grouped gate_up (SwiGLU fused)")
     roofline = {"bound": bound,
-                "kernel": ("nf4 decode step, one launch: router + permute + gate_up GEMV (SwiGLU) + down GEMV + combine"
-                           if one_launch else "nf4 grouped gate_up (SwiGLU fused)"),
+                "kernel": ("%s: router + permute + gate_up GEMV (SwiGLU) + down GEMV + combine, one launch per "
+                           "layer" % kname if one_launch else "nf4 grouped gate_up (SwiGLU fused)"),
                 "achieved": round(achieved, 1),
-                "peak": peak, "peak_source": peak_kind, "unit": unit, "frac": round(achieved / peak, 4),
+                "peak": peak, "peak_source": peak_kind + (" (MEASURED_PEAKS.json)" if peak_kind == "measured" else ""),
+                "unit": unit, "frac": round(achieved / peak, 4),
                 "traffic": (MEASURED_TRAFFIC[args.workload]["bytes"] if args.workload in MEASURED_TRAFFIC else None),
                 "traffic_source": (MEASURED_TRAFFIC[args.workload]["source"] if args.workload in MEASURED_TRAFFIC
                                    else None),
                 "algorithmic_bytes_per_launch": int(gu_bytes + dn_bytes) if one_launch else int(gu_bytes),
-                "kernel_us": round(stage_avg_us["permute"] if one_launch else stage_avg_us["gate_up"], 3),
-                "down_kernel_us": round(stage_avg_us["down"], 3),
+                "kernel_us": round(kernel_us, 3),
+                "kernel_us_source": ("ms_per_step / layers (the step is one launch per layer)" if one_launch
+                                     else "event-record nodes around the kernel in a replayed graph"),
+                "down_kernel_us": None if one_launch else round(stage_avg_us["down"], 3),
                 "down_achieved": (round(dn_bytes / (stage_avg_us["down"] * 1e-6) / 1e9, 1)
                                   if bound == "hbm" and not one_launch else None),
                 "layer_bytes": int(gu_bytes + dn_bytes + wl["E"] * H * 2),
-                "stage_us": {k_: round(v, 3) for k_, v in stage_avg_us.items()},
-                "event_node_us_subtracted": round(node_us, 3)}
+                "stage_us": stage_report}
+    if not one_launch:
+        roofline["event_node_us_subtracted"] = round(node_us, 3)
 
     # --- e2e through the public API: pinned H2D in, eager calls, D2H out ----------
     e2e = run_e2e(pkg, layers, wl, dev, args, X) if not args.skip_e2e else {"ms": float("nan"), "h2d": 0, "d2h": 0}
@@ -355,18 +402,15 @@ def run_ours(args, wl, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init N(0,0.02) weights quantized to NF4; N(0,1) tokens)",
-        "config": {"workload": args.workload, "desc": wl["desc"], "tokens_per_layer": T, "layers_per_step": Lc,
-                   "experts": wl["E"], "hidden": H, "intermediate": I, "top_k": k, "lora_rank": wl["lora"],
-                   "parallelism": "replicas" if world > 1 else "single-gpu",
-                   "l2": "inputs larger than L2: each step touches %.0f MB of expert weights" %
-                         (Lc * (gu_bytes + dn_bytes) / 1e6),
-                   "timing": "CUDA-graph replay of the step, CUDA events, max over ranks"},
+        "config": config_of(args, wl, world),
         "model_tokens_per_s": round(value / Lc, 1),
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "path": "public API (route + enable_fast module call), eager"},
         "gpu_launches": launches_per_layer * Lc * args.steps,
         "clocks": clocks.summary(since=clock_mark),
+        "timed_blocks": {"n": blocks, "steps_each": args.steps, "ms_min": round(min(block_ms), 4),
+                         "ms_median": round(ms, 4), "ms_max": round(max(block_ms), 4)},
         "unique_experts_per_layer": round(mean_uniq, 2),
     }
     if rank == 0 and args.cpu_seconds > 0:
@@ -727,16 +771,11 @@ def run_ep(args, wl, world, rank, local):
         "data": "synthetic (random-init N(0,0.02) weights quantized to %s; N(0,1) tokens; %s)" % (
             "FP8 e4m3 with e8m0 128x128 scales" if wl.get("fmt") == "fp8" else "NF4",
             "routes sampled from Zipf(1.1) expert popularity" if wl.get("routing") == "zipf" else "random router"),
-        "config": {"workload": args.workload, "desc": wl["desc"], "tokens_per_layer": wl["T"],
-                   "tokens_per_rank": T, "layers_cycled": Lc, "experts": E, "hidden": H, "intermediate": I,
-                   "top_k": k, "parallelism": f"ep{world}" if world > 1 else "single-gpu",
-                   "micro_batches": args.micro_batches or "default",
-                   "launch": "one CUDA graph per layer step, replayed" if graphs is not None else "eager",
-                   "exchange": ("peer-memory stores (CUDA IPC over NVLink)" if peer else
-                                "NCCL all-to-all" if world > 1 else "none (one rank)"),
-                   "l2": "inputs larger than L2: each step reads a %.0f MB layer slice per rank" %
-                         (layer_gb * 1e3 / world),
-                   "timing": "CUDA events around K eager steps, max over ranks"},
+        "config": config_of(args, wl, world),
+        "run": {"micro_batches": args.micro_batches or "default",
+                "launch": "one CUDA graph per layer step, replayed" if graphs is not None else "eager",
+                "exchange": ("peer-memory stores (CUDA IPC over NVLink)" if peer else
+                             "NCCL all-to-all" if world > 1 else "none (one rank)")},
         "roofline": roofline,
         "e2e": {"value": round(e2e_steps * wl["T"] / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2 * world, "d2h_bytes_per_step": T * H * 2 * world,
@@ -747,6 +786,32 @@ def run_ep(args, wl, world, rank, local):
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         result["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
     return result
+
+
+def prefill_record(args, world, rank, local):
+    """Config 3 (Qwen3 geometry, T=4096, LoRA r=16) timed in the same run: the prefill regime's
+    tensor-core figures beside the decode headline. Bounded: a few layers, 10 steps."""
+    import copy
+    a2 = copy.copy(args)
+    a2.workload, a2.steps, a2.warmup, a2.blocks = "qwen3-prefill", min(args.steps, 10), 3, 5
+    a2.skip_e2e, a2.cpu_seconds = True, 0.0
+    wl = dict(WORKLOADS["qwen3-prefill"])
+    r = run_ours(a2, wl, world, rank, local)
+    E, H, I, k, T, lr = wl["E"], wl["H"], wl["I"], wl["k"], wl["T"], wl["lora"]
+    R = T * k
+    layer_flops = 2.0 * R * H * 2 * I + 2.0 * R * I * H + 2.0 * R * lr * (H + 2 * I) + 2.0 * R * lr * (I + H)
+    layer_ms = r["ms_per_step"] / wl["layers"]
+    peaks, peak_kind = load_peaks()
+    ach = layer_flops / (layer_ms * 1e-3) / 1e12
+    torch.cuda.empty_cache()
+    return {"workload": "qwen3-prefill", "desc": wl["desc"], "value": r["value"], "unit": "tokens/s",
+            "ms_per_layer": round(layer_ms, 4), "roofline": r["roofline"],
+            "layer_tensor": {"bound": "tensor", "achieved": round(ach, 1), "peak": peaks["bf16_tflops"],
+                             "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
+                             "flops_per_layer": layer_flops,
+                             "what": "all of the layer (permute, LoRA-A, both grouped GEMMs, combine) over "
+                                     "its dense FLOPs, base + adapters"},
+            "clocks": r["clocks"], "timed_blocks": r["timed_blocks"]}
 
 
 def _cudart():
@@ -873,7 +938,7 @@ def run_reference(args, wl, rank):
     return {"metric": "MoE-layer tokens/s", "value": cb["value"], "unit": "tokens/s", "impl": "reference",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic", "config": {"workload": args.workload, "desc": wl["desc"]},
+            "data": "synthetic", "config": config_of(args, wl, int(os.environ.get("WORLD_SIZE", "1"))),
             "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
 
@@ -895,10 +960,18 @@ def main():
     ap.add_argument("--exchange", choices=["auto", "peer", "nccl"], default="auto",
                     help="expert-parallel exchange: peer-memory stores or NCCL all-to-alls")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the public-API e2e leg (profiling)")
+    ap.add_argument("--blocks", type=int, default=0,
+                    help="timed blocks of K steps (median reported); 0 = enough blocks for about one second")
+    ap.add_argument("--prefill-record", type=int, default=1,
+                    help="with the default decode workload on one GPU, also time config 3 (Qwen3 prefill) "
+                         "and add it as the line's `prefill` record")
     args = ap.parse_args()
     if args.workload == "auto":
-        world_env = int(os.environ.get("WORLD_SIZE", "1"))
-        args.workload = "mixtral-ep" if max(world_env, args.gpus) > 1 else "olmoe-decode"
+        # Under torch.distributed.run (WORLD_SIZE set, the driver's scaling series) every N, N=1
+        # included, runs the expert-parallel Mixtral layer, so the series compares one workload; a
+        # plain one-GPU run is the OLMoE decode step (config 2), the headline line.
+        launched = "WORLD_SIZE" in os.environ
+        args.workload = "mixtral-ep" if (launched or args.gpus > 1) else "olmoe-decode"
     wl = dict(WORKLOADS[args.workload])
     if args.layers:
         wl["layers"] = args.layers
@@ -910,6 +983,8 @@ def main():
         return
     world, rank, local = dist_setup(args.gpus)
     res = (run_ep if wl.get("ep") else run_train if wl.get("train") else run_ours)(args, wl, world, rank, local)
+    if args.workload == "olmoe-decode" and world == 1 and args.prefill_record:
+        res["prefill"] = prefill_record(args, world, rank, local)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -13,6 +13,7 @@ it is also registered as ``experts4bit_qlora_b200``.
 import sys as _sys
 
 from . import _native, ep, mxfp4, ops  # noqa: F401
+from ._native import check_errors
 from .experts import Experts4bit, ExpertsNbit, normalize_quant_type
 from .fast import disable_fast, enable_fast, fast_available
 from .fp8_experts import ExpertsFp8Blocks
@@ -20,12 +21,16 @@ from .ep import ExpertParallelMoE, PeerExchange, shard_experts
 from .lora import ExpertsLoRA
 from .train import disable_fast_train, enable_fast_train
 from .router import route, TopKRouter
+from .residency import (disable_hot_residency, disable_pipelined_residency, dispatched_modules,
+                        enable_hot_residency, enable_pipelined_residency, target_modules)
 
 __version__ = "0.1.0"
 
 __all__ = [
     "Experts4bit", "ExpertsNbit", "ExpertsLoRA", "enable_fast", "disable_fast", "fast_available",
-    "normalize_quant_type", "enable_fast_train", "disable_fast_train", "route", "TopKRouter", "ops", "ExpertParallelMoE", "PeerExchange", "shard_experts", "ExpertsFp8Blocks",
+    "normalize_quant_type", "check_errors", "enable_fast_train", "disable_fast_train", "route", "TopKRouter", "ops", "ExpertParallelMoE", "PeerExchange", "shard_experts", "ExpertsFp8Blocks",
+    "enable_hot_residency", "disable_hot_residency", "enable_pipelined_residency", "disable_pipelined_residency",
+    "target_modules", "dispatched_modules",
 ]
 
 _sys.modules.setdefault("experts4bit_qlora_b200", _sys.modules[__name__])

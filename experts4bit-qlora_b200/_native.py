@@ -17,13 +17,14 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libe4b.so")
 
 E4B_OK = 0
 E4B_ERR_EXPERT_INDEX = 6
+E4B_ERR_RANGE = 7
 E4B_ERR_TIMEOUT = 8
 BF16, F16, F32 = 0, 1, 2
 SOFTMAX_THEN_TOPK, TOPK_THEN_SOFTMAX = 0, 1
 EPI_NONE, EPI_SWIGLU, EPI_SILU = 0, 1, 2
 FMT_NF4, FMT_FP8_BLOCK128 = 0, 1
 PATH_STREAMING, PATH_TENSOR_CORE, PATH_DECODE_LAYER = 0, 1, 2
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # Every symbol include/e4b.h exports, in declaration order.
 EXPORTED_SYMBOLS = (
@@ -43,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "e4b_ep_comm_bytes", "e4b_ipc_export", "e4b_ipc_open", "e4b_ipc_close",
     "e4b_ep_dispatch_peer_workspace_bytes", "e4b_ep_dispatch_peer",
     "e4b_ep_experts_peer_workspace_bytes", "e4b_ep_experts_peer", "e4b_ep_combine_peer",
+    "e4b_gather_expert_rows",
     "e4b_selftest_wait_timeout",
     "e4b_read_device_error",
 )
@@ -62,13 +64,14 @@ class MoeDesc(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in (
         "num_experts", "hidden", "intermediate", "top_k", "tokens", "has_gate", "act_dtype",
         "weight_dtype", "out_dtype", "lora_rank", "lora_dtype")] + [("lora_scaling", ctypes.c_float),
-                                                                     ("weight_format", ctypes.c_int)]
+                                                                     ("weight_format", ctypes.c_int),
+                                                                     ("routed_experts", ctypes.c_int)]
 
 
 class MoeTensors(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "hidden", "topk_idx", "topk_w", "gate_up_packed", "gate_up_absmax", "down_packed", "down_absmax",
-        "gate_up_lora_A", "gate_up_lora_B", "down_lora_A", "down_lora_B", "out", "stage_events")]
+        "gate_up_lora_A", "gate_up_lora_B", "down_lora_A", "down_lora_B", "out", "stage_events", "expert_map")]
 
 MOE_STAGE_EVENTS = 7
 IPC_HANDLE_BYTES = 64
@@ -124,6 +127,7 @@ def _declare(lib):
         "e4b_ep_experts_peer": (I, [ctypes.POINTER(EpPeerDesc), ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors),
                                     P, SZ, P]),
         "e4b_ep_combine_peer": (I, [ctypes.POINTER(EpPeerDesc), P, P, I, I, I, P, I, P]),
+        "e4b_gather_expert_rows": (I, [P, I, P, P, I, P, I, P, P, P, P, P, SZ, P]),
         "e4b_selftest_wait_timeout": (I, [P, SZ, P]),
         "e4b_read_device_error": (I, [P, P, ctypes.POINTER(I)]),
     }
@@ -199,18 +203,29 @@ class _Workspaces:
     Reusing a buffer keeps its address stable across calls, which CUDA-graph
     replay needs. Calls on one device that share a purpose must be
     stream-ordered (the library is stream-ordered; this cache is not a pool).
+
+    Buffers start zero-filled: the library's workspace header (the sticky
+    error word and the decode kernel's counter block) must be zero before its
+    first use, and the library leaves it that way. A buffer that is outgrown
+    is kept alive, not freed: a CUDA graph captured before the growth still
+    writes to it on every replay.
     """
 
     def __init__(self):
         self._bufs: dict[tuple[int, str], torch.Tensor] = {}
+        self._retired: list[torch.Tensor] = []
+        self._lock = threading.Lock()
 
     def get(self, device: torch.device, nbytes: int, purpose: str = "moe") -> torch.Tensor:
         key = (device.index if device.index is not None else torch.cuda.current_device(), purpose)
-        buf = self._bufs.get(key)
-        if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
-            self._bufs[key] = buf
-        return buf
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                if buf is not None:
+                    self._retired.append(buf)
+                buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+                self._bufs[key] = buf
+            return buf
 
 
 workspaces = _Workspaces()
@@ -221,3 +236,57 @@ def read_device_error(ws: torch.Tensor) -> int:
     check(lib().e4b_read_device_error(ws.data_ptr(), stream_handle(ws.device), ctypes.byref(out)),
           "e4b_read_device_error")
     return out.value
+
+
+class _ErrorWatch:
+    """Surfaces the sticky device error word of a workspace without a per-call host sync.
+
+    After a call, a 4-byte asynchronous copy of the word goes to pinned host memory behind an
+    event; the next call on the same workspace looks at that copy once its event has completed
+    and, if an error was recorded, reads and clears the word (one sync, only then) and raises.
+    ``check_errors()`` synchronises and raises at once. Calls inside a CUDA-graph capture are
+    not watched (a capture cannot record host reads).
+    """
+
+    def __init__(self):
+        self._w: dict[int, tuple[torch.Tensor, torch.Tensor, object]] = {}
+        self._lock = threading.Lock()
+
+    def before(self, ws: torch.Tensor, what: str) -> None:
+        ent = self._w.get(ws.data_ptr())
+        if ent is None:
+            return
+        host, _, ev = ent
+        if ev.query() and int(host[0]) != 0:
+            self.raise_if_set(ws, what)
+
+    def after(self, ws: torch.Tensor) -> None:
+        if torch.cuda.is_current_stream_capturing():
+            return
+        with self._lock:
+            ent = self._w.get(ws.data_ptr())
+            if ent is None:
+                ent = (torch.zeros(1, dtype=torch.int32, pin_memory=True), ws, torch.cuda.Event())
+                self._w[ws.data_ptr()] = ent
+        host, _, ev = ent
+        host.copy_(ws[:4].view(torch.int32), non_blocking=True)
+        ev.record()
+
+    def raise_if_set(self, ws: torch.Tensor, what: str) -> None:
+        err = read_device_error(ws)
+        if err:
+            raise E4BError(err, what + " (device error recorded by an earlier call on this workspace)")
+
+    def check_all(self) -> None:
+        for ws_ptr, (host, ws, ev) in list(self._w.items()):
+            ev.synchronize()
+            self.raise_if_set(ws, "check_errors")
+
+
+error_watch = _ErrorWatch()
+
+
+def check_errors() -> None:
+    """Synchronise and raise ``E4BError`` if any watched workspace holds a device error."""
+    error_watch.check_all()
+

@@ -17,8 +17,11 @@ static __constant__ float c_nf4[16] = {
     0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
     0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
 
-// Device error word: first 4 bytes of every workspace the library is given.
-constexpr size_t kErrBytes = 256;
+// Workspace header: the device error word (first 4 bytes, sticky: set by the first error, cleared
+// only by e4b_read_device_error), a few words some entry points use, and at kFlowSyncOffset the
+// counter block of the flow decode kernel (zero when idle). Every layout starts after it.
+constexpr size_t kErrBytes = 1024;
+constexpr size_t kFlowSyncOffset = 512;
 
 __device__ __forceinline__ void raise_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
@@ -65,6 +68,26 @@ template <> __device__ __forceinline__ __half store_cast<__half>(float v, int* e
     v = copysignf(65504.f, v);
   }
   return __float2half_rn(v);
+}
+
+// Stack index of a routed expert id. Without a map the id indexes the [E, ...] stacks directly;
+// with one (a resident sub-stack), ids lie in [0, routed) and map[id] is the expert's index in the
+// stacks (-1: not resident). Ids that land outside [0, E) are clamped for memory safety and
+// reported as E4B_ERR_EXPERT_INDEX when `report`.
+__device__ __forceinline__ int stack_expert(int64_t raw, const int32_t* map, int routed, int E, int* err,
+                                            bool report) {
+  if (map) {
+    if (raw < 0 || raw >= routed) {
+      if (report) raise_error(err, E4B_ERR_EXPERT_INDEX);
+      return raw < 0 ? 0 : E - 1;
+    }
+    raw = map[raw];
+  }
+  if (raw < 0 || raw >= E) {
+    if (report) raise_error(err, E4B_ERR_EXPERT_INDEX);
+    return raw < 0 ? 0 : E - 1;
+  }
+  return (int)raw;
 }
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + __expf(-g)); }

@@ -19,9 +19,12 @@
 // kernel's, so the result equals the multi-kernel path bit for bit. Copy waits
 // are bounded (a timeout raises E4B_ERR_TIMEOUT and the kernel runs to its end);
 // the grid barriers are cooperative-launch grid syncs that every CTA reaches.
-// Errors are collected per CTA and folded into the workspace's error word by
-// CTA 0 after the last barrier, so each call reports its own errors.
+// Errors are collected per CTA and folded into the workspace's (sticky) error word
+// by CTA 0 after the last barrier.
 #include <cooperative_groups.h>
+
+#include <atomic>
+#include <mutex>
 
 #include "convert.cuh"
 #include "decode_layer.cuh"
@@ -113,6 +116,8 @@ struct DecodeArgs {
   const int64_t* topk_idx;
   const void* topk_w;
   int w_dtype;
+  const int32_t* emap;  // optional routed id -> stack index
+  int routed;
   const uint8_t* gu_packed;
   const float* gu_absmax;
   const uint8_t* dn_packed;
@@ -506,12 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     DTRACE(16);
   } else if (tid < R) {
-    int64_t e = a.topk_idx[tid];
-    if (e < 0 || e >= a.E) {
-      if (blockIdx.x == 0) atomicCAS(&tb.misc[1], 0, E4B_ERR_EXPERT_INDEX);
-      e = e < 0 ? 0 : a.E - 1;
-    }
-    tb.pick_e[tid] = (int)e;
+    int* errw = &tb.misc[1];
+    tb.pick_e[tid] = stack_expert(a.topk_idx[tid], a.emap, a.routed, a.E, blockIdx.x == 0 ? errw : nullptr,
+                                  blockIdx.x == 0);
     tb.w[tid] = load_as_f32(a.topk_w, a.w_dtype, tid);
   }
   __syncthreads();
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = tid; b < (int)gridDim.x; b += kThreads)
       if (a.cta_err[b]) atomicMin(&tb.misc[7], b);
     __syncthreads();
-    if (tid == 0) *a.err = tb.misc[7] == 0x7fffffff ? 0 : a.cta_err[tb.misc[7]];
+    if (tid == 0 && tb.misc[7] != 0x7fffffff) atomicCAS(a.err, 0, a.cta_err[tb.misc[7]]);  // sticky word
   };
   fold_errors();
 
@@ -700,18 +702,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   DTRACE(9);
 }
 
-int g_decode_enabled = -1;  // -1: not yet read from E4B_DECODE_KERNEL
-
 }  // namespace
 
+// One-launch decode kernels: 0 off (multi-kernel path), 1 the flow kernel where it applies and the
+// phase kernel elsewhere, 2 the phase kernel only. -1: not yet read from E4B_DECODE_KERNEL.
+std::atomic<int> g_decode_mode{-1};
+
+int decode_mode() {
+  int m = g_decode_mode.load(std::memory_order_relaxed);
+  if (m < 0) {
+    const char* v = getenv("E4B_DECODE_KERNEL");
+    const int env = v ? (v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1) : 1;
+    int expected = -1;
+    g_decode_mode.compare_exchange_strong(expected, env);
+    m = g_decode_mode.load(std::memory_order_relaxed);
+  }
+  return m;
+}
+
 size_t decode_layer_sync_bytes(int grid) { return (size_t)grid * sizeof(int); }
+
+static std::mutex g_dl_mu;  // guards the per-device caches below
 
 static int sm_count_cached() {
   static int sms[64] = {0};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  if (!sms[dev & 63]) cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
-  return sms[dev & 63];
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lk(g_dl_mu);
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  return sms[dev];
 }
 
 int decode_layer_grid() { return sm_count_cached(); }
@@ -719,11 +738,7 @@ int decode_layer_grid() { return sm_count_cached(); }
 bool decode_router_fusable(const e4b_moe_desc& d) { return (int64_t)d.tokens * d.num_experts <= kMaxLogits; }
 
 bool decode_layer_eligible(const e4b_moe_desc& d) {
-  if (g_decode_enabled < 0) {
-    const char* v = getenv("E4B_DECODE_KERNEL");
-    g_decode_enabled = (v && v[0] == '0') ? 0 : 1;
-  }
-  if (!g_decode_enabled) return false;
+  if (decode_mode() == 0) return false;
   if (d.weight_format != E4B_FMT_NF4 || d.lora_rank != 0) return false;
   if (d.tokens < 1 || d.tokens > 16 || (int64_t)d.tokens * d.top_k > kMaxPicks) return false;
   if (d.hidden % 256 || d.intermediate % 256) return false;
@@ -740,9 +755,10 @@ template <typename OutT, int NT>
 static e4b_status launch_decode(const DecodeArgs& a, cudaStream_t s) {
   static unsigned long long configured = 0;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return E4B_ERR_CUDA;
-  const unsigned long long bit = 1ull << (dev & 63);
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return E4B_ERR_CUDA;
+  const unsigned long long bit = 1ull << dev;
   auto kern = nf4_decode_layer_kernel<OutT, NT>;
+  std::lock_guard<std::mutex> lk(g_dl_mu);
   if (!(configured & bit)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DSmem::total) != cudaSuccess)
       return E4B_ERR_CUDA;
@@ -806,6 +822,8 @@ e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, 
   a.act_dtype = d.act_dtype;
   a.topk_idx = t->topk_idx;
   a.topk_w = t->topk_w;
+  a.emap = t->expert_map;
+  a.routed = d.routed_experts;
   a.w_dtype = router ? E4B_F32 : d.weight_dtype;
   a.gu_packed = static_cast<const uint8_t*>(t->gate_up_packed);
   a.gu_absmax = static_cast<const float*>(t->gate_up_absmax);
@@ -833,8 +851,8 @@ e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, 
 
 }  // namespace e4b
 
-extern "C" E4B_API int e4b_set_decode_kernel(int enabled) {
-  const int prev = e4b::g_decode_enabled;
-  e4b::g_decode_enabled = enabled ? 1 : 0;
+extern "C" E4B_API int e4b_set_decode_kernel(int mode) {
+  const int prev = e4b::decode_mode();
+  e4b::g_decode_mode.store(mode == 0 ? 0 : mode == 2 ? 2 : 1);
   return prev;
 }

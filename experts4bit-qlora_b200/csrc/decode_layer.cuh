@@ -22,6 +22,19 @@ struct DecodeRouter {
   float* logits;  // [T, E] fp32 scratch in global memory: logits computed across the grid (null: per CTA)
 };
 bool decode_router_fusable(const e4b_moe_desc& d);
+
+// 0 off, 1 flow kernel where it applies (else the phase kernel), 2 phase kernel only.
+int decode_mode();
+
+// The flow kernel (decode_flow.cu): the layer for 1..8 tokens and at most kFlowMaxPicks picks,
+// NF4, no adapters, H and I multiples of 256. `sync` is the workspace's counter block at
+// kFlowSyncOffset ((kFlowMaxPicks + 1) words, zero before the first launch, left zero by every
+// launch); h is [T*k, I] fp16 scratch. With `router`, the router runs inside the launch (its
+// logits never leave the thread-block cluster) and writes topk_idx / topk_w.
+constexpr int kFlowMaxPicks = 64;
+bool decode_flow_eligible(const e4b_moe_desc& d, bool fused_router);
+e4b_status launch_decode_flow(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* sync, int* err,
+                              cudaStream_t s, const DecodeRouter* router = nullptr);
 e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,
                                void* sync, int* err, cudaStream_t s, const DecodeRouter* router = nullptr);
 

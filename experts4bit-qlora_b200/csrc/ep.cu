@@ -294,7 +294,7 @@ extern "C" e4b_status e4b_ep_dispatch(const void* hidden, int act_dtype, const i
   pa.tile_a = kLoraRows;
   pa.tile_b = kUmmaTokens;
   pa.err = reinterpret_cast<int*>(ws);
-  pa.reset_err = 1;
+  pa.reset_err = 0;  // the error word is sticky: only e4b_read_device_error clears it
   e4b_status st = launch_permute(pa, s);
   if (st != E4B_OK) return st;
   const int R = T * k;
@@ -757,8 +757,8 @@ extern "C" e4b_status e4b_ep_dispatch_peer(const e4b_ep_peer_desc* pd, const voi
   pa.offsets = offsets;
   pa.tile_a = kLoraRows;
   pa.tile_b = kUmmaTokens;
-  pa.err = reinterpret_cast<int*>(own);  // the region's error word, cleared here once per layer
-  pa.reset_err = 1;
+  pa.err = reinterpret_cast<int*>(own);  // the region's error word
+  pa.reset_err = 0;  // the error word is sticky: only e4b_read_device_error clears it
   e4b_status st = launch_permute(pa, s);
   if (st != E4B_OK) return st;
   PushArgs a{};

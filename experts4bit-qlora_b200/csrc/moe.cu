@@ -303,6 +303,7 @@ static bool desc_ok(const e4b_moe_desc& d) {
   if (d.num_experts <= 0 || d.num_experts > 1024 || d.hidden <= 0 || d.intermediate <= 0) return false;
   if (d.top_k <= 0 || d.top_k > 32 || d.top_k > d.num_experts || d.tokens < 0) return false;
   if ((int64_t)d.tokens * d.top_k > (1 << 30)) return false;
+  if (d.routed_experts < 0 || d.routed_experts > (1 << 24)) return false;
   return true;
 }
 
@@ -327,7 +328,7 @@ extern "C" const char* e4b_status_string(e4b_status s) {
   return "unknown status";
 }
 
-extern "C" int e4b_abi_version(void) { return 3; }
+extern "C" int e4b_abi_version(void) { return 4; }
 
 extern "C" e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out) {
   if (!workspace || !error_out) return E4B_ERR_INVALID_ARG;
@@ -423,6 +424,7 @@ extern "C" e4b_status e4b_moe_decode_step(const e4b_moe_desc* desc, const e4b_mo
                                           float* topk_w, void* workspace, size_t workspace_bytes, void* stream) {
   if (!desc || !t || !desc_ok(*desc)) return E4B_ERR_INVALID_ARG;
   if (!router_w || !topk_idx || !topk_w) return E4B_ERR_INVALID_ARG;
+  if (t->expert_map || desc->routed_experts) return E4B_ERR_UNSUPPORTED;  // the router scores every stack row
   if (!is_any_dtype(router_w_dtype)) return E4B_ERR_UNSUPPORTED;
   if (kind != E4B_SOFTMAX_THEN_TOPK && kind != E4B_TOPK_THEN_SOFTMAX) return E4B_ERR_INVALID_ARG;
   const size_t need = e4b_moe_decode_step_workspace_bytes(desc);
@@ -437,9 +439,20 @@ extern "C" e4b_status e4b_moe_decode_step(const e4b_moe_desc* desc, const e4b_mo
   const size_t layer_bytes = align_up(moe_layout(d).total, 256);
   char* rws = ws + layer_bytes;
   cudaStream_t s = (cudaStream_t)stream;
-  if (d.tokens > 0 && decode_layer_eligible(d) && decode_router_fusable(d) && t->hidden && t->out && t->gate_up_packed && t->gate_up_absmax &&
-      t->down_packed && t->down_absmax && aligned16(t->hidden) && aligned16(t->out) && aligned16(t->gate_up_packed) &&
-      aligned16(t->down_packed) && is_act_dtype(d.act_dtype) && is_any_dtype(d.out_dtype)) {
+  const bool tensors_ok = t->hidden && t->out && t->gate_up_packed && t->gate_up_absmax && t->down_packed &&
+                          t->down_absmax && aligned16(t->hidden) && aligned16(t->out) &&
+                          aligned16(t->gate_up_packed) && aligned16(t->down_packed) &&
+                          aligned16(t->gate_up_absmax) && aligned16(t->down_absmax) && is_act_dtype(d.act_dtype) &&
+                          is_any_dtype(d.out_dtype);
+  if (d.tokens > 0 && tensors_ok && decode_flow_eligible(d, true)) {
+    const MoeLayout L = moe_layout(d);
+    DecodeRouter r{router_w, router_w_dtype, kind, norm_topk_prob, topk_idx, topk_w, nullptr};
+    mark_stage(&tt, 0, s);
+    e4b_status st = launch_decode_flow(d, &tt, ws + L.h, ws + kFlowSyncOffset, reinterpret_cast<int*>(ws), s, &r);
+    for (int i = 1; i < E4B_MOE_STAGE_EVENTS; ++i) mark_stage(&tt, i, s);
+    return st;
+  }
+  if (d.tokens > 0 && tensors_ok && decode_layer_eligible(d) && decode_router_fusable(d)) {
     const MoeLayout L = moe_layout(d);
     DecodeRouter r{router_w, router_w_dtype, kind, norm_topk_prob, topk_idx, topk_w,
                    reinterpret_cast<float*>(rws + kErrBytes)};
@@ -459,7 +472,7 @@ extern "C" e4b_status e4b_moe_decode_step(const e4b_moe_desc* desc, const e4b_mo
 extern "C" int e4b_moe_path(const e4b_moe_desc* desc) {
   if (!desc || !desc_ok(*desc)) return -1;
   const e4b_moe_desc& d = *desc;
-  if (decode_layer_eligible(d)) return E4B_PATH_DECODE_LAYER;
+  if (decode_flow_eligible(d, false) || decode_layer_eligible(d)) return E4B_PATH_DECODE_LAYER;
   const int64_t R = (int64_t)d.tokens * d.top_k;
   if (umma_worthwhile(R, d.num_experts) &&
       umma_eligible(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate, d.has_gate, d.act_dtype, d.lora_rank))
@@ -489,6 +502,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     return E4B_ERR_INVALID_ARG;
   if (d.lora_rank > 0 && (!t->gate_up_lora_A || !t->gate_up_lora_B || !t->down_lora_A || !t->down_lora_B))
     return E4B_ERR_INVALID_ARG;
+  if ((d.routed_experts > 0) != (t->expert_map != nullptr)) return E4B_ERR_INVALID_ARG;
   if (!aligned16(t->hidden) || !aligned16(t->gate_up_packed) || !aligned16(t->down_packed) || !aligned16(t->out))
     return E4B_ERR_ALIGNMENT;
   const MoeLayout L = moe_layout(d);
@@ -500,6 +514,11 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   const int R = T * k;
 
   mark_stage(t, 0, s);
+  if (decode_flow_eligible(d, false) && aligned16(t->gate_up_absmax) && aligned16(t->down_absmax)) {
+    e4b_status st = launch_decode_flow(d, t, ws + L.h, ws + kFlowSyncOffset, err, s);  // one launch
+    for (int i = 1; i < E4B_MOE_STAGE_EVENTS; ++i) mark_stage(t, i, s);
+    return st;
+  }
   if (decode_layer_eligible(d)) {  // one launch: permute, both GEMVs and the combine
     e4b_status st = launch_decode_layer(d, t, ws + L.h, ws + L.down_rows, ws + L.sync, err, s);
     for (int i = 1; i < E4B_MOE_STAGE_EVENTS; ++i) mark_stage(t, i, s);
@@ -510,6 +529,8 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   pa.T = T;
   pa.k = k;
   pa.E = E;
+  pa.emap = t->expert_map;
+  pa.routed = d.routed_experts;
   pa.inv = reinterpret_cast<int32_t*>(ws + L.inv);
   pa.sorted_token = reinterpret_cast<int32_t*>(ws + L.sorted_token);
   pa.offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
@@ -520,7 +541,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   pa.tile_a = kLoraRows;
   pa.tile_b = kUmmaTokens;
   pa.err = err;
-  pa.reset_err = 1;
+  pa.reset_err = 0;  // the error word is sticky: only e4b_read_device_error clears it
   __half* x16 = reinterpret_cast<__half*>(ws + L.x16);
   float* x_scale = reinterpret_cast<float*>(ws + L.x_scale);
   pa.conv.src = t->hidden;

@@ -47,12 +47,7 @@ __device__ void permute_one_warp(const PermuteArgs& a) {
   __syncwarp();
   int e = 0x7fffffff;
   if (lane < n) {
-    const int64_t raw = a.topk_idx[lane];
-    e = (int)raw;
-    if (raw < 0 || raw >= E) {
-      raise_error(a.err, E4B_ERR_EXPERT_INDEX);
-      e = raw < 0 ? 0 : E - 1;
-    }
+    e = stack_expert(a.topk_idx[lane], a.emap, a.routed, E, a.err, true);
   }
   const unsigned peers = __match_any_sync(0xffffffffu, e);
   const bool valid = lane < n;
@@ -124,12 +119,7 @@ permute_kernel(PermuteArgs a) {
   constexpr int kCache = 24;
   int ec[kCache];
   auto load_entry = [&](int i, bool flag) -> int {
-    const int64_t raw = a.topk_idx[i];
-    if (raw < 0 || raw >= E) {
-      if (flag) raise_error(a.err, E4B_ERR_EXPERT_INDEX);
-      return raw < 0 ? 0 : E - 1;
-    }
-    return (int)raw;
+    return stack_expert(a.topk_idx[i], a.emap, a.routed, E, a.err, flag);
   };
 #pragma unroll
   for (int it = 0; it < kCache; ++it) {
@@ -244,6 +234,6 @@ extern "C" e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, 
   a.inv = inv;
   a.offsets = offsets;
   a.err = static_cast<int*>(workspace);
-  a.reset_err = 1;
+  a.reset_err = 0;  // the error word is sticky: only e4b_read_device_error clears it
   return launch_permute(a, (cudaStream_t)stream);
 }

@@ -8,6 +8,8 @@ namespace e4b {
 struct PermuteArgs {
   const int64_t* topk_idx;  // [T*k]
   int T, k, E;
+  const int32_t* emap;      // optional routed id -> stack index (see stack_expert)
+  int routed;               // routed ids with a map
   int32_t* order;           // [T*k] sorted row -> flat index (nullable)
   int32_t* inv;             // [T*k] flat index -> sorted row (nullable)
   int32_t* sorted_token;    // [T*k] sorted row -> token (nullable)

@@ -11,9 +11,11 @@ storage). The fused forward itself is one ``e4b_moe_forward`` call: device
 permutation, grouped NF4 GEMMs with SwiGLU and LoRA fused, deterministic
 combine -- no host synchronisation, so it can be captured in a CUDA graph.
 
-The kernel's epilogue is SiLU(gate)*up (or SiLU for ``has_gate=False``); a base
-with another activation or an ``_apply_gate`` hook is reported ineligible and
-keeps its reference forward.
+The fused kernels' epilogue is SiLU(gate)*up (or SiLU for ``has_gate=False``). A
+base with another activation or an ``_apply_gate`` hook (a clamped SwiGLU, say)
+takes the epilogue route, as the reference does (engines/fast.py:137-156, :320-347):
+the grouped gate_up GEMM without an epilogue, the base's own ``_epilogue`` in
+torch, the grouped down GEMM, the fixed-order combine.
 """
 from __future__ import annotations
 
@@ -66,11 +68,49 @@ def _eligible(mod) -> Optional[str]:
         return "more than 1024 experts"
     if not mod.gate_up_proj.is_cuda:
         return "storage not on CUDA"
-    if hasattr(mod, "_apply_gate"):
-        return "custom activation hook (_apply_gate) is not fused by this kernel"
-    if getattr(mod, "act_fn", None) is not torch.nn.functional.silu:
-        return "activation is not SiLU"
     return None
+
+
+def _fused_epilogue(base) -> bool:
+    """Whether the kernels' own epilogue is the base's: SiLU(gate)*up / SiLU, no hook."""
+    return not hasattr(base, "_apply_gate") and getattr(base, "act_fn", None) is torch.nn.functional.silu
+
+
+def _run_epilogue_route(base, hs, top_k_index, top_k_weights, input_dtype, wrapper=None):
+    """The layer for a base whose activation the kernels do not fuse (``fast.py:137-156`` and
+    ``:214-257``): device permutation, grouped gate_up GEMM without an epilogue (+ the adapter's
+    delta), the base's own ``_epilogue``, grouped down GEMM (+ delta), the fixed-order combine."""
+    from .lora import _epilogue
+    T, H = hs.shape
+    k = top_k_index.shape[1]
+    E = base.num_experts
+    n1, _ = base._gate_up_shape
+    n2, k2 = base._down_shape
+    idx = top_k_index.long().contiguous()
+    order, inv, offsets = ops.permute(idx, E)
+    rows = torch.div(order, k, rounding_mode="floor")  # source token of every expert-sorted row
+    up = ops.grouped_nf4_gemm(hs, base.gate_up_proj.view(E, n1, H // 2), base.gate_up_absmax.view(E, n1, H // 64),
+                              offsets, a_rows=rows)
+    sizes = None
+    if wrapper is not None:  # the adapter per expert segment (host sizes, as the reference's loop)
+        sizes = (offsets[1:] - offsets[:-1]).tolist()
+        a_cat = hs.index_select(0, rows.long())
+        off = 0
+        for e, n in enumerate(sizes):
+            if n:
+                up[off:off + n] += wrapper._lora(a_cat[off:off + n], wrapper.gate_up_lora_A[e],
+                                                 wrapper.gate_up_lora_B[e])
+                off += n
+    h = _epilogue(base, up).contiguous()
+    down = ops.grouped_nf4_gemm(h, base.down_proj.view(E, n2, k2 // 2), base.down_absmax.view(E, n2, k2 // 64),
+                                offsets)
+    if wrapper is not None:
+        off = 0
+        for e, n in enumerate(sizes):
+            if n:
+                down[off:off + n] += wrapper._lora(h[off:off + n], wrapper.down_lora_A[e], wrapper.down_lora_B[e])
+                off += n
+    return ops.combine(down, inv, top_k_weights.contiguous(), T, k, out_dtype=input_dtype)
 
 
 def _grad_needed(mod, hidden_states) -> bool:
@@ -78,8 +118,10 @@ def _grad_needed(mod, hidden_states) -> bool:
                                         or any(p.requires_grad for p in mod.parameters()))
 
 
-def _run(base, hidden_states, top_k_index, top_k_weights, compute_dtype, input_dtype, lora=None):
+def _run(base, hidden_states, top_k_index, top_k_weights, compute_dtype, input_dtype, lora=None, wrapper=None):
     hs = hidden_states if hidden_states.dtype == compute_dtype else hidden_states.to(compute_dtype)
+    if not _fused_epilogue(base):
+        return _run_epilogue_route(base, hs.contiguous(), top_k_index, top_k_weights, input_dtype, wrapper)
     return ops.moe_forward(hs, top_k_index, top_k_weights, base.gate_up_proj, base.gate_up_absmax,
                            base.down_proj, base.down_absmax, base.num_experts, base.intermediate_dim,
                            has_gate=base.has_gate, out_dtype=input_dtype, lora=lora, check_errors=_CHECK)
@@ -124,7 +166,7 @@ def fused_experts_lora_forward(mod, hidden_states, top_k_index, top_k_weights):
     if base.gate_up_proj.numel() == 0 or base.down_proj.numel() == 0:
         return mod._e4b_fast_ref(hidden_states, top_k_index, top_k_weights)
     lora = (mod.gate_up_lora_A, mod.gate_up_lora_B, mod.down_lora_A, mod.down_lora_B, mod.scaling)
-    return _run(base, hidden_states, top_k_index, top_k_weights, compute_dtype, hidden_states.dtype, lora)
+    return _run(base, hidden_states, top_k_index, top_k_weights, compute_dtype, hidden_states.dtype, lora, mod)
 
 
 def enable_fast(model, verbose: bool = False) -> int:
@@ -218,4 +260,5 @@ def disable_fast(model) -> int:
             mod.forward = mod._e4b_fast_ref
             del mod._e4b_fast_ref
             restored += 1
+    _native.check_errors()  # a device error the fused calls recorded surfaces here at the latest
     return restored

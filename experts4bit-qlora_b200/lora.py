@@ -57,11 +57,12 @@ class ExpertsLoRA(nn.Module):
         nn.init.normal_(self.down_lora_A, std=1.0 / r)
 
     def _delegate_to_base(self) -> bool:
-        """Hand the whole forward to the base when an engine is attached to it and the
-        adapter is identically zero (``lora.py:181-214``)."""
+        """Hand the whole forward to the base when an engine ([fast], pipelined or hot
+        residency) is attached to it and the adapter is identically zero (``lora.py:181-214``)."""
         if torch.is_grad_enabled() or self.training:
             return False
-        if getattr(self.base, "_e4b_fast_ref", None) is None:
+        base = self.base
+        if all(getattr(base, a, None) is None for a in ("_e4b_fast_ref", "_e4b_pipe_ref", "_e4b_hot_ref")):
             return False
         return self._adapter_is_zero()
 

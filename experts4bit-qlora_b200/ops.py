@@ -159,17 +159,66 @@ def combine(rows: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, tokens: int,
 # --------------------------------------------------------------------------- #
 # Whole layer
 # --------------------------------------------------------------------------- #
+def _expect(t: torch.Tensor, what: str, device, dtypes, numel: int | None = None, shape=None) -> None:
+    """Raise ValueError unless ``t`` is a contiguous tensor on ``device`` with one of ``dtypes`` and the
+    given element count / shape: the kernels read raw pointers, so a mismatch would read out of bounds."""
+    if not isinstance(t, torch.Tensor):
+        raise ValueError(f"{what} must be a tensor")
+    if t.device != device:
+        raise ValueError(f"{what} is on {t.device}, expected {device}")
+    if t.dtype not in dtypes:
+        raise ValueError(f"{what} has dtype {t.dtype}, expected one of {tuple(dtypes)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{what} must be contiguous")
+    if numel is not None and t.numel() != numel:
+        raise ValueError(f"{what} has {t.numel()} elements, expected {numel}")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{what} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+
+
+def _check_layer(dev, E, H, I, has_gate, gate_up_packed, gate_up_absmax, down_packed, down_absmax, weight_format,
+                 lora=None):
+    n1 = 2 * I if has_gate else I
+    if weight_format == N.FMT_FP8_BLOCK128:
+        _expect(gate_up_packed, "gate_up weights", dev, (torch.uint8,), E * n1 * H)
+        _expect(down_packed, "down weights", dev, (torch.uint8,), E * H * I)
+        _expect(gate_up_absmax, "gate_up scales", dev, (torch.float32,), E * (n1 // 128) * (H // 128))
+        _expect(down_absmax, "down scales", dev, (torch.float32,), E * (H // 128) * (I // 128))
+    else:
+        _expect(gate_up_packed, "gate_up_proj", dev, (torch.uint8,), E * n1 * H // 2)
+        _expect(down_packed, "down_proj", dev, (torch.uint8,), E * H * I // 2)
+        _expect(gate_up_absmax, "gate_up_absmax", dev, (torch.float32,), E * n1 * H // 64)
+        _expect(down_absmax, "down_absmax", dev, (torch.float32,), E * H * I // 64)
+    if lora is not None:
+        A_gu, B_gu, A_dn, B_dn = lora[:4]
+        if A_gu.dim() != 3:
+            raise ValueError("LoRA A of gate_up must be [E, r, H]")
+        r = A_gu.shape[1]
+        dts = (A_gu.dtype,)
+        if A_gu.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise ValueError(f"LoRA dtype {A_gu.dtype} is not bf16/fp16/fp32")
+        for m, what, shape in ((A_gu, "gate_up LoRA A", (E, r, H)), (B_gu, "gate_up LoRA B", (E, n1, r)),
+                               (A_dn, "down LoRA A", (E, r, I)), (B_dn, "down LoRA B", (E, H, r))):
+            if m.device != dev or m.dtype not in dts or tuple(m.shape) != shape:
+                raise ValueError(f"{what}: expected {shape} {A_gu.dtype} on {dev}, got {tuple(m.shape)} "
+                                 f"{m.dtype} on {m.device}")
+
+
 def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor,
                 gate_up_packed: torch.Tensor, gate_up_absmax: torch.Tensor, down_packed: torch.Tensor,
                 down_absmax: torch.Tensor, num_experts: int, intermediate: int, has_gate: bool = True,
                 out_dtype=None, lora=None, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-                check_errors: bool = False, weight_format: int = N.FMT_NF4) -> torch.Tensor:
+                check_errors: bool = False, weight_format: int = N.FMT_NF4,
+                expert_map: torch.Tensor | None = None) -> torch.Tensor:
     """One fused expert layer through ``e4b_moe_forward``.
 
     ``hidden [T,H]`` must already be in the compute dtype (bf16/fp16).
     ``lora`` = ``(A_gu [E,r,H], B_gu [E,n1,r], A_dn [E,r,I], B_dn [E,H,r], scaling)`` or None.
     ``weight_format`` = ``FMT_FP8_BLOCK128``: the ``*_packed`` stacks are e4m3 bytes and the
     ``*_absmax`` stacks fp32 tile multipliers (bf16 activations, no adapters).
+    ``expert_map`` (int32 ``[routed]``): the stacks hold a sub-stack of ``num_experts`` resident
+    experts; the top-k ids lie in ``[0, routed)`` and ``expert_map[id]`` is the expert's index in
+    the stacks (-1 = not resident, a device error).
     """
     _cuda(hidden, "hidden_states")
     if hidden.dtype not in (torch.bfloat16, torch.float16):
@@ -181,11 +230,19 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     w = top_k_weights.contiguous()
     if w.dtype not in (torch.bfloat16, torch.float16, torch.float32):
         w = w.float()
+    if hidden.dim() != 2 or idx.dim() != 2 or idx.shape[0] != hidden.shape[0]:
+        raise ValueError(f"hidden {tuple(hidden.shape)} and top_k_index {tuple(idx.shape)} must be [T, H] and [T, k]")
     T, H = hidden.shape
     k = idx.shape[1]
+    dev = hidden.device
+    _expect(idx, "top_k_index", dev, (torch.int64,), shape=(T, k))
+    _expect(w, "top_k_weights", dev, (torch.bfloat16, torch.float16, torch.float32), shape=(T, k))
+    _check_layer(dev, num_experts, H, intermediate, has_gate, gate_up_packed, gate_up_absmax, down_packed,
+                 down_absmax, weight_format, lora)
     out_dtype = out_dtype or hidden.dtype
     if out is None:
         out = torch.empty(T, H, dtype=out_dtype, device=hidden.device)
+    _expect(out, "out", dev, (out_dtype,), shape=(T, H))
     d = MoeDesc_from(num_experts, H, intermediate, k, T, has_gate, hidden.dtype, w.dtype, out_dtype, lora,
                      weight_format)
     t = N.MoeTensors()
@@ -199,6 +256,10 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
         keep = mats
         t.gate_up_lora_A, t.gate_up_lora_B, t.down_lora_A, t.down_lora_B = (m.data_ptr() for m in mats)
     t.out = out.data_ptr()
+    if expert_map is not None:
+        _expect(expert_map, "expert_map", dev, (torch.int32,))
+        d.routed_experts = int(expert_map.numel())
+        t.expert_map = expert_map.data_ptr()
     L = N.lib()
     nbytes = L.e4b_moe_workspace_bytes(ctypes.byref(d))
     if nbytes == 0:
@@ -206,6 +267,8 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     ws = workspace if workspace is not None else N.workspaces.get(hidden.device, nbytes, "moe")
     if ws.numel() < nbytes:
         raise ValueError(f"workspace of {ws.numel()} bytes < required {nbytes}")
+    if not check_errors:
+        N.error_watch.before(ws, "e4b_moe_forward")
     N.check(L.e4b_moe_forward(ctypes.byref(d), ctypes.byref(t), ws.data_ptr(), ws.numel(),
                               N.stream_handle(hidden.device)), "e4b_moe_forward")
     del keep
@@ -213,6 +276,8 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
         err = N.read_device_error(ws)
         if err:
             raise N.E4BError(err, "e4b_moe_forward (device)")
+    else:
+        N.error_watch.after(ws)
     return out
 
 
@@ -234,6 +299,12 @@ def moe_decode_step(hidden: torch.Tensor, router_weight: torch.Tensor, top_k: in
     topk_idx = topk_idx if topk_idx is not None else torch.empty(T, top_k, dtype=torch.int64, device=dev)
     topk_w = topk_w if topk_w is not None else torch.empty(T, top_k, dtype=torch.float32, device=dev)
     wr = router_weight.contiguous()
+    _expect(wr, "router_weight", dev, (torch.bfloat16, torch.float16, torch.float32), shape=(num_experts, H))
+    _expect(out, "out", dev, (out_dtype,), shape=(T, H))
+    _expect(topk_idx, "topk_idx", dev, (torch.int64,), shape=(T, top_k))
+    _expect(topk_w, "topk_w", dev, (torch.float32,), shape=(T, top_k))
+    _check_layer(dev, num_experts, H, intermediate, has_gate, gate_up_packed, gate_up_absmax, down_packed,
+                 down_absmax, N.FMT_NF4)
     d = MoeDesc_from(num_experts, H, intermediate, top_k, T, has_gate, hidden.dtype, torch.float32, out_dtype, None)
     t = N.MoeTensors()
     t.hidden = hidden.data_ptr()
@@ -251,6 +322,8 @@ def moe_decode_step(hidden: torch.Tensor, router_weight: torch.Tensor, top_k: in
     ws = workspace if workspace is not None else N.workspaces.get(dev, nbytes, "moe_step")
     if ws.numel() < nbytes:
         raise ValueError(f"workspace of {ws.numel()} bytes < required {nbytes}")
+    if not check_errors:
+        N.error_watch.before(ws, "e4b_moe_decode_step")
     N.check(L.e4b_moe_decode_step(ctypes.byref(d), ctypes.byref(t), wr.data_ptr(), N.dtype_code(wr.dtype), kind,
                                   int(norm_topk_prob), topk_idx.data_ptr(), topk_w.data_ptr(), ws.data_ptr(),
                                   ws.numel(), N.stream_handle(dev)), "e4b_moe_decode_step")
@@ -259,6 +332,8 @@ def moe_decode_step(hidden: torch.Tensor, router_weight: torch.Tensor, top_k: in
         err = N.read_device_error(ws)
         if err:
             raise N.E4BError(err, "e4b_moe_decode_step (device)")
+    else:
+        N.error_watch.after(ws)
     return out, topk_w, topk_idx
 
 

@@ -191,10 +191,12 @@ def fused_experts_train_forward(lora_mod, hidden_states, top_k_index, top_k_weig
 
 
 def _train_ineligible(mod) -> Optional[str]:
-    from .fast import _eligible
+    from .fast import _eligible, _fused_epilogue
     reason = _eligible(mod.base)
     if reason is not None:
         return reason
+    if not _fused_epilogue(mod.base):
+        return "the training backward differentiates SiLU(gate)*up only (custom activation or _apply_gate)"
     if getattr(mod.base, "quant_type", None) == "fp8_block128":
         return "FP8 block storage has no training path"
     H, I = mod.base.hidden_dim, mod.base.intermediate_dim

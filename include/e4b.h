@@ -180,6 +180,11 @@ typedef struct {
   int lora_dtype;         /* adapter dtype: E4B_F32 or E4B_BF16 (or E4B_F16) */
   float lora_scaling;     /* alpha / r */
   int weight_format;      /* e4b_weight_format; FP8 takes no adapters and needs H, I % 128 == 0 */
+  /* Resident sub-stack (hot-expert residency, engines/hot_residency.py:39-104): 0 = the top-k ids
+   * index the [E, ...] stacks directly; > 0 = the ids lie in [0, routed_experts) and
+   * e4b_moe_tensors.expert_map[id] is the expert's index in the stacks (-1 = not resident,
+   * reported as E4B_ERR_EXPERT_INDEX). Adapters are indexed the same way. */
+  int routed_experts;
 } e4b_moe_desc;
 
 typedef struct {
@@ -201,6 +206,7 @@ typedef struct {
    * stream is being captured they are recorded as graph nodes, so a replayed
    * graph yields per-stage device times. */
   void* const* stage_events;
+  const int32_t* expert_map;       /* [routed_experts] id -> stack index, or NULL (see routed_experts) */
 } e4b_moe_tensors;
 
 #define E4B_MOE_STAGE_EVENTS 7
@@ -224,7 +230,10 @@ E4B_API e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tenso
 #define E4B_PATH_TENSOR_CORE 1
 #define E4B_PATH_DECODE_LAYER 2
 E4B_API int e4b_moe_path(const e4b_moe_desc* desc);
-E4B_API int e4b_set_decode_kernel(int enabled);
+/* mode 0: no one-launch kernel; 1 (default): the flow kernel (per-expert completion counters,
+ * up to 8 tokens and 64 picks) where it applies, else the phase kernel (grid-synchronised
+ * phases, up to 16 tokens and 128 picks); 2: the phase kernel only. */
+E4B_API int e4b_set_decode_kernel(int mode);
 
 /* No counterpart in the reference (its router is the model's own module): router
  * and expert layer in one call. Top-k of fp32 logits x . W_r^T (router_w [E, H],
@@ -298,8 +307,8 @@ E4B_API e4b_status e4b_ep_experts(const e4b_moe_desc* local, int world, const in
  * current call's number, so nothing changes on the host between calls and a
  * layer call can be captured in a CUDA graph and replayed. One region serves any
  * number of layers called in the same order on every rank. Waits give up after a
- * few seconds with E4B_ERR_TIMEOUT in the region's error word (read with
- * e4b_read_device_error(region, ...)); the dispatch of each layer clears that word. */
+ * few seconds with E4B_ERR_TIMEOUT in the region's error word (sticky: read and
+ * cleared with e4b_read_device_error(region, ...)). */
 #define E4B_IPC_HANDLE_BYTES 64
 #define E4B_EP_MAX_PEERS 16
 typedef struct {
@@ -329,6 +338,30 @@ E4B_API e4b_status e4b_ep_experts_peer(const e4b_ep_peer_desc* pd, const e4b_moe
                                const e4b_moe_tensors* t, void* workspace, size_t workspace_bytes, void* stream);
 E4B_API e4b_status e4b_ep_combine_peer(const e4b_ep_peer_desc* pd, const int32_t* inv, const void* topk_w,
                                int w_dtype, int T, int k, void* out, int out_dtype, void* stream);
+
+/* ---- Resident / streamed expert stacks ----------------------------------
+ * Replaces the address-table gather of the pipelined residency engine
+ * (experts4bit_qlora/engines/pipelined.py:117-150, `_gather_rows_addr`, and the
+ * resident-row dispatch of :300-340). Every expert's weights form one row-block of
+ * four segments (gate_up packed, gate_up absmax, down packed, down absmax) at
+ * seg_off_host[s] bytes, seg_bytes_host[s] long (both multiples of 16).
+ * src_table [num_experts] (device) holds each row-block's address: device memory,
+ * or pinned host memory (unified addressing). The fused layer reads four device
+ * stacks seg_dst_host[s] = [resident_rows + slots, seg_bytes_host[s]]: rows
+ * [0, resident_rows) hold resident experts, the rest one slot per pick. For pick
+ * j < slots (ids [slots], device int64): if resident_row[ids[j]] >= 0 (device int32
+ * [num_experts], nullable) the pick reads that row in place; otherwise slot j
+ * receives expert ids[j]'s segments unless have[j] == ids[j] already (device int64
+ * [slots], nullable: then every slot is copied), and have[j] is updated. local_ids
+ * [slots] (device int64, nullable) receives the stack row of every pick: the
+ * top-k index to pass to e4b_moe_forward over the stacks. The launch geometry does
+ * not depend on the ids, so a decode step built on it can be captured in a CUDA
+ * graph. An id outside [0, num_experts) is reported in the workspace's error word. */
+E4B_API e4b_status e4b_gather_expert_rows(const uint64_t* src_table, int num_experts, const int64_t* ids,
+                                  int64_t* have, int slots, const int32_t* resident_row, int resident_rows,
+                                  int64_t* local_ids, const uint64_t* seg_off_host, const uint64_t* seg_bytes_host,
+                                  void* const* seg_dst_host, void* workspace, size_t workspace_bytes,
+                                  void* stream);
 
 /* Self-test of the failure path (no counterpart in the reference): one kernel
  * waits, with the library's bounded wait, on an asynchronous copy that is never

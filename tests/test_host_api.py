@@ -19,7 +19,7 @@ def test_header_symbols_are_exported(e4b):
     lib = ctypes.CDLL(e4b._native.LIB_PATH)
     for name in declared:
         assert hasattr(lib, name), name
-    assert e4b._native.lib().e4b_abi_version() == e4b._native.ABI_VERSION == 3
+    assert e4b._native.lib().e4b_abi_version() == e4b._native.ABI_VERSION == 4
 
 
 def test_status_strings_and_argument_validation(e4b):
