@@ -17,6 +17,7 @@ from ._native import check_errors
 from .experts import Experts4bit, ExpertsNbit, normalize_quant_type
 from .fast import disable_fast, enable_fast, fast_available
 from .fp8_experts import ExpertsFp8Blocks
+from .mxfp4 import ExpertsMxfp4
 from .ep import ExpertParallelMoE, PeerExchange, shard_experts
 from .lora import ExpertsLoRA
 from .train import disable_fast_train, enable_fast_train
@@ -29,7 +30,7 @@ __version__ = "0.1.0"
 __all__ = [
     "Experts4bit", "ExpertsNbit", "ExpertsLoRA", "enable_fast", "disable_fast", "fast_available",
     "normalize_quant_type", "check_errors", "enable_fast_train", "disable_fast_train", "route", "TopKRouter", "ops", "ExpertParallelMoE", "PeerExchange", "shard_experts", "ExpertsFp8Blocks",
-    "enable_hot_residency", "disable_hot_residency", "enable_pipelined_residency", "disable_pipelined_residency",
+    "ExpertsMxfp4", "enable_hot_residency", "disable_hot_residency", "enable_pipelined_residency", "disable_pipelined_residency",
     "target_modules", "dispatched_modules",
 ]
 

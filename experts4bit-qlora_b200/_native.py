@@ -22,7 +22,7 @@ E4B_ERR_TIMEOUT = 8
 BF16, F16, F32 = 0, 1, 2
 SOFTMAX_THEN_TOPK, TOPK_THEN_SOFTMAX = 0, 1
 EPI_NONE, EPI_SWIGLU, EPI_SILU = 0, 1, 2
-FMT_NF4, FMT_FP8_BLOCK128 = 0, 1
+FMT_NF4, FMT_FP8_BLOCK128, FMT_MXFP4 = 0, 1, 2
 PATH_STREAMING, PATH_TENSOR_CORE, PATH_DECODE_LAYER = 0, 1, 2
 ABI_VERSION = 4
 

@@ -98,6 +98,11 @@ e4b_status launch_gather_rows16(const void* src, const int32_t* rows_map, int ro
 
 e4b_status check_weight_format(const e4b_moe_desc& d) {
   if (d.weight_format == E4B_FMT_NF4) return E4B_OK;
+  if (d.weight_format == E4B_FMT_MXFP4) {  // bf16 compute on the tensor cores, whole 128-wide tiles
+    if (d.lora_rank != 0 || d.act_dtype != E4B_BF16) return E4B_ERR_UNSUPPORTED;
+    if (d.hidden % 128 || d.intermediate % 128) return E4B_ERR_UNSUPPORTED;
+    return E4B_OK;
+  }
   if (d.weight_format != E4B_FMT_FP8_BLOCK128) return E4B_ERR_INVALID_ARG;
   // FP8 experts: whole 128x128 scale tiles, no adapters
   if (d.lora_rank != 0) return E4B_ERR_UNSUPPORTED;
@@ -150,6 +155,47 @@ e4b_status run_expert_stages(const e4b_moe_desc& d, const e4b_moe_tensors* t, co
   const int max_active = R < E ? R : E;
   const int lora_tiles = R / kLoraRows + max_active;
   e4b_status st = E4B_OK;
+  if (d.weight_format == E4B_FMT_MXFP4) {
+    // bf16 activation rows (expert-sorted), bf16 h and down rows: the reference's bf16 lane
+    GemvArgs g{};
+    g.a = x.x16;  // bf16 bytes in the same buffer
+    g.packed = t->gate_up_packed;
+    g.absmax = t->gate_up_absmax;  // e8m0 bytes
+    g.offsets = x.offsets;
+    g.active = x.active;
+    g.num_active = x.num_active;
+    g.E = E;
+    g.N = n1;
+    g.K = H;
+    g.epilogue = d.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
+    g.out = x.h;
+    g.out_dtype = E4B_BF16;
+    g.Nout = I;
+    g.tiles_per_expert = I / 16;
+    g.max_tasks = max_active * g.tiles_per_expert;
+    g.err = x.err;
+    mark_stage(t, 2, s);
+    if ((st = launch_umma(umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R), d.act_dtype, s, E4B_FMT_MXFP4)) !=
+        E4B_OK)
+      return st;
+    mark_stage(t, 3, s);
+    mark_stage(t, 4, s);
+    g.a = x.h;
+    g.packed = t->down_packed;
+    g.absmax = t->down_absmax;
+    g.N = H;
+    g.K = I;
+    g.epilogue = E4B_EPI_NONE;
+    g.out = x.down_rows;
+    g.Nout = H;
+    g.tiles_per_expert = H / 16;
+    g.max_tasks = max_active * g.tiles_per_expert;
+    if ((st = launch_umma(umma_args_from(g, x.umma_scratch, x.tile_b, R, 1, R), d.act_dtype, s, E4B_FMT_MXFP4)) !=
+        E4B_OK)
+      return st;
+    mark_stage(t, 5, s);
+    return E4B_OK;
+  }
   if (d.weight_format == E4B_FMT_FP8_BLOCK128) {
     mark_stage(t, 2, s);
     GemvArgs g{};
@@ -473,6 +519,7 @@ extern "C" int e4b_moe_path(const e4b_moe_desc* desc) {
   if (!desc || !desc_ok(*desc)) return -1;
   const e4b_moe_desc& d = *desc;
   if (decode_flow_eligible(d, false) || decode_layer_eligible(d)) return E4B_PATH_DECODE_LAYER;
+  if (d.weight_format == E4B_FMT_MXFP4) return E4B_PATH_TENSOR_CORE;
   const int64_t R = (int64_t)d.tokens * d.top_k;
   if (umma_worthwhile(R, d.num_experts) &&
       umma_eligible(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate, d.has_gate, d.act_dtype, d.lora_rank))
@@ -551,12 +598,15 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   pa.conv.rows = T;
   pa.conv.K = H;
   pa.conv_ctas = conv_ctas_for(T, 32);
-  const bool use_umma =
-      umma_worthwhile((int64_t)T * k, E) && umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype, d.lora_rank);
+  const bool mxfp4 = d.weight_format == E4B_FMT_MXFP4;
+  const bool use_umma = mxfp4 || (umma_worthwhile((int64_t)T * k, E) &&
+                                  umma_eligible(T, k, E, H, I, d.has_gate, d.act_dtype, d.lora_rank));
   if (use_umma) pa.conv.src = nullptr;  // converted below, in expert-sorted order
   e4b_status st = launch_permute(pa, s);
   if (st != E4B_OK) return st;
-  if (use_umma) {  // xs[r] = fp16(x[sorted_token[r]]): contiguous rows per expert for the TMA tiles
+  if (mxfp4) {  // xs[r] = x[sorted_token[r]] as is (bf16): the bf16 tensor-core operand
+    if ((st = launch_gather_rows16(t->hidden, pa.sorted_token, R, H, x16, s)) != E4B_OK) return st;
+  } else if (use_umma) {  // xs[r] = fp16(x[sorted_token[r]]): contiguous rows per expert for the TMA tiles
     ConvertArgs cv{};
     cv.src = t->hidden;
     cv.src_dtype = d.act_dtype;
@@ -590,7 +640,8 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   x.err = err;
   if ((st = run_expert_stages(d, t, x, s)) != E4B_OK) return st;
 
-  st = e4b_combine(x.down_rows, E4B_F16, pa.inv, t->topk_w, d.weight_dtype, T, k, H, t->out, d.out_dtype, stream);
+  st = e4b_combine(x.down_rows, mxfp4 ? E4B_BF16 : E4B_F16, pa.inv, t->topk_w, d.weight_dtype, T, k, H, t->out,
+                   d.out_dtype, stream);
   mark_stage(t, 6, s);
   return st;
 }

@@ -16,9 +16,12 @@
 //    (cudaGetSymbolAddress) with that device current; make that first call
 //    before any stream capture on the device.
 //  * Every call on a device shares the one array and it keeps the previous
-//    call's contents; the only word that must start at zero (the device error
-//    word) is cleared by the layer's first kernel. Calls that overlap on the GPU
-//    (different streams, no ordering between them) race on the array.
+//    call's contents. What must start at zero is the array's header: the decode
+//    kernel's counter block, zero at load (a static device array is zero-filled)
+//    and left zero by every launch, and the device error word, which keeps the
+//    first error any call records (nothing reads it back here). Calls that
+//    overlap on the GPU (different streams, no ordering between them) race on the
+//    array.
 #include <mutex>
 
 #include "common.cuh"

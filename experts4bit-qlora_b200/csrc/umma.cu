@@ -75,10 +75,10 @@ constexpr int kEpiMaxRank = 16;  // LoRA ranks above this take the streaming pat
 // chunk and need the 32 KB pair table; FP8 rows carry 64 bytes and no table.
 template <int FMT>
 struct SmemT {
-  static constexpr int wrow = FMT == E4B_FMT_NF4 ? kKc / 2 : kKc;  // weight bytes per row per chunk
+  static constexpr int wrow = FMT == E4B_FMT_FP8_BLOCK128 ? kKc : kKc / 2;  // weight bytes per row per chunk
   static constexpr int wbytes = kRows * wrow;                      // per group per stage
   static constexpr int lut = 0;
-  static constexpr int a = FMT == E4B_FMT_NF4 ? kLut : 0;          // [stage][group] 16 KB, 1024-aligned
+  static constexpr int a = FMT == E4B_FMT_FP8_BLOCK128 ? 0 : kLut;  // [stage][group] 16 KB, 1024-aligned
   static constexpr int b = a + kSA * 2 * kABytes;                 // [stage] 16 KB
   static constexpr int w = b + kSB * kBBytes;                     // [stage][group]
   static constexpr int epi = w + kSW * 2 * wbytes;                // epilogue staging
@@ -124,9 +124,21 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: fp16 A and B, fp32 D, both K-major, M = 128 tokens, N = n features.
-__device__ __forceinline__ uint32_t idesc_f16(int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTok >> 4) << 24);
+// kind::f16 instruction descriptor: fp16 (or, with bf16, bf16) A and B, fp32 D, both K-major,
+// M = 128 tokens, N = n features.
+__device__ __forceinline__ uint32_t idesc_f16(int n, bool bf16 = false) {
+  const uint32_t ab = bf16 ? (1u << 7) | (1u << 10) : 0u;
+  return (1u << 4) | ab | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTok >> 4) << 24);
+}
+
+// e2m1 values (OCP microscaling FP4), index = 4-bit code
+__constant__ float c_e2m1_umma[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+                                      -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+// 2^(s-127) as bf16 bits: exponent field s for s >= 1 (255: inf), subnormal 2^-127 for s = 0.
+__device__ __forceinline__ uint32_t e8m0_bf16x2(uint32_t s) {
+  const uint32_t b = s ? (s << 7) : 0x0040u;
+  return b | (b << 16);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
@@ -248,6 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
       reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
     }
+  } else if (FMT == E4B_FMT_MXFP4) {  // bf16 pair table, LOW nibble first (formats/mxfp4.py:87-88)
+    const float code = c_e2m1_umma[lane & 15];
+    for (int e = warp; e < 256; e += kThreads / 32) {
+      const float first = __shfl_sync(0xffffffffu, code, e & 15), second = __shfl_sync(0xffffffffu, code, e >> 4);
+      reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__nv_bfloat16>(first, second);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -298,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 3) {
     // ---------------- MMA issuer -------------------------------------------------------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(GROUPS * kRows);  // N = the tile's gate (+ up) rows
+      const uint32_t idesc = idesc_f16(GROUPS * kRows, FMT == E4B_FMT_MXFP4);  // N = the tile's gate (+ up) rows
       int n = 0, it = 0;
       for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
         const int buf = it & 1;
@@ -401,6 +419,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&a_ready[sa]);
         }
         if (g.rank && !wt.dead) lora_chunk(ti, row);
+        continue;
+      }
+      if (FMT == E4B_FMT_MXFP4) {
+        // e2m1 pairs -> bf16 through the pair table, times the block's 2^(s-127) (exact in bf16);
+        // a 64-wide chunk is two 32-element scale blocks
+        const uint8_t* sp = reinterpret_cast<const uint8_t*>(g.absmax) + ((int64_t)ti.e * g.N + row) * (g.K / 32);
+        for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
+          const int s = nw % kSW, sa = na % kSA;
+          uint32_t s0 = 0, s1 = 0;
+          if (h < GROUPS) {
+            s0 = e8m0_bf16x2(__ldg(sp + 2 * c));
+            s1 = e8m0_bf16x2(__ldg(sp + 2 * c + 1));
+          }
+          if (!wt.wait(&full_w[s], (nw / kSW) & 1)) break;
+          uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
+          if (h < GROUPS) {
+            const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
+            p0 = reinterpret_cast<const uint4*>(wsrc)[0];
+            p1 = reinterpret_cast<const uint4*>(wsrc)[1];
+          }
+          fence_proxy_async();
+          mbar_arrive(&w_empty[s]);
+          if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) break;
+          if (h < GROUPS) {
+            const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
+            const int swz = (smem_u32(adst) >> 7) & 7;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {  // unit q = elements 8q .. 8q+7, scale block q / 4
+              const uint32_t scw = q < 4 ? s0 : s1;
+              const __nv_bfloat162 sc2 = *reinterpret_cast<const __nv_bfloat162*>(&scw);
+              uint32_t o[4];
+#pragma unroll
+              for (int bb = 0; bb < 4; ++bb) {
+                const uint32_t byte = (words[q] >> (8 * bb)) & 0xffu;
+                uint32_t pr = *reinterpret_cast<const uint32_t*>(lut + ((byte << 7) | lane4));
+                __nv_bfloat162 v = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&pr), sc2);
+                o[bb] = *reinterpret_cast<uint32_t*>(&v);
+              }
+              *reinterpret_cast<uint4*>(adst + ((q ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+          fence_proxy_async();
+          mbar_arrive(&a_ready[sa]);
+        }
         continue;
       }
       const float* am = g.absmax + ((int64_t)ti.e * g.N + row) * (g.K / 64);
@@ -573,7 +636,7 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   if (bound < grid) grid = bound;
   if (grid < 1) return E4B_OK;
   CUtensorMap wmap;  // weight bytes [E*N rows][K bytes per row (K/2 for NF4)], box {bytes of a chunk, 128 rows}
-  const cuuint64_t row_bytes = FMT == E4B_FMT_NF4 ? (cuuint64_t)(g.K / 2) : (cuuint64_t)g.K;
+  const cuuint64_t row_bytes = FMT == E4B_FMT_FP8_BLOCK128 ? (cuuint64_t)g.K : (cuuint64_t)(g.K / 2);
   const cuuint64_t dims[2] = {row_bytes, (cuuint64_t)g.E * g.N};
   const cuuint64_t str[1] = {row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)Smem::wrow, kRows};
@@ -584,8 +647,8 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   const cuuint64_t bdims[2] = {(cuuint64_t)g.K, (cuuint64_t)u.x_rows};
   const cuuint64_t bstr[1] = {(cuuint64_t)g.K * 2};
   const cuuint32_t bbox[2] = {kKc, kTok};
-  if (!encode_tiled(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.a, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B))
-    return E4B_ERR_CUDA;
+  const CUtensorMapDataType bdt = FMT == E4B_FMT_MXFP4 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (!encode_tiled(&bmap, bdt, 2, g.a, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) return E4B_ERR_CUDA;
   CUtensorMap lmap = bmap;  // LoRA-A products: fp16 rows of 64 (rank values, zero padded), same boxes
   if (g.rank) {
     if (!u.lora_xa16) return E4B_ERR_INVALID_ARG;
@@ -611,6 +674,11 @@ e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s, int wei
       return two ? launch_groups<__nv_bfloat16, 2, E4B_FMT_FP8_BLOCK128>(u, s)
                  : launch_groups<__nv_bfloat16, 1, E4B_FMT_FP8_BLOCK128>(u, s);
     return two ? launch_groups<__half, 2, E4B_FMT_FP8_BLOCK128>(u, s) : launch_groups<__half, 1, E4B_FMT_FP8_BLOCK128>(u, s);
+  }
+  if (weight_format == E4B_FMT_MXFP4) {  // bf16 operands and bf16 outputs (h, down rows)
+    if (u.g.K % kKc || u.g.rank || u.g.out_dtype != E4B_BF16) return E4B_ERR_UNSUPPORTED;
+    return two ? launch_groups<__nv_bfloat16, 2, E4B_FMT_MXFP4>(u, s)
+               : launch_groups<__nv_bfloat16, 1, E4B_FMT_MXFP4>(u, s);
   }
   if (u.g.out_dtype == E4B_BF16)
     return two ? launch_groups<__nv_bfloat16, 2, E4B_FMT_NF4>(u, s) : launch_groups<__nv_bfloat16, 1, E4B_FMT_NF4>(u, s);

@@ -50,12 +50,25 @@ def _eligible_fp8(mod) -> Optional[str]:
     return None
 
 
+def _eligible_mxfp4(mod) -> Optional[str]:
+    """Eligibility of an MXFP4 stack for the fused MXFP4 layer (bf16 tensor-core GEMMs)."""
+    if mod.hidden_dim % 128 or mod.intermediate_dim % 128:
+        return "MXFP4 dims not multiples of 128"
+    if mod.num_experts > 1024:
+        return "more than 1024 experts"
+    if not mod.gate_up_proj.is_cuda:
+        return "storage not on CUDA"
+    if not _fused_epilogue(mod):
+        return "custom activation: the MXFP4 layer fuses SiLU(gate)*up / SiLU only"
+    return None
+
+
 def _eligible(mod) -> Optional[str]:
     """None if ``mod`` can take the fused path, else the reason (``fast.py:75-97``)."""
     if getattr(mod, "quant_type", None) == "fp8_block128":
         return _eligible_fp8(mod)
     if getattr(mod, "_e4b_mxfp4_arena", False):
-        return "storage is MXFP4 (arena), which the NF4 grouped kernel cannot read"
+        return _eligible_mxfp4(mod)
     if getattr(mod, "bits", None) != 4 or getattr(mod, "quant_type", None) != "nf4":
         return "storage is not nf4-4bit"
     if getattr(mod, "blocksize", None) != 64:
@@ -152,6 +165,20 @@ def fused_fp8_experts_forward(mod, hidden_states, top_k_index, top_k_weights):
                            weight_format=_native.FMT_FP8_BLOCK128)
 
 
+def fused_mxfp4_experts_forward(mod, hidden_states, top_k_index, top_k_weights):
+    """Fused inference forward of MXFP4 stacks (``engines/nvme_experts.py:769-868``): bf16
+    compute and no autograd graph, else the module's reference forward."""
+    if _grad_needed(mod, hidden_states):
+        return mod._e4b_fast_ref(hidden_states, top_k_index, top_k_weights)
+    compute_dtype = mod.compute_dtype if mod.compute_dtype is not None else hidden_states.dtype
+    if compute_dtype is not torch.bfloat16 or mod.gate_up_proj.numel() == 0:
+        return mod._e4b_fast_ref(hidden_states, top_k_index, top_k_weights)
+    return ops.moe_forward(hidden_states.to(torch.bfloat16), top_k_index, top_k_weights, mod.gate_up_proj,
+                           mod.gate_up_absmax, mod.down_proj, mod.down_absmax, mod.num_experts,
+                           mod.intermediate_dim, has_gate=mod.has_gate, out_dtype=hidden_states.dtype,
+                           check_errors=_CHECK, weight_format=_native.FMT_MXFP4)
+
+
 def fused_experts_lora_forward(mod, hidden_states, top_k_index, top_k_weights):
     """Fused inference forward of an ``ExpertsLoRA`` wrapper (``fast.py:163-257``):
     the adapter deltas run inside the grouped GEMMs, before the activation."""
@@ -187,6 +214,8 @@ def enable_fast(model, verbose: bool = False) -> int:
                 print(f"[e4b.fast] skip {type(mod).__name__}: custom forward")
             continue
         reason = _eligible(mod.base)
+        if reason is None and getattr(mod.base, "_e4b_mxfp4_arena", False):
+            reason = "MXFP4 base: the fused MXFP4 layer takes no adapters"
         if reason is not None:
             if verbose:
                 print(f"[e4b.fast] skip {type(mod).__name__}: {reason}")
@@ -240,7 +269,8 @@ def enable_fast(model, verbose: bool = False) -> int:
             if hasattr(mod, "_e4b_fast_ref"):
                 continue
             mod._e4b_fast_ref = mod.forward
-            mod.forward = fused_experts_forward.__get__(mod)
+            fwd = fused_mxfp4_experts_forward if getattr(mod, "_e4b_mxfp4_arena", False) else fused_experts_forward
+            mod.forward = fwd.__get__(mod)
             patched += 1
     if patched and getattr(model, "training", False):
         import warnings

@@ -179,7 +179,12 @@ def _expect(t: torch.Tensor, what: str, device, dtypes, numel: int | None = None
 def _check_layer(dev, E, H, I, has_gate, gate_up_packed, gate_up_absmax, down_packed, down_absmax, weight_format,
                  lora=None):
     n1 = 2 * I if has_gate else I
-    if weight_format == N.FMT_FP8_BLOCK128:
+    if weight_format == N.FMT_MXFP4:
+        _expect(gate_up_packed, "gate_up codes", dev, (torch.uint8,), E * n1 * H // 2)
+        _expect(down_packed, "down codes", dev, (torch.uint8,), E * H * I // 2)
+        _expect(gate_up_absmax, "gate_up e8m0 scales", dev, (torch.uint8,), E * n1 * H // 32)
+        _expect(down_absmax, "down e8m0 scales", dev, (torch.uint8,), E * H * I // 32)
+    elif weight_format == N.FMT_FP8_BLOCK128:
         _expect(gate_up_packed, "gate_up weights", dev, (torch.uint8,), E * n1 * H)
         _expect(down_packed, "down weights", dev, (torch.uint8,), E * H * I)
         _expect(gate_up_absmax, "gate_up scales", dev, (torch.float32,), E * (n1 // 128) * (H // 128))

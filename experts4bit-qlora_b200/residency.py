@@ -77,6 +77,8 @@ def dispatched_modules(model) -> list:
 
 
 def _eligible(mod) -> Optional[str]:
+    if getattr(mod, "_e4b_mxfp4_arena", False):
+        return "MXFP4 storage (the residency stacks hold NF4 row-blocks)"
     if getattr(mod, "bits", None) != 4 or getattr(mod, "quant_type", None) != "nf4":
         return "storage is not nf4-4bit"
     if getattr(mod, "blocksize", None) != 64:

@@ -195,6 +195,8 @@ def _train_ineligible(mod) -> Optional[str]:
     reason = _eligible(mod.base)
     if reason is not None:
         return reason
+    if getattr(mod.base, "_e4b_mxfp4_arena", False):
+        return "MXFP4 storage has no training path"
     if not _fused_epilogue(mod.base):
         return "the training backward differentiates SiLU(gate)*up only (custom activation or _apply_gate)"
     if getattr(mod.base, "quant_type", None) == "fp8_block128":

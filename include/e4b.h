@@ -64,8 +64,14 @@ typedef enum { E4B_EPI_NONE = 0, E4B_EPI_SWIGLU = 1, E4B_EPI_SILU = 2 } e4b_epil
  * E4B_FMT_FP8_BLOCK128: float8_e4m3fn bytes [out, in] per expert with one fp32
  *   multiplier per [128, 128] tile, [ceil(out/128), ceil(in/128)] per expert, the
  *   storage of formats/fp8_blocks.py:60-128 (an e8m0 scale is passed as its value
- *   2^(b-127)). The fused layer uses the weights at full precision, fp32(w) * scale. */
-typedef enum { E4B_FMT_NF4 = 0, E4B_FMT_FP8_BLOCK128 = 1 } e4b_weight_format;
+ *   2^(b-127)). The fused layer uses the weights at full precision, fp32(w) * scale.
+ * E4B_FMT_MXFP4: OCP microscaling FP4, the storage of formats/mxfp4.py and of the
+ *   reference's MXFP4 experts (engines/nvme_experts.py:769-868): e2m1 codes, two per
+ *   byte, LOW nibble first, [E, out, in/2] bytes, and one e8m0 exponent byte per 32
+ *   consecutive elements, [E, out, in/32] (passed in the *_absmax pointers). The
+ *   layer computes in bf16 (act_dtype E4B_BF16; code * 2^(s-127) is exact in bf16),
+ *   takes no adapters and needs hidden and intermediate % 128 == 0. */
+typedef enum { E4B_FMT_NF4 = 0, E4B_FMT_FP8_BLOCK128 = 1, E4B_FMT_MXFP4 = 2 } e4b_weight_format;
 
 E4B_API const char* e4b_status_string(e4b_status s);
 /* ABI version: bumped when a signature or a struct below changes. */

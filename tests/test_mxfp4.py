@@ -72,3 +72,70 @@ def test_scale_255_follows_ldexp():
     assert v[1] == np.float32(2.0 ** 127)
     assert v[2] == -np.inf
     assert v[3] == 0 and np.signbit(v[3])
+
+
+def test_quantizer_and_module_reference_loop(e4b):
+    """The MXFP4 module's reference loop is the NF4 module's loop over MXFP4-dequantized weights."""
+    from oracle import moe as M
+    mx = importlib.import_module("experts4bit-qlora_b200.mxfp4")
+    g = torch.Generator().manual_seed(3)
+    E, H, I, k, T = 4, 128, 128, 2, 5
+    gu = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    dn = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    m = mx.ExpertsMxfp4.from_float(gu, dn)
+    assert m.gate_up_proj.shape == (E, 2 * I * H // 2) and m.gate_up_absmax.dtype == torch.uint8
+    W = m._dequantize_expert(m.gate_up_proj, m.gate_up_absmax, m._gate_up_shape, 2, torch.float32)
+    # every block's scale is the smallest power of two that keeps amax / scale <= 6
+    blocks = gu[2].float().reshape(-1, 32)
+    sc = torch.exp2(m.gate_up_absmax[2].float() - 127)
+    assert torch.all(blocks.abs().amax(1) / sc <= 6) and torch.all(blocks.abs().amax(1) / sc > 3)
+    assert torch.all((W.reshape(-1, 32) / sc[:, None]).abs() <= 6)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    w = torch.rand(T, k, generator=g)
+    got = m(x, idx, w).float()
+    Wg = torch.stack([m._dequantize_expert(m.gate_up_proj, m.gate_up_absmax, m._gate_up_shape, e, torch.float32)
+                      for e in range(E)])
+    Wd = torch.stack([m._dequantize_expert(m.down_proj, m.down_absmax, m._down_shape, e, torch.float32)
+                      for e in range(E)])
+    ref = torch.zeros(T, H)
+    for t in range(T):
+        for s in range(k):
+            e = int(idx[t, s])
+            gg, u = (x[t].float() @ Wg[e].t()).chunk(2)
+            ref[t] += w[t, s] * ((torch.nn.functional.silu(gg) * u) @ Wd[e].t())
+    mxr, mean = M.rel_errors(got, ref)
+    assert mxr <= 2e-2 and mean <= 5e-3, (mxr, mean)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 7, 64, 700])
+def test_fused_mxfp4_layer_vs_fp32(e4b, T):
+    """The fused MXFP4 layer (bf16 tcgen05 GEMMs over exactly decoded weights) against fp32 math
+    on the same dequantized weights, through enable_fast."""
+    from oracle import moe as M
+    E, H, I, k = 16, 1024, 512, 4
+    g = torch.Generator(device="cuda").manual_seed(T)
+    gu = (torch.randn(E, 2 * I, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    dn = (torch.randn(E, H, I, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    m = e4b.ExpertsMxfp4.from_float(gu, dn).eval()
+    x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+    w, idx = torch.topk(torch.softmax(torch.randn(T, E, generator=g, device="cuda"), -1), k)
+    with torch.no_grad():
+        loop = m(x, idx, w)
+        assert e4b.enable_fast(m) == 1
+        got = m(x, idx, w)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    anchor = torch.zeros(T, H, device="cuda")
+    for e in torch.unique(idx).tolist():
+        tok, pos = torch.where(idx == e)
+        wg = m._dequantize_expert(m.gate_up_proj, m.gate_up_absmax, m._gate_up_shape, e, torch.float32)
+        wd = m._dequantize_expert(m.down_proj, m.down_absmax, m._down_shape, e, torch.float32)
+        gg, u = (x[tok].float() @ wg.t()).chunk(2, -1)
+        anchor.index_add_(0, tok, ((torch.nn.functional.silu(gg) * u) @ wd.t()) * w[tok, pos, None])
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    mxr, mean = M.rel_errors(got.float(), anchor)
+    assert mxr <= 1e-2 and mean <= 2e-3, (mxr, mean)
+    lmx, _ = M.rel_errors(loop.float(), anchor)
+    assert mxr <= max(2 * lmx, 5e-3)

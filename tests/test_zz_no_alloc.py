@@ -3,10 +3,11 @@
 Callers such as a serving runtime that owns every device allocation, or a plugin
 host that forbids cudaMalloc once started, cannot hand the library a workspace.
 e4b_moe_forward_static runs the same fused expert layer on a fixed device array
-inside the library. Here it is called through the C ABI, twice in a row (the
-array keeps the previous call's contents), and each result is checked against
-the workspace entry point e4b_moe_forward within the layer tolerances the other
-tests use. This file is collected last on purpose.
+inside the library. Here it is called through the C ABI, twice on the same
+inputs with a call on another layer shape in between (the array keeps whatever
+that call left behind), and each result must equal the workspace entry point
+e4b_moe_forward bit for bit: the same kernels run on the same bytes. This file
+is collected last on purpose.
 """
 import ctypes
 
@@ -46,16 +47,28 @@ def _static_call(e4b, x, idx, w, gp, ga, dp, da, E, I):
     return st, out
 
 
-@pytest.mark.parametrize("E,H,I,k,T", [(64, 2048, 1024, 8, 1), (16, 256, 128, 4, 33)])
-def test_static_scratch_matches_workspace_entry_point_twice(e4b, E, H, I, k, T):
+SHAPES = [(64, 2048, 1024, 8, 1), (16, 256, 128, 4, 33), (32, 1024, 512, 4, 300)]
+
+
+@pytest.mark.parametrize("case", range(len(SHAPES)))
+def test_static_scratch_matches_workspace_entry_point_twice(e4b, case):
+    E, H, I, k, T = SHAPES[case]
     x, idx, w, gp, ga, dp, da = _layer(E, H, I, k, T, seed=E + T)
     ref = e4b.ops.moe_forward(x, idx, w, gp, ga, dp, da, E, I)
+    oE, oH, oI, ok, oT = SHAPES[(case + 1) % len(SHAPES)]
+    other = _layer(oE, oH, oI, ok, oT, seed=7)
+    other_ref = e4b.ops.moe_forward(*other, oE, oI)
     for _ in range(2):
         st, out = _static_call(e4b, x, idx, w, gp, ga, dp, da, E, I)
         assert st == 0, e4b._native.status_string(st)
         torch.cuda.synchronize()
+        assert torch.equal(out, ref)
         mx, mean = M.rel_errors(out, ref)
         assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
+        st, out2 = _static_call(e4b, *other, oE, oI)  # another shape leaves its scratch behind
+        assert st == 0, e4b._native.status_string(st)
+        torch.cuda.synchronize()
+        assert torch.equal(out2, other_ref)
 
 
 def test_static_scratch_refuses_layers_beyond_its_size(e4b):
