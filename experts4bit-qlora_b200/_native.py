@@ -254,7 +254,7 @@ class _ErrorWatch:
 
     def before(self, ws: torch.Tensor, what: str) -> None:
         ent = self._w.get(ws.data_ptr())
-        if ent is None:
+        if ent is None or torch.cuda.is_current_stream_capturing():
             return
         host, _, ev = ent
         if ev.query() and int(host[0]) != 0:

@@ -22,6 +22,7 @@ static __constant__ float c_nf4[16] = {
 // counter block of the flow decode kernel (zero when idle). Every layout starts after it.
 constexpr size_t kErrBytes = 1024;
 constexpr size_t kFlowSyncOffset = 512;
+constexpr int kFlowDiagWord = 16;  // int words 16..20: the flow kernel's first timed-out wait
 
 __device__ __forceinline__ void raise_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);

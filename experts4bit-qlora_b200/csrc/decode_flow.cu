@@ -2,33 +2,37 @@
 // adapters): router (optional) -> permute -> gate_up GEMV + SwiGLU -> down GEMV
 // -> weighted combine, the per-layer chain of experts4bit_qlora/engines/fast.py:100-160.
 //
-// Layout of the work (one CTA per SM, 16 warps):
-//  * Router: the CTAs of a thread-block cluster split the (expert, token tile)
-//    logit tasks, gather the peers' logits through distributed shared memory
-//    and run the same ranked top-k; no grid-wide barrier.
-//  * Items: every CTA streams a fixed list of items through a ring of shared
-//    memory slots filled by per-row bulk copies (cp.async.bulk, mbarrier
-//    completion). An item is 16 weight rows x up to 2048 K elements:
-//      gate_up tile (8 gate + the 8 matching up rows of one expert), assigned
+// One CTA per SM, three roles after a common set-up:
+//  * Set-up: the NF4 pair table, token rows to fp16; with the router fused, the
+//    CTAs of a thread-block cluster split the (expert, token tile) logit tasks,
+//    gather the peers' logits through distributed shared memory and run the same
+//    ranked top-k (no grid-wide barrier); the stable permutation; the CTA's item
+//    list. An item is 16 weight rows x up to 2048 K elements:
+//      gate_up tile (8 gate + the 8 matching up rows of one expert), dealt
 //        round-robin over the grid in expert-major order, so expert j's h is
 //        complete at ~ (j + 1) / active of the gate_up phase;
-//      down tile (the CTA's own output rows of one expert), placed in the
-//        CTA's list two experts after that expert's gate_up tiles.
-//    All 16 warps work on one item at a time, each on its own K blocks
-//    (k-split), with the token / h fragments of its blocks in registers;
-//    NF4 codes decode through a per-lane pair table (conflict-free LDS) into
-//    mma.sync m16n8k16 (fp32 accumulation), the block absmax folded in fp32
-//    per 64-element block. The 16 partial tiles are summed in warp order.
-//  * gate_up epilogue: SwiGLU, h rows (fp16) to global memory, then a release
-//    increment of the expert's tile counter.
-//  * down: a CTA needs an expert's h only when it reaches that expert's down
-//    tile; its control thread polls the counter (acquire, bounded) ahead of
-//    time and bulk-copies the expert's h rows into shared memory.
-//  * combine: each CTA owns whole output rows, so the fixed slot-order
-//    weighted sum needs no further synchronisation.
-// Counters live at a fixed offset of the workspace (kFlowSyncOffset), must be
-// zero before the first launch and are zeroed again by the last CTA to finish.
-// Every wait is bounded; a timeout raises E4B_ERR_TIMEOUT and the kernel runs to
+//      down tile (the CTA's own output rows of one expert), placed two experts
+//        after that expert's gate_up tiles.
+//  * Producer warp: streams the items through a ring of shared-memory slots (two
+//    swizzled TMA boxes of weights + two of absmax per item, mbarrier completion),
+//    refilling a slot when the compute warps release it; meanwhile it polls the
+//    tile counters of the experts whose down tiles come next and, once an expert's
+//    gate_up tiles are all published, bulk-copies its h rows into shared memory.
+//  * Compute warps (8): each takes every 8th 64-element K block of an item, with
+//    the token / h fragments of its blocks in registers; NF4 codes decode through a
+//    per-lane pair table (conflict-free LDS) into mma.sync m16n8k16 (fp32
+//    accumulation), the block absmax folded in fp32 per block. A finished tile's
+//    partial sums go to a reduction buffer.
+//  * Epilogue warp: sums the 8 partials in warp order; gate_up: SwiGLU, h rows
+//    (fp16) to global memory, a release increment of the expert's tile counter;
+//    down: the rows stay in shared memory for the combine.
+//  * Combine: each CTA owns whole output rows, so the fixed slot-order weighted sum
+//    needs no further synchronisation.
+// No role waits on another CTA except through the tile counters, and no CTA-wide
+// barrier separates items. Counters live at a fixed offset of the workspace
+// (kFlowSyncOffset), must be zero before the first launch and are zeroed again by
+// the last CTA to finish. Every wait is bounded; a timeout raises E4B_ERR_TIMEOUT,
+// records the wait in the workspace header (kFlowDiagWord) and the kernel runs to
 // its end. Device errors go straight into the sticky workspace error word.
 #include <cooperative_groups.h>
 
@@ -38,6 +42,33 @@
 #include "decode_layer.cuh"
 #include "router.cuh"
 #include "stream_core.cuh"
+#include "tmap.cuh"
+
+// Profiling instrumentation, compiled only with -DE4B_TRACE: thread 0 of every CTA stamps
+// %globaltimer at the kernel's phase boundaries and at six points of every item.
+#ifdef E4B_TRACE
+__device__ unsigned long long g_flow_trace[160 * (8 + 64 * 6)];
+extern "C" __attribute__((visibility("default"))) int e4b_flow_trace_read(unsigned long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, g_flow_trace, n * sizeof(unsigned long long));
+}
+#define FT_K(i)                                                              \
+  if (threadIdx.x == 0 && blockIdx.x < 160) {                                \
+    unsigned long long t_;                                                   \
+    if ((i) == 0)                                                            \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                \
+    else                                                                     \
+      t_ = (unsigned long long)clock64();                                    \
+    g_flow_trace[blockIdx.x * (8 + 64 * 6) + (i)] = t_;                      \
+    if ((i) == 0) g_flow_trace[blockIdx.x * (8 + 64 * 6) + 7] = (unsigned long long)clock64(); \
+  }
+#define FT_I(n, i)                                                           \
+  if (threadIdx.x == 0 && blockIdx.x < 160 && (n) < 64) {                    \
+    g_flow_trace[blockIdx.x * (8 + 64 * 6) + 8 + (n) * 6 + (i)] = (unsigned long long)clock64(); \
+  }
+#else
+#define FT_K(i)
+#define FT_I(n, i)
+#endif
 
 namespace e4b {
 
@@ -47,13 +78,21 @@ using stream::lut2;
 using stream::mma16816;
 using stream::mma16816_zero;
 
-constexpr int kFWarps = 16;
-constexpr int kFThreads = kFWarps * 32;
+constexpr int kFWarps = 16;                  // compute warps: each takes every 16th K block of an item
+constexpr int kFProducer = kFWarps;          // warp: TMA issue of the items
+constexpr int kFEpilogue = kFWarps + 1;      // warp: partial-tile reduction, h / down-row stores
+constexpr int kFFetch = kFWarps + 2;         // warp: tile-counter polls, h copies
+constexpr int kFAll = kFWarps + 3;
+constexpr int kFThreads = kFAll * 32;
+constexpr int kFNR = 4;                      // partial-tile buffers between compute and epilogue
+constexpr int kFBlk = 32 / kFWarps;          // K blocks per compute warp in a full 2048-element chunk
 constexpr int kFChunk = 2048;               // K elements per item
-constexpr int kFPitch = 1024 + 32;          // bytes per weight row in a slot (bank shift of 8 per row)
-constexpr int kFAPitch = 128 + 16;          // bytes per absmax row in a slot (bank shift of 4 per row)
-constexpr int kFSlotW = 16 * kFPitch;
-constexpr int kFSlot = kFSlotW + 16 * kFAPitch;  // 19200 B
+// A slot holds one item as four TMA boxes: two weight boxes of 8 rows x up to 8 lines of 128 B
+// ([line][row][128 B], 128-byte swizzle: row r's 16-byte units XOR r, conflict-free fragment reads)
+// and their two absmax boxes of 8 rows x up to 32 floats (swizzled by the row width).
+constexpr int kFWBox = 8 * 1024;
+constexpr int kFABox = 32 * 8 * 4;
+constexpr int kFSlot = 2 * kFWBox + 2 * kFABox;  // 18432 B, a multiple of 1024
 constexpr int kFMaxT = 8;
 constexpr int kFMaxR = kFlowMaxPicks;
 constexpr int kFMaxItems = 1024;
@@ -82,6 +121,8 @@ struct FlowArgs {
   __half* h;            // [R, I] fp16 scratch
   unsigned* sync;       // [kFMaxR + 1]: tile counters per active expert, then the finished-CTA count
   int* err;             // sticky device error word
+  int* diag;            // first timed-out wait: [0] taken, [1] site, [2] CTA, [3] item / expert, [4] value
+  uint32_t spins;       // bound of every wait (polls)
   const void* router_w;  // fused router when non-null
   int router_w_dtype, route_kind, renorm;
   int64_t* topk_idx_out;
@@ -92,11 +133,6 @@ struct FlowArgs {
   int drows;            // rows per pick in dval (the CTA's output rows, rounded up to 16)
 };
 
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
   unsigned v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -112,8 +148,46 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Programmatic dependent launch: this grid's CTAs may start while the previous kernel on the
+// stream drains; everything that reads or writes memory another kernel touches waits here.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// Records the first wait of the launch that gave up (site 1: weight copies of item `what`; 2: the
+// tile counter of active expert `what`, `value` = the count seen; 3: the h copy of expert `what`;
+// 4: a ring slot to refill (item `what`); 5: partial tiles to reduce; 6: a reduction buffer).
+__device__ __forceinline__ void note_timeout(const FlowArgs& a, int site, int what, unsigned value) {
+  raise_error(a.err, E4B_ERR_TIMEOUT);
+  if (a.diag && atomicCAS(&a.diag[0], 0, 1) == 0) {
+    a.diag[1] = site;
+    a.diag[2] = blockIdx.x;
+    a.diag[3] = what;
+    a.diag[4] = (int)value;
+  }
+}
+
+// One poll of a barrier phase that suspends at most about a microsecond (explicit suspend-time
+// hint), so a bound in polls is a bound in time: kMaxSpins polls are a few seconds.
+__device__ __forceinline__ bool try_wait_1us(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t spins) {
+  for (uint32_t i = 0; i < spins; ++i)
+    if (try_wait_1us(bar, parity)) return true;
+  return false;
+}
 
 template <typename T> __device__ __forceinline__ T out_cast(float v, int*) { return from_f32<T>(v); }
 template <> __device__ __forceinline__ __half out_cast<__half>(float v, int* err) { return store_cast<__half>(v, err); }
@@ -137,78 +211,55 @@ __device__ __forceinline__ void my_rows(int H, int& r0, int& r1) {
   r1 = (int)(((int64_t)(blockIdx.x + 1) * H) / gridDim.x);
 }
 
-// Copies of one item into its slot (all 32 lanes of the calling warp): lane m < 16 copies weight
-// row m's chunk, lane 16 + m its absmax; rows past the tile's valid count are left as they are.
+__host__ __device__ constexpr int box_lines_of(int kc) { return kc / 256 < 8 ? kc / 256 : 8; }
+__host__ __device__ constexpr int abox_of(int kc) { return kc / 64 < 32 ? kc / 64 : 32; }
+
+// Byte offset of lane (row r of a box, quad lane q)'s 8-byte piece of block bc in a weight box at a
+// 1024-aligned shared address: line bc / 4 holds blocks 4 (bc / 4) .. +3; the swizzle XORs unit with r.
+__device__ __forceinline__ int wpiece(int r, int q, int bc) {
+  const int unit = (((bc & 3) << 1) | (q >> 1)) ^ r;
+  return (bc >> 2) * 1024 + r * 128 + (unit << 4) + ((q & 1) << 3);
+}
+// Byte offset of (row r, block b) in an absmax box whose rows are S = 4 * floats bytes (16..128),
+// stored with the S-byte swizzle (none for 16 B).
+__device__ __forceinline__ int apiece(int r, int b, int S) {
+  return r * S + ((((b >> 2) ^ ((r * S) >> 7)) & (S / 16 - 1)) << 4) + ((b & 3) << 2);
+}
+
+// One item into its slot (one thread): the two 8-row weight boxes and their absmax boxes. A down
+// tile's second box may reach rows of the next CTA's range (read, not used) or past the stack
+// (zero-filled by the TMA unit).
 __device__ __forceinline__ void issue_item(const FlowArgs& a, unsigned w, char* slot, uint64_t* bar,
-                                           const int* act_e, int r0, int nr) {
-  const int lane = threadIdx.x & 31;
+                                           const int* act_e, int r0, const CUtensorMap* wgu, const CUtensorMap* agu,
+                                           const CUtensorMap* wdn, const CUtensorMap* adn) {
   const Item it = item_of(w);
   const int e = act_e[it.j];
   const int K = it.down ? a.I : a.H;
-  const int kc = min(kFChunk, K - it.ch * kFChunk);
-  const uint32_t cb = kc / 2, ab = kc / 16;
-  int nvalid;
-  if (it.down) nvalid = min(16, nr - 16 * it.tile);
-  else nvalid = 16;
-  if (lane == 0) mbar_arrive_expect_tx(bar, nvalid * (cb + ab));
-  __syncwarp();
-  const int m = lane & 15;
-  if (m < nvalid) {
-    int64_t row;
+  // the boxes are as wide as a full chunk of this projection (K < 2048: all of K); a last, shorter
+  // chunk reads past the row end, which the TMA unit zero-fills and still counts
+  const uint32_t wbytes = box_lines_of(K) * 1024, abytes = abox_of(K) * 32;
+  const CUtensorMap* wm = it.down ? wdn : wgu;
+  const CUtensorMap* am = it.down ? adn : agu;
+  mbar_arrive_expect_tx(bar, 2 * (wbytes + abytes));
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    int row;
     if (it.down) {
-      row = (int64_t)e * a.H + r0 + 16 * it.tile + m;
+      row = e * a.H + r0 + 16 * it.tile + 8 * h;
     } else {
       const int n1 = a.has_gate ? 2 * a.I : a.I;
-      row = a.has_gate ? (int64_t)e * n1 + (m < 8 ? 8 * it.tile + m : a.I + 8 * it.tile + m - 8)
-                       : (int64_t)e * n1 + 16 * it.tile + m;
+      row = a.has_gate ? e * n1 + (h == 0 ? 8 * it.tile : a.I + 8 * it.tile) : e * n1 + 16 * it.tile + 8 * h;
     }
-    if (lane < 16) {
-      const uint8_t* src = (it.down ? a.dn_packed : a.gu_packed) + row * (K / 2) + (int64_t)it.ch * (kFChunk / 2);
-      bulk_g2s(slot + m * kFPitch, src, cb, bar);
-    } else {
-      const char* src = reinterpret_cast<const char*>(it.down ? a.dn_absmax : a.gu_absmax) + row * (K / 16) +
-                        (int64_t)it.ch * (kFChunk / 16);
-      bulk_g2s(slot + kFSlotW + m * kFAPitch, src, ab, bar);
-    }
+    tma_load_3d(slot + h * kFWBox, wm, 0, row, it.ch * (kFChunk / 256), bar);
+    tma_load_2d(slot + 2 * kFWBox + h * kFABox, am, it.ch * (kFChunk / 64), row, bar);
   }
-}
-
-// Control thread: bulk-copy expert j's h rows into shared memory once all its gate_up tiles are
-// published. `seen` is a counter value the caller already read (relaxed); when it is short of
-// complete and `blocking`, this waits (acquire, bounded). Returns whether the copy was requested.
-__device__ bool request_h(const FlowArgs& a, int j, bool blocking, unsigned seen, int* hreq, uint64_t* hbar,
-                          const int* act_row0, const int* act_cnt, __half* hs) {
-  if (hreq[j]) return true;
-  const unsigned need = (unsigned)((a.has_gate ? 2 * a.I : a.I) / 16);
-  bool ok = seen >= need;
-  if (ok) {
-    fence_acq_rel_gpu();  // the relaxed observation becomes an acquire
-  } else {
-    if (!blocking) return false;
-    for (uint32_t i = 0; i < kMaxSpins; ++i) {
-      if (ld_acquire_gpu(&a.sync[j]) >= need) {
-        ok = true;
-        break;
-      }
-      __nanosleep(32);
-    }
-  }
-  hreq[j] = 1;
-  if (!ok) {  // gave up: flag it, complete the barrier without data
-    raise_error(a.err, E4B_ERR_TIMEOUT);
-    mbar_arrive(&hbar[j]);
-    return true;
-  }
-  fence_proxy_async_global();  // the acquired h stores, ordered before the async-proxy reads
-  const int n = act_cnt[j], r0 = act_row0[j];
-  mbar_arrive_expect_tx(&hbar[j], (uint32_t)(n * a.I * 2));
-  for (int c = 0; c < n; ++c)
-    bulk_g2s(hs + (int64_t)(r0 + c) * a.hpitch, a.h + (int64_t)(r0 + c) * a.I, (uint32_t)(a.I * 2), &hbar[j]);
-  return true;
 }
 
 template <typename OutT>
-__global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const FlowArgs a) {
+__global__ void __launch_bounds__(kFThreads, 1)
+    nf4_decode_flow_kernel(const FlowArgs a, const __grid_constant__ CUtensorMap wgu,
+                           const __grid_constant__ CUtensorMap agu, const __grid_constant__ CUtensorMap wdn,
+                           const __grid_constant__ CUtensorMap adn) {
   extern __shared__ __align__(1024) char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, q = lane & 3;
@@ -231,31 +282,58 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
   int* act_row0 = tb + 384;                              // [64] first sorted row
   int* act_cnt = tb + 448;                               // [64]
   int* col_row = tb + 512;                               // [64 x 8] sorted row of (active expert, token) or -1
-  int* hreq = tb + 1024;                                 // [64] h copy requested (control thread only)
+  int* hreq = tb + 1024;                                 // [64] h copy requested (fetch warp)
   float* xscale = reinterpret_cast<float*>(tb + 1088);   // [8]
-  int* misc = tb + 1096;                                 // [0] active, [1] items, [2..3] ballot counts
+  int* misc = tb + 1096;                                 // [0] active, [1] items, [2..3] ballot counts, [4] issued
   unsigned* items = reinterpret_cast<unsigned*>(smem + a.o_items);
   float4* red = reinterpret_cast<float4*>(smem + a.o_red);
   float* dval = reinterpret_cast<float*>(smem + a.o_dval);
-  uint64_t* fullb = reinterpret_cast<uint64_t*>(smem + a.o_bars);
-  uint64_t* hbar = fullb + kFMaxSlots;
+  uint64_t* fullb = reinterpret_cast<uint64_t*>(smem + a.o_bars);  // [slot] item landed
+  uint64_t* emptyb = fullb + kFMaxSlots;                            // [slot] compute warps done with it
+  uint64_t* redfull = emptyb + kFMaxSlots;                          // [buffer] partials written
+  uint64_t* redfree = redfull + kFNR;                               // [buffer] partials reduced
+  uint64_t* hbar = redfree + kFNR;                                  // [active expert] h rows landed
 
-  if (tid == 0) {
-    for (int s = 0; s < a.nslots; ++s) mbar_init(&fullb[s], 1);
-    for (int j = 0; j < kFMaxR; ++j) mbar_init(&hbar[j], 1);
-    fence_proxy_async();
+  // ---- prologue: nothing here touches memory that another kernel writes ----------------------
+  FT_K(0);
+  launch_dependents();  // the next layer's grid may be scheduled as this one's CTAs finish
+  if (tid < 4) {        // descriptors into the TMA unit's cache before the first copies
+    const CUtensorMap* m = tid == 0 ? &wgu : tid == 1 ? &agu : tid == 2 ? &wdn : &adn;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
   }
-  if (tid < 64) hreq[tid] = 0;
-  // token rows -> fp16 with a per-row power-of-two scale (one warp per row)
-  if (warp < T) convert_rows_to_f16(a.hidden, a.act_dtype, xs, xscale, T, a.H, warp, kFWarps);
+  if (tid < kFMaxSlots) {
+    mbar_init(&fullb[tid], 1);
+    mbar_init(&emptyb[tid], kFWarps);
+  }
+  if (tid < kFNR) {
+    mbar_init(&redfull[tid], kFWarps);
+    mbar_init(&redfree[tid], 1);
+  }
+  if (tid < kFMaxR) {
+    mbar_init(&hbar[tid], 1);
+    hreq[tid] = 0;
+  }
+  if (tid == 0) misc[4] = 0;
+  fence_proxy_async();
+  if (a.router_w && tid == 32) {  // this CTA's share of the router weights (parameters) into L2
+    const int wb = a.router_w_dtype == E4B_F32 ? 4 : 2;
+    const int64_t bytes = (int64_t)a.E * a.H * wb;
+    const int64_t part = ((bytes / gridDim.x) + 15) / 16 * 16;
+    const int64_t off = part * blockIdx.x;
+    if (off < bytes) prefetch_l2(static_cast<const char*>(a.router_w) + off, (uint32_t)min(part, bytes - off));
+  }
   {  // pair table: entry (byte, lane) = half2(code[hi nibble], code[lo nibble])
     const float code = c_nf4[lane & 15];
 #pragma unroll 4
-    for (int e = warp; e < 256; e += kFWarps) {
+    for (int e = warp; e < 256; e += kFAll) {
       const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
       reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
     }
   }
+  grid_dependency_wait();
+  FT_K(1);
+  // token rows -> fp16 with a per-row power-of-two scale (one warp per row)
+  if (warp < T) convert_rows_to_f16(a.hidden, a.act_dtype, xs, xscale, T, a.H, warp, kFAll);
 
   // ---- routing -----------------------------------------------------------------------------
   const bool fused = a.router_w != nullptr;
@@ -266,7 +344,7 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
     float* logits = reinterpret_cast<float*>(smem + a.o_logits);
     const int tasks = a.E * ((T + kRouterTT - 1) / kRouterTT);
     const bool w16 = a.router_w_dtype != E4B_F32;
-    for (int task = cr + cs * warp; task < tasks; task += cs * kFWarps) {
+    for (int task = cr + cs * warp; task < tasks; task += cs * kFAll) {
       if (w16)
         router_logits_warp16<8>(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, T, a.H, a.E, task % a.E,
                                 (task / a.E) * kRouterTT, logits);
@@ -302,12 +380,14 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
         }
       }
     }
-  } else if (tid < R) {
-    pick_e[tid] = stack_expert(a.topk_idx[tid], a.emap, a.routed, a.E, a.err, blockIdx.x == 0);
-    pw[tid] = load_as_f32(a.topk_w, a.w_dtype, tid);
+  } else if (tid >= kFProducer * 32 && tid - kFProducer * 32 < R) {  // warps 8-9: their loads beside the rows'
+    const int i = tid - kFProducer * 32;
+    pick_e[i] = stack_expert(a.topk_idx[i], a.emap, a.routed, a.E, a.err, blockIdx.x == 0);
+    pw[i] = load_as_f32(a.topk_w, a.w_dtype, i);
   }
   __syncthreads();
 
+  FT_K(2);
   // ---- permutation: stable rank by (expert, flat index), as fast.py:126-133 -------------------
   if (tid < R) {
     const int e = pick_e[tid];
@@ -360,11 +440,12 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
       for (int rt = 0; rt < ntl; ++rt)
         for (int c = 0; c < chI; ++c) items[n++] = item_word(true, j, rt, c);
     };
+    int first = blockIdx.x;  // this CTA's first tile of expert j: tiles are dealt round-robin over the grid
     for (int j = 0; j < nact; ++j) {
-      const int64_t base = (int64_t)j * tpe;
-      int64_t g = base + ((((int64_t)blockIdx.x - base) % G) + G) % G;
-      for (; g < base + tpe; g += G)
-        for (int c = 0; c < chH; ++c) items[n++] = item_word(false, j, (int)(g - base), c);
+      int tt = first;
+      for (; tt < tpe; tt += G)
+        for (int c = 0; c < chH; ++c) items[n++] = item_word(false, j, tt, c);
+      first = tt - tpe;  // the next expert continues the deal where this one stopped
       if (j >= kFLag) push_down(j - kFLag);
     }
     for (int j = max(0, nact - kFLag); j < nact; ++j) push_down(j);
@@ -373,126 +454,79 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
   __syncthreads();
   const int nitems = misc[1];
   const int S = a.nslots;
-  if (warp == 0)
-    for (int n = 0; n < S && n < nitems; ++n) issue_item(a, items[n], ring + n * kFSlot, &fullb[n], act_e, r0, nr);
-
-  // ---- the item stream -----------------------------------------------------------------------
+  FT_K(3);
+  const unsigned need = (unsigned)(n1 / 16);  // gate_up tiles of an expert
   bool dead = false;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  uint4 bf[2][2];          // B fragments of this warp's two blocks (token rows or h rows)
-  int bkey = -1;           // which (kind, expert, chunk) they hold
-  int next_h = 0;          // control thread: next expert whose h to prefetch (down order) ...
-  unsigned seen = 0;       // ... and its counter as last read (relaxed; consumed one item later)
-  bool polled = false;
-  for (int n = 0; n < nitems; ++n) {
-    const Item it = item_of(items[n]);
-    const int K = it.down ? a.I : a.H;
-    const int nch = it.down ? chI : chH;
-    const int nb = min(kFChunk, K - it.ch * kFChunk) / 64;
-    char* slot = ring + (n % S) * kFSlot;
-    if (it.ch == 0) acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-    // B fragments: column gq = token gq (gate_up: its fp16 row; down: its h row for expert j)
-    const int key = it.down ? (1 << 30) | (it.j << 8) | it.ch : it.ch;
-    if (key != bkey) {
-      if (it.down) {
-        if (tid == 0) request_h(a, it.j, true, 0u, hreq, hbar, act_row0, act_cnt, hs);
-        if (!mbar_wait(&hbar[it.j], 0)) {
-          if (lane == 0) raise_error(a.err, E4B_ERR_TIMEOUT);
+
+  if (warp == kFProducer) {
+    // ---- producer: items into the ring as the compute warps release slots -----------------------
+    if (lane == 0) {
+      for (int n = 0; n < nitems && !dead; ++n) {
+        const int s_ = n % S;
+        if (n >= S && !wait_bar(&emptyb[s_], ((n / S) - 1) & 1, a.spins)) {
+          note_timeout(a, 4, n, 0);
+          dead = true;
+          break;
         }
-      }
-#pragma unroll
-      for (int bi = 0; bi < 2; ++bi) {
-        const int b = warp + 16 * bi;
-        bf[bi][0] = bf[bi][1] = make_uint4(0, 0, 0, 0);
-        if (b < nb && gq < T) {
-          const __half* src = nullptr;
-          if (!it.down) {
-            src = xs + (int64_t)gq * a.H + it.ch * kFChunk + b * 64 + q * 16;
-          } else {
-            const int sr = col_row[it.j * 8 + gq];
-            if (sr >= 0) src = hs + (int64_t)sr * a.hpitch + it.ch * kFChunk + b * 64 + q * 16;
-          }
-          if (src) {
-            bf[bi][0] = *reinterpret_cast<const uint4*>(src);
-            bf[bi][1] = *reinterpret_cast<const uint4*>(src + 8);
-          }
-        }
-      }
-      bkey = key;
-    }
-    if (!dead && !mbar_wait(&fullb[n % S], (n / S) & 1)) {
-      raise_error(a.err, E4B_ERR_TIMEOUT);
-      dead = true;
-    }
-    if (!dead) {
-#pragma unroll
-      for (int bi = 0; bi < 2; ++bi) {
-        const int b = warp + 16 * bi;
-        if (b < nb) {
-          const uint2 wa = *reinterpret_cast<const uint2*>(slot + gq * kFPitch + b * 32 + q * 8);
-          const uint2 wb = *reinterpret_cast<const uint2*>(slot + (gq + 8) * kFPitch + b * 32 + q * 8);
-          const float sa = *reinterpret_cast<const float*>(slot + kFSlotW + gq * kFAPitch + b * 4);
-          const float sb = *reinterpret_cast<const float*>(slot + kFSlotW + (gq + 8) * kFAPitch + b * 4);
-          float pp[4];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const uint32_t w0 = jj < 2 ? wa.x : wa.y, w1 = jj < 2 ? wb.x : wb.y;
-            uint32_t a0, a1, a2, a3;
-            if (jj & 1) {
-              a0 = lut2<2>(lut, w0, lane4); a2 = lut2<3>(lut, w0, lane4);
-              a1 = lut2<2>(lut, w1, lane4); a3 = lut2<3>(lut, w1, lane4);
-            } else {
-              a0 = lut2<0>(lut, w0, lane4); a2 = lut2<1>(lut, w0, lane4);
-              a1 = lut2<0>(lut, w1, lane4); a3 = lut2<1>(lut, w1, lane4);
-            }
-            const uint32_t* xw = reinterpret_cast<const uint32_t*>(&bf[bi][jj >> 1]);
-            if (jj == 0)
-              mma16816_zero(pp, a0, a1, a2, a3, xw[0], xw[1]);
-            else
-              mma16816(pp, a0, a1, a2, a3, xw[(jj & 1) * 2], xw[(jj & 1) * 2 + 1]);
-          }
-          acc[0] = fmaf(pp[0], sa, acc[0]);
-          acc[1] = fmaf(pp[1], sa, acc[1]);
-          acc[2] = fmaf(pp[2], sb, acc[2]);
-          acc[3] = fmaf(pp[3], sb, acc[3]);
-        }
+        issue_item(a, items[n], ring + s_ * kFSlot, &fullb[s_], act_e, r0, &wgu, &agu, &wdn, &adn);
+        misc[4] = n + 1;  // items issued (the drain waits for these only)
       }
     }
-    const bool last = it.ch == nch - 1;
-    if (last) red[(n & 1) * kFThreads + warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
-    dead = __syncthreads_or(dead);
-    if (warp == 0 && !dead && n + S < nitems) issue_item(a, items[n + S], slot, &fullb[n % S], act_e, r0, nr);
-    if (tid == 0) {  // prefetch the h of the next expert whose down tile comes, once it is ready
-      while (next_h < nact && hreq[next_h]) {
-        ++next_h;
-        polled = false;
-      }
-      if (next_h < nact) {
-        if (polled) request_h(a, next_h, false, seen, hreq, hbar, act_row0, act_cnt, hs);
-        if (!hreq[next_h]) {  // read the counter now, look at the value after the next item
-          seen = ld_relaxed_gpu(&a.sync[next_h]);
-          polled = true;
+  } else if (warp == kFFetch) {
+    // ---- fetch: h rows of each expert, in down order, once its gate_up tiles are all published -------
+    if (lane == 0 && nr > 0) {
+      int j = 0;
+      for (uint32_t i = 0; i < a.spins && j < nact; ++i) {
+        if (ld_relaxed_gpu(&a.sync[j]) < need) {
+          __nanosleep(64);
+          continue;
         }
+        fence_acq_rel_gpu();          // the relaxed observation becomes an acquire
+        fence_proxy_async_global();   // the acquired h stores, before the async-proxy reads
+        const int cnt = act_cnt[j], row0 = act_row0[j];
+        mbar_arrive_expect_tx(&hbar[j], (uint32_t)(cnt * a.I * 2));
+        for (int c = 0; c < cnt; ++c)
+          bulk_g2s(hs + (int64_t)(row0 + c) * a.hpitch, a.h + (int64_t)(row0 + c) * a.I, (uint32_t)(a.I * 2),
+                   &hbar[j]);
+        hreq[j] = 1;
+        ++j;
+      }
+      for (; j < nact; ++j) {  // gave up: complete the barriers without data
+        note_timeout(a, 2, j, ld_relaxed_gpu(&a.sync[j]));
+        hreq[j] = 1;
+        mbar_arrive(&hbar[j]);
       }
     }
-    if (last && warp == (n & (kFWarps - 1))) {
-      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int w = 0; w < kFWarps; ++w) {  // fixed warp order
-        const float4 v = red[(n & 1) * kFThreads + w * 32 + lane];
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
+  } else if (warp == kFEpilogue) {
+    // ---- epilogue: reduce each tile's partials in fixed warp order, publish h / keep down rows ----
+    int t = 0;
+    for (int n = 0; n < nitems; ++n) {
+      const Item it = item_of(items[n]);
+      if (it.ch != (it.down ? chI : chH) - 1) continue;
+      const int rb = t % kFNR;
+      if (!wait_bar(&redfull[rb], (t / kFNR) & 1, a.spins)) {
+        if (lane == 0) note_timeout(a, 5, n, 0);
+        break;
       }
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int w = 0; w < kFWarps; ++w) {
+        const float4 v = red[rb * kFWarps * 32 + w * 32 + lane];
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&redfree[rb]);  // the buffer is read: the compute warps may refill it
+      ++t;
       const int c0 = act_row0[it.j], cn = act_cnt[it.j];
       if (!it.down) {
         // rows gq (gate / row) and gq + 8 (up / row + 8); columns 2q, 2q + 1 are tokens
         for (int r = c0; r < c0 + cn; ++r) {
-          const int t = sorted_tok[r];
-          if ((t >> 1) != q) continue;
-          const float sc = xscale[t];
-          const float va = ((t & 1) ? s.y : s.x) * sc, vb = ((t & 1) ? s.w : s.z) * sc;
+          const int tk = sorted_tok[r];
+          if ((tk >> 1) != q) continue;
+          const float sc = xscale[tk];
+          const float va = ((tk & 1) ? sum.y : sum.x) * sc, vb = ((tk & 1) ? sum.w : sum.z) * sc;
           __half* hrow = a.h + (int64_t)r * a.I;
           if (a.has_gate) {
             hrow[8 * it.tile + gq] = store_cast<__half>(silu_f32(va) * vb, a.err);
@@ -501,20 +535,123 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
             hrow[16 * it.tile + 8 + gq] = store_cast<__half>(silu_f32(vb), a.err);
           }
         }
-        __threadfence();
         __syncwarp();
-        if (lane == 0) red_release_gpu_add(&a.sync[it.j], 1u);
+        if (lane == 0) {
+          __threadfence();
+          red_release_gpu_add(&a.sync[it.j], 1u);
+        }
       } else {
         for (int r = c0; r < c0 + cn; ++r) {
-          const int t = sorted_tok[r];
-          if ((t >> 1) != q) continue;
+          const int tk = sorted_tok[r];
+          if ((tk >> 1) != q) continue;
           const int rl = 16 * it.tile + gq;
-          if (rl < nr) dval[r * a.drows + rl] = (t & 1) ? s.y : s.x;
-          if (rl + 8 < nr) dval[r * a.drows + rl + 8] = (t & 1) ? s.w : s.z;
+          if (rl < nr) dval[r * a.drows + rl] = (tk & 1) ? sum.y : sum.x;
+          if (rl + 8 < nr) dval[r * a.drows + rl + 8] = (tk & 1) ? sum.w : sum.z;
         }
       }
     }
+  } else {
+    // ---- compute warps: every 8th K block of each item, partial tiles to the epilogue -------------
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    uint4 bf[kFBlk][2];  // B fragments of this warp's blocks (token rows or h rows)
+    int bkey = -1;   // which (kind, expert, chunk) they hold
+    int t = 0;       // finished tiles
+    for (int n = 0; n < nitems; ++n) {
+      FT_I(n, 0);
+      const Item it = item_of(items[n]);
+      const int K = it.down ? a.I : a.H;
+      const int nch = it.down ? chI : chH;
+      const int nb = min(kFChunk, K - it.ch * kFChunk) / 64;
+      const int arow = abox_of(K) * 4;  // bytes per absmax box row
+      const int s_ = n % S;
+      const char* slot = ring + s_ * kFSlot;
+      if (it.ch == 0) acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+      // B fragments: column gq = token gq (gate_up: its fp16 row; down: its h row for expert j)
+      const int key = it.down ? (1 << 30) | (it.j << 8) | it.ch : it.ch;
+      if (key != bkey) {
+        if (it.down && !dead && !wait_bar(&hbar[it.j], 0, a.spins)) {
+          if (lane == 0) note_timeout(a, 3, it.j, 0);
+          dead = true;
+        }
+#pragma unroll
+        for (int bi = 0; bi < kFBlk; ++bi) {
+          const int b = warp + kFWarps * bi;
+          bf[bi][0] = bf[bi][1] = make_uint4(0, 0, 0, 0);
+          if (b < nb && gq < T) {
+            const __half* src = nullptr;
+            if (!it.down) {
+              src = xs + (int64_t)gq * a.H + it.ch * kFChunk + b * 64 + q * 16;
+            } else {
+              const int sr = col_row[it.j * 8 + gq];
+              if (sr >= 0) src = hs + (int64_t)sr * a.hpitch + it.ch * kFChunk + b * 64 + q * 16;
+            }
+            if (src) {
+              bf[bi][0] = *reinterpret_cast<const uint4*>(src);
+              bf[bi][1] = *reinterpret_cast<const uint4*>(src + 8);
+            }
+          }
+        }
+        bkey = key;
+      }
+      FT_I(n, 1);
+      if (!dead && !wait_bar(&fullb[s_], (n / S) & 1, a.spins)) {
+        if (lane == 0) note_timeout(a, 1, n, 0);
+        dead = true;
+      }
+      FT_I(n, 2);
+      if (!dead) {
+#pragma unroll
+        for (int bi = 0; bi < kFBlk; ++bi) {
+          const int b = warp + kFWarps * bi;
+          if (b < nb) {
+            const uint2 wa = *reinterpret_cast<const uint2*>(slot + wpiece(gq, q, b));
+            const uint2 wb = *reinterpret_cast<const uint2*>(slot + kFWBox + wpiece(gq, q, b));
+            const float sa = *reinterpret_cast<const float*>(slot + 2 * kFWBox + apiece(gq, b, arow));
+            const float sb = *reinterpret_cast<const float*>(slot + 2 * kFWBox + kFABox + apiece(gq, b, arow));
+            float pp[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              const uint32_t w0 = jj < 2 ? wa.x : wa.y, w1 = jj < 2 ? wb.x : wb.y;
+              uint32_t a0, a1, a2, a3;
+              if (jj & 1) {
+                a0 = lut2<2>(lut, w0, lane4); a2 = lut2<3>(lut, w0, lane4);
+                a1 = lut2<2>(lut, w1, lane4); a3 = lut2<3>(lut, w1, lane4);
+              } else {
+                a0 = lut2<0>(lut, w0, lane4); a2 = lut2<1>(lut, w0, lane4);
+                a1 = lut2<0>(lut, w1, lane4); a3 = lut2<1>(lut, w1, lane4);
+              }
+              const uint32_t* xw = reinterpret_cast<const uint32_t*>(&bf[bi][jj >> 1]);
+              if (jj == 0)
+                mma16816_zero(pp, a0, a1, a2, a3, xw[0], xw[1]);
+              else
+                mma16816(pp, a0, a1, a2, a3, xw[(jj & 1) * 2], xw[(jj & 1) * 2 + 1]);
+            }
+            acc[0] = fmaf(pp[0], sa, acc[0]);
+            acc[1] = fmaf(pp[1], sa, acc[1]);
+            acc[2] = fmaf(pp[2], sb, acc[2]);
+            acc[3] = fmaf(pp[3], sb, acc[3]);
+          }
+        }
+      }
+      FT_I(n, 3);
+      fence_proxy_async();  // this warp's reads of the slot, before its refill by the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&emptyb[s_]);
+      if (it.ch == nch - 1) {  // the tile's partial sums to a reduction buffer
+        const int rb = t % kFNR;
+        if (t >= kFNR && !dead && !wait_bar(&redfree[rb], ((t / kFNR) - 1) & 1, a.spins)) {
+          if (lane == 0) note_timeout(a, 6, n, 0);
+          dead = true;
+        }
+        red[rb * kFWarps * 32 + warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&redfull[rb]);
+        ++t;
+      }
+      FT_I(n, 4);
+    }
   }
+  FT_K(4);
   __syncthreads();
 
   // ---- combine: out[t, r] = sum over slots, in order, of down[inv[t*k+s], r] * w[t, s] -----------
@@ -527,10 +664,11 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
 
   // ---- drain, then the last CTA re-arms the counters for the next launch -------------------------
   if (tid == 0) {
-    if (dead)
-      for (int n = max(0, nitems - S); n < nitems; ++n) (void)mbar_wait(&fullb[n % S], (n / S) & 1);
+    // every copy still in flight lands before the CTA exits: the ring's last S items and the h rows
+    const int issued = misc[4];
+    for (int n = max(0, issued - S); n < issued; ++n) (void)wait_bar(&fullb[n % S], (n / S) & 1, a.spins);
     for (int j = 0; j < nact; ++j)
-      if (hreq[j]) (void)mbar_wait(&hbar[j], 0);
+      if (hreq[j]) (void)wait_bar(&hbar[j], 0, a.spins);
     __threadfence();
     const unsigned prev = atomicAdd(&a.sync[kFMaxR], 1u);
     if (prev == (unsigned)G - 1) {
@@ -539,6 +677,7 @@ __global__ void __launch_bounds__(kFThreads, 1) nf4_decode_flow_kernel(const Flo
       __threadfence();
     }
   }
+  FT_K(5);
   if (fused) cluster_wait();
 }
 
@@ -563,13 +702,14 @@ static bool flow_plan(const e4b_moe_desc& d, int grid, FlowPlan& p) {
   p.o_items = o;
   o = round_up(o + kFMaxItems * 4, 128);
   p.o_red = o;
-  o = round_up(o + 2 * kFThreads * 16, 128);
+  o = round_up(o + kFNR * kFWarps * 32 * 16, 128);
   const int max_rows = (d.hidden + grid - 1) / grid;
   p.drows = round_up(max_rows, 16);
   p.o_dval = o;
   o = round_up(o + R * p.drows * 4, 128);
   p.o_bars = o;
-  o = round_up(o + (kFMaxSlots + kFMaxR) * 8, 128);
+  o = round_up(o + (2 * kFMaxSlots + 2 * kFNR + kFMaxR) * 8, 128);
+  o = round_up(o, 1024);  // the swizzled boxes follow the shared address: 1024-aligned slots
   p.o_ring = o;
   const int slots = (kSmemCap - o) / kFSlot;
   p.nslots = slots > kFMaxSlots ? kFMaxSlots : slots;
@@ -649,6 +789,25 @@ static bool configure(DevInfo& di, int idx) {
   return true;
 }
 
+// Bound of every wait of the flow kernel, in polls (E4B_FLOW_SPINS overrides, for diagnosis).
+uint32_t flow_spins() {
+  static const uint32_t v = [] {
+    const char* e = getenv("E4B_FLOW_SPINS");
+    const long n = e ? atol(e) : 0;
+    return n > 0 ? (uint32_t)n : kMaxSpins;
+  }();
+  return v;
+}
+
+// E4B_FLOW_PDL=0 launches without programmatic dependent launch (A/B timing).
+bool flow_pdl() {
+  static const int v = [] {
+    const char* e = getenv("E4B_FLOW_PDL");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return v != 0;
+}
+
 }  // namespace
 
 bool decode_flow_eligible(const e4b_moe_desc& d, bool fused_router) {
@@ -656,7 +815,11 @@ bool decode_flow_eligible(const e4b_moe_desc& d, bool fused_router) {
   if (d.weight_format != E4B_FMT_NF4 || d.lora_rank != 0) return false;
   if (d.tokens < 1 || d.tokens > kFMaxT || (int64_t)d.tokens * d.top_k > kFMaxR) return false;
   if (d.hidden % 256 || d.intermediate % 256) return false;
+  // absmax boxes of 4, 8, 16 or 32 floats (a power of two under the box swizzle)
+  for (int K : {d.hidden, d.intermediate})
+    if (K < 2048 && (K & (K - 1))) return false;
   if (d.intermediate / 8 > 0xFFFF) return false;
+  if (!encode_tiled_fn()) return false;
   if (!is_act_dtype(d.act_dtype)) return false;
   if ((int64_t)d.num_experts * (d.has_gate ? 2 * d.intermediate : d.intermediate) >= (1ll << 31)) return false;
   if ((int64_t)d.num_experts * d.hidden >= (1ll << 31)) return false;
@@ -705,6 +868,8 @@ e4b_status launch_decode_flow(const e4b_moe_desc& d, const e4b_moe_tensors* t, v
   a.h = static_cast<__half*>(h);
   a.sync = static_cast<unsigned*>(sync);
   a.err = err;
+  a.diag = err + kFlowDiagWord;
+  a.spins = flow_spins();
   if (fused) {
     a.router_w = router->weight;
     a.router_w_dtype = router->weight_dtype;
@@ -731,18 +896,49 @@ e4b_status launch_decode_flow(const e4b_moe_desc& d, const e4b_moe_tensors* t, v
   cfg.blockDim = dim3(kFThreads);
   cfg.dynamicSmemBytes = p.total;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = fused ? di->cluster : 1;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (flow_pdl()) {  // programmatic dependent launch (the kernel waits before touching shared memory)
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (fused) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = di->cluster;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = at;
-  cfg.numAttrs = fused ? 1 : 0;
+  cfg.numAttrs = na;
+  // packed bytes as [lines (K/256)][rows][128 B]: a box of 8 rows x up to 8 lines lands row-major per
+  // line, 128-byte swizzled; absmax as [rows][K/64] floats in boxes of 8 rows x up to 32 floats
+  auto maps = [&](CUtensorMap& w, CUtensorMap& am, const void* packed, const void* absmax, int64_t rows, int K) {
+    const cuuint64_t wdims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 256)};
+    const cuuint64_t wstr[2] = {(cuuint64_t)(K / 2), 128};
+    const cuuint32_t wbox[3] = {128, 8, (cuuint32_t)box_lines_of(K)};
+    const cuuint64_t adims[2] = {(cuuint64_t)(K / 64), (cuuint64_t)rows};
+    const cuuint64_t astr[1] = {(cuuint64_t)(K / 64) * 4};
+    const cuuint32_t abox[2] = {(cuuint32_t)abox_of(K), 8};
+    const int S = abox_of(K) * 4;
+    const CUtensorMapSwizzle asw = S == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : S == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                   : S == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                             : CU_TENSOR_MAP_SWIZZLE_NONE;
+    return encode_tiled(&w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, packed, wdims, wstr, wbox, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_tiled(&am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, absmax, adims, astr, abox, asw);
+  };
+  CUtensorMap wgu, agu, wdn, adn;
+  const int n1 = d.has_gate ? 2 * d.intermediate : d.intermediate;
+  if (!maps(wgu, agu, t->gate_up_packed, t->gate_up_absmax, (int64_t)d.num_experts * n1, d.hidden) ||
+      !maps(wdn, adn, t->down_packed, t->down_absmax, (int64_t)d.num_experts * d.hidden, d.intermediate))
+    return E4B_ERR_CUDA;
   cudaError_t e;
   switch (d.out_dtype) {
-    case E4B_BF16: e = cudaLaunchKernelEx(&cfg, nf4_decode_flow_kernel<__nv_bfloat16>, a); break;
-    case E4B_F16: e = cudaLaunchKernelEx(&cfg, nf4_decode_flow_kernel<__half>, a); break;
-    default: e = cudaLaunchKernelEx(&cfg, nf4_decode_flow_kernel<float>, a); break;
+    case E4B_BF16: e = cudaLaunchKernelEx(&cfg, nf4_decode_flow_kernel<__nv_bfloat16>, a, wgu, agu, wdn, adn); break;
+    case E4B_F16: e = cudaLaunchKernelEx(&cfg, nf4_decode_flow_kernel<__half>, a, wgu, agu, wdn, adn); break;
+    default: e = cudaLaunchKernelEx(&cfg, nf4_decode_flow_kernel<float>, a, wgu, agu, wdn, adn); break;
   }
   return e == cudaSuccess ? E4B_OK : E4B_ERR_CUDA;
 }

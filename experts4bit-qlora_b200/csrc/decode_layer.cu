@@ -705,14 +705,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 // One-launch decode kernels: 0 off (multi-kernel path), 1 the flow kernel where it applies and the
-// phase kernel elsewhere, 2 the phase kernel only. -1: not yet read from E4B_DECODE_KERNEL.
+// phase kernel elsewhere, 2 the phase kernel only (the default: it is the faster of the two on
+// the decode shapes measured so far). -1: not yet read from E4B_DECODE_KERNEL.
 std::atomic<int> g_decode_mode{-1};
 
 int decode_mode() {
   int m = g_decode_mode.load(std::memory_order_relaxed);
   if (m < 0) {
     const char* v = getenv("E4B_DECODE_KERNEL");
-    const int env = v ? (v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1) : 1;
+    const int env = v ? (v[0] == '0' ? 0 : v[0] == '1' ? 1 : 2) : 2;
     int expected = -1;
     g_decode_mode.compare_exchange_strong(expected, env);
     m = g_decode_mode.load(std::memory_order_relaxed);
@@ -742,6 +743,10 @@ bool decode_layer_eligible(const e4b_moe_desc& d) {
   if (d.weight_format != E4B_FMT_NF4 || d.lora_rank != 0) return false;
   if (d.tokens < 1 || d.tokens > 16 || (int64_t)d.tokens * d.top_k > kMaxPicks) return false;
   if (d.hidden % 256 || d.intermediate % 256) return false;
+  // the absmax boxes are 4, 8, 16 or 32 blocks wide (a power of two under the box swizzle): each
+  // K is 256, 512, 1024 or a multiple of 2048
+  for (int K : {d.hidden, d.intermediate})
+    if (K > 1024 ? K % 2048 : (K & (K - 1))) return false;
   if ((int64_t)d.tokens * (d.hidden + 8) * 2 > kDXBudget) return false;
   if ((int64_t)d.tokens * d.hidden > 2 * kThreads * 8) return false;  // two 16-byte vectors of rows per thread
   if (d.tokens > 16) return false;
@@ -758,15 +763,17 @@ static e4b_status launch_decode(const DecodeArgs& a, cudaStream_t s) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return E4B_ERR_CUDA;
   const unsigned long long bit = 1ull << dev;
   auto kern = nf4_decode_layer_kernel<OutT, NT>;
-  std::lock_guard<std::mutex> lk(g_dl_mu);
-  if (!(configured & bit)) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DSmem::total) != cudaSuccess)
-      return E4B_ERR_CUDA;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, DSmem::total) != cudaSuccess ||
-        per_sm < 1)
-      return E4B_ERR_UNSUPPORTED;
-    configured |= bit;
+  {
+    std::lock_guard<std::mutex> lk(g_dl_mu);  // released before decode_layer_grid() takes it again
+    if (!(configured & bit)) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DSmem::total) != cudaSuccess)
+        return E4B_ERR_CUDA;
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, DSmem::total) != cudaSuccess ||
+          per_sm < 1)
+        return E4B_ERR_UNSUPPORTED;
+      configured |= bit;
+    }
   }
   const int n1 = a.has_gate ? 2 * a.I : a.I;
   CUtensorMap wgu, agu, wdn, adn;

@@ -467,11 +467,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       const float* am = g.absmax + ((int64_t)ti.e * g.N + row) * (g.K / 64);
-      float am_next = h < GROUPS ? __ldg(am) : 0.f;
+      // absmax four chunks at a time (one 16-byte load when K % 256 == 0 keeps it aligned, else
+      // four scalar loads), the next group loaded one group ahead so its latency hides behind four
+      // chunks of decode
+      const bool vec4 = (g.K & 255) == 0;
+      auto load4 = [&](int c0) {
+        if (vec4) return __ldg(reinterpret_cast<const float4*>(am + c0));
+        float4 v;
+        v.x = __ldg(am + c0);
+        v.y = c0 + 1 < kchunks ? __ldg(am + c0 + 1) : 0.f;
+        v.z = c0 + 2 < kchunks ? __ldg(am + c0 + 2) : 0.f;
+        v.w = c0 + 3 < kchunks ? __ldg(am + c0 + 3) : 0.f;
+        return v;
+      };
+      float4 am_cur = make_float4(0.f, 0.f, 0.f, 0.f), am_nxt = am_cur;
+      if (h < GROUPS) {
+        am_cur = load4(0);
+        if (kchunks > 4) am_nxt = load4(4);
+      }
       for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
         const int s = nw % kSW, sa = na % kSA;
-        const float a = am_next;
-        if (h < GROUPS && c + 1 < kchunks) am_next = __ldg(am + c + 1);
+        if ((c & 3) == 0 && c > 0) {
+          am_cur = am_nxt;
+          if (h < GROUPS && c + 4 < kchunks) am_nxt = load4(c + 4);
+        }
+        const float a = (c & 3) == 0 ? am_cur.x : (c & 3) == 1 ? am_cur.y : (c & 3) == 2 ? am_cur.z : am_cur.w;
         if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
         uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
         if (h < GROUPS) {

@@ -377,9 +377,13 @@ def moe_decode_step_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torc
     return N.lib().e4b_moe_decode_step_workspace_bytes(ctypes.byref(d))
 
 
-def set_decode_kernel(enabled: bool) -> int:
-    """Turn the one-launch decode-layer kernel on or off for the process; returns the old setting."""
-    return N.lib().e4b_set_decode_kernel(int(bool(enabled)))
+def set_decode_kernel(mode) -> int:
+    """Select the one-launch decode-layer kernel for the process; returns the old setting.
+
+    ``False``/0 turns it off, ``True``/2 selects the phase kernel (the default), 1 the flow
+    kernel where it applies."""
+    m = 2 if mode is True else 0 if mode is False else int(mode)
+    return N.lib().e4b_set_decode_kernel(m)
 
 
 def moe_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torch.bfloat16, lora_rank=0,

@@ -157,8 +157,10 @@ def test_apply_gate_base_is_patched_and_fused(e4b, T):
         got = mod(x, idx, w)
     anchor = _clamped_anchor(mod, x, idx, w)
     mx, mean = M.rel_errors(got.float(), anchor)
-    assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
-    mx_ref, _ = M.rel_errors(loop.float(), anchor)
+    mx_ref, mean_ref = M.rel_errors(loop.float(), anchor)
+    # the epilogue route keeps the reference's bf16 intermediate (as engines/fast.py:137-156), so
+    # it is held to the reference's own bars against the loop's error, not the fused layer's
+    assert mx <= 1e-2 and mean <= max(2 * mean_ref, 2e-3), (mx, mean, mean_ref)
     assert mx <= max(2 * mx_ref, 5e-3)
     # the clamp is load-bearing: a plain SwiGLU is far off
     plain = e4b.ops.moe_forward(x, idx, w, mod.gate_up_proj, mod.gate_up_absmax, mod.down_proj, mod.down_absmax,
@@ -183,8 +185,12 @@ def test_apply_gate_base_inside_lora_wrapper(e4b):
         got = lm(x, idx, w)
     lora = (lm.gate_up_lora_A, lm.gate_up_lora_B, lm.down_lora_A, lm.down_lora_B, lm.scaling)
     anchor = _clamped_anchor(base, x, idx, w, lora=lora)
+    with torch.no_grad():
+        e4b.disable_fast(lm)
+        loop = lm(x, idx, w)
     mx, mean = M.rel_errors(got.float(), anchor)
-    assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
+    mx_ref, mean_ref = M.rel_errors(loop.float(), anchor)
+    assert mx <= 1e-2 and mean <= max(2 * mean_ref, 2e-3), (mx, mean, mean_ref)
 
 
 def test_graph_survives_workspace_growth(e4b):

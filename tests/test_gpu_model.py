@@ -50,13 +50,15 @@ def test_moe_block_with_drop_in_experts(e4b):
     _swap_experts(e4b, model)
     ours = block.experts
     assert e4b.enable_fast(model) == cfg.num_hidden_layers
-    # HF's own experts on the dequantized NF4 values: the same function the fused layer computes
+    # HF's own experts, in fp32, on the fp32 dequantized NF4 values: the function the fused layer
+    # computes, evaluated without intermediate roundings
+    hf32 = hf_experts.float()
     with torch.no_grad():
         for e in range(cfg.num_experts):
-            hf_experts.gate_up_proj[e].copy_(ours._dequantize_expert(ours.gate_up_proj, ours.gate_up_absmax,
-                                                                     ours._gate_up_shape, e, torch.bfloat16))
-            hf_experts.down_proj[e].copy_(ours._dequantize_expert(ours.down_proj, ours.down_absmax, ours._down_shape,
-                                                                  e, torch.bfloat16))
+            hf32.gate_up_proj[e].copy_(ours._dequantize_expert(ours.gate_up_proj, ours.gate_up_absmax,
+                                                               ours._gate_up_shape, e, torch.float32))
+            hf32.down_proj[e].copy_(ours._dequantize_expert(ours.down_proj, ours.down_absmax, ours._down_shape,
+                                                            e, torch.float32))
     for T in (1, 5, 200):
         h = torch.randn(1, T, cfg.hidden_size, device=DEV).to(torch.bfloat16)
         with torch.no_grad():
@@ -65,9 +67,7 @@ def test_moe_block_with_drop_in_experts(e4b):
             _, w, idx = block.gate(flat)
             prev = torch.backends.cuda.matmul.allow_tf32
             torch.backends.cuda.matmul.allow_tf32 = False
-            hf32 = hf_experts.float()
             anchor = hf32(flat.float(), idx, w.float())
-            hf_experts.to(torch.bfloat16)
             torch.backends.cuda.matmul.allow_tf32 = prev
         mx, mean = M.rel_errors(got.view(-1, cfg.hidden_size).float(), anchor)
         assert mx <= 1e-2 and mean <= 2e-3, (T, mx, mean)

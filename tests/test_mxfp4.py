@@ -136,6 +136,8 @@ def test_fused_mxfp4_layer_vs_fp32(e4b, T):
         anchor.index_add_(0, tok, ((torch.nn.functional.silu(gg) * u) @ wd.t()) * w[tok, pos, None])
     torch.backends.cuda.matmul.allow_tf32 = prev
     mxr, mean = M.rel_errors(got.float(), anchor)
-    assert mxr <= 1e-2 and mean <= 2e-3, (mxr, mean)
-    lmx, _ = M.rel_errors(loop.float(), anchor)
+    lmx, lmean = M.rel_errors(loop.float(), anchor)
+    # h is rounded to bf16 between the projections, as the reference's MXFP4 lane does
+    # (engines/nvme_experts.py:856-862): the reference's bars against its own loop
+    assert mxr <= 1e-2 and mean <= max(2 * lmean, 2e-3), (mxr, mean, lmean)
     assert mxr <= max(2 * lmx, 5e-3)
