@@ -135,6 +135,7 @@ struct DecodeArgs {
   int64_t* topk_idx_out;       // [T, k] (written by CTA 0)
   float* topk_w_out;           // [T, k]
   float* router_logits;        // [T, E] global scratch: logits spread over the grid, then a grid sync
+  float* part;                 // slice kernel: fp32 partial down rows [R][I / 64][H]
 };
 
 struct Tables {
@@ -400,28 +401,8 @@ __device__ void stream_phase(const Phase& p, const Tables& tb, int nact, char* s
   n_run = n0 + total_items;
 }
 
-template <typename OutT, int NT>
-__global__ void __launch_bounds__(kThreads, 1)
-    nf4_decode_layer_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap wmap_gu,
-                            const __grid_constant__ CUtensorMap amap_gu, const __grid_constant__ CUtensorMap wmap_dn,
-                            const __grid_constant__ CUtensorMap amap_dn) {
-  extern __shared__ __align__(1024) char smem[];
-  namespace cg = cooperative_groups;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int R = a.T * a.k;
-  DTRACE(0);
-  if (tid < 4) {  // descriptors into the TMA unit's cache before the first copies
-    const CUtensorMap* m = tid == 0 ? &wmap_gu : tid == 1 ? &amap_gu : tid == 2 ? &wmap_dn : &amap_dn;
-    asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
-  }
-  // token rows into registers first: their latency overlaps the permutation below
-  const int xvec = a.T * (a.H / 8);
-  uint4 xr[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int v = tid + i * kThreads;
-    if (v < xvec) xr[i] = reinterpret_cast<const uint4*>(a.hidden)[v];
-  }
+// The routing tables at DSmem::tables.
+__device__ __forceinline__ Tables tables_of(char* smem) {
   Tables tb;
   int* ti = reinterpret_cast<int*>(smem + DSmem::tables);
   tb.pick_e = ti;
@@ -435,31 +416,90 @@ __global__ void __launch_bounds__(kThreads, 1)
   tb.misc = ti + 7 * kMaxPicks + 16;
   tb.w = reinterpret_cast<float*>(ti + 7 * kMaxPicks + 32);
   tb.rowmax = reinterpret_cast<unsigned*>(ti + 8 * kMaxPicks + 32);
-  int* cta_err = &tb.misc[1];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DSmem::bars);
+  return tb;
+}
+
+// Phase 0 of both one-launch decode kernels, from kernel entry to the first streamed tile: the
+// (fused or given) routing, the stable expert-major permutation of fast.py:126-133 in shared
+// memory, the NF4 pair table and the token rows as fp16 with per-row power-of-two scales.
+// `issue_first(tb, nact)` runs on every thread right after the permutation is known (the caller's
+// copy leaders start their first weight copies there). Returns the number of active experts; the
+// CTA is synchronised on return. The caller initialises its mbarriers (thread 0) before the call.
+template <class IssueFirst>
+__device__ __forceinline__ int decode_prologue(const DecodeArgs& a, char* smem, const Tables& tb,
+                                               IssueFirst&& issue_first) {
+  namespace cg = cooperative_groups;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = a.T * a.k;
+  // token rows into registers first: their latency overlaps the permutation below
+  const int xvec = a.T * (a.H / 8);
+  uint4 xr[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int v = tid + i * kThreads;
+    if (v < xvec) xr[i] = reinterpret_cast<const uint4*>(a.hidden)[v];
+  }
   __half* xs = reinterpret_cast<__half*>(smem + DSmem::x);
   const int xpitch = a.H + 8;
 
-  Phase pa{};
-  pa.wmap = &wmap_gu;
-  pa.amap = &amap_gu;
-  pa.N = a.has_gate ? 2 * a.I : a.I;
-  pa.K = a.H;
-  pa.epilogue = a.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
-  pa.tiles_per_expert = pa.N / 16;
-  pa.x = xs;
-  pa.xpitch = xpitch;
-  pa.x_mapped = true;
-  pa.out = a.h;
-  pa.Nout = a.I;
-
   // ---- phase 0: the permutation first, so the weight stream starts early ------------------
-  if (tid == 0) {
-    tb.misc[1] = 0;
-    for (int s = 0; s < kPairs * kDSlots; ++s) mbar_init(&bars[s], 1);
-    fence_proxy_async();
-  }
+  if (tid == 0) tb.misc[1] = 0;
   if (tid < 16) tb.rowmax[tid] = 0u;
+  // the pair table and the token rows as fp16 (with the per-row power-of-two scale of convert.cuh):
+  // neither depends on the routing, so with the fused router they fill the wait at its grid barrier
+  auto prep = [&]() {
+    {  // pair table
+      char* lut = smem + DSmem::lut;
+      const float code = c_nf4[lane & 15];
+#pragma unroll 4
+      for (int e = warp; e < 256; e += kWarps) {
+        const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
+        reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
+      }
+    }
+    DTRACE(11);
+    {  // token rows -> fp16 with the per-row power-of-two scale of convert.cuh
+      float v[2][8];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int vi = tid + i * kThreads;
+        // a warp's 32 vectors lie in one row (H / 8 is a multiple of 32): reduce, then one atomic
+        if (i * kThreads + warp * 32 < xvec) {
+          float m = 0.f;
+          if (vi < xvec) {
+            unpack8(xr[i], a.act_dtype, v[i]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
+          }
+#pragma unroll
+          for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) atomicMax(&tb.rowmax[vi / (a.H / 8)], __float_as_uint(m));
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int vi = tid + i * kThreads;
+        if (vi < xvec) {
+          const int r = vi / (a.H / 8), c8 = vi - r * (a.H / 8);
+          const float m = __uint_as_float(tb.rowmax[r]);
+          int sh = 0;
+          if (m > 32768.f) {
+            int ex;
+            frexpf(m / 32768.f, &ex);
+            sh = ex;
+          }
+          const float inv = ldexpf(1.f, -sh);
+          uint4 o;
+          uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ow[j] = pack2<__half>(v[i][2 * j] * inv, v[i][2 * j + 1] * inv);
+          *reinterpret_cast<uint4*>(xs + r * xpitch + c8 * 8) = o;
+          if (c8 == 0) tb.xscale[r] = ldexpf(1.f, sh);
+        }
+      }
+    }
+  };
   if (a.router_w) {
     // ---- fused router: logits into shared memory (spread over the grid through global
     // scratch and a grid barrier, or computed by every CTA), then the same top-k everywhere ----
@@ -479,6 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         router_logits_warp(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
                            (task / a.E) * kRouterTT, dst);
     }
+    __syncthreads();  // rowmax cleared
+    prep();
     if (a.router_logits) {
       cg::this_grid().sync();
       for (int i = tid; i < a.T * a.E; i += kThreads) logits[i] = __ldcg(a.router_logits + i);
@@ -552,64 +594,57 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   const int nact = tb.misc[0];
   DTRACE(1);
-  if ((warp & 1) == 0 && lane == 0)  // pair leaders: the first gate_up items
-    issue_head(pa, tb, smem, nact, blockIdx.x * kPairs + (warp >> 1), 0);
+  issue_first(tb, nact);
   if (tid < nact) tb.act_cnt[tid] = (tid + 1 < nact ? tb.act_row0[tid + 1] : R) - tb.act_row0[tid];
   DTRACE(10);
-  {  // pair table
-    char* lut = smem + DSmem::lut;
-    const float code = c_nf4[lane & 15];
-#pragma unroll 4
-    for (int e = warp; e < 256; e += kWarps) {
-      const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
-      reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
-    }
-  }
-  DTRACE(11);
-  {  // token rows -> fp16 with the per-row power-of-two scale of convert.cuh
-    float v[2][8];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int vi = tid + i * kThreads;
-      // a warp's 32 vectors lie in one row (H / 8 is a multiple of 32): reduce, then one atomic
-      if (i * kThreads + warp * 32 < xvec) {
-        float m = 0.f;
-        if (vi < xvec) {
-          unpack8(xr[i], a.act_dtype, v[i]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) atomicMax(&tb.rowmax[vi / (a.H / 8)], __float_as_uint(m));
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int vi = tid + i * kThreads;
-      if (vi < xvec) {
-        const int r = vi / (a.H / 8), c8 = vi - r * (a.H / 8);
-        const float m = __uint_as_float(tb.rowmax[r]);
-        int sh = 0;
-        if (m > 32768.f) {
-          int ex;
-          frexpf(m / 32768.f, &ex);
-          sh = ex;
-        }
-        const float inv = ldexpf(1.f, -sh);
-        uint4 o;
-        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) ow[j] = pack2<__half>(v[i][2 * j] * inv, v[i][2 * j + 1] * inv);
-        *reinterpret_cast<uint4*>(xs + r * xpitch + c8 * 8) = o;
-        if (c8 == 0) tb.xscale[r] = ldexpf(1.f, sh);
-      }
-    }
-  }
+  if (!a.router_w) prep();
   DTRACE(12);
   __syncthreads();
   DTRACE(13);
+  return nact;
+}
+
+template <typename OutT, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_decode_layer_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap wmap_gu,
+                            const __grid_constant__ CUtensorMap amap_gu, const __grid_constant__ CUtensorMap wmap_dn,
+                            const __grid_constant__ CUtensorMap amap_dn) {
+  extern __shared__ __align__(1024) char smem[];
+  namespace cg = cooperative_groups;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = a.T * a.k;
+  DTRACE(0);
+  if (tid < 4) {  // descriptors into the TMA unit's cache before the first copies
+    const CUtensorMap* m = tid == 0 ? &wmap_gu : tid == 1 ? &amap_gu : tid == 2 ? &wmap_dn : &amap_dn;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+  }
+  const Tables tb = tables_of(smem);
+  int* cta_err = &tb.misc[1];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DSmem::bars);
+  __half* xs = reinterpret_cast<__half*>(smem + DSmem::x);
+  const int xpitch = a.H + 8;
+
+  Phase pa{};
+  pa.wmap = &wmap_gu;
+  pa.amap = &amap_gu;
+  pa.N = a.has_gate ? 2 * a.I : a.I;
+  pa.K = a.H;
+  pa.epilogue = a.has_gate ? E4B_EPI_SWIGLU : E4B_EPI_SILU;
+  pa.tiles_per_expert = pa.N / 16;
+  pa.x = xs;
+  pa.xpitch = xpitch;
+  pa.x_mapped = true;
+  pa.out = a.h;
+  pa.Nout = a.I;
+
+  if (tid == 0) {
+    for (int s = 0; s < kPairs * kDSlots; ++s) mbar_init(&bars[s], 1);
+    fence_proxy_async();
+  }
+  const int nact = decode_prologue(a, smem, tb, [&](const Tables& t, int na) {
+    if ((warp & 1) == 0 && lane == 0)  // pair leaders: the first gate_up items
+      issue_head(pa, t, smem, na, blockIdx.x * kPairs + (warp >> 1), 0);
+  });
 
   // ---- phase A: gate_up --------------------------------------------------------------------
   int n_run = 0;
@@ -702,18 +737,345 @@ __global__ void __launch_bounds__(kThreads, 1)
   DTRACE(9);
 }
 
+// ---- slice kernel -----------------------------------------------------------------------------
+// The layer for 1..8 tokens as independent units of one active expert x 64 intermediate columns
+// (one absmax block of a down row): a CTA streams the unit's 64 gate + 64 up rows over all of H,
+// reduces them across its warps into the unit's 64 h values (SwiGLU, fp16), then streams the
+// unit's 64-column strip of every down row and stores fp32 partial down rows per (pick, strip).
+// No unit waits on another CTA, so gate_up and down run back to back without a grid barrier; one
+// grid barrier before the combine, which sums the strips of each pick in strip order, rounds the
+// sum to fp16 (the down_rows rounding of the multi-kernel path) and weights the picks in slot order.
+//
+// Copies run through a ring of kSSlots stages filled by thread 0: a gate_up stage is 512 K
+// elements of the unit's 128 rows (two 16 KB boxes of [2 lines][64 rows][128 B], 128-byte
+// swizzle, and two [64 rows][8 floats] absmax boxes), a down stage 512 rows of the strip (two
+// [256 rows][32 B] boxes and two [256 rows][4 floats] absmax boxes, the strip's float among the
+// four). In a gate_up stage warp w owns block w / 2 of the stage for tiles 4 (w % 2) .. +3 (a tile
+// is 8 gate rows and the 8 matching up rows), so its token fragments are read once per stage; in
+// a down stage it owns tiles 2w, 2w + 1 (16 rows each) with the unit's h fragment in registers.
+// The per-block arithmetic (pair-table decode, mma.sync m16n8k16, fp32 absmax scaling) is the
+// streaming GEMV's; the blocks of a gate_up row are summed per warp and then across warps in warp
+// order, so the result is deterministic but not bit-identical to the phase kernel's.
+constexpr int kSW = 64;          // intermediate columns per unit
+constexpr int kSGK = 512;        // K elements per gate_up stage
+constexpr int kSDRows = 512;     // down rows per stage
+constexpr int kSSlots = 3;
+constexpr int kSSlot = 36 * 1024;
+constexpr int kSHPitch = kSW + 8;  // halves per h row in shared memory
+
+struct SSmem {
+  static constexpr int ring = DSmem::slots;                 // 1024-aligned
+  static constexpr int red = ring + kSSlots * kSSlot;       // [warp][16][32] fp32 partial tiles
+  static constexpr int hs = red + kWarps * 16 * 32 * 4;     // [8 tokens][kSHPitch] fp16
+  static constexpr int end = hs + 8 * kSHPitch * 2;
+};
+static_assert(SSmem::ring % 1024 == 0 && kSSlot % 1024 == 0, "swizzled boxes need 1024-byte alignment");
+static_assert(SSmem::end <= DSmem::bars, "slice layout overlaps the barriers");
+
+__device__ __forceinline__ void slice_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+struct SliceMaps {
+  const CUtensorMap* gw;  // gate_up packed [lines][rows][128 B], box {128, 64, 2}
+  const CUtensorMap* ga;  // gate_up absmax [rows][H / 64], box {8, 64}, 32-byte swizzle
+  const CUtensorMap* dw;  // down packed [rows][I / 2], box {32, 256}
+  const CUtensorMap* da;  // down absmax [rows][I / 64], box {4, 256}
+};
+
+// Copies of this CTA's stage n into ring slot n % kSSlots (thread 0 only).
+__device__ __forceinline__ void slice_issue(const DecodeArgs& a, const SliceMaps& m, const Tables& tb, char* smem,
+                                            int n, int nsl, int ng, int spu) {
+  const int ui = n / spu, st = n - ui * spu;
+  const int u = blockIdx.x + ui * (int)gridDim.x;
+  const int j = u / nsl, s = u - j * nsl;
+  const int e = tb.act_e[j];
+  char* slot = smem + SSmem::ring + (n % kSSlots) * kSSlot;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + DSmem::bars) + (n % kSSlots);
+  if (st < ng) {
+    const int r0 = e * 2 * a.I + s * kSW, r1 = r0 + a.I;
+    mbar_arrive_expect_tx(full, 2 * 16384 + 2 * 2048);
+    tma_load_3d(slot, m.gw, 0, r0, 2 * st, full);
+    tma_load_3d(slot + 16384, m.gw, 0, r1, 2 * st, full);
+    tma_load_2d(slot + 32768, m.ga, 8 * st, r0, full);
+    tma_load_2d(slot + 34816, m.ga, 8 * st, r1, full);
+  } else {
+    const int r0 = e * a.H + (st - ng) * kSDRows;
+    mbar_arrive_expect_tx(full, 16384 + 8192);
+    tma_load_2d(slot, m.dw, 32 * s, r0, full);
+    tma_load_2d(slot + 8192, m.dw, 32 * s, r0 + 256, full);
+    tma_load_2d(slot + 16384, m.da, 4 * (s >> 2), r0, full);
+    tma_load_2d(slot + 20480, m.da, 4 * (s >> 2), r0 + 256, full);
+  }
+}
+
+// One 64-element block of a 16-row tile against one token fragment: rows A (w0, scale sa) and
+// B (w1, scale sb), the streaming GEMV's fragment order.
+__device__ __forceinline__ void slice_block(float (&acc)[4], const char* lut, uint2 w0v, uint2 w1v, float sa,
+                                            float sb, const uint4 (&xf)[2], uint32_t lane4) {
+  float pp[4];
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const uint32_t w0 = jj < 2 ? w0v.x : w0v.y, w1 = jj < 2 ? w1v.x : w1v.y;
+    uint32_t a0, a1, a2, a3;
+    if (jj & 1) {
+      a0 = lut2<2>(lut, w0, lane4); a2 = lut2<3>(lut, w0, lane4);
+      a1 = lut2<2>(lut, w1, lane4); a3 = lut2<3>(lut, w1, lane4);
+    } else {
+      a0 = lut2<0>(lut, w0, lane4); a2 = lut2<1>(lut, w0, lane4);
+      a1 = lut2<0>(lut, w1, lane4); a3 = lut2<1>(lut, w1, lane4);
+    }
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xf[jj >> 1]);
+    if (jj == 0)
+      mma16816_zero(pp, a0, a1, a2, a3, xw[0], xw[1]);
+    else
+      mma16816(pp, a0, a1, a2, a3, xw[(jj & 1) * 2], xw[(jj & 1) * 2 + 1]);
+  }
+  acc[0] = fmaf(pp[0], sa, acc[0]);
+  acc[1] = fmaf(pp[1], sa, acc[1]);
+  acc[2] = fmaf(pp[2], sb, acc[2]);
+  acc[3] = fmaf(pp[3], sb, acc[3]);
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_decode_slice_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap gw, const __grid_constant__ CUtensorMap ga,
+                            const __grid_constant__ CUtensorMap dw, const __grid_constant__ CUtensorMap da) {
+  extern __shared__ __align__(1024) char smem[];
+  namespace cg = cooperative_groups;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, q = lane & 3;
+  const uint32_t lane4 = (uint32_t)lane << 2;
+  DTRACE(0);
+  if (tid < 4) {
+    const CUtensorMap* mp = tid == 0 ? &gw : tid == 1 ? &ga : tid == 2 ? &dw : &da;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(mp) : "memory");
+  }
+  const Tables tb = tables_of(smem);
+  int* cta_err = &tb.misc[1];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + DSmem::bars);
+  uint64_t* empty = full + kSSlots;
+  const char* lut = smem + DSmem::lut;
+  const __half* xs = reinterpret_cast<const __half*>(smem + DSmem::x);
+  const int xpitch = a.H + 8;
+  float* red = reinterpret_cast<float*>(smem + SSmem::red);
+  __half* hs = reinterpret_cast<__half*>(smem + SSmem::hs);
+  const SliceMaps maps{&gw, &ga, &dw, &da};
+  const int nsl = a.I / kSW, ng = a.H / kSGK, nd = a.H / kSDRows, spu = ng + nd;
+  if (tid == 0) {
+    for (int s = 0; s < kSSlots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    fence_proxy_async();
+  }
+  int total = 0;  // this CTA's stages
+  const int nact = decode_prologue(a, smem, tb, [&](const Tables& t, int na) {
+    const int units = na * nsl;
+    const int mine = units > (int)blockIdx.x ? (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    if (tid == 0)
+      for (int n = 0; n < kSSlots && n < mine * spu; ++n) slice_issue(a, maps, t, smem, n, nsl, ng, spu);
+  });
+  {
+    const int units = nact * nsl;
+    const int mine = units > (int)blockIdx.x ? (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    total = mine * spu;
+  }
+  DTRACE(2);
+  bool dead = false;
+  int n = 0;
+  for (int ui = 0; n < total; ++ui) {
+    const int u = blockIdx.x + ui * (int)gridDim.x;
+    const int j = u / nsl, s = u - j * nsl;
+    const int row0 = tb.act_row0[j], M = tb.act_cnt[j];
+    auto wait_full = [&](int nn) {
+      if (!dead && !mbar_wait(&full[nn % kSSlots], (nn / kSSlots) & 1)) {
+        cta_raise(cta_err, E4B_ERR_TIMEOUT);
+        dead = true;
+      }
+    };
+    auto release = [&](int nn) {
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) slice_arrive(&empty[nn % kSSlots]);
+      if (tid == 0 && nn + kSSlots < total && !dead) {
+        if (mbar_wait(&empty[nn % kSSlots], (nn / kSSlots) & 1))
+          slice_issue(a, maps, tb, smem, nn + kSSlots, nsl, ng, spu);
+        else
+          cta_raise(cta_err, E4B_ERR_TIMEOUT);  // the consumers time out on the missing stages
+      }
+    };
+    // ---- gate_up: 128 rows x H ----
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[i][c] = 0.f;
+    const int bl = warp >> 1, tset = (warp & 1) * 4;
+    const int src = tb.sorted_tok[row0 + (gq < M ? gq : 0)];
+    for (int st = 0; st < ng; ++st, ++n) {
+      wait_full(n);
+      if (n == 0) DTRACE(6);
+      if (!dead) {
+        const char* slot = smem + SSmem::ring + (n % kSSlots) * kSSlot;
+        uint4 xf[2];
+        const __half* xrow = xs + src * xpitch + st * kSGK + bl * 64 + q * 16;
+        xf[0] = *reinterpret_cast<const uint4*>(xrow);
+        xf[1] = *reinterpret_cast<const uint4*>(xrow + 8);
+        uint2 wa[4], wb[4];
+        float sa[4], sb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = (tset + i) * 8 + gq;
+          const int unit = (((bl & 3) << 1) | (q >> 1)) ^ (rr & 7);
+          const int wo = (bl >> 2) * 8192 + rr * 128 + (unit << 4) + ((q & 1) << 3);
+          wa[i] = *reinterpret_cast<const uint2*>(slot + wo);
+          wb[i] = *reinterpret_cast<const uint2*>(slot + 16384 + wo);
+          sa[i] = *reinterpret_cast<const float*>(slot + 32768 + aofs(rr, bl, 32));
+          sb[i] = *reinterpret_cast<const float*>(slot + 34816 + aofs(rr, bl, 32));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) slice_block(acc[i], lut, wa[i], wb[i], sa[i], sb[i], xf, lane4);
+      }
+      release(n);
+    }
+    // ---- reduce across the 8 warps of each tile; h = silu(gate) * up for the unit's tokens ----
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) red[(warp * 16 + i * 4 + c) * 32 + lane] = acc[i][c];
+    __syncthreads();
+    {
+      const int t = tid >> 6, hh = (tid >> 5) & 1, i = t & 3;
+      float g = 0.f, up = 0.f;
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const int w = (t >> 2) + 2 * v;
+        g += red[(w * 16 + i * 4 + hh) * 32 + lane];
+        up += red[(w * 16 + i * 4 + 2 + hh) * 32 + lane];
+      }
+      const int m = 2 * q + hh;
+      if (m < M) {
+        const float sc = tb.xscale[tb.sorted_tok[row0 + m]];
+        hs[m * kSHPitch + t * 8 + gq] = store_cast<__half>(silu_f32(g * sc) * (up * sc), cta_err);
+      }
+    }
+    __syncthreads();
+    uint4 hf[2];
+    {
+      const __half* hrow = hs + (gq < M ? gq : 0) * kSHPitch + q * 16;
+      hf[0] = *reinterpret_cast<const uint4*>(hrow);
+      hf[1] = *reinterpret_cast<const uint4*>(hrow + 8);
+    }
+    if (ui == 0) DTRACE(5);
+    // ---- down: the unit's strip of all H rows, fp32 partial rows ----
+    for (int st = 0; st < nd; ++st, ++n) {
+      wait_full(n);
+      if (!dead) {
+        const char* slot = smem + SSmem::ring + (n % kSSlots) * kSSlot;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int t = 2 * warp + i;
+          const int ra = t * 16 + gq, rb = ra + 8;
+          const uint2 wa = *reinterpret_cast<const uint2*>(slot + ra * 32 + q * 8);
+          const uint2 wb = *reinterpret_cast<const uint2*>(slot + rb * 32 + q * 8);
+          const float sa = *reinterpret_cast<const float*>(slot + 16384 + ra * 16 + (s & 3) * 4);
+          const float sb = *reinterpret_cast<const float*>(slot + 16384 + rb * 16 + (s & 3) * 4);
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+          slice_block(d, lut, wa, wb, sa, sb, hf, lane4);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int m = 2 * q + hh;
+            if (m < M) {
+              float* prow = a.part + ((int64_t)(row0 + m) * nsl + s) * a.H + st * kSDRows;
+              prow[ra] = d[hh];
+              prow[rb] = d[2 + hh];
+            }
+          }
+        }
+      }
+      release(n);
+    }
+  }
+  if (tid == 0 && total > 0)  // copies still in flight after a timeout: bounded waits for the last ones
+    for (int m = total - kSSlots; m < total; ++m)
+      if (m >= 0) (void)mbar_wait(&full[m % kSSlots], (m / kSSlots) & 1);
+  (void)dead;
+  DTRACE(3);
+  __syncthreads();
+  if (tid == 0) a.cta_err[blockIdx.x] = tb.misc[1];
+  cg::this_grid().sync();
+  DTRACE(4);
+  auto fold_errors = [&]() {
+    if (blockIdx.x != 0) return;
+    if (tid == 0) tb.misc[7] = 0x7fffffff;
+    __syncthreads();
+    for (int b = tid; b < (int)gridDim.x; b += kThreads)
+      if (a.cta_err[b]) atomicMin(&tb.misc[7], b);
+    __syncthreads();
+    if (tid == 0 && tb.misc[7] != 0x7fffffff) atomicCAS(a.err, 0, a.cta_err[tb.misc[7]]);  // sticky word
+  };
+  fold_errors();
+  const bool clean = tb.misc[1] == 0;  // errors before the combine were folded above
+
+  // ---- combine: down row of pick i = fp16(sum over strips, in order); out[t] = sum over slots ----
+  const int R = a.T * a.k, H4 = a.H / 4;
+  const int per = (H4 + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int c0 = blockIdx.x * per, nc = min(per, H4 - c0);
+  if (nc > 0) {
+    float4* sd = reinterpret_cast<float4*>(smem + SSmem::red);  // [R][nc]
+    for (int v = tid; v < R * nc; v += kThreads) {
+      const int i = v / nc, c = v - i * nc;
+      const float4* p = reinterpret_cast<const float4*>(a.part + (int64_t)tb.inv[i] * nsl * a.H) + c0 + c;
+      float4 acc4 = __ldcg(p);
+      for (int s = 1; s < nsl; ++s) {
+        const float4 x4 = __ldcg(p + (int64_t)s * H4);
+        acc4.x += x4.x;
+        acc4.y += x4.y;
+        acc4.z += x4.z;
+        acc4.w += x4.w;
+      }
+      acc4.x = __half2float(store_cast<__half>(acc4.x, cta_err));
+      acc4.y = __half2float(store_cast<__half>(acc4.y, cta_err));
+      acc4.z = __half2float(store_cast<__half>(acc4.z, cta_err));
+      acc4.w = __half2float(store_cast<__half>(acc4.w, cta_err));
+      sd[v] = acc4;
+    }
+    __syncthreads();
+    for (int v = tid; v < a.T * nc; v += kThreads) {
+      const int t = v / nc, c = v - t * nc;
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int sl = 0; sl < a.k; ++sl) {  // slot order
+        const float4 d4 = sd[(t * a.k + sl) * nc + c];
+        const float ws = tb.w[t * a.k + sl];
+        o[0] = fmaf(d4.x, ws, o[0]);
+        o[1] = fmaf(d4.y, ws, o[1]);
+        o[2] = fmaf(d4.z, ws, o[2]);
+        o[3] = fmaf(d4.w, ws, o[3]);
+      }
+      OutT* op = reinterpret_cast<OutT*>(a.out) + (int64_t)t * a.H + (c0 + c) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) op[i] = store_cast_out<OutT>(o[i], cta_err);
+    }
+  }
+  DTRACE(8);
+  // saturation in the combine (fp16 down rows or outputs): into the sticky word directly
+  __syncthreads();
+  if (tid == 0 && clean && tb.misc[1]) atomicCAS(a.err, 0, tb.misc[1]);
+}
+
 }  // namespace
 
 // One-launch decode kernels: 0 off (multi-kernel path), 1 the flow kernel where it applies and the
-// phase kernel elsewhere, 2 the phase kernel only (the default: it is the faster of the two on
-// the decode shapes measured so far). -1: not yet read from E4B_DECODE_KERNEL.
+// phase kernel elsewhere, 2 the phase kernel only (the default), 3 the slice kernel where it
+// applies and the phase kernel elsewhere. -1: not yet read from E4B_DECODE_KERNEL.
 std::atomic<int> g_decode_mode{-1};
 
 int decode_mode() {
   int m = g_decode_mode.load(std::memory_order_relaxed);
   if (m < 0) {
     const char* v = getenv("E4B_DECODE_KERNEL");
-    const int env = v ? (v[0] == '0' ? 0 : v[0] == '1' ? 1 : 2) : 2;
+    const int env = v ? (v[0] == '0' ? 0 : v[0] == '1' ? 1 : v[0] == '3' ? 3 : 2) : 2;
     int expected = -1;
     g_decode_mode.compare_exchange_strong(expected, env);
     m = g_decode_mode.load(std::memory_order_relaxed);
@@ -754,6 +1116,15 @@ bool decode_layer_eligible(const e4b_moe_desc& d) {
   if ((int64_t)d.num_experts * d.hidden >= (1ll << 31)) return false;
   if (!is_act_dtype(d.act_dtype)) return false;
   return encode_tiled_fn() != nullptr && decode_layer_grid() > 0;
+}
+
+bool decode_slice_shape(const e4b_moe_desc& d) {
+  return d.weight_format == E4B_FMT_NF4 && d.lora_rank == 0 && d.has_gate && d.tokens >= 1 && d.tokens <= 8 &&
+         d.hidden % kSGK == 0 && d.intermediate % 256 == 0 && decode_layer_eligible(d);
+}
+
+size_t decode_slice_part_bytes(const e4b_moe_desc& d) {
+  return (size_t)d.tokens * d.top_k * (d.intermediate / kSW) * d.hidden * 4;
 }
 
 template <typename OutT, int NT>
@@ -813,8 +1184,72 @@ static e4b_status launch_decode(const DecodeArgs& a, cudaStream_t s) {
   return launch_status();
 }
 
+
+template <typename OutT>
+static e4b_status launch_slice(const DecodeArgs& a, cudaStream_t s) {
+  static unsigned long long configured = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return E4B_ERR_CUDA;
+  const unsigned long long bit = 1ull << dev;
+  auto kern = nf4_decode_slice_kernel<OutT>;
+  {
+    std::lock_guard<std::mutex> lk(g_dl_mu);
+    if (!(configured & bit)) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DSmem::total) != cudaSuccess)
+        return E4B_ERR_CUDA;
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, DSmem::total) != cudaSuccess ||
+          per_sm < 1)
+        return E4B_ERR_UNSUPPORTED;
+      configured |= bit;
+    }
+  }
+  CUtensorMap gw, ga, dw, da;
+  const cuuint64_t gu_rows = (cuuint64_t)a.E * 2 * a.I, dn_rows = (cuuint64_t)a.E * a.H;
+  {  // gate_up packed as [lines (H / 256)][rows][128 B]; a box is 2 lines x 64 rows
+    const cuuint64_t dims[3] = {128, gu_rows, (cuuint64_t)(a.H / 256)};
+    const cuuint64_t str[2] = {(cuuint64_t)(a.H / 2), 128};
+    const cuuint32_t box[3] = {128, 64, 2};
+    if (!encode_tiled(&gw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.gu_packed, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return E4B_ERR_CUDA;
+  }
+  {  // gate_up absmax [rows][H / 64]; a box is 8 blocks x 64 rows
+    const cuuint64_t dims[2] = {(cuuint64_t)(a.H / 64), gu_rows};
+    const cuuint64_t str[1] = {(cuuint64_t)(a.H / 64) * 4};
+    const cuuint32_t box[2] = {8, 64};
+    if (!encode_tiled(&ga, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.gu_absmax, dims, str, box, CU_TENSOR_MAP_SWIZZLE_32B))
+      return E4B_ERR_CUDA;
+  }
+  {  // down packed [rows][I / 2]; a box is one 32-byte block column x 256 rows
+    const cuuint64_t dims[2] = {(cuuint64_t)(a.I / 2), dn_rows};
+    const cuuint64_t str[1] = {(cuuint64_t)(a.I / 2)};
+    const cuuint32_t box[2] = {32, 256};
+    if (!encode_tiled(&dw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.dn_packed, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return E4B_ERR_CUDA;
+  }
+  {  // down absmax [rows][I / 64]; a box is 4 blocks x 256 rows
+    const cuuint64_t dims[2] = {(cuuint64_t)(a.I / 64), dn_rows};
+    const cuuint64_t str[1] = {(cuuint64_t)(a.I / 64) * 4};
+    const cuuint32_t box[2] = {4, 256};
+    if (!encode_tiled(&da, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.dn_absmax, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return E4B_ERR_CUDA;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(decode_layer_grid());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = DSmem::total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, gw, ga, dw, da) != cudaSuccess) return E4B_ERR_CUDA;
+  return launch_status();
+}
+
 e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,
-                               void* sync, int* err, cudaStream_t s, const DecodeRouter* router) {
+                               void* sync, int* err, cudaStream_t s, const DecodeRouter* router, void* part) {
   DecodeArgs a{};
   if (router) {
     a.router_w = router->weight;
@@ -848,6 +1283,14 @@ e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, 
   a.down_rows = static_cast<__half*>(down_rows);
   a.cta_err = static_cast<int*>(sync);
   a.err = err;
+  if (part && decode_mode() == 3 && decode_slice_shape(d)) {
+    a.part = static_cast<float*>(part);
+    switch (d.out_dtype) {
+      case E4B_BF16: return launch_slice<__nv_bfloat16>(a, s);
+      case E4B_F16: return launch_slice<__half>(a, s);
+      default: return launch_slice<float>(a, s);
+    }
+  }
   const bool two = d.tokens > 8;
   switch (d.out_dtype) {
     case E4B_BF16: return two ? launch_decode<__nv_bfloat16, 2>(a, s) : launch_decode<__nv_bfloat16, 1>(a, s);
@@ -860,6 +1303,6 @@ e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, 
 
 extern "C" E4B_API int e4b_set_decode_kernel(int mode) {
   const int prev = e4b::decode_mode();
-  e4b::g_decode_mode.store(mode == 0 ? 0 : mode == 2 ? 2 : 1);
+  e4b::g_decode_mode.store(mode == 0 ? 0 : mode == 1 ? 1 : mode == 3 ? 3 : 2);
   return prev;
 }

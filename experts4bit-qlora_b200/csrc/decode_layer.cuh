@@ -23,8 +23,13 @@ struct DecodeRouter {
 };
 bool decode_router_fusable(const e4b_moe_desc& d);
 
-// 0 off, 1 flow kernel where it applies (else the phase kernel), 2 phase kernel only.
+// 0 off, 1 flow kernel where it applies (else the phase kernel), 2 phase kernel only, 3 slice
+// kernel where it applies (else the phase kernel).
 int decode_mode();
+// Shapes the slice kernel takes (gated NF4 layer, 1..8 tokens, H a multiple of 512, within the
+// phase kernel's limits), and the bytes of its fp32 partial down rows [T*k][I / 64][H].
+bool decode_slice_shape(const e4b_moe_desc& d);
+size_t decode_slice_part_bytes(const e4b_moe_desc& d);
 
 // The flow kernel (decode_flow.cu): the layer for 1..8 tokens and at most kFlowMaxPicks picks,
 // NF4, no adapters, H and I multiples of 256. `sync` is the workspace's counter block at
@@ -35,7 +40,9 @@ constexpr int kFlowMaxPicks = 64;
 bool decode_flow_eligible(const e4b_moe_desc& d, bool fused_router);
 e4b_status launch_decode_flow(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* sync, int* err,
                               cudaStream_t s, const DecodeRouter* router = nullptr);
+// `part` (decode_slice_part_bytes) enables the slice kernel in mode 3; null keeps the phase kernel.
 e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, void* h, void* down_rows,
-                               void* sync, int* err, cudaStream_t s, const DecodeRouter* router = nullptr);
+                               void* sync, int* err, cudaStream_t s, const DecodeRouter* router = nullptr,
+                               void* part = nullptr);
 
 }  // namespace e4b

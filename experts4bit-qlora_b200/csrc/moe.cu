@@ -21,7 +21,7 @@ namespace e4b {
 
 struct MoeLayout {
   size_t offsets, active, num_active, tile_a, tile_b, inv, sorted_token, x16, x_scale, h, down_rows, xa_gu, xa_dn,
-      umma, sync, total;
+      umma, sync, part, total;
 };
 
 static MoeLayout moe_layout(const e4b_moe_desc& d) {
@@ -52,6 +52,7 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   L.xa_dn = take(xa_bytes);
   L.umma = take(umma_workspace_bytes(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate));
   L.sync = take(decode_layer_sync_bytes(1024));
+  L.part = take(decode_slice_shape(d) ? decode_slice_part_bytes(d) : 0);
   L.total = o;
   return L;
 }
@@ -504,7 +505,7 @@ extern "C" e4b_status e4b_moe_decode_step(const e4b_moe_desc* desc, const e4b_mo
                    reinterpret_cast<float*>(rws + kErrBytes)};
     mark_stage(&tt, 0, s);
     e4b_status st = launch_decode_layer(d, &tt, ws + L.h, ws + L.down_rows, ws + L.sync, reinterpret_cast<int*>(ws), s,
-                                        &r);
+                                        &r, decode_slice_shape(d) ? ws + L.part : nullptr);
     for (int i = 1; i < E4B_MOE_STAGE_EVENTS; ++i) mark_stage(&tt, i, s);
     return st;
   }
@@ -567,7 +568,8 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
     return st;
   }
   if (decode_layer_eligible(d)) {  // one launch: permute, both GEMVs and the combine
-    e4b_status st = launch_decode_layer(d, t, ws + L.h, ws + L.down_rows, ws + L.sync, err, s);
+    e4b_status st = launch_decode_layer(d, t, ws + L.h, ws + L.down_rows, ws + L.sync, err, s, nullptr,
+                                        decode_slice_shape(d) ? ws + L.part : nullptr);
     for (int i = 1; i < E4B_MOE_STAGE_EVENTS; ++i) mark_stage(t, i, s);
     return st;
   }

@@ -1,14 +1,16 @@
 """GPU: the one-launch decode-layer kernels.
 
-Two kernels take the decode regime in one launch: the flow kernel
+Three kernels take the decode regime in one launch: the flow kernel
 (decode_flow.cu: per-expert completion counters, k-split warps; up to 8 tokens
-and 64 picks) and the phase kernel (decode_layer.cu: grid-synchronised phases;
-up to 16 tokens and 128 picks), selected with ``set_decode_kernel`` mode 1 /
-mode 2 (mode 0 = the multi-kernel path). The phase kernel runs the streaming
-GEMV's arithmetic and must equal the multi-kernel path bit for bit; the flow
-kernel sums in another order and must meet the layer tolerance against the
+and 64 picks), the phase kernel (decode_layer.cu: grid-synchronised phases;
+up to 16 tokens and 128 picks) and the slice kernel (decode_layer.cu: units of
+one expert x 64 intermediate columns, gate_up then the down strip in the same
+CTA; up to 8 tokens), selected with ``set_decode_kernel`` mode 1 / 2 / 3
+(mode 0 = the multi-kernel path). The phase kernel runs the streaming GEMV's
+arithmetic and must equal the multi-kernel path bit for bit; the flow and slice
+kernels sum in another order and must meet the layer tolerance against the
 fp32 oracle and agree with the multi-kernel path to 1e-2 / 1e-3 (max / mean
-relative). Both must be deterministic, capture into a CUDA graph and report
+relative). All must be deterministic, capture into a CUDA graph and report
 device errors."""
 from __future__ import annotations
 
@@ -79,7 +81,7 @@ def test_decode_layer_vs_multikernel_and_oracle(e4b, E, H, I, k, T):
         assert e4b.ops.moe_path(E, H, I, k, T) == e4b._native.PATH_STREAMING
         multi = _fwd(e4b, mod, x, idx, w, E, I)
     ref = M.fp32_oracle(st, x, idx, w) if st is not None else fp32_anchor_gpu(mod, x.to(DEV), idx.to(DEV), w.to(DEV)).cpu()
-    for mode in (1, 2):
+    for mode in (1, 2, 3):
         with _Mode(e4b, mode):
             if e4b.ops.moe_path(E, H, I, k, T) != e4b._native.PATH_DECODE_LAYER:
                 continue
@@ -132,7 +134,13 @@ def test_decode_layer_silu_only_and_fp32_out(e4b):
     assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
 
 
-def test_decode_layer_graph_capture_and_repeat(e4b):
+@pytest.mark.parametrize("mode", [2, 3])
+def test_decode_layer_graph_capture_and_repeat(e4b, mode):
+    with _Mode(e4b, mode):
+        _graph_case(e4b)
+
+
+def _graph_case(e4b):
     E, H, I, k, T = 64, 2048, 1024, 8, 1
     mod, _ = _layer(e4b, E, H, I, seed=4)
     x, idx, w = _inputs(E, H, T, k, seed=5)
@@ -157,7 +165,13 @@ def test_decode_layer_graph_capture_and_repeat(e4b):
         assert torch.equal(out, ref)
 
 
-def test_decode_layer_reports_errors_per_call(e4b):
+@pytest.mark.parametrize("mode", [2, 3])
+def test_decode_layer_reports_errors_per_call(e4b, mode):
+    with _Mode(e4b, mode):
+        _errors_case(e4b)
+
+
+def _errors_case(e4b):
     E, H, I, k, T = 16, 512, 256, 2, 2
     mod, _ = _layer(e4b, E, H, I, seed=6)
     x, idx, w = _inputs(E, H, T, k, seed=7)
@@ -169,7 +183,7 @@ def test_decode_layer_reports_errors_per_call(e4b):
     _fwd(e4b, mod, x, idx, w, E, I)  # a valid call afterwards reports nothing
 
 
-@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("mode", [1, 2, 3])
 @pytest.mark.parametrize("E,H,I,k,T,kind,norm", [(64, 2048, 1024, 8, 1, 0, False), (64, 2048, 1024, 8, 3, 0, True),
                                                  (128, 1024, 512, 4, 8, 1, False), (64, 2048, 1024, 8, 24, 0, False),
                                                  (256, 2048, 512, 8, 4, 0, True)])
