@@ -64,8 +64,8 @@ WORKLOADS = {
 # DRAM bytes (read + write) per launch of the dominant kernel, from the ncu captures summarised
 # under profiles/ (same kernels and shapes); workloads without a capture report null.
 MEASURED_TRAFFIC = {
-    "olmoe-decode": {"bytes": 28697088 + 3328, "kernel": "nf4_decode_layer_kernel",
-                     "source": "profiles/nf4_decode_step__olmoe_decode.md"},
+    "olmoe-decode": {"bytes": 28700416 + 21248, "kernel": "nf4_decode_slice_kernel",
+                     "source": "profiles/nf4_decode_slice__olmoe_decode.md"},
     "qwen3-prefill-base": {"bytes": 364481536 + 40394240, "kernel": "nf4_umma_kernel<__half, 2> (gate_up)",
                            "source": "profiles/nf4_umma__qwen3_prefill.md"},
 }
@@ -365,7 +365,9 @@ def run_ours(args, wl, world, rank, local):
         peak = peaks["bf16_tflops"]
         kernel_us = stage_avg_us["gate_up"]
         stage_report = {k_: round(v, 3) for k_, v in stage_avg_us.items()}
-    kname = {"olmoe-decode": "nf4_decode_flow_kernel"}.get(args.workload, "nf4 grouped gate_up (SwiGLU fused)")
+    decode_kernel = {"1": "nf4_decode_flow_kernel", "2": "nf4_decode_layer_kernel"}.get(
+        os.environ.get("E4B_DECODE_KERNEL", "3"), "nf4_decode_slice_kernel")
+    kname = decode_kernel if one_launch else "nf4 grouped gate_up (SwiGLU fused)"
     roofline = {"bound": bound,
                 "kernel": ("%s: router + permute + gate_up GEMV (SwiGLU) + down GEMV + combine, one launch per "
                            "layer" % kname if one_launch else "nf4 grouped gate_up (SwiGLU fused)"),

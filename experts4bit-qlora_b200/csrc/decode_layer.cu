@@ -55,9 +55,17 @@ extern "C" __attribute__((visibility("default"))) int e4b_decode_pair_read(unsig
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));        \
     g_dl_pair[(blockIdx.x * 8 + pair) * 4 + (i)] = t_;             \
   }
+// slice kernel: per CTA 32 stamps (stage waits and releases of warps 1 and 15, refills by thread 0)
+#define STRACE(w, i)                                               \
+  if (warp == (w) && lane == 0 && (i) < 32) {                      \
+    unsigned long long t_;                                         \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));        \
+    g_dl_pair[blockIdx.x * 32 + (i)] = t_;                         \
+  }
 #else
 #define DTRACE(i)
 #define PTRACE(i)
+#define STRACE(w, i)
 #endif
 
 namespace e4b {
@@ -136,6 +144,9 @@ struct DecodeArgs {
   float* topk_w_out;           // [T, k]
   float* router_logits;        // [T, E] global scratch: logits spread over the grid, then a grid sync
   float* part;                 // slice kernel: fp32 partial down rows [R][I / 64][H]
+  int cluster;                 // > 1: launched in clusters of this size; the router's tasks are split
+                               // over the cluster and the logits exchanged through distributed shared
+                               // memory (router_logits unused)
 };
 
 struct Tables {
@@ -506,22 +517,44 @@ __device__ __forceinline__ int decode_prologue(const DecodeArgs& a, char* smem, 
     float* logits = reinterpret_cast<float*>(smem + DSmem::logits);
     const int ttiles = (a.T + kRouterTT - 1) / kRouterTT, tasks = a.E * ttiles;
     const bool w16 = a.router_w_dtype != E4B_F32;  // 16-bit weights: all strips of a lane in flight
-    // With global scratch the (expert, token tile) tasks are spread one warp per SM across the
-    // grid and shared through a grid barrier; otherwise every CTA computes all of them.
-    float* dst = a.router_logits ? a.router_logits : logits;
-    const int w0 = a.router_logits ? warp * (int)gridDim.x + blockIdx.x : warp;
-    const int wstep = a.router_logits ? kWarps * (int)gridDim.x : kWarps;
+    // In clusters the (expert, token tile) tasks are split over the cluster's CTAs; with global
+    // scratch they are spread one warp per SM across the grid and shared through a grid barrier;
+    // otherwise every CTA computes all of them.
+    // the token rows (raw, already in registers) into the not yet used copy slots: the logit tasks
+    // read them from shared memory instead of every warp of the grid hitting the same lines of L2
+    uint16_t* xraw = reinterpret_cast<uint16_t*>(smem + DSmem::slots);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int v = tid + i * kThreads;
+      if (v < xvec) reinterpret_cast<uint4*>(xraw)[v] = xr[i];
+    }
+    __syncthreads();
+    const bool in_cluster = a.cluster > 1;
+    const int crank = in_cluster ? (int)cg::this_cluster().block_rank() : 0;
+    float* dst = (a.router_logits && !in_cluster) ? a.router_logits : logits;
+    const int w0 = in_cluster ? crank + a.cluster * warp : a.router_logits ? warp * (int)gridDim.x + blockIdx.x : warp;
+    const int wstep = in_cluster ? a.cluster * kWarps : a.router_logits ? kWarps * (int)gridDim.x : kWarps;
     for (int task = w0; task < tasks; task += wstep) {
       if (w16)
-        router_logits_warp16<8>(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
+        router_logits_warp16<8>(xraw, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
                                 (task / a.E) * kRouterTT, dst);
       else
-        router_logits_warp(a.hidden, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
+        router_logits_warp(xraw, a.act_dtype, a.router_w, a.router_w_dtype, a.T, a.H, a.E, task % a.E,
                            (task / a.E) * kRouterTT, dst);
     }
     __syncthreads();  // rowmax cleared
     prep();
-    if (a.router_logits) {
+    if (in_cluster) {
+      cg::cluster_group cl = cg::this_cluster();
+      cl.sync();
+      for (int i = tid; i < a.T * a.E; i += kThreads) {  // the peers' logits into this CTA's copy
+        const int owner = (((i / a.E) / kRouterTT) * a.E + i % a.E) % a.cluster;
+        if (owner != crank) logits[i] = *cl.map_shared_rank(logits + i, owner);
+      }
+      // peers keep their logits until every CTA of the cluster has read them: the matching wait
+      // is the kernel's last statement
+      asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    } else if (a.router_logits) {
       cg::this_grid().sync();
       for (int i = tid; i < a.T * a.E; i += kThreads) logits[i] = __ldcg(a.router_logits + i);
     }
@@ -769,6 +802,7 @@ struct SSmem {
   static constexpr int hs = red + kWarps * 16 * 32 * 4;     // [8 tokens][kSHPitch] fp16
   static constexpr int end = hs + 8 * kSHPitch * 2;
 };
+// the combine stages [R][ceil(H / 4 / grid)][I / 64] float4 strips in the ring (R <= 64 here)
 static_assert(SSmem::ring % 1024 == 0 && kSSlot % 1024 == 0, "swizzled boxes need 1024-byte alignment");
 static_assert(SSmem::end <= DSmem::bars, "slice layout overlaps the barriers");
 
@@ -893,16 +927,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         cta_raise(cta_err, E4B_ERR_TIMEOUT);
         dead = true;
       }
+      if (nn < 8) {
+        STRACE(1, nn);
+        STRACE(15, 24 + nn);
+      }
     };
     auto release = [&](int nn) {
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) slice_arrive(&empty[nn % kSSlots]);
+      if (nn < 8) STRACE(1, 8 + nn);
       if (tid == 0 && nn + kSSlots < total && !dead) {
         if (mbar_wait(&empty[nn % kSSlots], (nn / kSSlots) & 1))
           slice_issue(a, maps, tb, smem, nn + kSSlots, nsl, ng, spu);
         else
           cta_raise(cta_err, E4B_ERR_TIMEOUT);  // the consumers time out on the missing stages
+        if (nn < 8) STRACE(0, 16 + nn);
       }
     };
     // ---- gate_up: 128 rows x H ----
@@ -1023,13 +1063,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int per = (H4 + (int)gridDim.x - 1) / (int)gridDim.x;
   const int c0 = blockIdx.x * per, nc = min(per, H4 - c0);
   if (nc > 0) {
-    float4* sd = reinterpret_cast<float4*>(smem + SSmem::red);  // [R][nc]
+    // one float4 load per (pick, column, strip) thread, all in flight at once; then the strips of
+    // each (pick, column) summed in strip order from shared memory
+    float4* sp = reinterpret_cast<float4*>(smem + SSmem::ring);  // [R][nc][nsl]
+    float4* sd = reinterpret_cast<float4*>(smem + SSmem::red);   // [R][nc]
+    const int per_pick = nc * nsl;
+    for (int v = tid; v < R * per_pick; v += kThreads) {
+      const int i = v / per_pick, rem = v - i * per_pick, c = rem / nsl, s = rem - c * nsl;
+      sp[v] = __ldcg(reinterpret_cast<const float4*>(a.part + ((int64_t)tb.inv[i] * nsl + s) * a.H) + c0 + c);
+    }
+    __syncthreads();
     for (int v = tid; v < R * nc; v += kThreads) {
-      const int i = v / nc, c = v - i * nc;
-      const float4* p = reinterpret_cast<const float4*>(a.part + (int64_t)tb.inv[i] * nsl * a.H) + c0 + c;
-      float4 acc4 = __ldcg(p);
+      const float4* p = sp + v * nsl;
+      float4 acc4 = p[0];
       for (int s = 1; s < nsl; ++s) {
-        const float4 x4 = __ldcg(p + (int64_t)s * H4);
+        const float4 x4 = p[s];
         acc4.x += x4.x;
         acc4.y += x4.y;
         acc4.z += x4.z;
@@ -1062,12 +1110,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // saturation in the combine (fp16 down rows or outputs): into the sticky word directly
   __syncthreads();
   if (tid == 0 && clean && tb.misc[1]) atomicCAS(a.err, 0, tb.misc[1]);
+  if (a.cluster > 1 && a.router_w) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 }  // namespace
 
 // One-launch decode kernels: 0 off (multi-kernel path), 1 the flow kernel where it applies and the
-// phase kernel elsewhere, 2 the phase kernel only (the default), 3 the slice kernel where it
+// phase kernel elsewhere, 2 the phase kernel only, 3 (the default) the slice kernel where it
 // applies and the phase kernel elsewhere. -1: not yet read from E4B_DECODE_KERNEL.
 std::atomic<int> g_decode_mode{-1};
 
@@ -1075,7 +1124,7 @@ int decode_mode() {
   int m = g_decode_mode.load(std::memory_order_relaxed);
   if (m < 0) {
     const char* v = getenv("E4B_DECODE_KERNEL");
-    const int env = v ? (v[0] == '0' ? 0 : v[0] == '1' ? 1 : v[0] == '3' ? 3 : 2) : 2;
+    const int env = v ? (v[0] == '0' ? 0 : v[0] == '1' ? 1 : v[0] == '2' ? 2 : 3) : 3;
     int expected = -1;
     g_decode_mode.compare_exchange_strong(expected, env);
     m = g_decode_mode.load(std::memory_order_relaxed);
@@ -1118,9 +1167,18 @@ bool decode_layer_eligible(const e4b_moe_desc& d) {
   return encode_tiled_fn() != nullptr && decode_layer_grid() > 0;
 }
 
+static std::atomic<int> g_slice_no_cluster[64];
+static void slice_cluster_off(int dev) { g_slice_no_cluster[dev].store(1); }
+
 bool decode_slice_shape(const e4b_moe_desc& d) {
-  return d.weight_format == E4B_FMT_NF4 && d.lora_rank == 0 && d.has_gate && d.tokens >= 1 && d.tokens <= 8 &&
-         d.hidden % kSGK == 0 && d.intermediate % 256 == 0 && decode_layer_eligible(d);
+  if (!(d.weight_format == E4B_FMT_NF4 && d.lora_rank == 0 && d.has_gate && d.tokens >= 1 && d.tokens <= 8 &&
+        d.hidden % kSGK == 0 && d.intermediate % 256 == 0 && decode_layer_eligible(d)))
+    return false;
+  // the combine stages each CTA's [R][columns][strips] float4 partials in the copy ring
+  const int grid = decode_layer_grid() * 19 / 20;  // the smallest grid a clustered launch takes
+  if (grid < 1) return false;
+  const int64_t cols = (d.hidden / 4 + grid - 1) / grid;
+  return (int64_t)d.tokens * d.top_k * cols * (d.intermediate / kSW) * 16 <= (int64_t)kSSlots * kSSlot;
 }
 
 size_t decode_slice_part_bytes(const e4b_moe_desc& d) {
@@ -1234,17 +1292,80 @@ static e4b_status launch_slice(const DecodeArgs& a, cudaStream_t s) {
     if (!encode_tiled(&da, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.dn_absmax, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
       return E4B_ERR_CUDA;
   }
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(decode_layer_grid());
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = DSmem::total;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, a, gw, ga, dw, da) != cudaSuccess) return E4B_ERR_CUDA;
+  // The fused router runs over the whole grid through global scratch, or (on request) in clusters
+  // of 4 (or 2) CTAs when a grid of co-resident clusters covers (nearly) every SM and the device
+  // takes the clustered cooperative launch.
+  int grid = decode_layer_grid(), cs = 1;
+  if (a.router_w) {
+    std::lock_guard<std::mutex> lk(g_dl_mu);
+    static int cl_size[64] = {0}, cl_grid[64] = {0};
+    if (!cl_size[dev]) {
+      int best_cs = 1, best_grid = grid;
+      for (int c : {4, 2}) {
+        cudaLaunchConfig_t q{};
+        q.gridDim = dim3(grid / c * c);
+        q.blockDim = dim3(kThreads);
+        q.dynamicSmemBytes = DSmem::total;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = c;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        int ncl = 0;
+        if (cudaOccupancyMaxActiveClusters(&ncl, kern, &q) != cudaSuccess) {
+          cudaGetLastError();
+          continue;
+        }
+        const int g = ncl * c < grid / c * c ? ncl * c : grid / c * c;
+        if (g * 20 >= grid * 19) {  // within 5 % of the full grid
+          best_cs = c;
+          best_grid = g;
+          break;
+        }
+      }
+      cl_size[dev] = best_cs;
+      cl_grid[dev] = best_grid;
+    }
+    // clusters only on request (E4B_SLICE_CLUSTER=1): every CTA then runs logit tasks before its
+    // own set-up, which measured slower than the grid-wide split on the OLMoE decode step
+    static const bool no_cluster = [] {
+      const char* v = getenv("E4B_SLICE_CLUSTER");
+      return !(v && v[0] == '1');
+    }();
+    cs = (no_cluster || g_slice_no_cluster[dev].load()) ? 1 : cl_size[dev];
+    if (cs > 1) grid = cl_grid[dev];
+  }
+  for (;;) {
+    DecodeArgs la = a;
+    la.cluster = cs;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = DSmem::total;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    int na = 1;
+    if (cs > 1) {
+      attr[1].id = cudaLaunchAttributeClusterDimension;
+      attr[1].val.clusterDim.x = cs;
+      attr[1].val.clusterDim.y = 1;
+      attr[1].val.clusterDim.z = 1;
+      na = 2;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, la, gw, ga, dw, da);
+    if (e == cudaSuccess) break;
+    if (cs == 1) return E4B_ERR_CUDA;
+    cudaGetLastError();  // clustered cooperative launch refused: the grid-wide router from now on
+    cs = 1;
+    grid = decode_layer_grid();
+    slice_cluster_off(dev);
+  }
   return launch_status();
 }
 
@@ -1303,6 +1424,6 @@ e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, 
 
 extern "C" E4B_API int e4b_set_decode_kernel(int mode) {
   const int prev = e4b::decode_mode();
-  e4b::g_decode_mode.store(mode == 0 ? 0 : mode == 1 ? 1 : mode == 3 ? 3 : 2);
+  e4b::g_decode_mode.store(mode == 0 ? 0 : mode == 1 ? 1 : mode == 2 ? 2 : 3);
   return prev;
 }

@@ -380,9 +380,9 @@ def moe_decode_step_workspace_bytes(E, H, I, k, T, has_gate=True, act_dtype=torc
 def set_decode_kernel(mode) -> int:
     """Select the one-launch decode-layer kernel for the process; returns the old setting.
 
-    ``False``/0 turns it off, ``True``/2 selects the phase kernel (the default), 1 the flow
-    kernel where it applies."""
-    m = 2 if mode is True else 0 if mode is False else int(mode)
+    ``False``/0 turns it off, 1 selects the flow kernel where it applies, 2 the phase kernel,
+    ``True``/3 the slice kernel where it applies (the default)."""
+    m = 3 if mode is True else 0 if mode is False else int(mode)
     return N.lib().e4b_set_decode_kernel(m)
 
 

@@ -237,8 +237,10 @@ E4B_API e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_tenso
 #define E4B_PATH_DECODE_LAYER 2
 E4B_API int e4b_moe_path(const e4b_moe_desc* desc);
 /* mode 0: no one-launch kernel; 1: the flow kernel (per-expert completion counters, up to 8
- * tokens and 64 picks) where it applies, else the phase kernel; 2 (default): the phase kernel
- * only (grid-synchronised phases, up to 16 tokens and 128 picks). */
+ * tokens and 64 picks) where it applies, else the phase kernel; 2: the phase kernel only
+ * (grid-synchronised phases, up to 16 tokens and 128 picks); 3 (default): the slice kernel
+ * (units of one expert x 64 intermediate columns, gated layers, up to 8 tokens, H a multiple
+ * of 512) where it applies, else the phase kernel. Any other value selects 3. */
 E4B_API int e4b_set_decode_kernel(int mode);
 
 /* No counterpart in the reference (its router is the model's own module): router
