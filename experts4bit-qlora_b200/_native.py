@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "e4b_fp8_block_dequantize",
     "e4b_mxfp4_dequantize", "e4b_mxfp4_dequantize_host",
     "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
+    "e4b_grouped_nf4_dgrad_workspace_bytes", "e4b_grouped_nf4_dgrad",
     "e4b_combine",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
     "e4b_moe_decode_step_workspace_bytes", "e4b_moe_decode_step",
@@ -46,7 +47,7 @@ EXPORTED_SYMBOLS = (
     "e4b_ep_experts_peer_workspace_bytes", "e4b_ep_experts_peer", "e4b_ep_combine_peer",
     "e4b_gather_expert_rows",
     "e4b_selftest_wait_timeout",
-    "e4b_read_device_error",
+    "e4b_read_device_error", "e4b_watch_device_error",
 )
 
 
@@ -105,6 +106,8 @@ def _declare(lib):
         "e4b_mxfp4_dequantize_host": (I, [P, P, I64, I64, I64, I64, P, I]),
         "e4b_grouped_gemm_workspace_bytes": (SZ, [I, I, I, I]),
         "e4b_grouped_nf4_gemm": (I, [P, I, P, P, P, P, I, I, I, I, I, P, P, SZ, P]),
+        "e4b_grouped_nf4_dgrad_workspace_bytes": (SZ, [I, I, I, I]),
+        "e4b_grouped_nf4_dgrad": (I, [P, I, P, P, P, I, I, I, I, P, I, P, SZ, P]),
         "e4b_combine": (I, [P, I, P, P, I, I, I, I, P, I, P]),
         "e4b_moe_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
         "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
@@ -130,6 +133,7 @@ def _declare(lib):
         "e4b_gather_expert_rows": (I, [P, I, P, P, I, P, I, P, P, P, P, P, SZ, P]),
         "e4b_selftest_wait_timeout": (I, [P, SZ, P]),
         "e4b_read_device_error": (I, [P, P, ctypes.POINTER(I)]),
+        "e4b_watch_device_error": (I, [P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -241,11 +245,11 @@ def read_device_error(ws: torch.Tensor) -> int:
 class _ErrorWatch:
     """Surfaces the sticky device error word of a workspace without a per-call host sync.
 
-    After a call, a 4-byte asynchronous copy of the word goes to pinned host memory behind an
-    event; the next call on the same workspace looks at that copy once its event has completed
-    and, if an error was recorded, reads and clears the word (one sync, only then) and raises.
-    ``check_errors()`` synchronises and raises at once. Calls inside a CUDA-graph capture are
-    not watched (a capture cannot record host reads).
+    After a call, one library call (``e4b_watch_device_error``) queues a 4-byte copy of the
+    word into pinned host memory behind an event and returns what the previous copy found
+    once its event has completed; a non-zero value is read and cleared (one sync, only then)
+    and raised. ``check_errors()`` synchronises and raises at once. Calls inside a CUDA-graph
+    capture are not watched (a capture cannot record host reads).
     """
 
     def __init__(self):
@@ -253,34 +257,36 @@ class _ErrorWatch:
         self._lock = threading.Lock()
 
     def before(self, ws: torch.Tensor, what: str) -> None:
+        """Kept for callers that check before a launch: the watch itself runs in ``after``."""
+
+    def after(self, ws: torch.Tensor, what: str = "call") -> None:
         ent = self._w.get(ws.data_ptr())
-        if ent is None or torch.cuda.is_current_stream_capturing():
+        if ent is None:
+            if torch.cuda.is_current_stream_capturing():
+                return
+            with self._lock:
+                ent = self._w.get(ws.data_ptr())
+                if ent is None:
+                    ent = (torch.zeros(1, dtype=torch.int32, pin_memory=True), ws, torch.cuda.Event())
+                    self._w[ws.data_ptr()] = ent
+        elif torch.cuda.is_current_stream_capturing():
             return
         host, _, ev = ent
-        if ev.query() and int(host[0]) != 0:
-            self.raise_if_set(ws, what)
+        if lib().e4b_watch_device_error(ws.data_ptr(), host.data_ptr(), ev.cuda_event,
+                                        torch.cuda.current_stream(ws.device).cuda_stream):
+            self.raise_if_set(ws, what, host)
 
-    def after(self, ws: torch.Tensor) -> None:
-        if torch.cuda.is_current_stream_capturing():
-            return
-        with self._lock:
-            ent = self._w.get(ws.data_ptr())
-            if ent is None:
-                ent = (torch.zeros(1, dtype=torch.int32, pin_memory=True), ws, torch.cuda.Event())
-                self._w[ws.data_ptr()] = ent
-        host, _, ev = ent
-        host.copy_(ws[:4].view(torch.int32), non_blocking=True)
-        ev.record()
-
-    def raise_if_set(self, ws: torch.Tensor, what: str) -> None:
-        err = read_device_error(ws)
+    def raise_if_set(self, ws: torch.Tensor, what: str, host: torch.Tensor | None = None) -> None:
+        err = read_device_error(ws)  # synchronises: the copy queued before the clear has landed
+        if host is not None:
+            host.zero_()
         if err:
             raise E4BError(err, what + " (device error recorded by an earlier call on this workspace)")
 
     def check_all(self) -> None:
         for ws_ptr, (host, ws, ev) in list(self._w.items()):
             ev.synchronize()
-            self.raise_if_set(ws, "check_errors")
+            self.raise_if_set(ws, "check_errors", host)
 
 
 error_watch = _ErrorWatch()

@@ -388,6 +388,19 @@ extern "C" e4b_status e4b_read_device_error(void* workspace, void* stream, int* 
   return E4B_OK;
 }
 
+extern "C" int e4b_watch_device_error(void* workspace, int* host_word, void* event, void* stream) {
+  if (!workspace || !host_word || !event) return 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaEvent_t ev = (cudaEvent_t)event;
+  int prev = 0;
+  const cudaError_t q = cudaEventQuery(ev);
+  if (q == cudaSuccess) prev = *reinterpret_cast<volatile int*>(host_word);
+  else if (q != cudaErrorNotReady) cudaGetLastError();  // an event never recorded yet
+  if (cudaMemcpyAsync(host_word, workspace, sizeof(int), cudaMemcpyDeviceToHost, s) == cudaSuccess)
+    cudaEventRecord(ev, s);
+  return prev;
+}
+
 extern "C" size_t e4b_grouped_gemm_workspace_bytes(int R, int E, int N, int K) {
   (void)N;
   if (E <= 0 || R < 0 || K <= 0) return 0;
@@ -459,6 +472,57 @@ extern "C" e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int
     return launch_umma(umma_args_from(g, nullptr, tile_start, R, 1, R), a_dtype, s);
   }
   return launch_gemv_auto(g, R, R, s);
+}
+
+extern "C" size_t e4b_grouped_nf4_dgrad_workspace_bytes(int R, int E, int N, int K) {
+  (void)K;
+  if (E <= 0 || R < 0 || N <= 0) return 0;
+  return kErrBytes + align_up((size_t)R * N * 2, 256) + align_up((size_t)R * 4, 256) +
+         align_up((size_t)(E + 1) * 4, 256);
+}
+
+extern "C" e4b_status e4b_grouped_nf4_dgrad(const void* dy, int dy_dtype, const uint8_t* packed, const float* absmax,
+                                            const int32_t* offsets, int E, int R, int N, int K, void* dx,
+                                            int dx_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (E <= 0 || E > 1024 || R < 0 || N <= 0 || K <= 0) return E4B_ERR_INVALID_ARG;
+  if (!is_act_dtype(dy_dtype) || !(dx_dtype == E4B_F32 || is_act_dtype(dx_dtype))) return E4B_ERR_UNSUPPORTED;
+  if (!umma_dgrad_eligible(N, K)) return E4B_ERR_UNSUPPORTED;
+  if (R == 0) return E4B_OK;
+  if (!dy || !packed || !absmax || !offsets || !dx) return E4B_ERR_INVALID_ARG;
+  if (!aligned16(dy) || !aligned16(packed) || !aligned16(dx)) return E4B_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < e4b_grouped_nf4_dgrad_workspace_bytes(R, E, N, K)) return E4B_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return E4B_ERR_ALIGNMENT;
+  cudaStream_t s = (cudaStream_t)stream;
+  char* ws = static_cast<char*>(workspace);
+  __half* dy16 = reinterpret_cast<__half*>(ws + kErrBytes);
+  float* dy_scale = reinterpret_cast<float*>(reinterpret_cast<char*>(dy16) + align_up((size_t)R * N * 2, 256));
+  int32_t* tile_start = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(dy_scale) + align_up((size_t)R * 4, 256));
+  ConvertArgs cv{};
+  cv.src = dy;
+  cv.src_dtype = dy_dtype;
+  cv.dst = dy16;
+  cv.scale = dy_scale;
+  cv.rows = R;
+  cv.K = N;
+  convert_kernel<<<conv_ctas_for(R, 8), 256, 0, s>>>(cv);
+  if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
+  tiles_from_offsets_kernel<<<1, 1024, 0, s>>>(offsets, E, kUmmaTokens, tile_start);
+  if (launch_status() != E4B_OK) return E4B_ERR_CUDA;
+  GemvArgs g{};
+  g.a = dy16;
+  g.a_scale = dy_scale;
+  g.packed = packed;
+  g.absmax = absmax;
+  g.offsets = offsets;
+  g.E = E;
+  g.N = N;
+  g.K = K;
+  g.epilogue = E4B_EPI_NONE;
+  g.out = dx;
+  g.out_dtype = dx_dtype;
+  g.Nout = K;
+  g.err = reinterpret_cast<int*>(ws);
+  return launch_umma_dgrad(umma_args_from(g, nullptr, tile_start, R, 1, R), dx_dtype, s);
 }
 
 extern "C" size_t e4b_moe_decode_step_workspace_bytes(const e4b_moe_desc* desc) {

@@ -32,6 +32,8 @@
 // Tiles are ordered (expert, feature tile, token tile) so CTAs that run at the
 // same time share the weight tile through L2. Every wait is bounded; a timeout
 // raises E4B_ERR_TIMEOUT and all roles run to the common exit (TMEM is freed).
+#include <atomic>
+
 #include "async.cuh"
 #include "fp8.cuh"
 #include "umma.cuh"
@@ -703,6 +705,299 @@ e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s, int wei
   if (u.g.out_dtype == E4B_BF16)
     return two ? launch_groups<__nv_bfloat16, 2, E4B_FMT_NF4>(u, s) : launch_groups<__nv_bfloat16, 1, E4B_FMT_NF4>(u, s);
   return two ? launch_groups<__half, 2, E4B_FMT_NF4>(u, s) : launch_groups<__half, 1, E4B_FMT_NF4>(u, s);
+}
+
+// ---------------------------------------------------------------------------------------------
+// dgrad: dX[r, :] = dY[r, :] . W_e for the expert-sorted rows r of expert e (W_e [N, K] NF4,
+// blocks of 64 along K): the input gradient of a frozen grouped projection, the reference's
+// single-launch dgrad kernel (experts4bit_qlora/engines/fast.py:519-550) without materialising
+// a decoded stack. The contraction runs over N (the weight rows): per 64-row chunk the decode
+// warps turn 64 rows x 256 columns of the tile into fp16 and store each row's 64-column pieces
+// as 128-byte rows of MN-major, 128-byte-swizzled atoms (8 weight rows x 64 columns), which the
+// MMA reads as its N = 256 operand with the MN-major bit set (LBO: the next 64 columns, SBO: the
+// next 8 rows). The M = 128 operand is the tile's fp16 dY rows (per-row power-of-two scales,
+// multiplied back in the epilogue), K-major over N like the forward activations. Same roles and
+// rings as the forward kernel; the epilogue stores fp32 or 16-bit rows of 256 columns.
+namespace {
+
+// MN-major, 128-byte swizzle descriptor: atoms of 8 K-rows x 128 B, `lbo` bytes to the next atom
+// along MN, `sbo` bytes to the next 8 K-rows.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3fff);
+  d |= (uint64_t)((lbo >> 4) & 0x3fff) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3fff) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+constexpr int kDgCols = 256;  // output columns (of K) per tile
+constexpr int kDgAtom = 1024;
+
+}  // namespace
+
+template <typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_umma_dgrad_kernel(UmmaArgs u, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap) {
+  using Smem = SmemT<E4B_FMT_NF4>;
+  static_assert(Smem::wbytes * 2 == 64 * 128, "one packed stage holds 64 rows x 128 bytes");
+  static_assert(2 * kABytes == kDgCols * 64 * 2, "one decoded stage holds 64 rows x 256 columns");
+  extern __shared__ __align__(1024) char smem[];
+  const GemvArgs& g = u.g;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  char* lut = smem + Smem::lut;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::bars);
+  uint64_t* full_w = bars;
+  uint64_t* w_empty = full_w + kSW;
+  uint64_t* full_b = w_empty + kSW;
+  uint64_t* b_empty = full_b + kSB;
+  uint64_t* a_ready = b_empty + kSB;
+  uint64_t* a_empty = a_ready + kSA;
+  uint64_t* acc_full = a_empty + kSA;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Smem::tmem_slot);
+  int32_t* s_ts = reinterpret_cast<int32_t*>(smem + Smem::tables);
+  int32_t* s_offs = s_ts + 1025;
+  for (int i = tid; i <= g.E; i += kThreads) {
+    s_ts[i] = u.tile_start[i];
+    s_offs[i] = g.offsets[i];
+  }
+  const int nct = g.K / kDgCols;  // column tiles per expert
+  const int nchunks = g.N / 64;   // 64 weight rows per chunk
+  const int total_tiles = u.tile_start[g.E] * nct;
+  Waiter wt{false, g.err};
+  if (tid == 0) {
+    for (int s = 0; s < kSW; ++s) {
+      mbar_init(&full_w[s], 1);
+      mbar_init(&w_empty[s], 256);
+    }
+    for (int s = 0; s < kSB; ++s) {
+      mbar_init(&full_b[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < kSA; ++s) {
+      mbar_init(&a_ready[s], 256);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    fence_proxy_async();
+  }
+  if (warp == 3) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  {
+    const float code = c_nf4[lane & 15];
+    for (int e = warp; e < 256; e += kThreads / 32) {
+      const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
+      reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // packed rows: one box {128 B = 256 columns, 64 rows} per chunk, 128-byte swizzle
+    if (lane == 0) {
+      int n = 0;
+      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+        TileInfo ti;
+        tile_info(s_ts, s_offs, g.E, nct, t, ti);
+        for (int c = 0; c < nchunks; ++c, ++n) {
+          const int s = n % kSW;
+          if (!wt.wait(&w_empty[s], ((n / kSW) & 1) ^ 1)) break;
+          mbar_arrive_expect_tx(&full_w[s], 64 * 128);
+          tma_load_2d(smem + Smem::w + s * 2 * Smem::wbytes, &wmap, ti.ft * (kDgCols / 2), ti.e * g.N + c * 64,
+                      &full_w[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // dY rows: one box {64 columns of N, 128 rows} per chunk
+    if (lane == 0) {
+      int n = 0;
+      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+        TileInfo ti;
+        tile_info(s_ts, s_offs, g.E, nct, t, ti);
+        for (int c = 0; c < nchunks; ++c, ++n) {
+          const int s = n % kSB;
+          if (!wt.wait(&b_empty[s], ((n / kSB) & 1) ^ 1)) break;
+          mbar_arrive_expect_tx(&full_b[s], kBBytes);
+          tma_load_2d(smem + Smem::b + s * kBBytes, &bmap, c * 64, ti.row0 + ti.tt * kTok, &full_b[s]);
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // idle
+  } else if (warp == 3) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kDgCols) | (1u << 16);  // B (the decoded weights) MN-major
+      int n = 0, it = 0;
+      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        if (!wt.wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1)) break;
+        tc_fence_after();
+        for (int c = 0; c < nchunks; ++c, ++n) {
+          const int s = n % kSB, sa = n % kSA;
+          if (!wt.wait(&full_b[s], (n / kSB) & 1)) break;
+          if (!wt.wait(&a_ready[sa], (n / kSA) & 1)) break;
+          tc_fence_after();
+          const uint32_t ysm = smem_u32(smem + Smem::b + s * kBBytes);
+          const uint32_t wsm = smem_u32(smem + Smem::a + sa * 2 * kABytes);
+          for (int kk = 0; kk < 4; ++kk)  // 16 weight rows = two 8-row atoms per step
+            umma_f16(tmem + buf * kDgCols, sw128_desc(ysm + kk * 32),
+                     sw128_mn_desc(wsm + kk * 2 * kDgAtom, 8 * kDgAtom, kDgAtom), idesc, (c | kk) != 0);
+          umma_commit(&b_empty[s]);
+          umma_commit(&a_empty[sa]);
+        }
+        umma_commit(&acc_full[buf]);
+      }
+    }
+  } else if (warp < 12) {
+    // decode: thread (row rr of the chunk, column atom kb) turns 32 packed bytes into 64 fp16
+    const int d = tid - 128;
+    const int rr = d & 63, kb = d >> 6;
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    int nw = 0;
+    for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+      TileInfo ti;
+      tile_info(s_ts, s_offs, g.E, nct, t, ti);
+      const float* am = g.absmax + ((int64_t)ti.e * g.N + rr) * (g.K / 64) + ti.ft * 4 + kb;
+      float a_nxt = __ldg(am);
+      for (int c = 0; c < nchunks; ++c, ++nw) {
+        const int s = nw % kSW, sa = nw % kSA;
+        const float a = a_nxt;
+        if (c + 1 < nchunks) a_nxt = __ldg(am + (int64_t)(c + 1) * 64 * (g.K / 64));
+        if (!wt.wait(&full_w[s], (nw / kSW) & 1)) break;
+        const char* wrow = smem + Smem::w + s * 2 * Smem::wbytes + rr * 128;
+        const uint4 p0 = *reinterpret_cast<const uint4*>(wrow + (((2 * kb) ^ (rr & 7)) << 4));
+        const uint4 p1 = *reinterpret_cast<const uint4*>(wrow + (((2 * kb + 1) ^ (rr & 7)) << 4));
+        fence_proxy_async();
+        mbar_arrive(&w_empty[s]);
+        if (!wt.wait(&a_empty[sa], ((nw / kSA) & 1) ^ 1)) break;
+        const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const __half2 sc = __float2half2_rn(a);
+        char* adst = smem + Smem::a + sa * 2 * kABytes + (kb * 8 + (rr >> 3)) * kDgAtom + (rr & 7) * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {  // 16-byte unit q = columns 8q .. 8q+7 of the atom
+          uint32_t o[4];
+#pragma unroll
+          for (int bb = 0; bb < 4; ++bb) {
+            const uint32_t byte = (words[q] >> (8 * bb)) & 0xffu;
+            uint32_t pr = *reinterpret_cast<const uint32_t*>(lut + ((byte << 7) | lane4));
+            __half2 v = __hmul2(*reinterpret_cast<__half2*>(&pr), sc);
+            o[bb] = *reinterpret_cast<uint32_t*>(&v);
+          }
+          *reinterpret_cast<uint4*>(adst + ((q ^ (rr & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async();
+        mbar_arrive(&a_ready[sa]);
+      }
+    }
+  } else {
+    // epilogue: TMEM lane = row of the token tile, column = output column of the tile
+    const int ew = warp - 12;
+    const int r = ew * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
+      TileInfo ti;
+      tile_info(s_ts, s_offs, g.E, nct, t, ti);
+      const int buf = it & 1;
+      const int m = ti.tt * kTok + r;
+      const bool valid = m < ti.M;
+      const int64_t srow = ti.row0 + (valid ? m : 0);
+      const float sc = g.a_scale ? g.a_scale[srow] : 1.f;
+      if (!wt.wait(&acc_full[buf], (it >> 1) & 1)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + buf * kDgCols;
+      OutT* orow = reinterpret_cast<OutT*>(g.out) + srow * g.Nout + ti.ft * kDgCols;
+      for (int c0 = 0; c0 < kDgCols; c0 += 16) {
+        float v[16];
+        tmem_ld16(tbase + c0, v);
+        if (valid) {
+          if (sizeof(OutT) == 4) {
+            float4* dst = reinterpret_cast<float4*>(orow + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_float4(v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc, v[4 * j + 3] * sc);
+          } else {
+            uint32_t pk[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const OutT lo = store_cast<OutT>(v[2 * j] * sc, g.err), hi = store_cast<OutT>(v[2 * j + 1] * sc, g.err);
+              pk[j] = (uint32_t)(*reinterpret_cast<const uint16_t*>(&lo)) |
+                      ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 3) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+}
+
+bool umma_dgrad_eligible(int N, int K) { return N % 64 == 0 && K % kDgCols == 0 && encode_tiled_fn() != nullptr; }
+
+template <typename OutT>
+static e4b_status launch_dgrad_t(const UmmaArgs& u, cudaStream_t s) {
+  using Smem = SmemT<E4B_FMT_NF4>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return E4B_ERR_CUDA;
+  static std::atomic<unsigned long long> configured{0};
+  static int sm_count[64] = {0};
+  const unsigned long long bit = 1ull << dev;
+  if (!(configured.load() & bit)) {
+    if (cudaFuncSetAttribute(nf4_umma_dgrad_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total) !=
+        cudaSuccess)
+      return E4B_ERR_CUDA;
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sm_count[dev] = sms;
+    configured.fetch_or(bit);
+  }
+  const GemvArgs& g = u.g;
+  int grid = sm_count[dev];
+  const int bound = u.max_tiles * (g.K / kDgCols);
+  if (bound < grid) grid = bound;
+  if (grid < 1) return E4B_OK;
+  CUtensorMap wmap;  // packed rows [E*N][K/2 bytes], box {128 B, 64 rows}, 128-byte swizzle
+  const cuuint64_t dims[2] = {(cuuint64_t)(g.K / 2), (cuuint64_t)g.E * g.N};
+  const cuuint64_t str[1] = {(cuuint64_t)(g.K / 2)};
+  const cuuint32_t box[2] = {128, 64};
+  if (!encode_tiled(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, g.packed, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    return E4B_ERR_CUDA;
+  CUtensorMap bmap;  // fp16 dY rows [x_rows][N], box {64, 128 rows}, 128-byte swizzle
+  const cuuint64_t bdims[2] = {(cuuint64_t)g.N, (cuuint64_t)u.x_rows};
+  const cuuint64_t bstr[1] = {(cuuint64_t)g.N * 2};
+  const cuuint32_t bbox[2] = {64, kTok};
+  if (!encode_tiled(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.a, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B))
+    return E4B_ERR_CUDA;
+  nf4_umma_dgrad_kernel<OutT><<<grid, kThreads, Smem::total, s>>>(u, wmap, bmap);
+  return launch_status();
+}
+
+e4b_status launch_umma_dgrad(const UmmaArgs& u, int out_dtype, cudaStream_t s) {
+  if (!umma_dgrad_eligible(u.g.N, u.g.K)) return E4B_ERR_UNSUPPORTED;
+  switch (out_dtype) {
+    case E4B_F32: return launch_dgrad_t<float>(u, s);
+    case E4B_BF16: return launch_dgrad_t<__nv_bfloat16>(u, s);
+    case E4B_F16: return launch_dgrad_t<__half>(u, s);
+    default: return E4B_ERR_UNSUPPORTED;
+  }
 }
 
 }  // namespace e4b

@@ -26,4 +26,10 @@ bool umma_eligible(int T, int k, int E, int H, int I, int has_gate, int act_dtyp
 UmmaArgs umma_args_from(const GemvArgs& g, void* scratch, const int32_t* tile_start, int T, int k, int x_rows);
 e4b_status launch_umma(const UmmaArgs& u, int act_dtype, cudaStream_t s, int weight_format = E4B_FMT_NF4);
 
+// dgrad of a frozen grouped NF4 projection (umma.cu): out[r, :K] = a[r, :N] . W_e with `a` fp16
+// expert-sorted rows [x_rows, N] (per-row scales in g.a_scale), out_dtype fp32 / bf16 / fp16,
+// g.Nout = K. N a multiple of 64, K of 256; tile_start counts kUmmaTokens-row tiles.
+bool umma_dgrad_eligible(int N, int K);
+e4b_status launch_umma_dgrad(const UmmaArgs& u, int out_dtype, cudaStream_t s);
+
 }  // namespace e4b

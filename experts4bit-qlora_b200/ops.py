@@ -143,6 +143,34 @@ def grouped_nf4_gemm(a: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor
     return out
 
 
+def dgrad_eligible(n: int, k: int) -> bool:
+    """Shapes ``e4b_grouped_nf4_dgrad`` takes: ``W [E, n, k]`` with n % 64 == 0 and k % 256 == 0."""
+    return n % 64 == 0 and k % 256 == 0
+
+
+def grouped_nf4_dgrad(dy: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, offsets: torch.Tensor,
+                      out_dtype=torch.float32) -> torch.Tensor:
+    """Input gradient of a frozen grouped NF4 projection: ``dx[r] = dy[r] . W_e`` for the
+    expert-sorted rows of expert e (``offsets [E+1]``), with ``packed [E,N,K/2]`` /
+    ``absmax [E,N,K/64]`` decoded on the fly. ``dy [R, N]`` bf16/fp16; returns ``[R, K]``."""
+    _cuda(dy, "dy")
+    dy = dy.contiguous()
+    E, Nn, Kh = packed.shape
+    K = Kh * 2
+    R = dy.shape[0]
+    if dy.dim() != 2 or dy.shape[1] != Nn:
+        raise ValueError(f"dy must be [R, {Nn}], got {tuple(dy.shape)}")
+    out = torch.empty(R, K, dtype=out_dtype, device=dy.device)
+    L = N.lib()
+    ws = N.workspaces.get(dy.device, L.e4b_grouped_nf4_dgrad_workspace_bytes(R, E, Nn, K), "dgrad")
+    offs = offsets.to(torch.int32).contiguous()
+    N.check(L.e4b_grouped_nf4_dgrad(dy.data_ptr(), N.dtype_code(dy.dtype), packed.contiguous().data_ptr(),
+                                    absmax.contiguous().data_ptr(), offs.data_ptr(), E, R, Nn, K, out.data_ptr(),
+                                    N.dtype_code(out_dtype), ws.data_ptr(), ws.numel(), N.stream_handle(dy.device)),
+            "e4b_grouped_nf4_dgrad")
+    return out
+
+
 def combine(rows: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, tokens: int, k: int,
             out_dtype=torch.bfloat16) -> torch.Tensor:
     _cuda(rows, "rows")
@@ -176,8 +204,28 @@ def _expect(t: torch.Tensor, what: str, device, dtypes, numel: int | None = None
         raise ValueError(f"{what} has shape {tuple(t.shape)}, expected {tuple(shape)}")
 
 
+_VALIDATED: dict = {}  # stacks already checked for this geometry (bounded; keys hold no tensors)
+
+
 def _check_layer(dev, E, H, I, has_gate, gate_up_packed, gate_up_absmax, down_packed, down_absmax, weight_format,
                  lora=None):
+    key = None
+    if lora is None:
+        key = (dev, E, H, I, has_gate, weight_format) + tuple(
+            (m.data_ptr(), m.numel(), m.dtype, m.device) for m in (gate_up_packed, gate_up_absmax, down_packed,
+                                                                   down_absmax))
+        if key in _VALIDATED:
+            return
+    _check_layer_full(dev, E, H, I, has_gate, gate_up_packed, gate_up_absmax, down_packed, down_absmax,
+                      weight_format, lora)
+    if key is not None:
+        if len(_VALIDATED) > 4096:
+            _VALIDATED.clear()
+        _VALIDATED[key] = True
+
+
+def _check_layer_full(dev, E, H, I, has_gate, gate_up_packed, gate_up_absmax, down_packed, down_absmax,
+                      weight_format, lora=None):
     n1 = 2 * I if has_gate else I
     if weight_format == N.FMT_MXFP4:
         _expect(gate_up_packed, "gate_up codes", dev, (torch.uint8,), E * n1 * H // 2)
@@ -272,8 +320,6 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     ws = workspace if workspace is not None else N.workspaces.get(hidden.device, nbytes, "moe")
     if ws.numel() < nbytes:
         raise ValueError(f"workspace of {ws.numel()} bytes < required {nbytes}")
-    if not check_errors:
-        N.error_watch.before(ws, "e4b_moe_forward")
     N.check(L.e4b_moe_forward(ctypes.byref(d), ctypes.byref(t), ws.data_ptr(), ws.numel(),
                               N.stream_handle(hidden.device)), "e4b_moe_forward")
     del keep
@@ -282,7 +328,7 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
         if err:
             raise N.E4BError(err, "e4b_moe_forward (device)")
     else:
-        N.error_watch.after(ws)
+        N.error_watch.after(ws, "e4b_moe_forward")
     return out
 
 
@@ -327,8 +373,6 @@ def moe_decode_step(hidden: torch.Tensor, router_weight: torch.Tensor, top_k: in
     ws = workspace if workspace is not None else N.workspaces.get(dev, nbytes, "moe_step")
     if ws.numel() < nbytes:
         raise ValueError(f"workspace of {ws.numel()} bytes < required {nbytes}")
-    if not check_errors:
-        N.error_watch.before(ws, "e4b_moe_decode_step")
     N.check(L.e4b_moe_decode_step(ctypes.byref(d), ctypes.byref(t), wr.data_ptr(), N.dtype_code(wr.dtype), kind,
                                   int(norm_topk_prob), topk_idx.data_ptr(), topk_w.data_ptr(), ws.data_ptr(),
                                   ws.numel(), N.stream_handle(dev)), "e4b_moe_decode_step")
@@ -338,7 +382,7 @@ def moe_decode_step(hidden: torch.Tensor, router_weight: torch.Tensor, top_k: in
         if err:
             raise N.E4BError(err, "e4b_moe_decode_step (device)")
     else:
-        N.error_watch.after(ws)
+        N.error_watch.after(ws, "e4b_moe_decode_step")
     return out, topk_w, topk_idx
 
 

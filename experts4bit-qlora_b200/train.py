@@ -13,12 +13,12 @@ Forward: the device permutation (``e4b_permute``) and the grouped NF4 GEMMs
 (``e4b_grouped_nf4_gemm``: tcgen05 tiles at prefill sizes) for both frozen
 projections; the adapter products per expert.
 
-Backward (recompute-decode, as the reference's per-expert decode loop): the frozen
-stacks are dequantised once per backward (``e4b_nf4_dequantize``, one launch per
-stack, bf16, freed after the step; B200's memory holds a whole stack), and every
-per-expert product -- ``dL/dh = dD . W_down``, ``dL/dx = dP . W_gate_up``, the adapter
-products and the four adapter gradients -- runs as one batched GEMM over the experts'
-row segments padded to the longest. ``dL/d top_k_weights`` is the row dot product of
+Backward: the input gradients of the frozen projections, ``dL/dh = dD . W_down`` and
+``dL/dx = dP . W_gate_up``, run on the library's dgrad kernel with ``dgrad=True``
+(``e4b_grouped_nf4_dgrad``: tcgen05 tiles, each weight tile decoded into shared memory,
+nothing materialised), else on one decode of each stack per backward (``e4b_nf4_dequantize``,
+freed after the step) and batched GEMMs; the adapter products and the four adapter
+gradients run as batched GEMMs over the experts' row segments padded to the longest. ``dL/d top_k_weights`` is the row dot product of
 the incoming gradient with the unweighted down rows. Nothing is saved that depends
 on the frozen weights, so the decoded stacks never live past one backward.
 
@@ -117,12 +117,14 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
         ctx.lora_mod = lora_mod
         ctx.seg = seg
         ctx.meta = (T, k, E, H, I, n1, s)
-        ctx.save_for_backward(token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn)
+        ctx.save_for_backward(token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn,
+                              offsets)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn = ctx.saved_tensors
+        (token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn,
+         offsets) = ctx.saved_tensors
         lora_mod, seg = ctx.lora_mod, ctx.seg
         base = lora_mod.base
         T, k, E, H, I, n1, s = ctx.meta
@@ -133,17 +135,23 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
         grad_w = torch.zeros(T * k, dtype=torch.float32, device=grad_out.device)
         grad_w[order] = d_w
         dd = (g_rows * w_rows.float().view(-1, 1)).to(cdt)             # dL/d down rows
-        # frozen stacks decoded once for this backward (bf16, freed on return)
-        W_dn = ops.nf4_dequantize(base.down_proj, base.down_absmax, (E, H, I), cdt)
+        dgrad = getattr(lora_mod, "_e4b_dgrad", False)
         ddp = seg.pad(dd)                                               # [Ea, L, H]
-        dh = torch.bmm(ddp, W_dn if seg.Ea == E else W_dn[eid])        # [Ea, L, I]
-        del W_dn
+        if dgrad and ops.dgrad_eligible(H, I):
+            # dL/dh of the frozen down projection on the tensor cores, nothing decoded to memory
+            dh_w = ops.grouped_nf4_dgrad(dd, base.down_proj.view(E, H, I // 2), base.down_absmax.view(E, H, I // 64),
+                                         offsets)                       # [R, I] fp32
+        else:
+            # the frozen stack decoded once for this backward (compute dtype, freed on return)
+            W_dn = ops.nf4_dequantize(base.down_proj, base.down_absmax, (E, H, I), cdt)
+            dh_w = seg.unpad(torch.bmm(ddp, W_dn if seg.Ea == E else W_dn[eid]).float())
+            del W_dn
         ddp32 = ddp.to(B_dn.dtype)
         t_dn = torch.bmm(ddp32, B_dn[eid])                              # [Ea, L, r]
         gB_dn = s * torch.bmm(ddp32.transpose(1, 2), xa_dn)             # [Ea, H, r]
         hp = seg.pad(h).to(A_dn.dtype)
         gA_dn = s * torch.bmm(t_dn.transpose(1, 2), hp)                 # [Ea, r, I]
-        dh = seg.unpad(dh.float() + s * torch.bmm(t_dn, A_dn[eid]))     # [R, I] fp32
+        dh = dh_w + seg.unpad(s * torch.bmm(t_dn, A_dn[eid])).float()  # [R, I] fp32
         # SiLU(gate) * up
         pf = proj.float()
         if base.has_gate:
@@ -154,16 +162,20 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
             sg = torch.sigmoid(pf)
             dproj = dh * (sg * (1 + pf * (1 - sg)))
         dproj = dproj.to(cdt)
-        W_gu = ops.nf4_dequantize(base.gate_up_proj, base.gate_up_absmax, (E, n1, H), cdt)
         dpp = seg.pad(dproj)                                            # [Ea, L, n1]
-        dx = torch.bmm(dpp, W_gu if seg.Ea == E else W_gu[eid])        # [Ea, L, H]
-        del W_gu
+        if dgrad and ops.dgrad_eligible(n1, H):
+            dx_w = ops.grouped_nf4_dgrad(dproj, base.gate_up_proj.view(E, n1, H // 2),
+                                         base.gate_up_absmax.view(E, n1, H // 64), offsets)  # [R, H] fp32
+        else:
+            W_gu = ops.nf4_dequantize(base.gate_up_proj, base.gate_up_absmax, (E, n1, H), cdt)
+            dx_w = seg.unpad(torch.bmm(dpp, W_gu if seg.Ea == E else W_gu[eid]).float())
+            del W_gu
         dpp32 = dpp.to(B_gu.dtype)
         t_gu = torch.bmm(dpp32, B_gu[eid])                              # [Ea, L, r]
         gB_gu = s * torch.bmm(dpp32.transpose(1, 2), xa_gu)             # [Ea, n1, r]
         xp = seg.pad(x).to(A_gu.dtype)
         gA_gu = s * torch.bmm(t_gu.transpose(1, 2), xp)                 # [Ea, r, H]
-        dx = seg.unpad(dx.float() + s * torch.bmm(t_gu, A_gu[eid]))     # [R, H] fp32
+        dx = dx_w + seg.unpad(s * torch.bmm(t_gu, A_gu[eid])).float()  # [R, H] fp32
         grad_hidden = dx[inv].view(T, k, H).sum(1)                      # slot order, no atomics
 
         def scatter(g_act, like):
@@ -209,10 +221,11 @@ def _train_ineligible(mod) -> Optional[str]:
 
 def enable_fast_train(model, verbose: bool = False, dgrad: bool = False) -> int:
     """Route ``ExpertsLoRA`` training through the fused path; returns the patch count
-    (``fast.py:555-660``). ``dgrad`` is accepted for the reference's signature and recorded
-    on the module: this backward always decodes each frozen stack once and runs the
-    input-gradient products as batched GEMMs, which is what the reference's single-launch
-    dgrad kernel option selects."""
+    (``fast.py:555-660``). ``dgrad=True`` takes the input gradients of both frozen projections
+    through the library's dgrad kernel (``e4b_grouped_nf4_dgrad``: tcgen05, weights decoded
+    tile by tile, nothing materialised), as the reference's option selects its single-launch
+    dgrad kernel; ``dgrad=False`` decodes each frozen stack once per backward and runs the
+    products as batched GEMMs over the experts' row segments."""
     from .experts import Experts4bit, ExpertsNbit
     from .lora import ExpertsLoRA
 

@@ -161,6 +161,20 @@ E4B_API e4b_status e4b_grouped_nf4_gemm(const void* a, int a_dtype, const int32_
                                 int epilogue, void* out, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* Replaces the single-launch dgrad kernel of grouped-nf4-gemm >= 0.7.0 that
+ * fused_grouped_lora's backward calls with dgrad_kernel=True
+ * (engines/fast.py:519-550, :453-552): the input gradient of a frozen grouped
+ * projection, dx[r, :] = dy[r, :] . W_e for the rows r of expert e, with W_e the
+ * NF4 stack packed [E, N, K/2], absmax [E, N, K/64] and no decoded stack in
+ * memory. dy [R, N] (bf16/f16) rows grouped by expert as offsets [E+1]
+ * (int32, device); dx [R, K] in dx_dtype (f32, bf16 or f16). N % 64 == 0,
+ * K % 256 == 0. fp32 accumulation on the tensor cores (dy as fp16 under a
+ * per-row power-of-two scale). workspace: e4b_grouped_nf4_dgrad_workspace_bytes. */
+E4B_API size_t e4b_grouped_nf4_dgrad_workspace_bytes(int R, int E, int N, int K);
+E4B_API e4b_status e4b_grouped_nf4_dgrad(const void* dy, int dy_dtype, const uint8_t* packed, const float* absmax,
+                                 const int32_t* offsets, int E, int R, int N, int K, void* dx, int dx_dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Combine (R7) -------------------------------------------------------- */
 
 /* Replaces engines/fast.py:158-160 + _scatter_combine (:260-278): out[t] =
@@ -381,6 +395,15 @@ E4B_API e4b_status e4b_selftest_wait_timeout(void* workspace, size_t workspace_b
 /* Reads (and clears) the device error word of a workspace used by the calls
  * above. Synchronises `stream`; for debugging and tests, not the hot path. */
 E4B_API e4b_status e4b_read_device_error(void* workspace, void* stream, int* error_out);
+
+/* Asynchronous watch of that word, for hosts that surface device errors without a
+ * sync per call: returns the value the previous watch of this (workspace,
+ * host_word, event) triple copied, if `event` (a cudaEvent_t) has completed,
+ * else 0; then queues a 4-byte copy of the word into `host_word` (pinned host
+ * memory) on `stream` and records `event` behind it. Non-zero: an earlier call
+ * recorded that error; read and clear it with e4b_read_device_error. Not for use
+ * inside a stream capture. */
+E4B_API int e4b_watch_device_error(void* workspace, int* host_word, void* event, void* stream);
 
 #ifdef __cplusplus
 }

@@ -72,7 +72,7 @@ def test_error_word_is_sticky_across_clean_calls(e4b, monkeypatch):
     clean = torch.randn(T, H, device=DEV).to(torch.bfloat16)
     huge = (clean.float() * 4000).to(torch.bfloat16)
     monkeypatch.setattr(e4b._native.error_watch, "before", lambda ws, what: None)
-    monkeypatch.setattr(e4b._native.error_watch, "after", lambda ws: None)
+    monkeypatch.setattr(e4b._native.error_watch, "after", lambda ws, what="": None)
     ws = torch.zeros(1 << 24, dtype=torch.uint8, device=DEV)
     args = (mod.gate_up_proj, mod.gate_up_absmax, mod.down_proj, mod.down_absmax, E, I)
     for T_ in (4, 1):  # the flow kernel (T=1) and the multi-kernel path's shapes alike

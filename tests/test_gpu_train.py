@@ -71,14 +71,19 @@ def _ok(m):
     return m["forward"] < FWD_TOL and all(v < GRAD_TOL for k, v in m.items() if k != "forward")
 
 
-@pytest.mark.parametrize("geom", [(8, 128, 192, 64), (8, 256, 256, 512)], ids=["reference_fixture", "tensor_core"])
-def test_fused_train_matches_reference_forward_and_gradients(e4b, geom):
+@pytest.mark.parametrize("dgrad", [False, True], ids=["decode_once", "dgrad_kernel"])
+@pytest.mark.parametrize("geom", [(8, 128, 192, 64), (8, 256, 256, 512), (8, 512, 768, 384)],
+                         ids=["reference_fixture", "tensor_core", "qwen3_widths"])
+def test_fused_train_matches_reference_forward_and_gradients(e4b, geom, dgrad):
+    """With dgrad=True the tensor-core geometries take both input gradients through
+    e4b_grouped_nf4_dgrad (the reference fixture's widths are not multiples of 256 and keep
+    the decode-once path)."""
     E, H, I, T = geom
     ref = _build(e4b, E, H, I)
     cand = _build(e4b, E, H, I)
     for (n, p), (_, q) in zip(cand.named_parameters(), ref.named_parameters()):
         assert torch.equal(p, q), n
-    assert e4b.enable_fast_train(cand) == 1
+    assert e4b.enable_fast_train(cand, dgrad=dgrad) == 1
     m = _parity(cand, ref, _inputs(E, H, n_tok=T))
     print("\nfused train vs loop: " + "  ".join(f"{k}={v:.2e}" for k, v in m.items()))
     assert _ok(m), m
