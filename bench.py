@@ -64,7 +64,7 @@ WORKLOADS = {
 # DRAM bytes (read + write) per launch of the dominant kernel, from the ncu captures summarised
 # under profiles/ (same kernels and shapes); workloads without a capture report null.
 MEASURED_TRAFFIC = {
-    "olmoe-decode": {"bytes": 28700416 + 21248, "kernel": "nf4_decode_slice_kernel",
+    "olmoe-decode": {"bytes": 28703744 + 768, "kernel": "nf4_decode_slice_kernel",
                      "source": "profiles/nf4_decode_slice__olmoe_decode.md"},
     "qwen3-prefill-base": {"bytes": 364481536 + 40394240, "kernel": "nf4_umma_kernel<__half, 2> (gate_up)",
                            "source": "profiles/nf4_umma__qwen3_prefill.md"},

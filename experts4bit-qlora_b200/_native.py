@@ -267,7 +267,9 @@ class _ErrorWatch:
             with self._lock:
                 ent = self._w.get(ws.data_ptr())
                 if ent is None:
-                    ent = (torch.zeros(1, dtype=torch.int32, pin_memory=True), ws, torch.cuda.Event())
+                    ev = torch.cuda.Event()
+                    ev.record()  # torch creates the CUDA event on its first record
+                    ent = (torch.zeros(1, dtype=torch.int32, pin_memory=True), ws, ev)
                     self._w[ws.data_ptr()] = ent
         elif torch.cuda.is_current_stream_capturing():
             return
