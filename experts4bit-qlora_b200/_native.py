@@ -197,7 +197,15 @@ def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
+    """The raw cudaStream_t of torch's current stream on ``device`` (a hot-path call: torch's
+    private raw-stream query when present, which skips building a Stream object)."""
+    if _raw_stream is not None:
+        idx = device.index if isinstance(device, torch.device) else device
+        return _raw_stream(idx if idx is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -274,8 +282,7 @@ class _ErrorWatch:
         elif torch.cuda.is_current_stream_capturing():
             return
         host, _, ev = ent
-        if lib().e4b_watch_device_error(ws.data_ptr(), host.data_ptr(), ev.cuda_event,
-                                        torch.cuda.current_stream(ws.device).cuda_stream):
+        if lib().e4b_watch_device_error(ws.data_ptr(), host.data_ptr(), ev.cuda_event, stream_handle(ws.device)):
             self.raise_if_set(ws, what, host)
 
     def raise_if_set(self, ws: torch.Tensor, what: str, host: torch.Tensor | None = None) -> None:
