@@ -843,21 +843,77 @@ __device__ __forceinline__ void slice_issue(const DecodeArgs& a, const SliceMaps
   }
 }
 
+// The NF4 codebook as fp16 bytes in registers, for the byte-permute decode: l0..l3 hold the low
+// bytes of codes 0-3, 4-7, 8-11, 12-15 and h0..h3 the high bytes.
+struct Nf4Bytes {
+  uint32_t l0, l1, l2, l3, h0, h1, h2, h3;
+};
+
+__device__ __forceinline__ Nf4Bytes nf4_bytes() {
+  uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int v = 0; v < 16; ++v) {
+    const uint32_t b = __half_as_ushort(__float2half_rn(c_nf4[v]));
+    lo[v >> 2] |= (b & 0xffu) << (8 * (v & 3));
+    hi[v >> 2] |= (b >> 8) << (8 * (v & 3));
+  }
+  return Nf4Bytes{lo[0], lo[1], lo[2], lo[3], hi[0], hi[1], hi[2], hi[3]};
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+  return d;
+}
+__device__ __forceinline__ uint32_t bytesel(uint32_t a, uint32_t b, uint32_t m) {  // (a & ~m) | (b & m)
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xD8;" : "=r"(d) : "r"(a), "r"(b), "r"(m));
+  return d;
+}
+
+// The four fp16 pairs of a packed word (byte j -> the pair table's entry j: code[high nibble] in
+// the low half) with no shared memory: a 3-bit index selects a byte of an 8-entry half of the
+// table (prmt), bit 3 of each nibble (spread to a byte mask by prmt's sign replication) picks
+// the half. Bit-identical to the pair-table lookups.
+__device__ __forceinline__ void nf4_decode_word(uint32_t w, const Nf4Bytes& T, uint32_t (&o)[4]) {
+  const uint32_t t = w << 4;
+  const uint32_t s = w & 0x77777777u, sh = s >> 16;
+  const uint32_t m0 = prmt(t, w, 0xD9C8u), m1 = prmt(t, w, 0xFBEAu);
+  const uint32_t la = bytesel(prmt(T.l0, T.l1, s), prmt(T.l2, T.l3, s), m0);
+  const uint32_t ha = bytesel(prmt(T.h0, T.h1, s), prmt(T.h2, T.h3, s), m0);
+  const uint32_t lb = bytesel(prmt(T.l0, T.l1, sh), prmt(T.l2, T.l3, sh), m1);
+  const uint32_t hb = bytesel(prmt(T.h0, T.h1, sh), prmt(T.h2, T.h3, sh), m1);
+  o[0] = prmt(la, ha, 0x4051u);
+  o[1] = prmt(la, ha, 0x6273u);
+  o[2] = prmt(lb, hb, 0x4051u);
+  o[3] = prmt(lb, hb, 0x6273u);
+}
+
 // One 64-element block of a 16-row tile against one token fragment: rows A (w0, scale sa) and
-// B (w1, scale sb), the streaming GEMV's fragment order.
+// B (w1, scale sb), the streaming GEMV's fragment order. PW of the block's first-half words
+// (w0v.x, then w1v.x) are decoded in registers, the rest through the shared pair table: the
+// split balances the shared-memory pipe against the integer pipe.
+template <int PW>
 __device__ __forceinline__ void slice_block(float (&acc)[4], const char* lut, uint2 w0v, uint2 w1v, float sa,
-                                            float sb, const uint4 (&xf)[2], uint32_t lane4) {
+                                            float sb, const uint4 (&xf)[2], uint32_t lane4, const Nf4Bytes& T) {
+  uint32_t r0[4], r1[4];  // register-decoded pairs of w0v.x / w1v.x (entries 0..3 = bytes 0..3)
+  if (PW >= 1) nf4_decode_word(w0v.x, T, r0);
+  if (PW >= 2) nf4_decode_word(w1v.x, T, r1);
   float pp[4];
 #pragma unroll
   for (int jj = 0; jj < 4; ++jj) {
     const uint32_t w0 = jj < 2 ? w0v.x : w0v.y, w1 = jj < 2 ? w1v.x : w1v.y;
     uint32_t a0, a1, a2, a3;
     if (jj & 1) {
-      a0 = lut2<2>(lut, w0, lane4); a2 = lut2<3>(lut, w0, lane4);
-      a1 = lut2<2>(lut, w1, lane4); a3 = lut2<3>(lut, w1, lane4);
+      a0 = (jj < 2 && PW >= 1) ? r0[2] : lut2<2>(lut, w0, lane4);
+      a2 = (jj < 2 && PW >= 1) ? r0[3] : lut2<3>(lut, w0, lane4);
+      a1 = (jj < 2 && PW >= 2) ? r1[2] : lut2<2>(lut, w1, lane4);
+      a3 = (jj < 2 && PW >= 2) ? r1[3] : lut2<3>(lut, w1, lane4);
     } else {
-      a0 = lut2<0>(lut, w0, lane4); a2 = lut2<1>(lut, w0, lane4);
-      a1 = lut2<0>(lut, w1, lane4); a3 = lut2<1>(lut, w1, lane4);
+      a0 = (jj < 2 && PW >= 1) ? r0[0] : lut2<0>(lut, w0, lane4);
+      a2 = (jj < 2 && PW >= 1) ? r0[1] : lut2<1>(lut, w0, lane4);
+      a1 = (jj < 2 && PW >= 2) ? r1[0] : lut2<0>(lut, w1, lane4);
+      a3 = (jj < 2 && PW >= 2) ? r1[1] : lut2<1>(lut, w1, lane4);
     }
     const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xf[jj >> 1]);
     if (jj == 0)
@@ -871,7 +927,7 @@ __device__ __forceinline__ void slice_block(float (&acc)[4], const char* lut, ui
   acc[3] = fmaf(pp[3], sb, acc[3]);
 }
 
-template <typename OutT>
+template <typename OutT, int PW>
 __global__ void __launch_bounds__(kThreads, 1)
     nf4_decode_slice_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap gw, const __grid_constant__ CUtensorMap ga,
                             const __grid_constant__ CUtensorMap dw, const __grid_constant__ CUtensorMap da) {
@@ -895,6 +951,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* red = reinterpret_cast<float*>(smem + SSmem::red);
   __half* hs = reinterpret_cast<__half*>(smem + SSmem::hs);
   const SliceMaps maps{&gw, &ga, &dw, &da};
+  const Nf4Bytes nfb = nf4_bytes();
   const int nsl = a.I / kSW, ng = a.H / kSGK, nd = a.H / kSDRows, spu = ng + nd;
   if (tid == 0) {
     for (int s = 0; s < kSSlots; ++s) {
@@ -975,7 +1032,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           sb[i] = *reinterpret_cast<const float*>(slot + 34816 + aofs(rr, bl, 32));
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) slice_block(acc[i], lut, wa[i], wb[i], sa[i], sb[i], xf, lane4);
+        for (int i = 0; i < 4; ++i) slice_block<PW>(acc[i], lut, wa[i], wb[i], sa[i], sb[i], xf, lane4, nfb);
       }
       release(n);
     }
@@ -1022,7 +1079,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float sa = *reinterpret_cast<const float*>(slot + 16384 + ra * 16 + (s & 3) * 4);
           const float sb = *reinterpret_cast<const float*>(slot + 16384 + rb * 16 + (s & 3) * 4);
           float d[4] = {0.f, 0.f, 0.f, 0.f};
-          slice_block(d, lut, wa, wb, sa, sb, hf, lane4);
+          slice_block<PW>(d, lut, wa, wb, sa, sb, hf, lane4, nfb);
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int m = 2 * q + hh;
@@ -1243,13 +1300,13 @@ static e4b_status launch_decode(const DecodeArgs& a, cudaStream_t s) {
 }
 
 
-template <typename OutT>
+template <typename OutT, int PW>
 static e4b_status launch_slice(const DecodeArgs& a, cudaStream_t s) {
   static unsigned long long configured = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return E4B_ERR_CUDA;
   const unsigned long long bit = 1ull << dev;
-  auto kern = nf4_decode_slice_kernel<OutT>;
+  auto kern = nf4_decode_slice_kernel<OutT, PW>;
   {
     std::lock_guard<std::mutex> lk(g_dl_mu);
     if (!(configured & bit)) {
@@ -1406,11 +1463,21 @@ e4b_status launch_decode_layer(const e4b_moe_desc& d, const e4b_moe_tensors* t, 
   a.err = err;
   if (part && decode_mode() == 3 && decode_slice_shape(d)) {
     a.part = static_cast<float*>(part);
-    switch (d.out_dtype) {
-      case E4B_BF16: return launch_slice<__nv_bfloat16>(a, s);
-      case E4B_F16: return launch_slice<__half>(a, s);
-      default: return launch_slice<float>(a, s);
-    }
+    // words of each block decoded in registers instead of the shared pair table (E4B_SLICE_PW)
+    static const int pw = [] {
+      const char* v = getenv("E4B_SLICE_PW");
+      return v ? (v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1) : 1;
+    }();
+#define E4B_SLICE_LAUNCH(P)                                                   \
+  switch (d.out_dtype) {                                                      \
+    case E4B_BF16: return launch_slice<__nv_bfloat16, P>(a, s);               \
+    case E4B_F16: return launch_slice<__half, P>(a, s);                       \
+    default: return launch_slice<float, P>(a, s);                             \
+  }
+    if (pw == 0) E4B_SLICE_LAUNCH(0)
+    if (pw == 2) E4B_SLICE_LAUNCH(2)
+    E4B_SLICE_LAUNCH(1)
+#undef E4B_SLICE_LAUNCH
   }
   const bool two = d.tokens > 8;
   switch (d.out_dtype) {

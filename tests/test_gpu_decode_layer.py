@@ -212,3 +212,40 @@ def _router_fused_case(e4b, E, H, I, k, T, kind, norm):
     assert torch.equal(out, ref)
     mx, mean = M.rel_errors(out.float().cpu(), M.fp32_oracle(st, x.cpu(), idx.cpu(), w.cpu()))
     assert mx <= 1e-2 and mean <= 2e-3, (mx, mean)
+
+
+_PW_SCRIPT = r"""
+import importlib, sys, torch
+sys.path.insert(0, sys.argv[1])
+e4b = importlib.import_module("experts4bit-qlora_b200")
+E, H, I, k, T = 64, 2048, 1024, 8, 3
+g = torch.Generator(device="cuda").manual_seed(7)
+mod = e4b.Experts4bit.from_float((torch.randn(E, 2 * I, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16),
+                                 (torch.randn(E, H, I, generator=g, device="cuda") * 0.02).to(torch.bfloat16))
+x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+w, idx = torch.topk(torch.softmax(torch.randn(T, E, generator=g, device="cuda"), -1), k)
+out = e4b.ops.moe_forward(x, idx, w, mod.gate_up_proj, mod.gate_up_absmax, mod.down_proj, mod.down_absmax, E, I,
+                          check_errors=True)
+torch.save(out.cpu(), sys.argv[2])
+"""
+
+
+def test_slice_register_decode_is_bit_identical(tmp_path):
+    """The slice kernel decodes 0, 1 or 2 words of each block with byte permutes in registers
+    (E4B_SLICE_PW) and the rest through the shared pair table: the same fp16 values either way,
+    so the layer output is identical bit for bit."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = tmp_path / "pw.py"
+    script.write_text(_PW_SCRIPT)
+    outs = []
+    for pw in ("0", "1", "2"):
+        path = tmp_path / f"out{pw}.pt"
+        env = dict(os.environ, E4B_SLICE_PW=pw, E4B_DECODE_KERNEL="3")
+        r = subprocess.run([sys.executable, str(script), root, str(path)], env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(torch.load(path))
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
