@@ -496,7 +496,13 @@ def run_train(args, wl, world, rank, local):
         return a.elapsed_time(b) / n
 
     ref_ms = timed(3, 1)  # the unpatched per-expert loop (the reference's training forward)
-    if pkg.enable_fast_train(mod) != 1:
+    # the backward's input gradients decoded once per stack + batched GEMMs (dgrad=False), then
+    # through the library's dgrad kernel (dgrad=True, the timed configuration)
+    if pkg.enable_fast_train(mod, dgrad=False) != 1:
+        raise SystemExit("enable_fast_train declined the layer")
+    decode_once_ms = timed(max(args.steps // 2, 1), 2)
+    pkg.disable_fast_train(mod)
+    if pkg.enable_fast_train(mod, dgrad=True) != 1:
         raise SystemExit("enable_fast_train declined the layer")
     with ClockSampler(local) as clocks:
         ms = timed(args.steps, max(args.warmup, 3))
@@ -519,6 +525,10 @@ def run_train(args, wl, world, rank, local):
                      "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4), "traffic": None},
         "reference_loop": {"value": round(T / (ref_ms * 1e-3), 1), "unit": "tokens/s",
                            "what": "the unpatched ExpertsLoRA per-expert loop, same GPU, same step"},
+        "dgrad": "kernel (enable_fast_train(dgrad=True): e4b_grouped_nf4_dgrad for both input gradients)",
+        "decode_once": {"value": round(T / (decode_once_ms * 1e-3), 1), "unit": "tokens/s",
+                        "what": "enable_fast_train(dgrad=False): each frozen stack decoded once per backward, "
+                                "batched GEMMs"},
         "clocks": clocks.summary(),
     }
 
