@@ -169,6 +169,32 @@ def test_combine_fixed_order(ops, T, k, H):
     torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("T,k,H", [(5, 4, 64), (33, 8, 128), (1, 2, 2048)])
+def test_combine_bit_exact_against_slot_order_fma(ops, T, k, H):
+    """The combine's contract is bit identity, not a tolerance: out[t] = fma(row_k-1, w_k-1, ...
+    fma(row_0, w_0, 0)) in fp32, slot by slot (the fixed order of fast.py:260-278). The model
+    evaluates each fma as one rounding of the exact product-plus-sum (the product of two fp32
+    values is exact in fp64; the sum is rounded once to fp64 and once to fp32, which differs from
+    a single rounding only at exact fp32 ties, vanishingly rare on random data)."""
+    import numpy as np
+    g = torch.Generator().manual_seed(100 + T)
+    E = 16
+    idx = torch.randint(0, E, (T, k), generator=g)
+    order, tok, pos, counts, off = M.permute(idx, E)
+    rows = torch.randn(T * k, H, generator=g).to(torch.bfloat16)
+    w = torch.rand(T, k, generator=g)
+    inv = torch.empty(T * k, dtype=torch.int32)
+    inv[order] = torch.arange(T * k, dtype=torch.int32)
+    got = ops.combine(rows.to(DEV), inv.to(DEV), w.to(DEV), T, k, torch.float32).cpu().numpy()
+    r64 = rows.float().numpy().astype(np.float64)
+    w64 = w.numpy().astype(np.float64)
+    acc = np.zeros((T, H), dtype=np.float32)
+    for s in range(k):
+        prod = r64[inv[torch.arange(T) * k + s].long().numpy()] * w64[:, s:s + 1]
+        acc = (prod + acc.astype(np.float64)).astype(np.float32)
+    assert np.array_equal(got, acc)
+
+
 @pytest.mark.parametrize("K", [128, 768, 2048])
 def test_gemv_matches_fp16_code_model_to_one_ulp(ops, K):
     """The decode GEMV computes sum_b absmax_b * sum_i fp16(code_i) * fp16(x_i) with fp32 tensor-core
