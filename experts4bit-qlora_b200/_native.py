@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "e4b_grouped_gemm_workspace_bytes", "e4b_grouped_nf4_gemm",
     "e4b_grouped_nf4_dgrad_workspace_bytes", "e4b_grouped_nf4_dgrad",
     "e4b_combine",
+    "e4b_swiglu_forward", "e4b_swiglu_backward", "e4b_combine_row_grads",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
     "e4b_moe_decode_step_workspace_bytes", "e4b_moe_decode_step",
     "e4b_moe_path", "e4b_set_decode_kernel",
@@ -109,6 +110,9 @@ def _declare(lib):
         "e4b_grouped_nf4_dgrad_workspace_bytes": (SZ, [I, I, I, I]),
         "e4b_grouped_nf4_dgrad": (I, [P, I, P, P, P, I, I, I, I, P, I, P, SZ, P]),
         "e4b_combine": (I, [P, I, P, P, I, I, I, I, P, I, P]),
+        "e4b_swiglu_forward": (I, [P, I, ctypes.c_int64, I, I, P, P]),
+        "e4b_swiglu_backward": (I, [P, I, P, ctypes.c_int64, I, I, P, P]),
+        "e4b_combine_row_grads": (I, [P, P, P, P, I, ctypes.c_int64, I, P, P, P]),
         "e4b_moe_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
         "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
         "e4b_moe_forward_static": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P]),

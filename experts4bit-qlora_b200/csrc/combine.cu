@@ -1,7 +1,7 @@
 // Weighted, deterministic un-permute (R7): replaces engines/fast.py:158-160 and
 // _scatter_combine (:260-278). out[t] = sum over s = 0..k-1, in slot order, of
-// fp32(rows[inv[t*k+s]]) * fp32(w[t,s]); no atomics, so repeated calls are
-// bit-identical.
+// fp32(rows[inv[t*k+s]]) * fp32(w[t,s]) (w = NULL: weight 1, the plain slot sum the
+// training backward needs for dL/dx); no atomics, so repeated calls are bit-identical.
 #include "common.cuh"
 
 namespace e4b {
@@ -19,22 +19,25 @@ __global__ void __launch_bounds__(256) combine_kernel(const TR* __restrict__ row
   const int t = blockIdx.x;
   if (threadIdx.x < k) {
     s_row[threadIdx.x] = (int64_t)inv[(int64_t)t * k + threadIdx.x] * H;
-    s_w[threadIdx.x] = load_as_f32(w, w_dtype, (int64_t)t * k + threadIdx.x);
+    s_w[threadIdx.x] = w ? load_as_f32(w, w_dtype, (int64_t)t * k + threadIdx.x) : 1.f;
   }
   __syncthreads();
   for (int h = threadIdx.x * 8; h < H; h += blockDim.x * 8) {
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    constexpr int kVec = sizeof(TR) == 4 ? 2 : 1;  // 16-byte vectors per 8 elements
     for (int s0 = 0; s0 < k; s0 += 8) {
-      uint4 v[8];
+      uint4 v[8][kVec];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (s0 + u < k) v[u] = *reinterpret_cast<const uint4*>(rows + s_row[s0 + u] + h);
+        if (s0 + u < k)
+#pragma unroll
+          for (int q = 0; q < kVec; ++q) v[u][q] = reinterpret_cast<const uint4*>(rows + s_row[s0 + u] + h)[q];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         if (s0 + u >= k) break;
-        const TR* vv = reinterpret_cast<const TR*>(&v[u]);
+        const TR* vv = reinterpret_cast<const TR*>(&v[u][0]);
         const float ws = s_w[s0 + u];
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] = fmaf(to_f32(vv[i]), ws, acc[i]);  // slot order
@@ -70,14 +73,17 @@ using namespace e4b;
 extern "C" e4b_status e4b_combine(const void* rows, int rows_dtype, const int32_t* inv, const void* w, int w_dtype,
                                   int T, int k, int H, void* out, int out_dtype, void* stream) {
   if (T < 0 || k <= 0 || k > kMaxK || H <= 0) return E4B_ERR_INVALID_ARG;
-  if (!is_act_dtype(rows_dtype) || !is_any_dtype(w_dtype) || !is_any_dtype(out_dtype) || H % 8)
+  if (!(is_act_dtype(rows_dtype) || rows_dtype == E4B_F32) || (w && !is_any_dtype(w_dtype)) ||
+      !is_any_dtype(out_dtype) || H % 8)
     return E4B_ERR_UNSUPPORTED;
   if (T == 0) return E4B_OK;
-  if (!rows || !inv || !w || !out) return E4B_ERR_INVALID_ARG;
+  if (!rows || !inv || !out) return E4B_ERR_INVALID_ARG;
   if (!aligned16(rows) || !aligned16(out)) return E4B_ERR_ALIGNMENT;
   cudaStream_t s = (cudaStream_t)stream;
   if (rows_dtype == E4B_BF16)
     launch_rows<__nv_bfloat16>(rows, inv, w, w_dtype, T, k, H, out, out_dtype, s);
+  else if (rows_dtype == E4B_F32)
+    launch_rows<float>(rows, inv, w, w_dtype, T, k, H, out, out_dtype, s);
   else
     launch_rows<__half>(rows, inv, w, w_dtype, T, k, H, out, out_dtype, s);
   return launch_status();

@@ -171,17 +171,63 @@ def grouped_nf4_dgrad(dy: torch.Tensor, packed: torch.Tensor, absmax: torch.Tens
     return out
 
 
-def combine(rows: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, tokens: int, k: int,
+def combine(rows: torch.Tensor, inv: torch.Tensor, w: torch.Tensor | None, tokens: int, k: int,
             out_dtype=torch.bfloat16) -> torch.Tensor:
     _cuda(rows, "rows")
     rows = rows.contiguous()
     H = rows.shape[1]
     out = torch.empty(tokens, H, dtype=out_dtype, device=rows.device)
-    w = w.contiguous()
+    w = w.contiguous() if w is not None else None  # None: every weight 1 (the plain slot sum)
     N.check(N.lib().e4b_combine(rows.data_ptr(), N.dtype_code(rows.dtype), inv.to(torch.int32).contiguous().data_ptr(),
-                                w.data_ptr(), N.dtype_code(w.dtype), tokens, k, H, out.data_ptr(),
-                                N.dtype_code(out_dtype), N.stream_handle(rows.device)), "e4b_combine")
+                                N.ptr(w), N.dtype_code(w.dtype) if w is not None else N.F32, tokens, k, H,
+                                out.data_ptr(), N.dtype_code(out_dtype), N.stream_handle(rows.device)), "e4b_combine")
     return out
+
+
+def swiglu_forward(proj: torch.Tensor, has_gate: bool = True) -> torch.Tensor:
+    """``act(gate) * up`` of expert-sorted projection rows ``[R, 2I]`` (or ``act(proj)``)."""
+    _cuda(proj, "proj")
+    proj = proj.contiguous()
+    R, n1 = proj.shape
+    I = n1 // 2 if has_gate else n1
+    h = torch.empty(R, I, dtype=proj.dtype, device=proj.device)
+    N.check(N.lib().e4b_swiglu_forward(proj.data_ptr(), N.dtype_code(proj.dtype), R, I, int(has_gate), h.data_ptr(),
+                                       N.stream_handle(proj.device)), "e4b_swiglu_forward")
+    return h
+
+
+def swiglu_backward(proj: torch.Tensor, dh: torch.Tensor, has_gate: bool = True) -> torch.Tensor:
+    """dL/d(proj) in proj's dtype from dL/dh (fp32 ``[R, I]``)."""
+    _cuda(proj, "proj")
+    proj = proj.contiguous()
+    dh = dh.float().contiguous()
+    R, n1 = proj.shape
+    I = n1 // 2 if has_gate else n1
+    if tuple(dh.shape) != (R, I):
+        raise ValueError(f"dh must be [{R}, {I}], got {tuple(dh.shape)}")
+    dproj = torch.empty_like(proj)
+    N.check(N.lib().e4b_swiglu_backward(proj.data_ptr(), N.dtype_code(proj.dtype), dh.data_ptr(), R, I, int(has_gate),
+                                        dproj.data_ptr(), N.stream_handle(proj.device)), "e4b_swiglu_backward")
+    return dproj
+
+
+def combine_row_grads(grad: torch.Tensor, token_rows: torch.Tensor, w_rows: torch.Tensor, down: torch.Tensor):
+    """Gradients of ``out[t] = sum_s w down[row]`` per expert-sorted row: ``(dd [R, H] in down's dtype,
+    dw fp32 [R])`` from dL/dout (fp32 ``[T, H]``)."""
+    _cuda(grad, "grad")
+    grad = grad.float().contiguous()
+    down = down.contiguous()
+    rows = token_rows.long().contiguous()
+    w = w_rows.float().contiguous()
+    R, H = down.shape
+    if grad.shape[1] != H or rows.numel() != R or w.numel() != R:
+        raise ValueError("combine_row_grads: grad [T, H], token_rows [R], w_rows [R], down [R, H]")
+    dd = torch.empty_like(down)
+    dw = torch.empty(R, dtype=torch.float32, device=down.device)
+    N.check(N.lib().e4b_combine_row_grads(grad.data_ptr(), rows.data_ptr(), w.data_ptr(), down.data_ptr(),
+                                          N.dtype_code(down.dtype), R, H, dd.data_ptr(), dw.data_ptr(),
+                                          N.stream_handle(down.device)), "e4b_combine_row_grads")
+    return dd, dw
 
 
 # --------------------------------------------------------------------------- #

@@ -70,13 +70,6 @@ class _Segments:
         return xp.reshape(self.Ea * self.L, -1).index_select(0, self.pos)
 
 
-def _swiglu(proj, has_gate, act):
-    if has_gate:
-        g, u = proj.chunk(2, dim=-1)
-        return act(g) * u
-    return act(proj)
-
-
 class _FusedExpertsLoRATrain(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden, top_k_weights, A_gu, B_gu, A_dn, B_dn, lora_mod, top_k_index):
@@ -104,16 +97,15 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
         xa_gu = torch.bmm(xp, A_gu[eid].transpose(1, 2))              # [Ea, L, r]
         d_gu = s * torch.bmm(xa_gu, B_gu[eid].transpose(1, 2))        # [Ea, L, n1]
         proj = proj + seg.unpad(d_gu).to(proj.dtype)
-        h = _swiglu(proj, base.has_gate, base.act_fn)                 # [R, I]
+        h = ops.swiglu_forward(proj, base.has_gate)                   # [R, I], act rounded as lora._epilogue
         down = ops.grouped_nf4_gemm(h.contiguous(), dn_p, dn_a, offsets)
         hp = seg.pad(h).to(A_dn.dtype)
         xa_dn = torch.bmm(hp, A_dn[eid].transpose(1, 2))              # [Ea, L, r]
         d_dn = s * torch.bmm(xa_dn, B_dn[eid].transpose(1, 2))        # [Ea, L, H]
         down = down + seg.unpad(d_dn).to(down.dtype)                  # [R, H] compute dtype
-        w_rows = top_k_weights.reshape(-1)[order]
-        inv = inv.long()
-        # weighted rows summed per token over its k slots in slot order (no atomics)
-        out = (down * w_rows.view(-1, 1))[inv].view(T, k, H).float().sum(1)
+        w_rows = top_k_weights.reshape(-1)[order].float()
+        # weighted rows summed per token over its k slots in slot order, fp32 (no atomics)
+        out = ops.combine(down, inv, top_k_weights.float(), T, k, torch.float32)
         ctx.lora_mod = lora_mod
         ctx.seg = seg
         ctx.meta = (T, k, E, H, I, n1, s)
@@ -130,11 +122,10 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
         T, k, E, H, I, n1, s = ctx.meta
         cdt = proj.dtype
         eid = seg.eid
-        g_rows = grad_out.float().index_select(0, token_rows)          # [R, H]
-        d_w = (g_rows * down.float()).sum(-1)                           # dL/d w_rows
+        # dL/d down rows (grad_out[token] * w) and dL/d w_rows (grad_out[token] . down), one pass
+        dd, d_w = ops.combine_row_grads(grad_out, token_rows, w_rows, down)
         grad_w = torch.zeros(T * k, dtype=torch.float32, device=grad_out.device)
         grad_w[order] = d_w
-        dd = (g_rows * w_rows.float().view(-1, 1)).to(cdt)             # dL/d down rows
         dgrad = getattr(lora_mod, "_e4b_dgrad", False)
         ddp = seg.pad(dd)                                               # [Ea, L, H]
         if dgrad and ops.dgrad_eligible(H, I):
@@ -152,16 +143,7 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
         hp = seg.pad(h).to(A_dn.dtype)
         gA_dn = s * torch.bmm(t_dn.transpose(1, 2), hp)                 # [Ea, r, I]
         dh = dh_w + seg.unpad(s * torch.bmm(t_dn, A_dn[eid])).float()  # [R, I] fp32
-        # SiLU(gate) * up
-        pf = proj.float()
-        if base.has_gate:
-            g, u = pf.chunk(2, dim=-1)
-            sg = torch.sigmoid(g)
-            dproj = torch.cat([dh * u * (sg * (1 + g * (1 - sg))), dh * (g * sg)], dim=-1)
-        else:
-            sg = torch.sigmoid(pf)
-            dproj = dh * (sg * (1 + pf * (1 - sg)))
-        dproj = dproj.to(cdt)
+        dproj = ops.swiglu_backward(proj, dh, base.has_gate)          # SiLU(gate) * up, in the compute dtype
         dpp = seg.pad(dproj)                                            # [Ea, L, n1]
         if dgrad and ops.dgrad_eligible(n1, H):
             dx_w = ops.grouped_nf4_dgrad(dproj, base.gate_up_proj.view(E, n1, H // 2),
@@ -176,7 +158,7 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
         xp = seg.pad(x).to(A_gu.dtype)
         gA_gu = s * torch.bmm(t_gu.transpose(1, 2), xp)                 # [Ea, r, H]
         dx = dx_w + seg.unpad(s * torch.bmm(t_gu, A_gu[eid])).float()  # [R, H] fp32
-        grad_hidden = dx[inv].view(T, k, H).sum(1)                      # slot order, no atomics
+        grad_hidden = ops.combine(dx, inv, None, T, k, torch.float32)  # slot order, no atomics
 
         def scatter(g_act, like):
             full = torch.zeros_like(like)

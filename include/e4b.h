@@ -179,10 +179,32 @@ E4B_API e4b_status e4b_grouped_nf4_dgrad(const void* dy, int dy_dtype, const uin
 
 /* Replaces engines/fast.py:158-160 + _scatter_combine (:260-278): out[t] =
  * sum over s = 0..k-1 (in slot order, fp32) of w[t,s] * rows[inv[t*k+s]].
- * rows [T*k, H] (rows_dtype), w [T,k] (w_dtype), out [T,H] (out_dtype). No
- * atomics: bit-identical across runs. */
+ * rows [T*k, H] (rows_dtype bf16, f16 or f32), w [T,k] (w_dtype; NULL: every
+ * weight 1, the slot sum of the training backward's dL/dx), out [T,H] (out_dtype).
+ * No atomics: bit-identical across runs. */
 E4B_API e4b_status e4b_combine(const void* rows, int rows_dtype, const int32_t* inv, const void* w, int w_dtype, int T,
                        int k, int H, void* out, int out_dtype, void* stream);
+
+/* ---- Training path element-wise steps (fast.py:453-552) ------------------ */
+
+/* The differentiable layer of enable_fast_train (engines/fast.py:453-552) between its
+ * grouped GEMMs, each one pass over the expert-sorted rows (replacing the torch
+ * element-wise chains the reference runs there):
+ * e4b_swiglu_forward: h [R, I] = act(gate) * up of proj [R, 2I] (has_gate; gate =
+ *   columns [0, I)) or act(proj) [R, I], act = SiLU rounded to the dtype as
+ *   lora._epilogue (lora.py:102-128) computes it; bf16/f16.
+ * e4b_swiglu_backward: dproj [R, 2I] (or [R, I]) from dL/dh (fp32 [R, I]) and proj.
+ * e4b_combine_row_grads: for the combine out[t] = sum_s w[t,s] down[row(t,s)], given
+ *   dL/dout (fp32 [T, H]), the token of each sorted row (int64 [R]) and its weight
+ *   (fp32 [R]): dd [R, H] = dL/dout[token] * w in the dtype, dw [R] = dL/dout[token] .
+ *   down[r] in fp32 (the top-k weights' gradient, _scatter_combine :260-278). */
+E4B_API e4b_status e4b_swiglu_forward(const void* proj, int dtype, int64_t R, int I, int has_gate, void* h,
+                              void* stream);
+E4B_API e4b_status e4b_swiglu_backward(const void* proj, int dtype, const float* dh, int64_t R, int I, int has_gate,
+                               void* dproj, void* stream);
+E4B_API e4b_status e4b_combine_row_grads(const float* grad, const int64_t* token_rows, const float* w_rows,
+                                 const void* down, int dtype, int64_t R, int H, void* dd, float* dw,
+                                 void* stream);
 
 /* ---- Whole expert layer (R2-R7 + LoRA R5) -------------------------------- */
 

@@ -1,6 +1,6 @@
-"""CPU: the training path's autograd math (train.py) with its three device calls --
-permutation, grouped NF4 GEMM, stack dequantization -- replaced by CPU stand-ins built on
-the oracle and the host codec. Forward and every gradient of the fused autograd function
+"""CPU: the training path's autograd math (train.py) with its device calls -- permutation,
+grouped NF4 GEMM, stack dequantization, the SwiGLU and combine steps -- replaced by CPU
+stand-ins built on the oracle, the host codec and the same formulas in torch. Forward and every gradient of the fused autograd function
 must match autograd through the ``ExpertsLoRA`` loop on the same NF4 bytes (the GPU test,
 test_gpu_train.py, checks the real kernels under the same contract)."""
 import importlib
@@ -35,8 +35,35 @@ def _cpu_ops(e4b):
             out[lo:hi] = (x[lo:hi].float() @ W[e].float().t()).to(a.dtype)
         return out
 
+    def swiglu_forward(proj, has_gate=True):
+        if has_gate:
+            g, u = proj.chunk(2, dim=-1)
+            return torch.nn.functional.silu(g) * u
+        return torch.nn.functional.silu(proj)
+
+    def swiglu_backward(proj, dh, has_gate=True):
+        pf = proj.float()
+        if has_gate:
+            g, u = pf.chunk(2, dim=-1)
+            s = torch.sigmoid(g)
+            return torch.cat([dh * u * (s * (1 + g * (1 - s))), dh * (g * s)], dim=-1).to(proj.dtype)
+        s = torch.sigmoid(pf)
+        return (dh * (s * (1 + pf * (1 - s)))).to(proj.dtype)
+
+    def combine(rows, inv, w, T, k, out_dtype=torch.bfloat16):
+        r = rows.float()[inv.long()].view(T, k, -1)
+        if w is not None:
+            r = r * w.float().view(T, k, 1)
+        return r.sum(1).to(out_dtype)
+
+    def combine_row_grads(grad, token_rows, w_rows, down):
+        g = grad.float()[token_rows.long()]
+        return (g * w_rows.float().view(-1, 1)).to(down.dtype), (g * down.float()).sum(-1)
+
     return types.SimpleNamespace(permute=permute, grouped_nf4_gemm=grouped_nf4_gemm,
-                                 nf4_dequantize=real.nf4_dequantize)
+                                 nf4_dequantize=real.nf4_dequantize, swiglu_forward=swiglu_forward,
+                                 swiglu_backward=swiglu_backward, combine=combine,
+                                 combine_row_grads=combine_row_grads, dgrad_eligible=lambda n, k: False)
 
 
 @pytest.mark.parametrize("has_gate", [True, False])
