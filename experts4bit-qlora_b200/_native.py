@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "e4b_grouped_nf4_dgrad_workspace_bytes", "e4b_grouped_nf4_dgrad",
     "e4b_combine",
     "e4b_swiglu_forward", "e4b_swiglu_backward", "e4b_combine_row_grads",
+    "e4b_lora_rank_down", "e4b_lora_rank_up", "e4b_lora_outer",
     "e4b_moe_workspace_bytes", "e4b_moe_forward",
     "e4b_moe_decode_step_workspace_bytes", "e4b_moe_decode_step",
     "e4b_moe_path", "e4b_set_decode_kernel",
@@ -113,6 +114,12 @@ def _declare(lib):
         "e4b_swiglu_forward": (I, [P, I, ctypes.c_int64, I, I, P, P]),
         "e4b_swiglu_backward": (I, [P, I, P, ctypes.c_int64, I, I, P, P]),
         "e4b_combine_row_grads": (I, [P, P, P, P, I, ctypes.c_int64, I, P, P, P]),
+        "e4b_lora_rank_down": (I, [P, I, I, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, I, I, P, I,
+                                   ctypes.c_float, P, P]),
+        "e4b_lora_rank_up": (I, [P, I, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, I, P, I, ctypes.c_float, I,
+                                 P, I, I, P]),
+        "e4b_lora_outer": (I, [P, I, I, I, P, I, P, I, ctypes.c_float, P, ctypes.c_int64, ctypes.c_int64,
+                               ctypes.c_int64, P]),
         "e4b_moe_workspace_bytes": (SZ, [ctypes.POINTER(MoeDesc)]),
         "e4b_moe_forward": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P, SZ, P]),
         "e4b_moe_forward_static": (I, [ctypes.POINTER(MoeDesc), ctypes.POINTER(MoeTensors), P]),

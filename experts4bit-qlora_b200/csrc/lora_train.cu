@@ -1,0 +1,213 @@
+// Rank-r adapter products of the training path (train.py; reference engines/fast.py:453-552 and
+// lora.py:251-256) over expert-sorted rows, in fp32 on the CUDA cores, with no padding of the
+// experts' row segments:
+//   rank-down   Y[row, j]  = scale * sum_k X[row, k] * M_e(j, k)          (x . A^T, dD . B, h . A^T)
+//   rank-up     Z[row, n] (+)= scale * sum_j Y[row, j] * M_e(j, n)       (xa . B^T, t . A)
+//   outer       G_e(a, j)  = scale * sum_{rows of e} P[row, a] * Y[row, j]  (the adapter gradients)
+// M_e(j, k) = M[e * sE + j * sj + k * sk]: the same kernels read A [E, r, K] and B [E, N, r]
+// in either orientation. The row tiles (expert, first row, rows) come from the host, which knows
+// the experts' row counts already (the training forward's one sync). Ranks up to 16. Every sum
+// has a fixed order, so results repeat bit for bit.
+#include "common.cuh"
+
+namespace e4b {
+namespace {
+
+constexpr int kRk = 16;     // rank slots per row (ranks below 16 leave the rest unused)
+constexpr int kTileR = 32;  // rows per tile
+constexpr int kKc = 256;    // K elements per staged chunk of M
+
+template <typename TX>
+__global__ void __launch_bounds__(256) rank_down_kernel(const TX* __restrict__ X, int ldx, const float* __restrict__ M,
+                                                        int64_t sE, int64_t sj, int64_t sk, int rk, int K,
+                                                        const int* __restrict__ tiles, float scale,
+                                                        float* __restrict__ Y) {
+  __shared__ float ms[kRk][kKc];
+  const int e = tiles[blockIdx.x * 3], row0 = tiles[blockIdx.x * 3 + 1], nrows = tiles[blockIdx.x * 3 + 2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc[4][kRk];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int j = 0; j < kRk; ++j) acc[r][j] = 0.f;
+  const float* Me = M + (int64_t)e * sE;
+  for (int kc = 0; kc < K; kc += kKc) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kRk * kKc; i += blockDim.x) {
+      const int j = i / kKc, kk = i - j * kKc;
+      ms[j][kk] = (j < rk && kc + kk < K) ? Me[j * sj + (int64_t)(kc + kk) * sk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int i = 0; i < kKc / 32; ++i) {
+      const int kk = lane + 32 * i;
+      if (kc + kk >= K) break;
+      float xv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int rr = warp * 4 + r;
+        xv[r] = rr < nrows ? to_f32(X[(int64_t)(row0 + rr) * ldx + kc + kk]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kRk; ++j) {
+        const float m = ms[j][kk];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][j] = fmaf(xv[r], m, acc[r][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int rr = warp * 4 + r;
+#pragma unroll
+    for (int j = 0; j < kRk; ++j) {
+      float v = acc[r][j];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == j && j < rk && rr < nrows) Y[(int64_t)(row0 + rr) * rk + j] = v * scale;
+    }
+  }
+}
+
+// mode 0: out = v (fp32); 1: out += v (fp32); 2: out = T(float(out) + float(T(v))) (16-bit out,
+// the adapter delta rounded to the dtype and added as the reference adds it to its projection)
+template <typename TO>
+__global__ void __launch_bounds__(256) rank_up_kernel(const float* __restrict__ Y, int rk, const float* __restrict__ M,
+                                                      int64_t sE, int64_t sj, int64_t sn, int N,
+                                                      const int* __restrict__ tiles, float scale, int mode,
+                                                      TO* __restrict__ out, int ldo) {
+  __shared__ float ys[kTileR][kRk];
+  const int e = tiles[blockIdx.x * 3], row0 = tiles[blockIdx.x * 3 + 1], nrows = tiles[blockIdx.x * 3 + 2];
+  for (int i = threadIdx.x; i < kTileR * kRk; i += blockDim.x) {
+    const int rr = i / kRk, j = i - rr * kRk;
+    ys[rr][j] = (rr < nrows && j < rk) ? Y[(int64_t)(row0 + rr) * rk + j] : 0.f;
+  }
+  __syncthreads();
+  const int n = blockIdx.y * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float m[kRk];
+#pragma unroll
+  for (int j = 0; j < kRk; ++j) m[j] = j < rk ? M[(int64_t)e * sE + j * sj + (int64_t)n * sn] : 0.f;
+  for (int rr = 0; rr < nrows; ++rr) {
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRk; ++j) v = fmaf(ys[rr][j], m[j], v);
+    v *= scale;
+    TO* o = out + (int64_t)(row0 + rr) * ldo + n;
+    if (mode == 0)
+      *o = from_f32<TO>(v);
+    else if (mode == 1)
+      *o = from_f32<TO>(to_f32(*o) + v);
+    else
+      *o = from_f32<TO>(to_f32(*o) + to_f32(from_f32<TO>(v)));
+  }
+}
+
+template <typename TP>
+__global__ void __launch_bounds__(256) outer_kernel(const TP* __restrict__ P, int ldp, int A, const float* __restrict__ Y,
+                                                    int rk, const int* __restrict__ segs, float scale,
+                                                    float* __restrict__ G, int64_t gE, int64_t ga, int64_t gj) {
+  __shared__ float ys[kTileR][kRk];
+  const int e = segs[blockIdx.x * 3], row0 = segs[blockIdx.x * 3 + 1], nrows = segs[blockIdx.x * 3 + 2];
+  const int a = blockIdx.y * blockDim.x + threadIdx.x;
+  float acc[kRk];
+#pragma unroll
+  for (int j = 0; j < kRk; ++j) acc[j] = 0.f;
+  for (int r0 = 0; r0 < nrows; r0 += kTileR) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kTileR * kRk; i += blockDim.x) {
+      const int rr = i / kRk, j = i - rr * kRk;
+      ys[rr][j] = (r0 + rr < nrows && j < rk) ? Y[(int64_t)(row0 + r0 + rr) * rk + j] : 0.f;
+    }
+    __syncthreads();
+    if (a < A) {
+      const int lim = min(kTileR, nrows - r0);
+      for (int rr = 0; rr < lim; ++rr) {
+        const float p = to_f32(P[(int64_t)(row0 + r0 + rr) * ldp + a]);
+#pragma unroll
+        for (int j = 0; j < kRk; ++j) acc[j] = fmaf(p, ys[rr][j], acc[j]);
+      }
+    }
+  }
+  if (a < A)
+#pragma unroll
+    for (int j = 0; j < kRk; ++j)
+      if (j < rk) G[(int64_t)e * gE + (int64_t)a * ga + (int64_t)j * gj] = acc[j] * scale;
+}
+
+}  // namespace
+}  // namespace e4b
+
+using namespace e4b;
+
+extern "C" e4b_status e4b_lora_rank_down(const void* X, int x_dtype, int ldx, const float* M, int64_t sE, int64_t sj,
+                                         int64_t sk, int rk, int K, const int32_t* tiles, int ntiles, float scale,
+                                         float* Y, void* stream) {
+  if (rk < 1 || rk > kRk || K < 1 || ntiles < 0) return E4B_ERR_INVALID_ARG;
+  if (ntiles == 0) return E4B_OK;
+  if (!X || !M || !tiles || !Y) return E4B_ERR_INVALID_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (x_dtype) {
+    case E4B_BF16:
+      rank_down_kernel<__nv_bfloat16><<<ntiles, 256, 0, s>>>((const __nv_bfloat16*)X, ldx, M, sE, sj, sk, rk, K, tiles,
+                                                             scale, Y);
+      break;
+    case E4B_F16:
+      rank_down_kernel<__half><<<ntiles, 256, 0, s>>>((const __half*)X, ldx, M, sE, sj, sk, rk, K, tiles, scale, Y);
+      break;
+    case E4B_F32:
+      rank_down_kernel<float><<<ntiles, 256, 0, s>>>((const float*)X, ldx, M, sE, sj, sk, rk, K, tiles, scale, Y);
+      break;
+    default: return E4B_ERR_UNSUPPORTED;
+  }
+  return launch_status();
+}
+
+extern "C" e4b_status e4b_lora_rank_up(const float* Y, int rk, const float* M, int64_t sE, int64_t sj, int64_t sn, int N,
+                                       const int32_t* tiles, int ntiles, float scale, int mode, void* out,
+                                       int out_dtype, int ldo, void* stream) {
+  if (rk < 1 || rk > kRk || N < 1 || ntiles < 0 || mode < 0 || mode > 2) return E4B_ERR_INVALID_ARG;
+  if (ntiles == 0) return E4B_OK;
+  if (!Y || !M || !tiles || !out) return E4B_ERR_INVALID_ARG;
+  if ((mode == 2) != (out_dtype != E4B_F32)) return E4B_ERR_UNSUPPORTED;
+  cudaStream_t s = (cudaStream_t)stream;
+  const dim3 grid(ntiles, (N + 255) / 256);
+  switch (out_dtype) {
+    case E4B_F32:
+      rank_up_kernel<float><<<grid, 256, 0, s>>>(Y, rk, M, sE, sj, sn, N, tiles, scale, mode, (float*)out, ldo);
+      break;
+    case E4B_BF16:
+      rank_up_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(Y, rk, M, sE, sj, sn, N, tiles, scale, mode,
+                                                         (__nv_bfloat16*)out, ldo);
+      break;
+    case E4B_F16:
+      rank_up_kernel<__half><<<grid, 256, 0, s>>>(Y, rk, M, sE, sj, sn, N, tiles, scale, mode, (__half*)out, ldo);
+      break;
+    default: return E4B_ERR_UNSUPPORTED;
+  }
+  return launch_status();
+}
+
+extern "C" e4b_status e4b_lora_outer(const void* P, int p_dtype, int ldp, int A, const float* Y, int rk,
+                                     const int32_t* segs, int nsegs, float scale, float* G, int64_t gE, int64_t ga,
+                                     int64_t gj, void* stream) {
+  if (rk < 1 || rk > kRk || A < 1 || nsegs < 0) return E4B_ERR_INVALID_ARG;
+  if (nsegs == 0) return E4B_OK;
+  if (!P || !Y || !segs || !G) return E4B_ERR_INVALID_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  const dim3 grid(nsegs, (A + 255) / 256);
+  switch (p_dtype) {
+    case E4B_BF16:
+      outer_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)P, ldp, A, Y, rk, segs, scale, G, gE, ga,
+                                                       gj);
+      break;
+    case E4B_F16:
+      outer_kernel<__half><<<grid, 256, 0, s>>>((const __half*)P, ldp, A, Y, rk, segs, scale, G, gE, ga, gj);
+      break;
+    case E4B_F32:
+      outer_kernel<float><<<grid, 256, 0, s>>>((const float*)P, ldp, A, Y, rk, segs, scale, G, gE, ga, gj);
+      break;
+    default: return E4B_ERR_UNSUPPORTED;
+  }
+  return launch_status();
+}

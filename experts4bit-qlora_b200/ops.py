@@ -184,6 +184,70 @@ def combine(rows: torch.Tensor, inv: torch.Tensor, w: torch.Tensor | None, token
     return out
 
 
+class RowTiles:
+    """Expert-sorted rows as device tables for the adapter kernels: ``tiles`` [(expert, first row,
+    rows <= 32)] and ``segs`` [(expert, first row, rows)] of the experts with rows, built from the
+    host copy of the offsets [E+1]."""
+
+    def __init__(self, offsets_host, device):
+        import numpy as np
+        off = np.asarray(offsets_host, dtype=np.int64)
+        cnt = off[1:] - off[:-1]
+        act = np.nonzero(cnt > 0)[0]
+        ntile = (cnt[act] + 31) // 32
+        e_t = np.repeat(act, ntile)
+        first = np.repeat(np.cumsum(ntile) - ntile, ntile)
+        j = np.arange(int(ntile.sum())) - first
+        row0 = off[e_t] + 32 * j
+        rows = np.minimum(32, off[e_t + 1] - row0)
+        self.ntiles, self.nsegs = int(len(e_t)), int(len(act))
+        tiles = np.stack([e_t, row0, rows], 1).astype(np.int32).reshape(-1)
+        segs = np.stack([act, off[act], cnt[act]], 1).astype(np.int32).reshape(-1)
+        both = torch.from_numpy(np.concatenate([tiles, segs])).pin_memory()
+        dev = both.to(device, non_blocking=True)
+        self.tiles, self.segs = dev[:tiles.size], dev[tiles.size:]
+        self._host = both  # kept until the copy has run
+
+
+def lora_rank_down(X: torch.Tensor, M: torch.Tensor, strides, rk: int, tiles: RowTiles,
+                   scale: float = 1.0) -> torch.Tensor:
+    """``Y [R, rk] = scale * X[row] . M_e(j, :)`` over expert-sorted rows (fp32, ranks <= 16);
+    ``strides = (sE, sj, sk)`` address ``M_e(j, k)`` in the fp32 tensor ``M``."""
+    X = X.contiguous()
+    M = M.float().contiguous()
+    R, K = X.shape
+    Y = torch.empty(R, rk, dtype=torch.float32, device=X.device)
+    N.check(N.lib().e4b_lora_rank_down(X.data_ptr(), N.dtype_code(X.dtype), K, M.data_ptr(), *strides, rk, K,
+                                       tiles.tiles.data_ptr(), tiles.ntiles, float(scale), Y.data_ptr(),
+                                       N.stream_handle(X.device)), "e4b_lora_rank_down")
+    return Y
+
+
+def lora_rank_up(Y: torch.Tensor, M: torch.Tensor, strides, n: int, tiles: RowTiles, out: torch.Tensor,
+                 scale: float = 1.0) -> torch.Tensor:
+    """``out[row, :n] += scale * Y[row] . M_e(:, n)`` in place: fp32 ``out`` accumulates; a 16-bit
+    ``out`` gets the delta rounded to its dtype first (as a 16-bit projection plus its delta)."""
+    M = M.float().contiguous()
+    rk = Y.shape[1]
+    mode = 1 if out.dtype == torch.float32 else 2
+    N.check(N.lib().e4b_lora_rank_up(Y.data_ptr(), rk, M.data_ptr(), *strides, n, tiles.tiles.data_ptr(),
+                                     tiles.ntiles, float(scale), mode, out.data_ptr(), N.dtype_code(out.dtype),
+                                     out.shape[1], N.stream_handle(Y.device)), "e4b_lora_rank_up")
+    return out
+
+
+def lora_outer(P: torch.Tensor, Y: torch.Tensor, tiles: RowTiles, G: torch.Tensor, strides,
+               scale: float = 1.0) -> torch.Tensor:
+    """``G_e(a, j) = scale * sum over the rows of e of P[row, a] * Y[row, j]`` into the fp32 tensor
+    ``G`` (``strides = (gE, ga, gj)``); experts without rows are left as they are."""
+    P = P.contiguous()
+    A = P.shape[1]
+    N.check(N.lib().e4b_lora_outer(P.data_ptr(), N.dtype_code(P.dtype), A, A, Y.data_ptr(), Y.shape[1],
+                                   tiles.segs.data_ptr(), tiles.nsegs, float(scale), G.data_ptr(), *strides,
+                                   N.stream_handle(P.device)), "e4b_lora_outer")
+    return G
+
+
 def swiglu_forward(proj: torch.Tensor, has_gate: bool = True) -> torch.Tensor:
     """``act(gate) * up`` of expert-sorted projection rows ``[R, 2I]`` (or ``act(proj)``)."""
     _cuda(proj, "proj")

@@ -70,6 +70,78 @@ class _Segments:
         return xp.reshape(self.Ea * self.L, -1).index_select(0, self.pos)
 
 
+class _Adapters:
+    """The rank-r adapter products over expert-sorted rows. Ranks up to 16 run on the library's
+    segment kernels (fp32, no padding: ``e4b_lora_rank_down`` / ``_rank_up`` / ``_outer``); larger
+    ranks as batched GEMMs over the segments padded to the longest."""
+
+    def __init__(self, offs_host, R, dev, rank):
+        self.kernels = rank <= 16
+        self.rank = rank
+        if self.kernels:
+            self.tiles = ops.RowTiles(offs_host, dev)
+        else:
+            self.seg = _Segments(offs_host, R, dev)
+
+    def down_A(self, X, A):
+        """``X[row] . A_e^T`` -> [R, r] (A [E, r, K])."""
+        E, r, K = A.shape
+        if self.kernels:
+            return ops.lora_rank_down(X, A, (r * K, K, 1), r, self.tiles)
+        s = self.seg
+        return s.unpad(torch.bmm(s.pad(X).to(A.dtype), A[s.eid].transpose(1, 2))).float()
+
+    def down_B(self, X, B):
+        """``X[row] . B_e`` -> [R, r] (B [E, N, r])."""
+        E, Nn, r = B.shape
+        if self.kernels:
+            return ops.lora_rank_down(X, B, (Nn * r, 1, r), r, self.tiles)
+        s = self.seg
+        return s.unpad(torch.bmm(s.pad(X).to(B.dtype), B[s.eid])).float()
+
+    def add_up_B(self, Y, B, out, scale):
+        """``out[row] += scale * Y[row] . B_e^T`` (B [E, N, r]); 16-bit ``out`` takes the delta
+        rounded to its dtype."""
+        E, Nn, r = B.shape
+        if self.kernels:
+            return ops.lora_rank_up(Y, B, (Nn * r, 1, r), Nn, self.tiles, out, scale)
+        s = self.seg
+        d = s.unpad(scale * torch.bmm(s.pad(Y).to(B.dtype), B[s.eid].transpose(1, 2)))
+        return out + (d.to(out.dtype) if out.dtype != torch.float32 else d.float())
+
+    def add_up_A(self, Y, A, out, scale):
+        """``out[row] += scale * Y[row] . A_e`` (A [E, r, K], fp32 ``out``)."""
+        E, r, K = A.shape
+        if self.kernels:
+            return ops.lora_rank_up(Y, A, (r * K, K, 1), K, self.tiles, out, scale)
+        s = self.seg
+        return out + s.unpad(scale * torch.bmm(s.pad(Y).to(A.dtype), A[s.eid])).float()
+
+    def grad_B(self, P, Y, like, scale):
+        """dL/dB: ``G_e[n, j] = scale * sum over e's rows of P[row, n] * Y[row, j]`` (like B [E, N, r])."""
+        E, Nn, r = like.shape
+        if self.kernels:
+            G = torch.zeros(E, Nn, r, dtype=torch.float32, device=P.device)
+            return ops.lora_outer(P, Y, self.tiles, G, (Nn * r, r, 1), scale).to(like.dtype)
+        s = self.seg
+        g = scale * torch.bmm(s.pad(P).to(like.dtype).transpose(1, 2), s.pad(Y).to(like.dtype))
+        full = torch.zeros_like(like)
+        full[s.eid] = g.to(like.dtype)
+        return full
+
+    def grad_A(self, Y, P, like, scale):
+        """dL/dA: ``G_e[j, k] = scale * sum over e's rows of Y[row, j] * P[row, k]`` (like A [E, r, K])."""
+        E, r, K = like.shape
+        if self.kernels:
+            G = torch.zeros(E, r, K, dtype=torch.float32, device=P.device)
+            return ops.lora_outer(P, Y, self.tiles, G, (r * K, 1, K), scale).to(like.dtype)
+        s = self.seg
+        g = scale * torch.bmm(s.pad(Y).to(like.dtype).transpose(1, 2), s.pad(P).to(like.dtype))
+        full = torch.zeros_like(like)
+        full[s.eid] = g.to(like.dtype)
+        return full
+
+
 class _FusedExpertsLoRATrain(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden, top_k_weights, A_gu, B_gu, A_dn, B_dn, lora_mod, top_k_index):
@@ -84,30 +156,26 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
         token_rows = order // k
         offs_host = offsets.tolist()  # one host sync, as the reference's sizes .tolist()
         R = T * k
-        seg = _Segments(offs_host, R, dev)
+        ad = _Adapters(offs_host, R, dev, A_gu.shape[1])
         gu_p = base.gate_up_proj.view(E, n1, H // 2)
         gu_a = base.gate_up_absmax.view(E, n1, H // 64)
         dn_p = base.down_proj.view(E, H, I // 2)
         dn_a = base.down_absmax.view(E, H, I // 64)
         x = hidden.index_select(0, token_rows)                       # [R, H] compute dtype
         proj = ops.grouped_nf4_gemm(hidden, gu_p, gu_a, offsets, a_rows=token_rows.to(torch.int32))
-        eid = seg.eid
-        # adapter delta of gate_up, in the adapter dtype, added to the bf16 base projection
-        xp = seg.pad(x).to(A_gu.dtype)                                # [Ea, L, H]
-        xa_gu = torch.bmm(xp, A_gu[eid].transpose(1, 2))              # [Ea, L, r]
-        d_gu = s * torch.bmm(xa_gu, B_gu[eid].transpose(1, 2))        # [Ea, L, n1]
-        proj = proj + seg.unpad(d_gu).to(proj.dtype)
+        # adapter delta of gate_up in fp32, rounded to the compute dtype and added to the projection
+        xa_gu = ad.down_A(x, A_gu)                                    # [R, r] fp32
+        proj = ad.add_up_B(xa_gu, B_gu, proj, s)
         h = ops.swiglu_forward(proj, base.has_gate)                   # [R, I], act rounded as lora._epilogue
         down = ops.grouped_nf4_gemm(h.contiguous(), dn_p, dn_a, offsets)
-        hp = seg.pad(h).to(A_dn.dtype)
-        xa_dn = torch.bmm(hp, A_dn[eid].transpose(1, 2))              # [Ea, L, r]
-        d_dn = s * torch.bmm(xa_dn, B_dn[eid].transpose(1, 2))        # [Ea, L, H]
-        down = down + seg.unpad(d_dn).to(down.dtype)                  # [R, H] compute dtype
+        xa_dn = ad.down_A(h, A_dn)                                    # [R, r] fp32
+        down = ad.add_up_B(xa_dn, B_dn, down, s)                      # [R, H] compute dtype
         w_rows = top_k_weights.reshape(-1)[order].float()
         # weighted rows summed per token over its k slots in slot order, fp32 (no atomics)
         out = ops.combine(down, inv, top_k_weights.float(), T, k, torch.float32)
         ctx.lora_mod = lora_mod
-        ctx.seg = seg
+        ctx.ad = ad
+        ctx.offs_host = offs_host
         ctx.meta = (T, k, E, H, I, n1, s)
         ctx.save_for_backward(token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn,
                               offsets)
@@ -117,57 +185,46 @@ class _FusedExpertsLoRATrain(torch.autograd.Function):
     def backward(ctx, grad_out):
         (token_rows, order, inv, proj, h, down, xa_gu, xa_dn, w_rows, x, A_gu, B_gu, A_dn, B_dn,
          offsets) = ctx.saved_tensors
-        lora_mod, seg = ctx.lora_mod, ctx.seg
+        lora_mod, ad = ctx.lora_mod, ctx.ad
         base = lora_mod.base
         T, k, E, H, I, n1, s = ctx.meta
         cdt = proj.dtype
-        eid = seg.eid
+        R = T * k
         # dL/d down rows (grad_out[token] * w) and dL/d w_rows (grad_out[token] . down), one pass
         dd, d_w = ops.combine_row_grads(grad_out, token_rows, w_rows, down)
         grad_w = torch.zeros(T * k, dtype=torch.float32, device=grad_out.device)
         grad_w[order] = d_w
         dgrad = getattr(lora_mod, "_e4b_dgrad", False)
-        ddp = seg.pad(dd)                                               # [Ea, L, H]
+        seg = None
         if dgrad and ops.dgrad_eligible(H, I):
             # dL/dh of the frozen down projection on the tensor cores, nothing decoded to memory
-            dh_w = ops.grouped_nf4_dgrad(dd, base.down_proj.view(E, H, I // 2), base.down_absmax.view(E, H, I // 64),
-                                         offsets)                       # [R, I] fp32
+            dh = ops.grouped_nf4_dgrad(dd, base.down_proj.view(E, H, I // 2), base.down_absmax.view(E, H, I // 64),
+                                       offsets)                         # [R, I] fp32
         else:
             # the frozen stack decoded once for this backward (compute dtype, freed on return)
+            seg = _Segments(ctx.offs_host, R, dd.device)
             W_dn = ops.nf4_dequantize(base.down_proj, base.down_absmax, (E, H, I), cdt)
-            dh_w = seg.unpad(torch.bmm(ddp, W_dn if seg.Ea == E else W_dn[eid]).float())
+            dh = seg.unpad(torch.bmm(seg.pad(dd), W_dn if seg.Ea == E else W_dn[seg.eid]).float())
             del W_dn
-        ddp32 = ddp.to(B_dn.dtype)
-        t_dn = torch.bmm(ddp32, B_dn[eid])                              # [Ea, L, r]
-        gB_dn = s * torch.bmm(ddp32.transpose(1, 2), xa_dn)             # [Ea, H, r]
-        hp = seg.pad(h).to(A_dn.dtype)
-        gA_dn = s * torch.bmm(t_dn.transpose(1, 2), hp)                 # [Ea, r, I]
-        dh = dh_w + seg.unpad(s * torch.bmm(t_dn, A_dn[eid])).float()  # [R, I] fp32
-        dproj = ops.swiglu_backward(proj, dh, base.has_gate)          # SiLU(gate) * up, in the compute dtype
-        dpp = seg.pad(dproj)                                            # [Ea, L, n1]
+        t_dn = ad.down_B(dd, B_dn)                                      # [R, r] fp32
+        gB_dn = ad.grad_B(dd, xa_dn, B_dn, s)                           # [E, H, r]
+        gA_dn = ad.grad_A(t_dn, h, A_dn, s)                             # [E, r, I]
+        dh = ad.add_up_A(t_dn, A_dn, dh, s)                             # [R, I] fp32
+        dproj = ops.swiglu_backward(proj, dh, base.has_gate)            # SiLU(gate) * up, in the compute dtype
         if dgrad and ops.dgrad_eligible(n1, H):
-            dx_w = ops.grouped_nf4_dgrad(dproj, base.gate_up_proj.view(E, n1, H // 2),
-                                         base.gate_up_absmax.view(E, n1, H // 64), offsets)  # [R, H] fp32
+            dx = ops.grouped_nf4_dgrad(dproj, base.gate_up_proj.view(E, n1, H // 2),
+                                       base.gate_up_absmax.view(E, n1, H // 64), offsets)  # [R, H] fp32
         else:
+            seg = seg or _Segments(ctx.offs_host, R, dd.device)
             W_gu = ops.nf4_dequantize(base.gate_up_proj, base.gate_up_absmax, (E, n1, H), cdt)
-            dx_w = seg.unpad(torch.bmm(dpp, W_gu if seg.Ea == E else W_gu[eid]).float())
+            dx = seg.unpad(torch.bmm(seg.pad(dproj), W_gu if seg.Ea == E else W_gu[seg.eid]).float())
             del W_gu
-        dpp32 = dpp.to(B_gu.dtype)
-        t_gu = torch.bmm(dpp32, B_gu[eid])                              # [Ea, L, r]
-        gB_gu = s * torch.bmm(dpp32.transpose(1, 2), xa_gu)             # [Ea, n1, r]
-        xp = seg.pad(x).to(A_gu.dtype)
-        gA_gu = s * torch.bmm(t_gu.transpose(1, 2), xp)                 # [Ea, r, H]
-        dx = dx_w + seg.unpad(s * torch.bmm(t_gu, A_gu[eid])).float()  # [R, H] fp32
+        t_gu = ad.down_B(dproj, B_gu)                                   # [R, r] fp32
+        gB_gu = ad.grad_B(dproj, xa_gu, B_gu, s)                        # [E, n1, r]
+        gA_gu = ad.grad_A(t_gu, x, A_gu, s)                             # [E, r, H]
+        dx = ad.add_up_A(t_gu, A_gu, dx, s)                             # [R, H] fp32
         grad_hidden = ops.combine(dx, inv, None, T, k, torch.float32)  # slot order, no atomics
-
-        def scatter(g_act, like):
-            full = torch.zeros_like(like)
-            full[eid] = g_act.to(like.dtype)
-            return full
-
-        return (grad_hidden.to(cdt), grad_w.view(T, k),
-                scatter(gA_gu, A_gu), scatter(gB_gu, B_gu), scatter(gA_dn, A_dn), scatter(gB_dn, B_dn),
-                None, None)
+        return grad_hidden.to(cdt), grad_w.view(T, k), gA_gu, gB_gu, gA_dn, gB_dn, None, None
 
 
 def fused_experts_train_forward(lora_mod, hidden_states, top_k_index, top_k_weights):

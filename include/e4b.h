@@ -206,6 +206,26 @@ E4B_API e4b_status e4b_combine_row_grads(const float* grad, const int64_t* token
                                  const void* down, int dtype, int64_t R, int H, void* dd, float* dw,
                                  void* stream);
 
+/* The rank-r adapter products of the same training path (lora.py:251-256 inside
+ * fast.py:453-552), fp32 on expert-sorted rows with no padding of the experts'
+ * segments (ranks 1..16). M_e(j, k) = M[e*sE + j*sj + k*sk] (fp32), so A [E, r, K]
+ * and B [E, N, r] are read in either orientation. `tiles` [ntiles][3] int32 =
+ * (expert, first row, rows <= 32); `segs` [nsegs][3] = (expert, first row, rows),
+ * one per expert with rows.
+ * e4b_lora_rank_down: Y [R, rk] = scale * X[row, :K] . M_e(j, :).
+ * e4b_lora_rank_up: out[row, n] = scale * Y[row] . M_e(:, n) for n < N (mode 0, fp32
+ *   out), += (mode 1, fp32), or out = dtype(out + dtype(delta)) (mode 2, bf16/f16).
+ * e4b_lora_outer: G[e*gE + a*ga + j*gj] = scale * sum over e's rows of P[row, a] * Y[row, j]. */
+E4B_API e4b_status e4b_lora_rank_down(const void* X, int x_dtype, int ldx, const float* M, int64_t sE, int64_t sj,
+                              int64_t sk, int rk, int K, const int32_t* tiles, int ntiles, float scale, float* Y,
+                              void* stream);
+E4B_API e4b_status e4b_lora_rank_up(const float* Y, int rk, const float* M, int64_t sE, int64_t sj, int64_t sn, int N,
+                            const int32_t* tiles, int ntiles, float scale, int mode, void* out, int out_dtype,
+                            int ldo, void* stream);
+E4B_API e4b_status e4b_lora_outer(const void* P, int p_dtype, int ldp, int A, const float* Y, int rk,
+                          const int32_t* segs, int nsegs, float scale, float* G, int64_t gE, int64_t ga, int64_t gj,
+                          void* stream);
+
 /* ---- Whole expert layer (R2-R7 + LoRA R5) -------------------------------- */
 
 typedef struct {

@@ -153,3 +153,41 @@ def test_combine_row_grads_and_unit_weight_combine(e4b):
     x = torch.randn(R, H, generator=g, device=DEV)
     s = e4b.ops.combine(x, inv, None, T, k, torch.float32)
     assert torch.allclose(s, x[inv.long()].view(T, k, H).sum(1), rtol=1e-6, atol=1e-5)
+
+
+def test_adapter_segment_kernels_match_per_expert_fp32(e4b):
+    """e4b_lora_rank_down / _rank_up / _outer against per-expert fp32 matmuls over ragged segments
+    (an empty expert, a one-row expert, segments across several 32-row tiles)."""
+    E, r, H, Nn = 5, 16, 512, 384
+    counts = [70, 0, 1, 33, 96]
+    g = torch.Generator(device=DEV).manual_seed(9)
+    offs = [0]
+    for c in counts:
+        offs.append(offs[-1] + c)
+    R = offs[-1]
+    tiles = e4b.ops.RowTiles(offs, torch.device(DEV))
+    X = torch.randn(R, H, generator=g, device=DEV).to(torch.bfloat16)
+    A = torch.randn(E, r, H, generator=g, device=DEV) * 0.05
+    B = torch.randn(E, Nn, r, generator=g, device=DEV) * 0.05
+    Y = e4b.ops.lora_rank_down(X, A, (r * H, H, 1), r, tiles)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        want = torch.zeros(R, r, device=DEV)
+        for e in range(E):
+            want[offs[e]:offs[e + 1]] = X[offs[e]:offs[e + 1]].float() @ A[e].t()
+        assert torch.allclose(Y, want, rtol=1e-4, atol=1e-4)
+        out = torch.zeros(R, Nn, device=DEV)
+        e4b.ops.lora_rank_up(Y, B, (Nn * r, 1, r), Nn, tiles, out, 0.5)
+        want_up = torch.zeros(R, Nn, device=DEV)
+        for e in range(E):
+            want_up[offs[e]:offs[e + 1]] = 0.5 * (Y[offs[e]:offs[e + 1]] @ B[e].t())
+        assert torch.allclose(out, want_up, rtol=1e-4, atol=1e-5)
+        P = torch.randn(R, Nn, generator=g, device=DEV).to(torch.bfloat16)
+        G = torch.zeros(E, Nn, r, device=DEV)
+        e4b.ops.lora_outer(P, Y, tiles, G, (Nn * r, r, 1), 2.0)
+        for e in range(E):
+            we = 2.0 * (P[offs[e]:offs[e + 1]].float().t() @ Y[offs[e]:offs[e + 1]])
+            assert torch.allclose(G[e], we, rtol=1e-4, atol=1e-4), e
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev

@@ -60,7 +60,50 @@ def _cpu_ops(e4b):
         g = grad.float()[token_rows.long()]
         return (g * w_rows.float().view(-1, 1)).to(down.dtype), (g * down.float()).sum(-1)
 
-    return types.SimpleNamespace(permute=permute, grouped_nf4_gemm=grouped_nf4_gemm,
+    class RowTiles:
+        def __init__(self, offs, device):
+            self.offs = list(offs)
+
+        def rows(self):
+            for e in range(len(self.offs) - 1):
+                if self.offs[e + 1] > self.offs[e]:
+                    yield e, self.offs[e], self.offs[e + 1]
+
+    def _m(M, strides, e, d0, d1):  # M_e(j, k) as a [d0, d1] fp32 matrix
+        sE, sj, sk = strides
+        flat = M.float().reshape(-1)
+        j = torch.arange(d0).view(-1, 1)
+        kk = torch.arange(d1).view(1, -1)
+        return flat[e * sE + j * sj + kk * sk]
+
+    def lora_rank_down(X, M, strides, rk, tiles, scale=1.0):
+        Y = torch.zeros(X.shape[0], rk)
+        for e, a, b in tiles.rows():
+            Y[a:b] = scale * (X[a:b].float() @ _m(M, strides, e, rk, X.shape[1]).t())
+        return Y
+
+    def lora_rank_up(Y, M, strides, n, tiles, out, scale=1.0):
+        out = out.clone()
+        for e, a, b in tiles.rows():
+            d = scale * (Y[a:b] @ _m(M, strides, e, Y.shape[1], n))
+            if out.dtype == torch.float32:
+                out[a:b] += d
+            else:
+                out[a:b] = out[a:b] + d.to(out.dtype)
+        return out
+
+    def lora_outer(P, Y, tiles, G, strides, scale=1.0):
+        gE, ga, gj = strides
+        flat = G.view(-1)
+        A = P.shape[1]
+        for e, a0, b0 in tiles.rows():
+            g = scale * (P[a0:b0].float().t() @ Y[a0:b0])           # [A, rk]
+            idx = e * gE + torch.arange(A).view(-1, 1) * ga + torch.arange(Y.shape[1]).view(1, -1) * gj
+            flat[idx.reshape(-1)] = g.reshape(-1)
+        return G
+
+    return types.SimpleNamespace(RowTiles=RowTiles, lora_rank_down=lora_rank_down, lora_rank_up=lora_rank_up,
+                                 lora_outer=lora_outer, permute=permute, grouped_nf4_gemm=grouped_nf4_gemm,
                                  nf4_dequantize=real.nf4_dequantize, swiglu_forward=swiglu_forward,
                                  swiglu_backward=swiglu_backward, combine=combine,
                                  combine_row_grads=combine_row_grads, dgrad_eligible=lambda n, k: False)
