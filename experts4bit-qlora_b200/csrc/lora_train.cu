@@ -8,6 +8,8 @@
 // in either orientation. The row tiles (expert, first row, rows) come from the host, which knows
 // the experts' row counts already (the training forward's one sync). Ranks up to 16. Every sum
 // has a fixed order, so results repeat bit for bit.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace e4b {
@@ -22,7 +24,7 @@ __global__ void __launch_bounds__(256) rank_down_kernel(const TX* __restrict__ X
                                                         int64_t sE, int64_t sj, int64_t sk, int rk, int K,
                                                         const int* __restrict__ tiles, float scale,
                                                         float* __restrict__ Y) {
-  __shared__ float ms[kRk][kKc];
+  __shared__ __align__(16) float ms[kRk][kKc];
   const int e = tiles[blockIdx.x * 3], row0 = tiles[blockIdx.x * 3 + 1], nrows = tiles[blockIdx.x * 3 + 2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float acc[4][kRk];
@@ -38,21 +40,39 @@ __global__ void __launch_bounds__(256) rank_down_kernel(const TX* __restrict__ X
       ms[j][kk] = (j < rk && kc + kk < K) ? Me[j * sj + (int64_t)(kc + kk) * sk] : 0.f;
     }
     __syncthreads();
-#pragma unroll 2
-    for (int i = 0; i < kKc / 32; ++i) {
-      const int kk = lane + 32 * i;
-      if (kc + kk >= K) break;
-      float xv[4];
+    // lane owns 8 consecutive k of the chunk: one 16-byte (two for fp32) load per row
+    const int kk = lane * 8;
+    if (kc + kk < K) {
+      float xv[4][8];
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int rr = warp * 4 + r;
-        xv[r] = rr < nrows ? to_f32(X[(int64_t)(row0 + rr) * ldx + kc + kk]) : 0.f;
+        if (rr < nrows) {
+          const TX* xp = X + (int64_t)(row0 + rr) * ldx + kc + kk;
+          if (sizeof(TX) == 2) {
+            const uint4 u = *reinterpret_cast<const uint4*>(xp);
+            const TX* e = reinterpret_cast<const TX*>(&u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[r][i] = to_f32(e[i]);
+          } else {
+            const float4 u0 = reinterpret_cast<const float4*>(xp)[0], u1 = reinterpret_cast<const float4*>(xp)[1];
+            xv[r][0] = u0.x; xv[r][1] = u0.y; xv[r][2] = u0.z; xv[r][3] = u0.w;
+            xv[r][4] = u1.x; xv[r][5] = u1.y; xv[r][6] = u1.z; xv[r][7] = u1.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xv[r][i] = 0.f;
+        }
       }
 #pragma unroll
       for (int j = 0; j < kRk; ++j) {
-        const float m = ms[j][kk];
+        const float4 m0 = *reinterpret_cast<const float4*>(&ms[j][kk]);
+        const float4 m1 = *reinterpret_cast<const float4*>(&ms[j][kk + 4]);
+        const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][j] = fmaf(xv[r], m, acc[r][j]);
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[r][j] = fmaf(xv[r][i], m[i], acc[r][j]);
       }
     }
   }
@@ -70,7 +90,26 @@ __global__ void __launch_bounds__(256) rank_down_kernel(const TX* __restrict__ X
 }
 
 // mode 0: out = v (fp32); 1: out += v (fp32); 2: out = T(float(out) + float(T(v))) (16-bit out,
-// the adapter delta rounded to the dtype and added as the reference adds it to its projection)
+// the adapter delta rounded to the dtype and added as the reference adds it to its projection).
+// A thread owns 4 consecutive columns (N % 4 == 0) for the tile's rows: vector loads and stores.
+__device__ __forceinline__ void up_add4_impl(float4& c, const float (&v)[4]) {
+  c.x += v[0];
+  c.y += v[1];
+  c.z += v[2];
+  c.w += v[3];
+}
+template <typename TO>
+__device__ __forceinline__ void up_add4_impl(uint2& c, const float (&v)[4]) {
+  TO* e = reinterpret_cast<TO*>(&c);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) e[i] = from_f32<TO>(to_f32(e[i]) + to_f32(from_f32<TO>(v[i])));
+}
+template <typename TO, typename V>
+__device__ __forceinline__ void up_add4(V& c, const float (&v)[4]) {
+  if constexpr (sizeof(TO) == 4) up_add4_impl(c, v);
+  else up_add4_impl<TO>(c, v);
+}
+
 template <typename TO>
 __global__ void __launch_bounds__(256) rank_up_kernel(const float* __restrict__ Y, int rk, const float* __restrict__ M,
                                                       int64_t sE, int64_t sj, int64_t sn, int N,
@@ -83,23 +122,39 @@ __global__ void __launch_bounds__(256) rank_up_kernel(const float* __restrict__ 
     ys[rr][j] = (rr < nrows && j < rk) ? Y[(int64_t)(row0 + rr) * rk + j] : 0.f;
   }
   __syncthreads();
-  const int n = blockIdx.y * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  float m[kRk];
+  const int n0 = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+  if (n0 >= N) return;
+  float m[4][kRk];
 #pragma unroll
-  for (int j = 0; j < kRk; ++j) m[j] = j < rk ? M[(int64_t)e * sE + j * sj + (int64_t)n * sn] : 0.f;
-  for (int rr = 0; rr < nrows; ++rr) {
-    float v = 0.f;
+  for (int c = 0; c < 4; ++c)
 #pragma unroll
-    for (int j = 0; j < kRk; ++j) v = fmaf(ys[rr][j], m[j], v);
-    v *= scale;
-    TO* o = out + (int64_t)(row0 + rr) * ldo + n;
-    if (mode == 0)
-      *o = from_f32<TO>(v);
-    else if (mode == 1)
-      *o = from_f32<TO>(to_f32(*o) + v);
-    else
-      *o = from_f32<TO>(to_f32(*o) + to_f32(from_f32<TO>(v)));
+    for (int j = 0; j < kRk; ++j) m[c][j] = j < rk ? M[(int64_t)e * sE + j * sj + (int64_t)(n0 + c) * sn] : 0.f;
+  // rows in batches of 8: the batch's read-modify-writes are in flight together
+  using V = typename std::conditional<sizeof(TO) == 4, float4, uint2>::type;
+  for (int r0 = 0; r0 < nrows; r0 += 8) {
+    V cur[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b)
+      if (r0 + b < nrows && mode != 0) cur[b] = *reinterpret_cast<const V*>(out + (int64_t)(row0 + r0 + b) * ldo + n0);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      if (r0 + b >= nrows) break;
+      float v[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < kRk; ++j) a = fmaf(ys[r0 + b][j], m[c][j], a);
+        v[c] = a * scale;
+      }
+      if (mode == 0) {
+        float4 z = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(out + (int64_t)(row0 + r0 + b) * ldo + n0) = z;
+      } else {
+        up_add4<TO, V>(cur[b], v);
+        *reinterpret_cast<V*>(out + (int64_t)(row0 + r0 + b) * ldo + n0) = cur[b];
+      }
+    }
   }
 }
 
@@ -107,7 +162,7 @@ template <typename TP>
 __global__ void __launch_bounds__(256) outer_kernel(const TP* __restrict__ P, int ldp, int A, const float* __restrict__ Y,
                                                     int rk, const int* __restrict__ segs, float scale,
                                                     float* __restrict__ G, int64_t gE, int64_t ga, int64_t gj) {
-  __shared__ float ys[kTileR][kRk];
+  __shared__ __align__(16) float ys[kTileR][kRk];
   const int e = segs[blockIdx.x * 3], row0 = segs[blockIdx.x * 3 + 1], nrows = segs[blockIdx.x * 3 + 2];
   const int a = blockIdx.y * blockDim.x + threadIdx.x;
   float acc[kRk];
@@ -122,10 +177,18 @@ __global__ void __launch_bounds__(256) outer_kernel(const TP* __restrict__ P, in
     __syncthreads();
     if (a < A) {
       const int lim = min(kTileR, nrows - r0);
+#pragma unroll 4
       for (int rr = 0; rr < lim; ++rr) {
         const float p = to_f32(P[(int64_t)(row0 + r0 + rr) * ldp + a]);
+        const float4* y4 = reinterpret_cast<const float4*>(ys[rr]);
 #pragma unroll
-        for (int j = 0; j < kRk; ++j) acc[j] = fmaf(p, ys[rr][j], acc[j]);
+        for (int q = 0; q < kRk / 4; ++q) {
+          const float4 y = y4[q];
+          acc[4 * q] = fmaf(p, y.x, acc[4 * q]);
+          acc[4 * q + 1] = fmaf(p, y.y, acc[4 * q + 1]);
+          acc[4 * q + 2] = fmaf(p, y.z, acc[4 * q + 2]);
+          acc[4 * q + 3] = fmaf(p, y.w, acc[4 * q + 3]);
+        }
       }
     }
   }
@@ -146,6 +209,7 @@ extern "C" e4b_status e4b_lora_rank_down(const void* X, int x_dtype, int ldx, co
   if (rk < 1 || rk > kRk || K < 1 || ntiles < 0) return E4B_ERR_INVALID_ARG;
   if (ntiles == 0) return E4B_OK;
   if (!X || !M || !tiles || !Y) return E4B_ERR_INVALID_ARG;
+  if (K % 8 || ldx % 8 || !aligned16(X)) return E4B_ERR_UNSUPPORTED;  // 8-element row loads
   cudaStream_t s = (cudaStream_t)stream;
   switch (x_dtype) {
     case E4B_BF16:
@@ -169,9 +233,9 @@ extern "C" e4b_status e4b_lora_rank_up(const float* Y, int rk, const float* M, i
   if (rk < 1 || rk > kRk || N < 1 || ntiles < 0 || mode < 0 || mode > 2) return E4B_ERR_INVALID_ARG;
   if (ntiles == 0) return E4B_OK;
   if (!Y || !M || !tiles || !out) return E4B_ERR_INVALID_ARG;
-  if ((mode == 2) != (out_dtype != E4B_F32)) return E4B_ERR_UNSUPPORTED;
+  if ((mode == 2) != (out_dtype != E4B_F32) || N % 4 || ldo % 4) return E4B_ERR_UNSUPPORTED;
   cudaStream_t s = (cudaStream_t)stream;
-  const dim3 grid(ntiles, (N + 255) / 256);
+  const dim3 grid(ntiles, (N / 4 + 255) / 256);
   switch (out_dtype) {
     case E4B_F32:
       rank_up_kernel<float><<<grid, 256, 0, s>>>(Y, rk, M, sE, sj, sn, N, tiles, scale, mode, (float*)out, ldo);

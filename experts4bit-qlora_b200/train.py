@@ -17,10 +17,10 @@ Backward: the input gradients of the frozen projections, ``dL/dh = dD . W_down``
 ``dL/dx = dP . W_gate_up``, run on the library's dgrad kernel with ``dgrad=True``
 (``e4b_grouped_nf4_dgrad``: tcgen05 tiles, each weight tile decoded into shared memory,
 nothing materialised), else on one decode of each stack per backward (``e4b_nf4_dequantize``,
-freed after the step) and batched GEMMs; the adapter products and the four adapter
-gradients run as batched GEMMs over the experts' row segments padded to the longest. ``dL/d top_k_weights`` is the row dot product of
-the incoming gradient with the unweighted down rows. Nothing is saved that depends
-on the frozen weights, so the decoded stacks never live past one backward.
+freed after the step) and batched GEMMs. The SwiGLU forward and backward, the combine and its
+row gradients are single library kernels; the rank-r adapter products and the four adapter
+gradients run on the library's segment kernels over the expert-sorted rows (fp32, no padding;
+ranks up to 16, larger ranks as batched GEMMs over padded segments).
 
 Numerics: bf16 compute with fp32 adapter math, as ``ExpertsLoRA.forward``; the
 frozen projections accumulate in fp32 on fp16 operands (the NF4 value is exact in
