@@ -444,6 +444,17 @@ __device__ __forceinline__ int decode_prologue(const DecodeArgs& a, char* smem, 
   namespace cg = cooperative_groups;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int R = a.T * a.k;
+  // the router rows this warp's logit tasks read, into L2 while the token rows load (grid-wide
+  // split only: there each warp has at most a few tasks)
+  if (a.router_w && a.router_logits && a.cluster <= 1) {
+    const int tasks = a.E * ((a.T + kRouterTT - 1) / kRouterTT);
+    const int esz = a.router_w_dtype == E4B_F32 ? 4 : 2;
+    for (int task = warp * (int)gridDim.x + blockIdx.x; task < tasks; task += kWarps * (int)gridDim.x) {
+      const char* row = static_cast<const char*>(a.router_w) + (int64_t)(task % a.E) * a.H * esz;
+      for (int off = lane * 128; off < a.H * esz; off += 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
+    }
+  }
   // token rows into registers first: their latency overlaps the permutation below
   const int xvec = a.T * (a.H / 8);
   uint4 xr[2];
