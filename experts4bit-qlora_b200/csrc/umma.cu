@@ -14,7 +14,8 @@
 // One persistent CTA per SM, 16 warps with fixed roles, 64-wide K chunks (one
 // quantization block per row per chunk) through three rings of their own depth --
 // packed weights 4 deep, activation tiles 4 deep, decoded weight tiles 2 deep:
-//   warp 0      TMA: packed NF4 bytes of the tile's rows (2-D boxes {32 B, 128 rows});
+//   warp 0      TMA: packed NF4 bytes of the tile's rows (2-D boxes {32 B, 128 rows}, 32-byte
+//               swizzle);
 //   warp 1      TMA of the 128 token rows (fp16, expert-sorted), one box per chunk,
 //               landing in the 128-byte-swizzled K-major operand layout;
 //   warp 3      allocates TMEM, issues tcgen05.mma (one thread), commits;
@@ -438,8 +439,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
           if (h < GROUPS) {
             const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
-            p0 = reinterpret_cast<const uint4*>(wsrc)[0];
-            p1 = reinterpret_cast<const uint4*>(wsrc)[1];
+            const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
+            p0 = reinterpret_cast<const uint4*>(wsrc)[sw];
+            p1 = reinterpret_cast<const uint4*>(wsrc)[sw ^ 1];
           }
           fence_proxy_async();
           mbar_arrive(&w_empty[s]);
@@ -498,8 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
         if (h < GROUPS) {
           const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
-          p0 = reinterpret_cast<const uint4*>(wsrc)[0];
-          p1 = reinterpret_cast<const uint4*>(wsrc)[1];
+          const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
+          p0 = reinterpret_cast<const uint4*>(wsrc)[sw];
+          p1 = reinterpret_cast<const uint4*>(wsrc)[sw ^ 1];
         }
         fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
         mbar_arrive(&w_empty[s]);  // packed bytes are in registers: the slot can be refilled
@@ -662,7 +665,10 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   const cuuint64_t dims[2] = {row_bytes, (cuuint64_t)g.E * g.N};
   const cuuint64_t str[1] = {row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)Smem::wrow, kRows};
-  if (!encode_tiled(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, g.packed, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+  // 32-byte rows (NF4, MXFP4) land with the 32-byte swizzle: a quarter-warp's 16-byte reads of rows
+  // r .. r+7 then hit distinct banks; FP8's 64-byte rows are read in a rotated unit order instead
+  const CUtensorMapSwizzle wsw = Smem::wrow == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (!encode_tiled(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, g.packed, dims, str, box, wsw))
     return E4B_ERR_CUDA;
   if (g.a_rows) return E4B_ERR_UNSUPPORTED;  // activations must be expert-sorted rows
   CUtensorMap bmap;  // fp16 activation rows [x_rows][K], box {64 halves, 128 rows}, 128-byte swizzle
