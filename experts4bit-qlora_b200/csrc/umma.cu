@@ -11,7 +11,7 @@
 // matching up rows form one N = 256 operand, so one MMA per k-step covers both
 // and silu(gate) * up happens in the thread that owns the token.
 //
-// One persistent CTA per SM, 16 warps with fixed roles, 64-wide K chunks (one
+// One persistent CTA per SM, 24 warps with fixed roles, 64-wide K chunks (one
 // quantization block per row per chunk) through three rings of their own depth --
 // packed weights 4 deep, activation tiles 4 deep, decoded weight tiles 2 deep:
 //   warp 0      TMA: packed NF4 bytes of the tile's rows (2-D boxes {32 B, 128 rows}, 32-byte
@@ -19,10 +19,10 @@
 //   warp 1      TMA of the 128 token rows (fp16, expert-sorted), one box per chunk,
 //               landing in the 128-byte-swizzled K-major operand layout;
 //   warp 3      allocates TMEM, issues tcgen05.mma (one thread), commits;
-//   warps 4-11  NF4 -> fp16 decode: one thread per weight row, 32 pair-table
-//               lookups per chunk, scaled by the block's absmax, stored into the
-//               swizzled, K-major weight operand;
-//   warps 12-15 epilogue: tcgen05.ld of the finished accumulators (double
+//   warps 4-19  NF4 -> fp16 decode: two threads per weight row, each 16 pair-table
+//               lookups per chunk (its half of the row's 64 elements), scaled by the
+//               block's absmax, stored into the swizzled, K-major weight operand;
+//   warps 20-23 epilogue: tcgen05.ld of the finished accumulators (double
 //               buffered, so it overlaps the next tile's MMAs), one token row per
 //               thread: activation scale, activation, 16-byte stores.
 // With an adapter, each tile takes one more chunk: the activation warp loads the
@@ -68,7 +68,9 @@ constexpr int kSA = 2;  // decoded-A ring depth (produced on chip)
 constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA M)
 constexpr int kRows = 128;          // weight rows per group (UMMA M)
 constexpr int kKc = 64;             // K per chunk
-constexpr int kThreads = 512;
+constexpr int kThreads = 512;     // dgrad kernel: 4 control warps, 8 decode warps, 4 epilogue warps
+constexpr int kDec = 512;         // forward kernel: decode threads (two per weight row)
+constexpr int kFwdThreads = 128 + kDec + 128;  // forward kernel: control, decode, epilogue warps
 constexpr int kABytes = kRows * kKc * 2;        // 16 KB fp16 per group
 constexpr int kBBytes = kTok * kKc * 2;         // 16 KB fp16
 constexpr int kLut = 256 * 128;
@@ -200,7 +202,7 @@ __device__ __forceinline__ void tile_info(const int32_t* ts, const int32_t* offs
 }  // namespace
 
 template <typename OutT, int GROUPS, int FMT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     nf4_umma_kernel(UmmaArgs u, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ CUtensorMap lmap) {
   using Smem = SmemT<FMT>;
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Smem::tmem_slot);
   int32_t* s_ts = reinterpret_cast<int32_t*>(smem + Smem::tables);
   int32_t* s_offs = s_ts + 1025;
-  for (int i = tid; i <= u.g.E; i += kThreads) {
+  for (int i = tid; i <= u.g.E; i += kFwdThreads) {
     s_ts[i] = u.tile_start[i];
     s_offs[i] = u.g.offsets[i];
   }
@@ -237,14 +239,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kSW; ++s) {
       mbar_init(&full_w[s], 1);
-      mbar_init(&w_empty[s], 256);
+      mbar_init(&w_empty[s], kDec);
     }
     for (int s = 0; s < kSB; ++s) {
       mbar_init(&full_b[s], 1);
       mbar_init(&b_empty[s], 1);
     }
     for (int s = 0; s < kSA; ++s) {
-      mbar_init(&a_ready[s], 256);
+      mbar_init(&a_ready[s], kDec);
       mbar_init(&a_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -259,13 +261,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (FMT == E4B_FMT_NF4) {  // pair table: entry e of lane l at (e << 7) | (l << 2)
     const float code = c_nf4[lane & 15];
-    for (int e = warp; e < 256; e += kThreads / 32) {
+    for (int e = warp; e < 256; e += kFwdThreads / 32) {
       const float lo = __shfl_sync(0xffffffffu, code, e >> 4), hi = __shfl_sync(0xffffffffu, code, e & 15);
       reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__half>(lo, hi);
     }
   } else if (FMT == E4B_FMT_MXFP4) {  // bf16 pair table, LOW nibble first (formats/mxfp4.py:87-88)
     const float code = c_e2m1_umma[lane & 15];
-    for (int e = warp; e < 256; e += kThreads / 32) {
+    for (int e = warp; e < 256; e += kFwdThreads / 32) {
       const float first = __shfl_sync(0xffffffffu, code, e & 15), second = __shfl_sync(0xffffffffu, code, e >> 4);
       reinterpret_cast<uint32_t*>(lut)[e * 32 + lane] = pack2<__nv_bfloat16>(first, second);
     }
@@ -343,10 +345,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&acc_full[buf]);
       }
     }
-  } else if (warp < 12) {
-    // ---------------- NF4 decode: one weight row per thread ---------------------------------
-    const int d = tid - 128;          // 0..255
-    const int h = d >> 7, r = d & 127;  // group, row within the tile
+  } else if (warp < 4 + kDec / 32) {
+    // ---------------- decode: two threads per weight row, each half of the row's chunk -------
+    const int d = tid - 128;            // 0..kDec-1
+    const int part = d >> 8;            // 0: elements 0..31 of the chunk, 1: elements 32..63
+    const int h = (d >> 7) & 1, r = d & 127;  // group, row within the tile
     const uint32_t lane4 = (uint32_t)lane << 2;
     int nw = 0, na = 0;  // packed-weight ring items, decoded-weight ring items (the LoRA chunk has no packed weights)
     // LoRA chunk of a tile: this row's LoRA-B values (rank <= 16, fp16) as K elements 0..15 of the
@@ -354,18 +357,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto lora_chunk = [&](const TileInfo& ti, int row) -> bool {
       const int sa = na % kSA;
       if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) return false;
-      if (h < GROUPS) {
-        float v[16];
+      if (h < GROUPS) {  // part p writes unit p: the row's LoRA-B values 8p .. 8p+7
+        float v[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          v[j] = j < g.rank ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + row) * g.rank + j) : 0.f;
+        for (int j = 0; j < 8; ++j)
+          v[j] = 8 * part + j < g.rank
+                     ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + row) * g.rank + 8 * part + j)
+                     : 0.f;
         char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
         const int swz = (smem_u32(adst) >> 7) & 7;
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-          *reinterpret_cast<uint4*>(adst + ((u ^ swz) << 4)) =
-              make_uint4(pack2<__half>(v[8 * u], v[8 * u + 1]), pack2<__half>(v[8 * u + 2], v[8 * u + 3]),
-                         pack2<__half>(v[8 * u + 4], v[8 * u + 5]), pack2<__half>(v[8 * u + 6], v[8 * u + 7]));
+        *reinterpret_cast<uint4*>(adst + ((part ^ swz) << 4)) =
+            make_uint4(pack2<__half>(v[0], v[1]), pack2<__half>(v[2], v[3]), pack2<__half>(v[4], v[5]),
+                       pack2<__half>(v[6], v[7]));
       }
       fence_proxy_async();
       mbar_arrive(&a_ready[sa]);
@@ -391,12 +394,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = nw % kSW, sa = na % kSA;
           const float scale = h < GROUPS ? __ldg(sc + (c >> 1)) * inv_ref : 0.f;
           if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
-          uint4 p[4];
+          uint4 p[2];
           const int rot = r & 3;  // rotated unit order spreads a quarter-warp over the banks
-          if (h < GROUPS) {
+          if (h < GROUPS) {       // part p: the row's 16-byte units 2p, 2p+1 (rotated)
             const uint4* wsrc = reinterpret_cast<const uint4*>(smem + Smem::w + (s * 2 + h) * kWBytes + r * 64);
 #pragma unroll
-            for (int u4 = 0; u4 < 4; ++u4) p[u4] = wsrc[(u4 + rot) & 3];
+            for (int u4 = 0; u4 < 2; ++u4) p[u4] = wsrc[(2 * part + u4 + rot) & 3];
           }
           fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
           mbar_arrive(&w_empty[s]);
@@ -405,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
             const int swz = (smem_u32(adst) >> 7) & 7;
 #pragma unroll
-            for (int u4 = 0; u4 < 4; ++u4) {  // 16 weight bytes -> A units 2U, 2U+1 (8 fp16 each)
-              const int U = (u4 + rot) & 3;
+            for (int u4 = 0; u4 < 2; ++u4) {  // 16 weight bytes -> A units 2U, 2U+1 (8 fp16 each)
+              const int U = (2 * part + u4 + rot) & 3;
               const uint32_t wd[4] = {p[u4].x, p[u4].y, p[u4].z, p[u4].w};
               uint32_t o[8];
 #pragma unroll
@@ -430,34 +433,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* sp = reinterpret_cast<const uint8_t*>(g.absmax) + ((int64_t)ti.e * g.N + row) * (g.K / 32);
         for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
           const int s = nw % kSW, sa = na % kSA;
-          uint32_t s0 = 0, s1 = 0;
-          if (h < GROUPS) {
-            s0 = e8m0_bf16x2(__ldg(sp + 2 * c));
-            s1 = e8m0_bf16x2(__ldg(sp + 2 * c + 1));
-          }
+          uint32_t s0 = 0;  // part p: scale block p of the chunk (elements 32p .. 32p+31)
+          if (h < GROUPS) s0 = e8m0_bf16x2(__ldg(sp + 2 * c + part));
           if (!wt.wait(&full_w[s], (nw / kSW) & 1)) break;
-          uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
+          uint4 p0 = make_uint4(0, 0, 0, 0);
           if (h < GROUPS) {
             const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
             const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
-            p0 = reinterpret_cast<const uint4*>(wsrc)[sw];
-            p1 = reinterpret_cast<const uint4*>(wsrc)[sw ^ 1];
+            p0 = reinterpret_cast<const uint4*>(wsrc)[part ^ sw];
           }
           fence_proxy_async();
           mbar_arrive(&w_empty[s]);
           if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) break;
           if (h < GROUPS) {
-            const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            const uint32_t words[4] = {p0.x, p0.y, p0.z, p0.w};
             char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
             const int swz = (smem_u32(adst) >> 7) & 7;
+            const __nv_bfloat162 sc2 = *reinterpret_cast<const __nv_bfloat162*>(&s0);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {  // unit q = elements 8q .. 8q+7, scale block q / 4
-              const uint32_t scw = q < 4 ? s0 : s1;
-              const __nv_bfloat162 sc2 = *reinterpret_cast<const __nv_bfloat162*>(&scw);
+            for (int qq = 0; qq < 4; ++qq) {  // unit q = elements 8q .. 8q+7
+              const int q = 4 * part + qq;
               uint32_t o[4];
 #pragma unroll
               for (int bb = 0; bb < 4; ++bb) {
-                const uint32_t byte = (words[q] >> (8 * bb)) & 0xffu;
+                const uint32_t byte = (words[qq] >> (8 * bb)) & 0xffu;
                 uint32_t pr = *reinterpret_cast<const uint32_t*>(lut + ((byte << 7) | lane4));
                 __nv_bfloat162 v = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&pr), sc2);
                 o[bb] = *reinterpret_cast<uint32_t*>(&v);
@@ -497,27 +496,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float a = (c & 3) == 0 ? am_cur.x : (c & 3) == 1 ? am_cur.y : (c & 3) == 2 ? am_cur.z : am_cur.w;
         if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
-        uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
-        if (h < GROUPS) {
+        uint4 p0 = make_uint4(0, 0, 0, 0);
+        if (h < GROUPS) {  // part p: the row's 16-byte unit p (elements 32p .. 32p+31)
           const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
           const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
-          p0 = reinterpret_cast<const uint4*>(wsrc)[sw];
-          p1 = reinterpret_cast<const uint4*>(wsrc)[sw ^ 1];
+          p0 = reinterpret_cast<const uint4*>(wsrc)[part ^ sw];
         }
         fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
         mbar_arrive(&w_empty[s]);  // packed bytes are in registers: the slot can be refilled
         if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) break;
         if (h < GROUPS) {
-          const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+          const uint32_t words[4] = {p0.x, p0.y, p0.z, p0.w};
           const __half2 sc = __float2half2_rn(a);
           char* adst = smem + Smem::a + (sa * 2 + h) * kABytes + r * 128;
           const int swz = (smem_u32(adst) >> 7) & 7;  // 128-byte swizzle follows the shared address
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {  // 16-byte unit q = 8 elements = packed word q
+          for (int qq = 0; qq < 4; ++qq) {  // 16-byte unit q = 8 elements = packed word q
+            const int q = 4 * part + qq;
             uint32_t o[4];
 #pragma unroll
             for (int bb = 0; bb < 4; ++bb) {
-              const uint32_t byte = (words[q] >> (8 * bb)) & 0xffu;
+              const uint32_t byte = (words[qq] >> (8 * bb)) & 0xffu;
               uint32_t pr = *reinterpret_cast<const uint32_t*>(lut + ((byte << 7) | lane4));
               __half2 v = __hmul2(*reinterpret_cast<__half2*>(&pr), sc);
               o[bb] = *reinterpret_cast<uint32_t*>(&v);
@@ -535,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // TMEM lane = token, column = feature: a thread owns one token row of the tile (the LoRA
     // delta is already in the accumulator: the MMA's extra K step). Gate column j and up column
     // 128 + j meet in one thread, and the row's 16-feature pieces leave as 16-byte stores.
-    const int ew = warp - 12;          // TMEM lanes 32*ew .. 32*ew+31
+    const int ew = warp - (4 + kDec / 32);  // TMEM lanes 32*ew .. 32*ew+31 (ew = warp % 4)
     const int r = ew * 32 + lane;      // token within the tile
     int it = 0;
     for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
@@ -686,7 +685,7 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
                       CU_TENSOR_MAP_SWIZZLE_128B))
       return E4B_ERR_CUDA;
   }
-  nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kThreads, Smem::total, s>>>(u, wmap, bmap, lmap);
+  nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kFwdThreads, Smem::total, s>>>(u, wmap, bmap, lmap);
   return launch_status();
 }
 
