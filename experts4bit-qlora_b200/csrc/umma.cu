@@ -13,7 +13,7 @@
 //
 // One persistent CTA per SM, 24 warps with fixed roles, 64-wide K chunks (one
 // quantization block per row per chunk) through three rings of their own depth --
-// packed weights 4 deep, activation tiles 4 deep, decoded weight tiles 2 deep:
+// packed weights 4 deep, activation tiles 3 deep, decoded weight tiles 3 deep:
 //   warp 0      TMA: packed NF4 bytes of the tile's rows (2-D boxes {32 B, 128 rows}, 32-byte
 //               swizzle);
 //   warp 1      TMA of the 128 token rows (fp16, expert-sorted), one box per chunk,
@@ -34,11 +34,13 @@
 // same time share the weight tile through L2. Every wait is bounded; a timeout
 // raises E4B_ERR_TIMEOUT and all roles run to the common exit (TMEM is freed).
 #include <atomic>
+#include <cstdlib>
 
 #include "async.cuh"
 #include "fp8.cuh"
 #include "umma.cuh"
 #include "tmap.cuh"
+#include "nf4_prmt.cuh"
 
 // Profiling instrumentation, compiled only with -DE4B_TRACE: per-CTA cycles each role
 // spends waiting (clock64), read back with e4b_umma_stats_read.
@@ -63,8 +65,8 @@ namespace e4b {
 namespace {
 
 constexpr int kSW = 4;  // packed-weight ring depth (HBM latency)
-constexpr int kSB = 5;  // activation ring depth
-constexpr int kSA = 2;  // decoded-A ring depth (produced on chip)
+constexpr int kSB = 3;  // activation ring depth
+constexpr int kSA = 3;  // decoded-weight ring depth: the decode runs up to two chunks ahead of the MMA
 constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA M)
 constexpr int kRows = 128;          // weight rows per group (UMMA M)
 constexpr int kKc = 64;             // K per chunk
@@ -200,6 +202,9 @@ __device__ __forceinline__ void tile_info(const int32_t* ts, const int32_t* offs
 }
 
 }  // namespace
+
+static_assert(SmemT<E4B_FMT_NF4>::total <= 232448 && SmemT<E4B_FMT_FP8_BLOCK128>::total <= 232448,
+              "shared memory budget");
 
 template <typename OutT, int GROUPS, int FMT>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -351,6 +356,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int part = d >> 8;            // 0: elements 0..31 of the chunk, 1: elements 32..63
     const int h = (d >> 7) & 1, r = d & 127;  // group, row within the tile
     const uint32_t lane4 = (uint32_t)lane << 2;
+    const Nf4Bytes nfb = nf4_bytes();
     int nw = 0, na = 0;  // packed-weight ring items, decoded-weight ring items (the LoRA chunk has no packed weights)
     // LoRA chunk of a tile: this row's LoRA-B values (rank <= 16, fp16) as K elements 0..15 of the
     // weight operand; the MMA issues a single K = 16 step for it, so the rest of the row is unused.
@@ -514,6 +520,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int qq = 0; qq < 4; ++qq) {  // 16-byte unit q = 8 elements = packed word q
             const int q = 4 * part + qq;
             uint32_t o[4];
+            if (u.nf4_regs) {  // the same fp16 pairs from registers (byte permutes)
+              uint32_t pr4[4];
+              nf4_decode_word(words[qq], nfb, pr4);
+#pragma unroll
+              for (int bb = 0; bb < 4; ++bb) {
+                __half2 v = __hmul2(*reinterpret_cast<__half2*>(&pr4[bb]), sc);
+                o[bb] = *reinterpret_cast<uint32_t*>(&v);
+              }
+            } else
 #pragma unroll
             for (int bb = 0; bb < 4; ++bb) {
               const uint32_t byte = (words[qq] >> (8 * bb)) & 0xffu;
@@ -685,7 +700,13 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
                       CU_TENSOR_MAP_SWIZZLE_128B))
       return E4B_ERR_CUDA;
   }
-  nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kFwdThreads, Smem::total, s>>>(u, wmap, bmap, lmap);
+  static const int nf4_regs = [] {  // E4B_UMMA_NF4_REGS=1: NF4 decode in registers
+    const char* v = getenv("E4B_UMMA_NF4_REGS");
+    return v && v[0] == '1' ? 1 : 0;
+  }();
+  UmmaArgs ua = u;
+  ua.nf4_regs = nf4_regs;
+  nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kFwdThreads, Smem::total, s>>>(ua, wmap, bmap, lmap);
   return launch_status();
 }
 
