@@ -14,7 +14,7 @@ struct UmmaArgs {
   int x_rows;                      // rows of the activation matrix g.a
   void* scratch;
   const __half* lora_xa16;         // [x_rows, 64] fp16: scaling * (x16_row . A^T), zero padded (rank > 0)
-  int nf4_regs;                    // NF4 decode by register byte permutes instead of the shared pair table
+  int nf4_regs;                    // bit 0: NF4 decode by register byte permutes; bit 1: late slot release
 };
 
 // Rows per expert (on average) from which the tensor-core path beats the GEMV, which
