@@ -500,6 +500,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         am_cur = load4(0);
         if (kchunks > 4) am_nxt = load4(4);
       }
+      const bool pipelined = (u.nf4_regs & 6) == 6;
+      uint4 p_next = make_uint4(0, 0, 0, 0);
       for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
         const int s = nw % kSW, sa = na % kSA;
         if ((c & 3) == 0 && c > 0) {
@@ -507,12 +509,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (h < GROUPS && c + 4 < kchunks) am_nxt = load4(c + 4);
         }
         const float a = (c & 3) == 0 ? am_cur.x : (c & 3) == 1 ? am_cur.y : (c & 3) == 2 ? am_cur.z : am_cur.w;
-        if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
-        uint4 p0 = make_uint4(0, 0, 0, 0);
-        if (h < GROUPS) {  // part p: the row's 16-byte unit p (elements 32p .. 32p+31)
-          const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
-          const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
-          p0 = reinterpret_cast<const uint4*>(wsrc)[part ^ sw];
+        // part p reads the row's 16-byte unit p (elements 32p .. 32p+31); with the pipelined decode
+        // (flags 2 | 4) the next chunk's unit is loaded before this chunk's decode
+        auto load_unit = [&](int slot) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (h < GROUPS) {
+            const char* wsrc = smem + Smem::w + (slot * 2 + h) * kWBytes + r * 32;
+            const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
+            v = reinterpret_cast<const uint4*>(wsrc)[part ^ sw];
+          }
+          return v;
+        };
+        uint4 p0;
+        if (pipelined && c > 0) {
+          p0 = p_next;
+        } else {
+          if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
+          p0 = load_unit(s);
+        }
+        if (pipelined && c + 1 < kchunks) {
+          const int s1 = (nw + 1) % kSW;
+          if (!wt.wait(&full_w[s1], ((nw + 1) / kSW) & 1)) break;
+          p_next = load_unit(s1);
         }
         if (!(u.nf4_regs & 2)) {  // release the packed slot now (else after the decode, one fence for both)
           fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
@@ -710,10 +728,11 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
       return E4B_ERR_CUDA;
   }
   // E4B_UMMA_FLAGS: bit 0 NF4 decode in registers; bit 1 a decode thread releases its packed-weight
-  // slot after the chunk's decode, behind the one proxy fence that also publishes the decoded tile
+  // slot after the chunk's decode, behind the one proxy fence that also publishes the decoded tile;
+  // bit 2 (with bit 1) the NF4 decode loads the next chunk's packed unit before decoding this one
   static const int nf4_regs = [] {
     const char* v = getenv("E4B_UMMA_FLAGS");
-    return v ? atoi(v) & 3 : 2;  // late release by default: gate_up 477 -> 450 us on Qwen3, FP8 prefill +10 %
+    return v ? atoi(v) & 7 : 6;  // late release + pipelined decode by default (Qwen3 gate_up 477 -> 420 us)
   }();
   UmmaArgs ua = u;
   ua.nf4_regs = nf4_regs;
