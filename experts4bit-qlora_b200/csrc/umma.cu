@@ -64,8 +64,8 @@ namespace e4b {
 
 namespace {
 
-constexpr int kSW = 4;  // packed-weight ring depth (HBM latency)
-constexpr int kSB = 3;  // activation ring depth
+constexpr int kSW = 3;  // packed-weight ring depth (HBM latency)
+constexpr int kSB = 4;  // activation ring depth
 constexpr int kSA = 3;  // decoded-weight ring depth: the decode runs up to two chunks ahead of the MMA
 constexpr int kTok = kUmmaTokens;  // 128 tokens per tile (UMMA M)
 constexpr int kRows = 128;          // weight rows per group (UMMA M)
