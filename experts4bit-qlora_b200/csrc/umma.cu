@@ -396,16 +396,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int kb = 0; kb < g.K / kFp8Block; ++kb) m = fmaxf(m, __ldg(sc + kb));
           inv_ref = m > 0.f ? 1.f / m : 0.f;
         }
+        const bool pipelined = (u.nf4_regs & 6) == 6;  // next chunk's units loaded before this decode
+        const int rot = r & 3;  // rotated unit order spreads a quarter-warp over the banks
+        auto load_units = [&](int slot, uint4 (&q)[2]) {  // part p: the row's 16-byte units 2p, 2p+1
+          if (h < GROUPS) {
+            const uint4* wsrc = reinterpret_cast<const uint4*>(smem + Smem::w + (slot * 2 + h) * kWBytes + r * 64);
+#pragma unroll
+            for (int u4 = 0; u4 < 2; ++u4) q[u4] = wsrc[(2 * part + u4 + rot) & 3];
+          }
+        };
+        uint4 pn[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
           const int s = nw % kSW, sa = na % kSA;
           const float scale = h < GROUPS ? __ldg(sc + (c >> 1)) * inv_ref : 0.f;
-          if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
-          uint4 p[2];
-          const int rot = r & 3;  // rotated unit order spreads a quarter-warp over the banks
-          if (h < GROUPS) {       // part p: the row's 16-byte units 2p, 2p+1 (rotated)
-            const uint4* wsrc = reinterpret_cast<const uint4*>(smem + Smem::w + (s * 2 + h) * kWBytes + r * 64);
-#pragma unroll
-            for (int u4 = 0; u4 < 2; ++u4) p[u4] = wsrc[(2 * part + u4 + rot) & 3];
+          uint4 p[2] = {pn[0], pn[1]};
+          if (!(pipelined && c > 0)) {
+            if (!(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
+            load_units(s, p);
+          }
+          if (pipelined && c + 1 < kchunks) {
+            const int s1 = (nw + 1) % kSW;
+            if (!wt.wait(&full_w[s1], ((nw + 1) / kSW) & 1)) break;
+            load_units(s1, pn);
           }
           if (!(u.nf4_regs & 2)) {  // release the packed slot now (else after the decode, one fence for both)
             fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
@@ -440,16 +452,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // e2m1 pairs -> bf16 through the pair table, times the block's 2^(s-127) (exact in bf16);
         // a 64-wide chunk is two 32-element scale blocks
         const uint8_t* sp = reinterpret_cast<const uint8_t*>(g.absmax) + ((int64_t)ti.e * g.N + row) * (g.K / 32);
+        const bool pipelined = (u.nf4_regs & 6) == 6;
+        uint4 pn = make_uint4(0, 0, 0, 0);
         for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
           const int s = nw % kSW, sa = na % kSA;
           uint32_t s0 = 0;  // part p: scale block p of the chunk (elements 32p .. 32p+31)
           if (h < GROUPS) s0 = e8m0_bf16x2(__ldg(sp + 2 * c + part));
-          if (!wt.wait(&full_w[s], (nw / kSW) & 1)) break;
-          uint4 p0 = make_uint4(0, 0, 0, 0);
-          if (h < GROUPS) {
-            const char* wsrc = smem + Smem::w + (s * 2 + h) * kWBytes + r * 32;
-            const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
-            p0 = reinterpret_cast<const uint4*>(wsrc)[part ^ sw];
+          auto load_unit = [&](int slot) {
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (h < GROUPS) {
+              const char* wsrc = smem + Smem::w + (slot * 2 + h) * kWBytes + r * 32;
+              const int sw = (r >> 2) & 1;  // the 32-byte swizzle of the box (rows r and r + 4 apart)
+              v = reinterpret_cast<const uint4*>(wsrc)[part ^ sw];
+            }
+            return v;
+          };
+          uint4 p0 = pn;
+          if (!(pipelined && c > 0)) {
+            if (!wt.wait(&full_w[s], (nw / kSW) & 1)) break;
+            p0 = load_unit(s);
+          }
+          if (pipelined && c + 1 < kchunks) {  // next chunk's unit before this chunk's decode
+            const int s1 = (nw + 1) % kSW;
+            if (!wt.wait(&full_w[s1], ((nw + 1) / kSW) & 1)) break;
+            pn = load_unit(s1);
           }
           if (!(u.nf4_regs & 2)) {  // release the packed slot now (else after the decode, one fence for both)
             fence_proxy_async();  // generic reads of the slot before its refill by the async proxy
@@ -729,7 +755,7 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   }
   // E4B_UMMA_FLAGS: bit 0 NF4 decode in registers; bit 1 a decode thread releases its packed-weight
   // slot after the chunk's decode, behind the one proxy fence that also publishes the decoded tile;
-  // bit 2 (with bit 1) the NF4 decode loads the next chunk's packed unit before decoding this one
+  // bit 2 (with bit 1) the decode loads the next chunk's packed units before decoding this one
   static const int nf4_regs = [] {
     const char* v = getenv("E4B_UMMA_FLAGS");
     return v ? atoi(v) & 7 : 6;  // late release + pipelined decode by default (Qwen3 gate_up 477 -> 420 us)
