@@ -21,7 +21,7 @@ namespace e4b {
 
 struct MoeLayout {
   size_t offsets, active, num_active, tile_a, tile_b, inv, sorted_token, x16, x_scale, h, down_rows, xa_gu, xa_dn,
-      umma, sync, part, total;
+      umma, sync, part, perm, total;
 };
 
 static MoeLayout moe_layout(const e4b_moe_desc& d) {
@@ -53,6 +53,7 @@ static MoeLayout moe_layout(const e4b_moe_desc& d) {
   L.umma = take(umma_workspace_bytes(d.tokens, d.top_k, d.num_experts, d.hidden, d.intermediate));
   L.sync = take(decode_layer_sync_bytes(1024));
   L.part = take(decode_slice_shape(d) ? decode_slice_part_bytes(d) : 0);
+  L.perm = take(permute_scratch_bytes(R, d.num_experts));
   L.total = o;
   return L;
 }
@@ -654,6 +655,7 @@ extern "C" e4b_status e4b_moe_forward(const e4b_moe_desc* desc, const e4b_moe_te
   pa.tile_a = kLoraRows;
   pa.tile_b = kUmmaTokens;
   pa.err = err;
+  if (permute_scratch_bytes((int64_t)T * k, E)) pa.seg_scratch = reinterpret_cast<int32_t*>(ws + L.perm);
   pa.reset_err = 0;  // the error word is sticky: only e4b_read_device_error clears it
   __half* x16 = reinterpret_cast<__half*>(ws + L.x16);
   float* x_scale = reinterpret_cast<float*>(ws + L.x_scale);

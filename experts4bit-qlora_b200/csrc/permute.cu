@@ -1,7 +1,8 @@
 // Permutation (R2): the device-side replacement for engines/fast.py:126-135.
 //
 // order = argsort(flat top-k ids, stable); counts = bincount; offsets =
-// exclusive scan -- computed in one CTA of 32 warps with no host round trip.
+// exclusive scan -- computed in one CTA of 32 warps with no host round trip (large
+// inputs: the same passes over the grid, below).
 // Each warp owns a contiguous segment of the flat array, so ranks within an
 // expert follow flat order exactly (stable): pass 1 counts per (warp, expert),
 // pass 2 scans expert-major / warp-minor, pass 3 re-walks each segment in order
@@ -199,7 +200,137 @@ permute_kernel(PermuteArgs a) {
 
 size_t permute_smem_bytes(int E) { return (size_t)32 * E * sizeof(int); }
 
+// ---- multi-CTA permutation for large inputs --------------------------------------------------
+// The one-CTA kernel walks every entry on one SM. Above kMultiMin entries the same three passes
+// run over the grid: segments of kSeg consecutive flat entries (one warp each) count per expert
+// into global scratch; one CTA scans expert-major / segment-minor into the offsets, the tile
+// prefixes, the active list and each segment's base per expert; every warp then re-walks its
+// segment and places its entries with __match_any_sync ranks. Segments are contiguous and
+// ordered, so ranks within an expert follow flat order: the same stable result as the one-CTA
+// kernel.
+constexpr int kMultiMin = 8192;
+constexpr int kSeg = 256;
+
+size_t permute_scratch_bytes(int64_t n, int E) {
+  if (n <= kMultiMin) return 0;
+  return (size_t)((n + kSeg - 1) / kSeg) * E * sizeof(int32_t);
+}
+
+__global__ void __launch_bounds__(1024) permute_count_kernel(PermuteArgs a, int nseg, int count_ctas) {
+  if ((int)blockIdx.x >= count_ctas) {  // conversion CTAs: one row per warp
+    convert_rows_to_f16(a.conv.src, a.conv.src_dtype, a.conv.dst, a.conv.scale, a.conv.rows, a.conv.K,
+                        (blockIdx.x - count_ctas) * (blockDim.x >> 5) + (threadIdx.x >> 5),
+                        a.conv_ctas * (blockDim.x >> 5));
+    return;
+  }
+  extern __shared__ int wc[];  // [32][E]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, E = a.E, n = a.T * a.k;
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) wc[i] = 0;
+  __syncthreads();
+  const int seg = blockIdx.x * 32 + warp;
+  if (seg < nseg) {
+    const int s0 = seg * kSeg, s1 = min(n, s0 + kSeg);
+    const unsigned lt = (1u << lane) - 1u;
+    for (int base = s0; base < s1; base += 32) {
+      const int i = base + lane;
+      const bool valid = i < s1;
+      const int e = valid ? stack_expert(a.topk_idx[i], a.emap, a.routed, E, a.err, true) : -1;
+      const unsigned act = __ballot_sync(0xffffffffu, valid);
+      const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+      if (valid && (peers & lt) == 0) wc[warp * E + e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) {
+    const int w = i / E, e = i - w * E;
+    const int sg = blockIdx.x * 32 + w;
+    if (sg < nseg) a.seg_scratch[(int64_t)sg * E + e] = wc[i];
+  }
+}
+
+__global__ void __launch_bounds__(1024) permute_scan_kernel(PermuteArgs a, int nseg) {
+  __shared__ int s_scan[32];
+  const int E = a.E, n = a.T * a.k, e = threadIdx.x;
+  int c = 0;
+  if (e < E) {  // prefix over segments, written back in place
+    for (int sg = 0; sg < nseg; ++sg) {
+      const int v = a.seg_scratch[(int64_t)sg * E + e];
+      a.seg_scratch[(int64_t)sg * E + e] = c;
+      c += v;
+    }
+  }
+  int tot;
+  const int off = block_exclusive_scan(c, s_scan, &tot);
+  if (e < E) {
+    a.offsets[e] = off;
+    for (int sg = 0; sg < nseg; ++sg) a.seg_scratch[(int64_t)sg * E + e] += off;
+  }
+  if (threadIdx.x == 0) a.offsets[E] = n;
+  const int pos = block_exclusive_scan(c > 0 ? 1 : 0, s_scan, &tot);
+  if (e < E && c > 0 && a.active) a.active[pos] = e;
+  if (threadIdx.x == 0 && a.num_active) *a.num_active = tot;
+  for (int j = 0; j < 2; ++j) {
+    int* ts = j == 0 ? a.tile_start_a : a.tile_start_b;
+    const int bm = j == 0 ? a.tile_a : a.tile_b;
+    if (!ts) continue;
+    const int nt = e < E ? (c + bm - 1) / bm : 0;
+    const int p = block_exclusive_scan(nt, s_scan, &tot);
+    if (e < E) ts[e] = p;
+    if (threadIdx.x == 0) ts[E] = tot;
+  }
+}
+
+__global__ void __launch_bounds__(1024) permute_place_kernel(PermuteArgs a, int nseg) {
+  extern __shared__ int wc[];  // [32][E]: this CTA's segments' running bases
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, E = a.E, n = a.T * a.k;
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) {
+    const int w = i / E, e = i - w * E;
+    const int sg = blockIdx.x * 32 + w;
+    wc[i] = sg < nseg ? a.seg_scratch[(int64_t)sg * E + e] : 0;
+  }
+  __syncthreads();
+  const int seg = blockIdx.x * 32 + warp;
+  if (seg >= nseg) return;
+  const int s0 = seg * kSeg, s1 = min(n, s0 + kSeg);
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = s0; base < s1; base += 32) {
+    const int i = base + lane;
+    const bool valid = i < s1;
+    const int e = valid ? stack_expert(a.topk_idx[i], a.emap, a.routed, E, a.err, false) : -1;
+    const unsigned act = __ballot_sync(0xffffffffu, valid);
+    const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+    int pos = 0;
+    if (valid) pos = wc[warp * E + e] + __popc(peers & lt);
+    __syncwarp();
+    if (valid && (peers & lt) == 0) wc[warp * E + e] += __popc(peers);
+    __syncwarp();
+    if (valid) {
+      if (a.order) a.order[pos] = i;
+      if (a.inv) a.inv[i] = pos;
+      if (a.sorted_token) a.sorted_token[pos] = i / a.k;
+    }
+  }
+}
+
 e4b_status launch_permute(const PermuteArgs& a, cudaStream_t s) {
+  const int64_t n = (int64_t)a.T * a.k;
+  if (a.seg_scratch && n > kMultiMin) {
+    const int nseg = (int)((n + kSeg - 1) / kSeg);
+    const int ctas = (nseg + 31) / 32;
+    const size_t smem = permute_smem_bytes(a.E);
+    if (smem > 48 * 1024) {
+      if (cudaFuncSetAttribute(permute_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+              cudaSuccess ||
+          cudaFuncSetAttribute(permute_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+              cudaSuccess)
+        return E4B_ERR_CUDA;
+    }
+    permute_count_kernel<<<ctas + (a.conv.src ? a.conv_ctas : 0), 1024, smem, s>>>(a, nseg, ctas);
+    permute_scan_kernel<<<1, 1024, 0, s>>>(a, nseg);
+    permute_place_kernel<<<ctas, 1024, smem, s>>>(a, nseg);
+    return launch_status();
+  }
   const size_t smem = permute_smem_bytes(a.E);
   if (smem > 48 * 1024) {
     if (cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -214,10 +345,8 @@ e4b_status launch_permute(const PermuteArgs& a, cudaStream_t s) {
 using namespace e4b;
 
 extern "C" size_t e4b_permute_workspace_bytes(int T, int k, int E) {
-  (void)T;
-  (void)k;
-  if (E < 0) return 0;
-  return kErrBytes;
+  if (E < 0 || T < 0 || k < 0) return 0;
+  return kErrBytes + permute_scratch_bytes((int64_t)T * k, E);
 }
 
 extern "C" e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, int32_t* order, int32_t* inv,
@@ -235,5 +364,7 @@ extern "C" e4b_status e4b_permute(const int64_t* topk_idx, int T, int k, int E, 
   a.offsets = offsets;
   a.err = static_cast<int*>(workspace);
   a.reset_err = 0;  // the error word is sticky: only e4b_read_device_error clears it
+  if (permute_scratch_bytes((int64_t)T * k, E))
+    a.seg_scratch = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + kErrBytes);
   return launch_permute(a, (cudaStream_t)stream);
 }

@@ -23,9 +23,13 @@ struct PermuteArgs {
   int reset_err;            // zero *err before validating (first kernel of a call)
   ConvertArgs conv;         // optional: rows converted to fp16 by CTAs 1.. of the same launch
   int conv_ctas;
+  int32_t* seg_scratch;     // optional: permute_scratch_bytes(T*k, E) of global memory; with it,
+                            // large inputs take the multi-CTA permutation (same result)
 };
 
 size_t permute_smem_bytes(int E);
+// Global scratch of the multi-CTA permutation (0 below its size threshold).
+size_t permute_scratch_bytes(int64_t n, int E);
 e4b_status launch_permute(const PermuteArgs& a, cudaStream_t s);
 
 }  // namespace e4b

@@ -109,7 +109,7 @@ def test_router_tie_known_answer(ops):
 
 
 @pytest.mark.parametrize("T,k,E", [(1, 8, 64), (5, 8, 64), (4096, 8, 128), (8192, 2, 8), (16384, 8, 256),
-                                   (33, 4, 16), (0, 2, 4), (3, 3, 1000)])
+                                   (33, 4, 16), (0, 2, 4), (3, 3, 1000), (1100, 8, 1000), (2049, 4, 3)])
 def test_permute_bit_exact(ops, T, k, E):
     g = torch.Generator().manual_seed(T + E)
     idx = torch.randint(0, E, (T, k), generator=g)
