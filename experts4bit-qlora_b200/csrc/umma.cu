@@ -34,6 +34,7 @@
 // same time share the weight tile through L2. Every wait is bounded; a timeout
 // raises E4B_ERR_TIMEOUT and all roles run to the common exit (TMEM is freed).
 #include <atomic>
+#include <cstdio>
 #include <cstdlib>
 
 #include "async.cuh"
@@ -45,7 +46,7 @@
 // Profiling instrumentation, compiled only with -DE4B_TRACE: per-CTA cycles each role
 // spends waiting (clock64), read back with e4b_umma_stats_read.
 #ifdef E4B_TRACE
-__device__ unsigned long long g_umma_stats[148 * 8];
+__device__ unsigned long long g_umma_stats[148 * 16];
 extern "C" __attribute__((visibility("default"))) int e4b_umma_stats_read(unsigned long long* host) {
   return (int)cudaMemcpyFromSymbol(host, g_umma_stats, sizeof(g_umma_stats));
 }
@@ -53,7 +54,7 @@ extern "C" __attribute__((visibility("default"))) int e4b_umma_stats_read(unsign
   ({                                                                                 \
     const long long t0_ = clock64();                                                 \
     const bool ok_ = (expr);                                                         \
-    if (blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 8 + (slot)], (unsigned long long)(clock64() - t0_)); \
+    if (blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 16 + (slot)], (unsigned long long)(clock64() - t0_)); \
     ok_;                                                                             \
   })
 #else
@@ -103,6 +104,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity);
+
 // Bounded wait that remembers a timeout: after the first timeout every later
 // wait of this thread returns at once, so all roles reach the common exit.
 struct Waiter {
@@ -111,6 +114,15 @@ struct Waiter {
   __device__ bool wait(uint64_t* bar, uint32_t parity) {
     if (dead) return false;
     if (mbar_wait(bar, parity)) return true;
+    dead = true;
+    raise_error(err, E4B_ERR_TIMEOUT);
+    return false;
+  }
+  // the same with cluster-scope acquire, for barriers the other CTA of a pair arrives on
+  __device__ bool waitc(uint64_t* bar, uint32_t parity) {
+    if (dead) return false;
+    for (uint32_t i = 0; i < kMaxSpins; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
     dead = true;
     raise_error(err, E4B_ERR_TIMEOUT);
     return false;
@@ -160,6 +172,61 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// ---- CTA-pair (cta_group::2) helpers: the even CTA of a cluster of two issues the MMA ----------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `p`'s counterpart in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Tiled TMA load (no multicast) into this CTA's shared memory whose completion counts on the
+// barrier at `bar_caddr` (shared::cluster), which may be the even CTA's.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* map, int c0, int c1, uint32_t bar_caddr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar_caddr)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(dtmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+// Arrive (once) on the barrier at `bar_caddr` when the pair's MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_caddr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_caddr)
+               : "memory");
+}
+
+// silu for the accumulator epilogue: the quotient with the fast approximate divide (a reciprocal
+// and a multiply, about 2 ulp of fp32) instead of the IEEE division sequence; the result is then
+// rounded to the 16-bit output type, far coarser. For x below about -87, exp(-x) overflows and the
+// quotient is 0 (the exact value is below 1e-36 in magnitude).
+__device__ __forceinline__ float silu_epi(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
@@ -206,7 +273,13 @@ __device__ __forceinline__ void tile_info(const int32_t* ts, const int32_t* offs
 static_assert(SmemT<E4B_FMT_NF4>::total <= 232448 && SmemT<E4B_FMT_FP8_BLOCK128>::total <= 232448,
               "shared memory budget");
 
-template <typename OutT, int GROUPS, int FMT>
+// PAIR (NF4, GROUPS == 2): clusters of two CTAs run tcgen05.mma.cta_group::2 with M = 256 tokens
+// (128 per CTA) and N = 256 features. Each CTA decodes only its own group of 128 weight rows
+// (four decode threads per row) and loads its own 128 token rows, so per MMA FLOP a CTA decodes
+// half as many weights and its shared memory serves half the weight operand. The even CTA issues
+// the MMAs, waits on both CTAs' operands (TMA completion and decode warps arrive on its barriers)
+// and commits to the barriers of both; each CTA's epilogue reads its own 128 TMEM lanes.
+template <typename OutT, int GROUPS, int FMT, bool PAIR = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     nf4_umma_kernel(UmmaArgs u, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ CUtensorMap lmap) {
@@ -232,13 +305,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   int32_t* s_ts = reinterpret_cast<int32_t*>(smem + Smem::tables);
   int32_t* s_offs = s_ts + 1025;
   for (int i = tid; i <= u.g.E; i += kFwdThreads) {
-    s_ts[i] = u.tile_start[i];
+    if (!PAIR) s_ts[i] = u.tile_start[i];
     s_offs[i] = u.g.offsets[i];
   }
+  const uint32_t crank = PAIR ? cluster_rank() : 0;  // PAIR: 0 issues the MMAs
+  if (PAIR && warp == 2) {  // token-pair tiles: prefix of ceil(count / 256) per expert
+    int carry = 0;
+    for (int base = 0; base < u.g.E; base += 32) {
+      const int e = base + lane;
+      const int v = e < u.g.E ? (u.g.offsets[e + 1] - u.g.offsets[e] + 2 * kTok - 1) / (2 * kTok) : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (e < u.g.E) s_ts[e + 1] = carry + incl;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_ts[0] = 0;
+  }
+  // work units: tiles (one CTA) or token-pair tiles (one cluster of two)
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int unit_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   const int nft = g.N / (GROUPS * kRows);  // feature tiles per expert (SwiGLU: gate+up rows per tile)
   const int kchunks = g.K / kKc;
-  const int total_tiles = u.tile_start[g.E] * nft;
   Waiter wt{false, g.err};
 
   if (tid == 0) {
@@ -251,18 +343,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&b_empty[s], 1);
     }
     for (int s = 0; s < kSA; ++s) {
-      mbar_init(&a_ready[s], kDec);
+      // PAIR: the even CTA's barrier also takes one arrival forwarded from the odd CTA's
+      mbar_init(&a_ready[s], PAIR && crank == 0 ? kDec + 1 : kDec);
       mbar_init(&a_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], PAIR ? 8 : 128);  // PAIR: one arrival per epilogue warp of each CTA
     }
     fence_proxy_async();
+    if (PAIR) asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 3) {  // 512 TMEM columns: two buffers x (gate, up) x 128 fp32 columns
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   if (FMT == E4B_FMT_NF4) {  // pair table: entry e of lane l at (e << 7) | (l << 2)
     const float code = c_nf4[lane & 15];
@@ -279,19 +378,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // the other CTA's barriers are initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int total_tiles = s_ts[g.E] * nft;
 
-  if (warp == 0) {
+#ifdef E4B_TRACE
+  const bool mma_only = !PAIR && (u.nf4_regs & 16);
+#else
+  constexpr bool mma_only = false;
+#endif
+  if (mma_only && warp != 3 && warp < 4 + kDec / 32) {
+    // trace builds only: producers and decode idle
+  } else if (warp == 0) {
     // ---------------- TMA producer: packed weight rows -------------------------------------
     if (lane == 0) {
       int n = 0;
-      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+      for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step) {
         TileInfo ti;
         tile_info(s_ts, s_offs, g.E, nft, t, ti);
         for (int c = 0; c < kchunks; ++c, ++n) {
           const int s = n % kSW;
           if (!STAT_WAIT(0, wt.wait(&w_empty[s], ((n / kSW) & 1) ^ 1))) break;
+          if (PAIR) {  // this CTA's group only
+            mbar_arrive_expect_tx(&full_w[s], kWBytes);
+            const int row = ti.e * g.N + group_row0(g, ti.ft, (int)crank, GROUPS);
+            tma_load_2d(smem + Smem::w + (s * 2) * kWBytes, &wmap, c * Smem::wrow, row, &full_w[s]);
+            continue;
+          }
           mbar_arrive_expect_tx(&full_w[s], GROUPS * kWBytes);
 #pragma unroll
           for (int h = 0; h < GROUPS; ++h) {
@@ -307,12 +421,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // to the next expert or are zero-filled past the matrix, and are discarded by the epilogue.
     if (lane == 0) {
       int n = 0;
-      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+      for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step) {
         TileInfo ti;
         tile_info(s_ts, s_offs, g.E, nft, t, ti);
         for (int c = 0; c < kchunks + (g.rank ? 1 : 0); ++c, ++n) {  // + the tile's LoRA-A chunk
           const int s = n % kSB;
           if (!STAT_WAIT(1, wt.wait(&b_empty[s], ((n / kSB) & 1) ^ 1))) break;
+          if (PAIR) {  // both CTAs' boxes complete on the even CTA's barrier
+            const int trow = ti.row0 + ti.tt * 2 * kTok + (int)crank * kTok;
+            const uint32_t fb = cluster_addr(&full_b[s], 0);
+            if (crank == 0) mbar_arrive_expect_tx(&full_b[s], 2 * kBBytes);
+            if (c < kchunks)
+              tma_load_2d_pair(smem + Smem::b + s * kBBytes, &bmap, c * kKc, trow, fb);
+            else
+              tma_load_2d_pair(smem + Smem::b + s * kBBytes, &lmap, 0, trow, fb);
+            continue;
+          }
           mbar_arrive_expect_tx(&full_b[s], kBBytes);
           if (c < kchunks)
             tma_load_2d(smem + Smem::b + s * kBBytes, &bmap, c * kKc, ti.row0 + ti.tt * kTok, &full_b[s]);
@@ -322,13 +446,74 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else if (warp == 2) {
-    // idle
+    // PAIR, odd CTA: forward each completed decoded-weight stage to the even CTA's a_ready with
+    // one cluster-scope release (decode threads arrive locally, so their own loads in flight are
+    // not drained by a cluster-scope release per chunk)
+    if (PAIR && crank == 1 && lane == 0) {
+      int n = 0;
+      for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step)
+        for (int c = 0; c < kchunks + (g.rank ? 1 : 0); ++c, ++n) {
+          const int sa = n % kSA;
+          if (!wt.wait(&a_ready[sa], (n / kSA) & 1)) break;
+          mbar_arrive_remote(cluster_addr(&a_ready[sa], 0));
+        }
+    }
   } else if (warp == 3) {
     // ---------------- MMA issuer -------------------------------------------------------------
-    if (lane == 0) {
+    if (PAIR && lane == 0 && crank == 0) {
+      // M = 256: the A operand's rows 0..127 are this CTA's token tile, 128..255 the other CTA's
+      // (same shared-memory offsets); N = 256: rows 0..127 of B from this CTA's decoded group,
+      // 128..255 from the other CTA's. Each CTA's TMEM receives its own 128 token rows.
+      const uint32_t idesc = (1u << 4) | ((uint32_t)((GROUPS * kRows) >> 3) << 17) | ((uint32_t)((2 * kTok) >> 4) << 24);
+      int n = 0, it = 0;
+      for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step, ++it) {
+        const int buf = it & 1;
+        if (!STAT_WAIT(4, wt.waitc(&acc_empty[buf], ((it >> 1) & 1) ^ 1))) break;
+        tc_fence_after();
+        for (int c = 0; c < kchunks + (g.rank ? 1 : 0); ++c, ++n) {
+          const int s = n % kSB, sa = n % kSA;
+          if (!STAT_WAIT(2, wt.waitc(&full_b[s], (n / kSB) & 1))) break;
+          if (!STAT_WAIT(3, wt.waitc(&a_ready[sa], (n / kSA) & 1))) break;
+          tc_fence_after();
+          const uint32_t xsm = smem_u32(smem + Smem::b + s * kBBytes);
+          const uint32_t wsm = smem_u32(smem + Smem::a + (sa * 2) * kABytes);
+          const int ksteps = c < kchunks ? kKc / 16 : 1;
+          for (int kk = 0; kk < ksteps; ++kk)
+            umma_f16_pair(tmem + buf * 256, sw128_desc(xsm + kk * 32), sw128_desc(wsm + kk * 32), idesc,
+                          (c | kk) != 0);
+          umma_commit_pair(cluster_addr(&b_empty[s], 0));
+          umma_commit_pair(cluster_addr(&b_empty[s], 1));
+          umma_commit_pair(cluster_addr(&a_empty[sa], 0));
+          umma_commit_pair(cluster_addr(&a_empty[sa], 1));
+        }
+        umma_commit_pair(cluster_addr(&acc_full[buf], 0));
+        umma_commit_pair(cluster_addr(&acc_full[buf], 1));
+      }
+    } else if (!PAIR && lane == 0) {
       const uint32_t idesc = idesc_f16(GROUPS * kRows, FMT == E4B_FMT_MXFP4);  // N = the tile's gate (+ up) rows
       int n = 0, it = 0;
-      for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
+#ifdef E4B_TRACE
+      if (u.nf4_regs & 16) {  // trace builds only: MMAs on whatever the first ring slots hold, no operand waits
+        for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step, ++it) {
+          const int buf = it & 1;
+          if (!STAT_WAIT(4, wt.wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1))) break;
+          tc_fence_after();
+          for (int c = 0; c < kchunks; ++c) {
+            if (u.nf4_regs & 64) {  // a completed barrier's wait and the fence, as the fed loop does
+              if (!STAT_WAIT(2, wt.wait(&full_w[0], 1))) break;
+              tc_fence_after();
+            }
+            const uint32_t xsm = smem_u32(smem + Smem::b + (c % kSB) * kBBytes);
+            const uint32_t wsm = smem_u32(smem + Smem::a + ((c % kSA) * 2) * kABytes);
+            for (int kk = 0; kk < kKc / 16; ++kk)
+              umma_f16(tmem + buf * 256, sw128_desc(xsm + kk * 32), sw128_desc(wsm + kk * 32), idesc, (c | kk) != 0);
+            if (u.nf4_regs & 32) umma_commit(&b_empty[0]);  // commit cost, barrier unused in this mode
+          }
+          umma_commit(&acc_full[buf]);
+        }
+      } else
+#endif
+      for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step, ++it) {
         const int buf = it & 1;
         if (!STAT_WAIT(4, wt.wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1))) break;
         tc_fence_after();
@@ -381,7 +566,102 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       ++na;
       return true;
     };
-    for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x) {
+    if constexpr (PAIR) {
+      // Four threads per weight row of this CTA's group: lane l of decode warp w owns row
+      // 8w + l / 4 and elements 16q .. 16q+15 of each chunk, q = l % 4 (packed bytes 8q .. 8q+7,
+      // operand units 2q, 2q+1). Waits are warp-uniform: the warp arrives once on the even CTA's
+      // a_ready after its lanes' stores and proxy fences.
+      const int q = lane & 3;
+      const int pr = ((d >> 5) << 3) | (lane >> 2);
+      auto wok = [&](bool ok) {
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) wt.dead = true;
+        return ok;
+      };
+      auto load_half = [&](int slot) {
+        const char* wsrc = smem + Smem::w + (slot * 2) * kWBytes + pr * 32;
+        const int sw = (pr >> 2) & 1;  // the 32-byte swizzle of the box
+        return *reinterpret_cast<const uint2*>(wsrc + (((q >> 1) ^ sw) << 4) + ((q & 1) << 3));
+      };
+      for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step) {
+        TileInfo ti;
+        tile_info(s_ts, s_offs, g.E, nft, t, ti);
+        const int row = group_row0(g, ti.ft, (int)crank, GROUPS) + pr;
+        const float* am = g.absmax + ((int64_t)ti.e * g.N + row) * (g.K / 64);
+        // absmax four chunks at a time, the next four loaded one group ahead
+        const bool vec4 = (g.K & 255) == 0;
+        auto load4 = [&](int c0) {
+          if (vec4) return __ldg(reinterpret_cast<const float4*>(am + c0));
+          float4 v;
+          v.x = __ldg(am + c0);
+          v.y = c0 + 1 < kchunks ? __ldg(am + c0 + 1) : 0.f;
+          v.z = c0 + 2 < kchunks ? __ldg(am + c0 + 2) : 0.f;
+          v.w = c0 + 3 < kchunks ? __ldg(am + c0 + 3) : 0.f;
+          return v;
+        };
+        float4 am_cur = load4(0), am_nxt = kchunks > 4 ? load4(4) : am_cur;
+        uint2 p_next = make_uint2(0, 0);
+        for (int c = 0; c < kchunks; ++c, ++nw, ++na) {
+          const int s = nw % kSW, sa = na % kSA;
+          if ((c & 3) == 0 && c > 0) {
+            am_cur = am_nxt;
+            if (c + 4 < kchunks) am_nxt = load4(c + 4);
+          }
+          const float a = (c & 3) == 0 ? am_cur.x : (c & 3) == 1 ? am_cur.y : (c & 3) == 2 ? am_cur.z : am_cur.w;
+          uint2 p0 = p_next;
+          if (c == 0) {
+            if (!wok(tid == 128 ? STAT_WAIT(5, wt.wait(&full_w[s], (nw / kSW) & 1)) : wt.wait(&full_w[s], (nw / kSW) & 1))) break;
+            p0 = load_half(s);
+          }
+          if (c + 1 < kchunks) {  // next chunk's bytes before this chunk's decode
+            const int s1 = (nw + 1) % kSW;
+            if (!wok(wt.wait(&full_w[s1], ((nw + 1) / kSW) & 1))) break;
+            p_next = load_half(s1);
+          }
+          if (!wok(wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1))) break;
+          const uint32_t words[2] = {p0.x, p0.y};
+          const __half2 sc = __float2half2_rn(a);
+          char* adst = smem + Smem::a + (sa * 2) * kABytes + pr * 128;
+          const int swz = (smem_u32(adst) >> 7) & 7;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            uint32_t o[4];
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+              const uint32_t byte = (words[j] >> (8 * bb)) & 0xffu;
+              uint32_t pv = *reinterpret_cast<const uint32_t*>(lut + ((byte << 7) | lane4));
+              __half2 v = __hmul2(*reinterpret_cast<__half2*>(&pv), sc);
+              o[bb] = *reinterpret_cast<uint32_t*>(&v);
+            }
+            *reinterpret_cast<uint4*>(adst + (((2 * q + j) ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+          fence_proxy_async();
+          mbar_arrive(&w_empty[s]);  // this thread's packed bytes were consumed above
+          mbar_arrive(&a_ready[sa]);  // this CTA's barrier; the odd CTA's is forwarded (warp 2)
+        }
+        if (g.rank && !wt.dead) {  // LoRA-B values of the row: quarters 0, 1 write units 0, 1
+          const int sa = na % kSA;
+          if (!wok(wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1))) break;
+          if (q < 2) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              v[j] = 8 * q + j < g.rank
+                         ? load_as_f32(g.lora_B, g.lora_dtype, ((int64_t)ti.e * g.N + row) * g.rank + 8 * q + j)
+                         : 0.f;
+            char* adst = smem + Smem::a + (sa * 2) * kABytes + pr * 128;
+            const int swz = (smem_u32(adst) >> 7) & 7;
+            *reinterpret_cast<uint4*>(adst + ((q ^ swz) << 4)) =
+                make_uint4(pack2<__half>(v[0], v[1]), pack2<__half>(v[2], v[3]), pack2<__half>(v[4], v[5]),
+                           pack2<__half>(v[6], v[7]));
+          }
+          fence_proxy_async();
+          mbar_arrive(&a_ready[sa]);
+          ++na;
+        }
+      }
+    } else
+    for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step) {
       TileInfo ti;
       tile_info(s_ts, s_offs, g.E, nft, t, ti);
       const int row = group_row0(g, ti.ft, h, GROUPS) + r;
@@ -563,6 +843,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mbar_arrive(&w_empty[s]);
         }
         if (!wt.wait(&a_empty[sa], ((na / kSA) & 1) ^ 1)) break;
+#ifdef E4B_TRACE
+        if (u.nf4_regs & 8) {  // trace builds only: skip the decode (timing of the other roles)
+          fence_proxy_async();
+          if (u.nf4_regs & 2) mbar_arrive(&w_empty[s]);
+          mbar_arrive(&a_ready[sa]);
+          continue;
+        }
+#endif
         if (h < GROUPS) {
           const uint32_t words[4] = {p0.x, p0.y, p0.z, p0.w};
           const __half2 sc = __float2half2_rn(a);
@@ -605,7 +893,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int ew = warp - (4 + kDec / 32);  // TMEM lanes 32*ew .. 32*ew+31 (ew = warp % 4)
     const int r = ew * 32 + lane;      // token within the tile
     int it = 0;
-    for (int t = blockIdx.x; t < total_tiles && !wt.dead; t += gridDim.x, ++it) {
+    for (int t = unit0; t < total_tiles && !wt.dead; t += unit_step, ++it) {
       TileInfo ti;
       tile_info(s_ts, s_offs, g.E, nft, t, ti);
       const int buf = it & 1;
@@ -623,12 +911,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         wsa = ma;
         wsb = mb;
       }
-      const int m = ti.tt * kTok + r;
+      const int m = PAIR ? ti.tt * 2 * kTok + (int)crank * kTok + r : ti.tt * kTok + r;
       const bool valid = m < ti.M;
       const int64_t srow = ti.row0 + (valid ? m : 0);
       float sc = 1.f;
       if (g.a_scale) sc = g.a_scale[g.a_rows ? g.a_rows[srow] : srow];
-      if (!(r == 0 ? STAT_WAIT(6, wt.wait(&acc_full[buf], (it >> 1) & 1)) : wt.wait(&acc_full[buf], (it >> 1) & 1))) break;
+      if (PAIR) {  // warp-uniform wait: the warp later arrives once on the even CTA's acc_empty
+        if (!__all_sync(0xffffffffu, wt.wait(&acc_full[buf], (it >> 1) & 1))) {
+          wt.dead = true;
+          break;
+        }
+      } else if (!(r == 0 ? STAT_WAIT(6, wt.wait(&acc_full[buf], (it >> 1) & 1)) : wt.wait(&acc_full[buf], (it >> 1) & 1))) {
+        break;
+      }
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + buf * 256;
       const bool swiglu = g.epilogue == E4B_EPI_SWIGLU;
@@ -640,16 +935,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float sh = sc * (hh == 0 ? wsa : wsb);
         for (int c0 = 0; c0 < kRows; c0 += 16) {
           float va[16], vb[16];
+#ifdef E4B_TRACE
+          long long tp0 = clock64();
+#endif
           tmem_ld16(tbase + hh * kRows + c0, va);
           if (GROUPS == 2 && swiglu) tmem_ld16(tbase + kRows + c0, vb);
+#ifdef E4B_TRACE
+          long long tp1 = clock64();
+          if (r == 0 && blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 16 + 8], (unsigned long long)(tp1 - tp0));
+#endif
           float o[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float ya = va[i] * sh;
             if (GROUPS == 2 && swiglu)
-              o[i] = silu_f32(ya) * (vb[i] * (sc * wsb));
+              o[i] = silu_epi(ya) * (vb[i] * (sc * wsb));
             else if (g.epilogue == E4B_EPI_SILU)
-              o[i] = silu_f32(ya);
+              o[i] = silu_epi(ya);
             else
               o[i] = ya;
           }
@@ -661,23 +963,41 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               pk[j] = (uint32_t)(*reinterpret_cast<const uint16_t*>(&lo)) |
                       ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
             }
+#ifdef E4B_TRACE
+            long long tp2 = clock64();
+            if (r == 0 && blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 16 + 9], (unsigned long long)(tp2 - tp1));
+#endif
             uint4* dst = reinterpret_cast<uint4*>(orow + hh * kRows + c0);
             dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+#ifdef E4B_TRACE
+            if (r == 0 && blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 16 + 10], (unsigned long long)(clock64() - tp2));
+#endif
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      if (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(cluster_addr(&acc_empty[buf], 0));
+      } else {
+        mbar_arrive(&acc_empty[buf]);
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // no CTA leaves while the other may still arrive on its barriers
   tc_fence_after();
-  if (warp == 3) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  if (warp == 3) {
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
 #ifdef E4B_TRACE
-  if (tid == 0 && blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 8 + 7], (unsigned long long)(clock64() - t_start));
+  if (tid == 0 && blockIdx.x < 148) atomicAdd(&g_umma_stats[blockIdx.x * 16 + 7], (unsigned long long)(clock64() - t_start));
 #endif
 }
 
@@ -758,10 +1078,52 @@ static e4b_status launch_groups(const UmmaArgs& u, cudaStream_t s) {
   // bit 2 (with bit 1) the decode loads the next chunk's packed units before decoding this one
   static const int nf4_regs = [] {
     const char* v = getenv("E4B_UMMA_FLAGS");
-    return v ? atoi(v) & 7 : 6;  // late release + pipelined decode by default (Qwen3 gate_up 477 -> 420 us)
+#ifdef E4B_TRACE
+    return v ? atoi(v) & 127 : 6;
+#else
+    return v ? atoi(v) & 7 : 6;
+#endif  // late release + pipelined decode by default (Qwen3 gate_up 477 -> 420 us)
   }();
   UmmaArgs ua = u;
   ua.nf4_regs = nf4_regs;
+  if constexpr (FMT == E4B_FMT_NF4 && GROUPS == 2) {
+    // E4B_UMMA_PAIR=1: clusters of two CTAs with tcgen05.mma.cta_group::2 (M = 256 tokens)
+    static const bool pair = [] {
+      const char* v = getenv("E4B_UMMA_PAIR");
+      return v && atoi(v) != 0;
+    }();
+    if (pair) {
+      auto kern = nf4_umma_kernel<OutT, GROUPS, FMT, true>;
+      static int pair_clusters[64] = {0};
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.blockDim = dim3(kFwdThreads);
+      cfg.dynamicSmemBytes = Smem::total;
+      cfg.stream = s;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (!pair_clusters[dev & 63]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total) != cudaSuccess)
+          return E4B_ERR_CUDA;
+        cfg.gridDim = dim3(2 * (sm_count[dev & 63] / 2));
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) return E4B_ERR_CUDA;
+        pair_clusters[dev & 63] = n;
+      }
+      int clusters = pair_clusters[dev & 63];
+      if (bound < clusters) clusters = bound;  // token-pair tiles never outnumber the tiles
+      cfg.gridDim = dim3(2 * clusters);
+#ifdef E4B_TRACE
+      fprintf(stderr, "[umma pair] clusters %d (max active %d), grid %d\n", clusters, pair_clusters[dev & 63], 2 * clusters);
+#endif
+      if (cudaLaunchKernelEx(&cfg, kern, ua, wmap, bmap, lmap) != cudaSuccess) return E4B_ERR_CUDA;
+      return launch_status();
+    }
+  }
   nf4_umma_kernel<OutT, GROUPS, FMT><<<grid, kFwdThreads, Smem::total, s>>>(ua, wmap, bmap, lmap);
   return launch_status();
 }

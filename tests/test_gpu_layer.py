@@ -268,3 +268,47 @@ def test_compat_gemm_4bit_grouped_drives_reference_shape(e4b):
     ref = torch.cat([a[int(off[e]):int(off[e + 1])].cpu().float() @ Wf[e].t() for e in range(E)])
     mx, mean = M.rel_errors(up.cpu(), ref)
     assert mx <= MAX_REL and mean <= MEAN_REL
+
+
+_PAIR_SCRIPT = r"""
+import importlib, sys, torch
+sys.path.insert(0, sys.argv[1])
+e4b = importlib.import_module("experts4bit-qlora_b200")
+E, H, I, k, T, r = 128, 2048, 768, 8, 700, 16
+g = torch.Generator(device="cuda").manual_seed(11)
+base = e4b.Experts4bit.from_float((torch.randn(E, 2 * I, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16),
+                                  (torch.randn(E, H, I, generator=g, device="cuda") * 0.02).to(torch.bfloat16))
+lm = e4b.ExpertsLoRA(base, r=r, alpha=16, dtype=torch.bfloat16).to("cuda").eval()
+with torch.no_grad():
+    for p in (lm.gate_up_lora_A, lm.gate_up_lora_B, lm.down_lora_A, lm.down_lora_B):
+        p.copy_(torch.randn(p.shape, generator=g, device="cuda") * 0.01)
+x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+w, idx = torch.topk(torch.softmax(torch.randn(T, E, generator=g, device="cuda"), -1), k)
+assert e4b.enable_fast(lm) == 1
+with torch.no_grad():
+    out = lm(x, idx, w)
+torch.save(out.cpu(), sys.argv[2])
+"""
+
+
+def test_cta_pair_tensor_core_path_matches_single_cta(tmp_path):
+    """E4B_UMMA_PAIR=1 runs the NF4 tensor-core GEMMs (gate_up with SwiGLU and the LoRA step,
+    down with 256 features per tile) as clusters of two CTAs with tcgen05.mma.cta_group::2. Same
+    decoded operands and K order as the one-CTA kernel; the layer outputs agree to the layer bar
+    against each other (the one-CTA path is anchored to fp32 by the tests above)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = tmp_path / "pair.py"
+    script.write_text(_PAIR_SCRIPT)
+    outs = []
+    for pair in ("0", "1"):
+        path = tmp_path / f"out{pair}.pt"
+        env = dict(os.environ, E4B_UMMA_PAIR=pair)
+        res = subprocess.run([sys.executable, str(script), root, str(path)], env=env, capture_output=True, text=True,
+                             timeout=600)
+        assert res.returncode == 0, res.stderr[-2000:]
+        outs.append(torch.load(path).float())
+    mx, mean = M.rel_errors(outs[1], outs[0])
+    assert mx <= 1e-3 and mean <= 1e-4, (mx, mean)
