@@ -25,6 +25,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <new>
 
 #include "convert.cuh"
 #include "decode_layer.cuh"
@@ -1307,7 +1308,36 @@ static e4b_status launch_slice(const DecodeArgs& a, cudaStream_t s) {
     }
   }
   CUtensorMap gw, ga, dw, da;
+  // The four maps depend only on the stacks' addresses and the layer geometry: a small cache per
+  // device (a model's layers, round robin) saves their encoding on every decode step.
+  struct MapSet {
+    const void* p[4];
+    int E, H, I;
+    CUtensorMap m[4];
+  };
+  constexpr int kMapSets = 64;
+  static MapSet* map_cache[64] = {nullptr};
+  static int map_next[64] = {0};
+  const void* keys[4] = {a.gu_packed, a.gu_absmax, a.dn_packed, a.dn_absmax};
+  bool cached = false;
+  {
+    std::lock_guard<std::mutex> lk(g_dl_mu);
+    if (MapSet* c = map_cache[dev]) {
+      for (int i = 0; i < kMapSets && !cached; ++i) {
+        const MapSet& ms = c[i];
+        if (ms.p[0] == keys[0] && ms.p[1] == keys[1] && ms.p[2] == keys[2] && ms.p[3] == keys[3] && ms.E == a.E &&
+            ms.H == a.H && ms.I == a.I) {
+          gw = ms.m[0];
+          ga = ms.m[1];
+          dw = ms.m[2];
+          da = ms.m[3];
+          cached = true;
+        }
+      }
+    }
+  }
   const cuuint64_t gu_rows = (cuuint64_t)a.E * 2 * a.I, dn_rows = (cuuint64_t)a.E * a.H;
+  if (!cached) {
   {  // gate_up packed as [lines (H / 256)][rows][128 B]; a box is 2 lines x 64 rows
     const cuuint64_t dims[3] = {128, gu_rows, (cuuint64_t)(a.H / 256)};
     const cuuint64_t str[2] = {(cuuint64_t)(a.H / 2), 128};
@@ -1335,6 +1365,21 @@ static e4b_status launch_slice(const DecodeArgs& a, cudaStream_t s) {
     const cuuint32_t box[2] = {4, 256};
     if (!encode_tiled(&da, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.dn_absmax, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
       return E4B_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lk(g_dl_mu);
+  if (!map_cache[dev]) map_cache[dev] = new (std::nothrow) MapSet[kMapSets]();
+  if (MapSet* c = map_cache[dev]) {
+    MapSet& ms = c[map_next[dev]];
+    map_next[dev] = (map_next[dev] + 1) % kMapSets;
+    for (int i = 0; i < 4; ++i) ms.p[i] = keys[i];
+    ms.E = a.E;
+    ms.H = a.H;
+    ms.I = a.I;
+    ms.m[0] = gw;
+    ms.m[1] = ga;
+    ms.m[2] = dw;
+    ms.m[3] = da;
+  }
   }
   // The fused router runs over the whole grid through global scratch, or (on request) in clusters
   // of 4 (or 2) CTAs when a grid of co-resident clusters covers (nearly) every SM and the device

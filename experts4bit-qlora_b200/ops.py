@@ -97,7 +97,9 @@ def router_topk(x: torch.Tensor, router_weight: torch.Tensor, k: int, kind: int 
     w = torch.empty(T, k, dtype=torch.float32, device=dev)
     logits = torch.empty(T, E, dtype=torch.float32, device=dev) if return_logits else None
     L = N.lib()
-    nbytes = L.e4b_router_workspace_bytes(T, E)
+    nbytes = _ROUTER_WS.get((T, E))
+    if nbytes is None:
+        nbytes = _ROUTER_WS[(T, E)] = L.e4b_router_workspace_bytes(T, E)
     ws = N.workspaces.get(dev, nbytes, "router")
     N.check(L.e4b_router_topk(x.data_ptr(), N.dtype_code(x.dtype), wr.data_ptr(), N.dtype_code(wr.dtype), T, H, E, k,
                               kind, int(norm_topk_prob), N.ptr(logits), idx.data_ptr(), w.data_ptr(),
@@ -315,6 +317,8 @@ def _expect(t: torch.Tensor, what: str, device, dtypes, numel: int | None = None
 
 
 _VALIDATED: dict = {}  # stacks already checked for this geometry (bounded; keys hold no tensors)
+_DESCS: dict = {}  # layer descriptor per call signature (bounded)
+_ROUTER_WS: dict = {}  # router workspace size per (T, E)
 
 
 def _check_layer(dev, E, H, I, has_gate, gate_up_packed, gate_up_absmax, down_packed, down_absmax, weight_format,
@@ -406,8 +410,17 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     if out is None:
         out = torch.empty(T, H, dtype=out_dtype, device=hidden.device)
     _expect(out, "out", dev, (out_dtype,), shape=(T, H))
-    d = MoeDesc_from(num_experts, H, intermediate, k, T, has_gate, hidden.dtype, w.dtype, out_dtype, lora,
-                     weight_format)
+    routed = int(expert_map.numel()) if expert_map is not None else 0
+    sig = (num_experts, H, intermediate, k, T, bool(has_gate), hidden.dtype, w.dtype, out_dtype, weight_format,
+           routed, None if lora is None else (lora[0].shape[1], lora[0].dtype, float(lora[4])))
+    d = _DESCS.get(sig)  # the descriptor is only read by the library
+    if d is None:
+        d = MoeDesc_from(num_experts, H, intermediate, k, T, has_gate, hidden.dtype, w.dtype, out_dtype, lora,
+                         weight_format)
+        d.routed_experts = routed
+        if len(_DESCS) > 4096:
+            _DESCS.clear()
+        _DESCS[sig] = d
     t = N.MoeTensors()
     t.hidden, t.topk_idx, t.topk_w = hidden.data_ptr(), idx.data_ptr(), w.data_ptr()
     t.gate_up_packed, t.gate_up_absmax = gate_up_packed.data_ptr(), gate_up_absmax.data_ptr()
@@ -421,10 +434,9 @@ def moe_forward(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     t.out = out.data_ptr()
     if expert_map is not None:
         _expect(expert_map, "expert_map", dev, (torch.int32,))
-        d.routed_experts = int(expert_map.numel())
         t.expert_map = expert_map.data_ptr()
     L = N.lib()
-    nbytes = L.e4b_moe_workspace_bytes(ctypes.byref(d))
+    nbytes = L.e4b_moe_workspace_bytes(ctypes.byref(d))  # depends on the decode-kernel selection too
     if nbytes == 0:
         raise ValueError("invalid expert-layer geometry for the fused kernel")
     ws = workspace if workspace is not None else N.workspaces.get(hidden.device, nbytes, "moe")
