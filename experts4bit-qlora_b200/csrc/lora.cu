@@ -6,6 +6,8 @@
 // A CTA takes 64 rows of one expert; each of its 4 warps computes 16 rows x all
 // ranks with mma.sync m16n8k16 (fp16 operands, fp32 accumulation), the 64-wide K
 // chunks of the rows and of A[e] staged in padded shared memory.
+#include <cstdlib>
+
 #include "lora.cuh"
 
 namespace e4b {
@@ -112,10 +114,169 @@ __global__ void __launch_bounds__(128) lora_a_kernel(LoraAArgs g) {
   }
 }
 
+namespace {
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {  // bytes 0: zero fill
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Eight adapter values (lora dtype) from 16-byte-aligned storage as fp16, rounded like
+// __float2half_rn(load_as_f32(...)) element by element.
+__device__ __forceinline__ uint4 lora8_as_f16(const void* base, int dtype, int64_t i) {
+  uint32_t o[4];
+  if (dtype == E4B_F32) {
+    const float4 lo = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + i);
+    const float4 hi = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + i + 4);
+    o[0] = pack2<__half>(lo.x, lo.y);
+    o[1] = pack2<__half>(lo.z, lo.w);
+    o[2] = pack2<__half>(hi.x, hi.y);
+    o[3] = pack2<__half>(hi.z, hi.w);
+  } else {
+    const uint4 r = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + i);
+    if (dtype == E4B_F16) return r;
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = pack2<__half>(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+}  // namespace
+
+// The same products as lora_a_kernel (same fragments, same K order, so bit-identical) for ranks
+// <= 16 with 128-wide K chunks double-buffered: the next chunk's activation rows (cp.async) and
+// adapter rows (16-byte loads, converted in registers) are in flight while the tensor cores work
+// on this chunk; one barrier per chunk.
+template <int NR>
+__global__ void __launch_bounds__(128) lora_a_pipe_kernel(LoraAArgs g) {
+  constexpr int kKc = 128;
+  constexpr int kPitch = kKc + 8;  // 272-byte rows: 16-byte aligned, conflict-free fragment reads
+  __shared__ __align__(16) __half xs[2][kLoraRows][kPitch];
+  __shared__ __align__(16) __half as[2][8 * NR][kPitch];
+  const int t = blockIdx.x;
+  if (t >= g.tile_start[g.E]) return;
+  int lo = 0, hi = g.E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (g.tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  const int e = lo;
+  const int r0 = g.offsets[e] + (t - g.tile_start[e]) * kLoraRows;
+  const int rend = g.offsets[e + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, q = lane & 3;
+  const int nch = (g.K + kKc - 1) / kKc;
+  // this thread's activation rows (source rows fixed over the chunks)
+  int64_t srow[kLoraRows * (kKc / 8) / 128];
+#pragma unroll
+  for (int u = 0; u < kLoraRows * (kKc / 8) / 128; ++u) {
+    const int r = r0 + ((threadIdx.x + 128 * u) >> 4);
+    srow[u] = r < rend ? (g.a_rows ? (int64_t)g.a_rows[r] : (int64_t)r) : -1;
+  }
+  auto issue_x = [&](int c, int buf) {
+    const int k0 = c * kKc;
+#pragma unroll
+    for (int u = 0; u < kLoraRows * (kKc / 8) / 128; ++u) {
+      const int i = threadIdx.x + 128 * u, rr = i >> 4, v = i & 15;
+      const bool ok = srow[u] >= 0 && k0 + v * 8 < g.K;
+      const __half* src = ok ? g.a + srow[u] * g.K + k0 + v * 8 : g.a;
+      cp_async16(&xs[buf][rr][v * 8], src, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  auto load_a = [&](int c, uint4 (&av)[NR]) {
+    const int k0 = c * kKc;
+#pragma unroll
+    for (int u = 0; u < NR; ++u) {
+      const int i = threadIdx.x + 128 * u, j = i >> 4, v = i & 15;
+      av[u] = (j < g.rank && k0 + v * 8 < g.K)
+                  ? lora8_as_f16(g.loraA, g.lora_dtype, ((int64_t)e * g.rank + j) * g.K + k0 + v * 8)
+                  : make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto store_a = [&](int buf, const uint4 (&av)[NR]) {
+#pragma unroll
+    for (int u = 0; u < NR; ++u) {
+      const int i = threadIdx.x + 128 * u;
+      *reinterpret_cast<uint4*>(&as[buf][i >> 4][(i & 15) * 8]) = av[u];
+    }
+  };
+  float acc[NR][4];
+#pragma unroll
+  for (int n = 0; n < NR; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+  uint4 av[NR];
+  issue_x(0, 0);
+  load_a(0, av);
+  store_a(0, av);
+  for (int c = 0; c < nch; ++c) {
+    const int buf = c & 1;
+    cp_async_wait_all();
+    __syncthreads();  // chunk c visible; every warp is done with chunk c - 1 (the other buffer)
+    if (c + 1 < nch) {
+      issue_x(c + 1, buf ^ 1);
+      load_a(c + 1, av);
+    }
+#pragma unroll
+    for (int ks = 0; ks < kKc; ks += 16) {
+      const int rw = warp * 16 + gq;
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw][ks + 2 * q]);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw + 8][ks + 2 * q]);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw][ks + 2 * q + 8]);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw + 8][ks + 2 * q + 8]);
+#pragma unroll
+      for (int n = 0; n < NR; ++n) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&as[buf][n * 8 + gq][ks + 2 * q]);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&as[buf][n * 8 + gq][ks + 2 * q + 8]);
+        mma_f16(acc[n], a0, a1, a2, a3, b0, b1);
+      }
+    }
+    if (c + 1 < nch) store_a(buf ^ 1, av);  // nobody reads that buffer until the next barrier
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = r0 + warp * 16 + gq + 8 * h;
+    if (r >= rend) continue;
+    if (g.xa16) {
+#pragma unroll
+      for (int n = 0; n < NR; ++n) {
+        const int j = n * 8 + 2 * q;
+        *reinterpret_cast<__half2*>(g.xa16 + (int64_t)r * 64 + j) =
+            __floats2half2_rn(j < g.rank ? g.scaling * acc[n][2 * h] : 0.f,
+                              j + 1 < g.rank ? g.scaling * acc[n][2 * h + 1] : 0.f);
+      }
+      if (NR == 1) *reinterpret_cast<__half2*>(g.xa16 + (int64_t)r * 64 + 8 + 2 * q) = __floats2half2_rn(0.f, 0.f);
+      continue;
+    }
+    float sc = g.scaling;
+    if (g.a_scale) sc *= g.a_scale[g.a_rows ? g.a_rows[r] : r];
+#pragma unroll
+    for (int n = 0; n < NR; ++n)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int j = n * 8 + 2 * q + c;
+        if (j < g.rank) g.xa[(int64_t)r * g.rank + j] = sc * acc[n][2 * h + c];
+      }
+  }
+}
+
 e4b_status launch_lora_a(const LoraAArgs& g, cudaStream_t s) {
   if (g.max_tiles <= 0) return E4B_OK;
   if (g.K % 64) return E4B_ERR_UNSUPPORTED;
   const int nr = (g.rank + 7) / 8;
+  // pipelined kernel: ranks <= 16, 16-byte aligned activation and adapter storage (E4B_LORA_A_PIPE=0: off)
+  static const bool pipe = [] {
+    const char* v = getenv("E4B_LORA_A_PIPE");
+    return !(v && v[0] == '0');
+  }();
+  if (pipe && nr <= 2 && !((uintptr_t)g.a & 15) && !((uintptr_t)g.loraA & 15)) {
+    if (nr <= 1)
+      lora_a_pipe_kernel<1><<<g.max_tiles, 128, 0, s>>>(g);
+    else
+      lora_a_pipe_kernel<2><<<g.max_tiles, 128, 0, s>>>(g);
+    return launch_status();
+  }
   if (nr <= 1)
     lora_a_kernel<1><<<g.max_tiles, 128, 0, s>>>(g);
   else if (nr <= 2)

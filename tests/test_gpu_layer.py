@@ -312,3 +312,24 @@ def test_cta_pair_tensor_core_path_matches_single_cta(tmp_path):
         outs.append(torch.load(path).float())
     mx, mean = M.rel_errors(outs[1], outs[0])
     assert mx <= 1e-3 and mean <= 1e-4, (mx, mean)
+
+
+def test_pipelined_lora_a_prepass_is_bit_identical(tmp_path):
+    """The LoRA-A pre-pass for ranks <= 16 double-buffers its K chunks (cp.async rows, vector
+    adapter loads); the tensor-core fragments and their K order are those of the one-buffer
+    kernel (E4B_LORA_A_PIPE=0), so the layer output is identical bit for bit."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = tmp_path / "lora_a.py"
+    script.write_text(_PAIR_SCRIPT)
+    outs = []
+    for pipe in ("0", "1"):
+        path = tmp_path / f"out{pipe}.pt"
+        env = dict(os.environ, E4B_LORA_A_PIPE=pipe)
+        res = subprocess.run([sys.executable, str(script), root, str(path)], env=env, capture_output=True, text=True,
+                             timeout=600)
+        assert res.returncode == 0, res.stderr[-2000:]
+        outs.append(torch.load(path))
+    assert torch.equal(outs[0], outs[1])
