@@ -24,25 +24,45 @@ __device__ __forceinline__ void load8(const void* src, int dtype, int64_t i, flo
   }
 }
 
-// Rows of a 16-bit (bf16/fp16) source, K % 8 == 0, one warp per row. Up to 8
-// 16-byte vectors per lane stay in registers so the row is read once with all
-// loads in flight (longer rows take a second, cached read).
+__device__ __forceinline__ void expand8(uint4 r, int dtype, float (&v)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (dtype == E4B_BF16) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
+// Rows of a 16-bit (bf16/fp16) source, K % 8 == 0, one warp per row. Up to 8 16-byte vectors per
+// lane stay in registers as loaded (16-bit, 32 registers) so the row is read once with all loads
+// in flight and the kernel keeps a high occupancy (longer rows take a second, cached read); they
+// are expanded to fp32 twice, for the row maximum and for the scaled store.
 __device__ __forceinline__ void convert_rows_to_f16(const void* src, int src_dtype, __half* dst, float* scale,
                                                     int rows, int K, int first_warp, int num_warps) {
   const int lane = threadIdx.x & 31;
   const int nv = K / 8;
   for (int r = first_warp; r < rows; r += num_warps) {
     const int64_t base = (int64_t)r * K;
-    float v[8][8];
+    uint4 raw[8];
     float m = 0.f;
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int c = lane + 32 * u;
-      if (c < nv) {
-        load8(src, src_dtype, base + c * 8, v[u]);
+      raw[u] = c < nv ? *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(src) + (base + c * 8) * 2)
+                      : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[u][j]));
-      }
+    for (int u = 0; u < 8; ++u) {
+      float v[8];
+      expand8(raw[u], src_dtype, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
     }
     for (int c = lane + 256; c < nv; c += 32) {
       float t[8];
@@ -68,7 +88,11 @@ __device__ __forceinline__ void convert_rows_to_f16(const void* src, int src_dty
     };
 #pragma unroll
     for (int u = 0; u < 8; ++u)
-      if (lane + 32 * u < nv) put(lane + 32 * u, v[u]);
+      if (lane + 32 * u < nv) {
+        float v[8];
+        expand8(raw[u], src_dtype, v);
+        put(lane + 32 * u, v);
+      }
     for (int c = lane + 256; c < nv; c += 32) {
       float t[8];
       load8(src, src_dtype, base + c * 8, t);
