@@ -231,10 +231,15 @@ __global__ void __launch_bounds__(1024) permute_count_kernel(PermuteArgs a, int 
   if (seg < nseg) {
     const int s0 = seg * kSeg, s1 = min(n, s0 + kSeg);
     const unsigned lt = (1u << lane) - 1u;
-    for (int base = s0; base < s1; base += 32) {
+    int64_t ids[kSeg / 32];  // the segment's expert ids, all loads in flight at once
+#pragma unroll
+    for (int j = 0; j < kSeg / 32; ++j) ids[j] = s0 + 32 * j + lane < s1 ? a.topk_idx[s0 + 32 * j + lane] : 0;
+#pragma unroll
+    for (int j = 0; j < kSeg / 32; ++j) {
+      const int base = s0 + 32 * j;
       const int i = base + lane;
       const bool valid = i < s1;
-      const int e = valid ? stack_expert(a.topk_idx[i], a.emap, a.routed, E, a.err, true) : -1;
+      const int e = valid ? stack_expert(ids[j], a.emap, a.routed, E, a.err, true) : -1;
       const unsigned act = __ballot_sync(0xffffffffu, valid);
       const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
       if (valid && (peers & lt) == 0) wc[warp * E + e] += __popc(peers);
@@ -252,19 +257,35 @@ __global__ void __launch_bounds__(1024) permute_count_kernel(PermuteArgs a, int 
 __global__ void __launch_bounds__(1024) permute_scan_kernel(PermuteArgs a, int nseg) {
   __shared__ int s_scan[32];
   const int E = a.E, n = a.T * a.k, e = threadIdx.x;
+  // Prefix over segments, written back in place. Sixteen segments' counts are loaded before any
+  // of their stores, so one memory round trip covers sixteen segments instead of one.
+  constexpr int kB = 16;
   int c = 0;
-  if (e < E) {  // prefix over segments, written back in place
-    for (int sg = 0; sg < nseg; ++sg) {
-      const int v = a.seg_scratch[(int64_t)sg * E + e];
-      a.seg_scratch[(int64_t)sg * E + e] = c;
-      c += v;
+  if (e < E) {
+    for (int sg0 = 0; sg0 < nseg; sg0 += kB) {
+      int v[kB];
+#pragma unroll
+      for (int j = 0; j < kB; ++j) v[j] = sg0 + j < nseg ? a.seg_scratch[(int64_t)(sg0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < kB; ++j)
+        if (sg0 + j < nseg) {
+          a.seg_scratch[(int64_t)(sg0 + j) * E + e] = c;
+          c += v[j];
+        }
     }
   }
   int tot;
   const int off = block_exclusive_scan(c, s_scan, &tot);
   if (e < E) {
     a.offsets[e] = off;
-    for (int sg = 0; sg < nseg; ++sg) a.seg_scratch[(int64_t)sg * E + e] += off;
+    for (int sg0 = 0; sg0 < nseg; sg0 += kB) {
+      int v[kB];
+#pragma unroll
+      for (int j = 0; j < kB; ++j) v[j] = sg0 + j < nseg ? a.seg_scratch[(int64_t)(sg0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < kB; ++j)
+        if (sg0 + j < nseg) a.seg_scratch[(int64_t)(sg0 + j) * E + e] = v[j] + off;
+    }
   }
   if (threadIdx.x == 0) a.offsets[E] = n;
   const int pos = block_exclusive_scan(c > 0 ? 1 : 0, s_scan, &tot);
@@ -294,10 +315,15 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteArgs a, int 
   if (seg >= nseg) return;
   const int s0 = seg * kSeg, s1 = min(n, s0 + kSeg);
   const unsigned lt = (1u << lane) - 1u;
-  for (int base = s0; base < s1; base += 32) {
+  int64_t ids[kSeg / 32];
+#pragma unroll
+  for (int j = 0; j < kSeg / 32; ++j) ids[j] = s0 + 32 * j + lane < s1 ? a.topk_idx[s0 + 32 * j + lane] : 0;
+#pragma unroll
+  for (int j = 0; j < kSeg / 32; ++j) {
+    const int base = s0 + 32 * j;
     const int i = base + lane;
     const bool valid = i < s1;
-    const int e = valid ? stack_expert(a.topk_idx[i], a.emap, a.routed, E, a.err, false) : -1;
+    const int e = valid ? stack_expert(ids[j], a.emap, a.routed, E, a.err, false) : -1;
     const unsigned act = __ballot_sync(0xffffffffu, valid);
     const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
     int pos = 0;
