@@ -10,6 +10,8 @@
 // has a fixed order, so results repeat bit for bit.
 #include <type_traits>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace e4b {
@@ -19,12 +21,34 @@ constexpr int kRk = 16;     // rank slots per row (ranks below 16 leave the rest
 constexpr int kTileR = 32;  // rows per tile
 constexpr int kKc = 256;    // K elements per staged chunk of M
 
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int bytes) {  // bytes 0: zero fill
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(bytes)
+               : "memory");
+}
+
+// Shared memory of rank_down_kernel: two stages of the M chunk (fp32) and of the tile's X rows.
+template <typename TX>
+constexpr int rank_down_smem() {
+  return 2 * kRk * kKc * 4 + 2 * kTileR * kKc * (int)sizeof(TX);
+}
+
 template <typename TX>
 __global__ void __launch_bounds__(256) rank_down_kernel(const TX* __restrict__ X, int ldx, const float* __restrict__ M,
                                                         int64_t sE, int64_t sj, int64_t sk, int rk, int K,
                                                         const int* __restrict__ tiles, float scale,
                                                         float* __restrict__ Y) {
-  __shared__ __align__(16) float ms[kRk][kKc];
+  // Double-buffered over K chunks: the next chunk's M values and X rows are copied into shared
+  // memory by cp.async while this chunk's FMAs run, one barrier per chunk. Every lane accumulates
+  // its k in the same order as a one-buffer loop.
+  extern __shared__ __align__(16) char smem_raw[];
+  float (*ms)[kRk][kKc] = reinterpret_cast<float (*)[kRk][kKc]>(smem_raw);
+  TX (*xs)[kTileR][kKc] = reinterpret_cast<TX (*)[kTileR][kKc]>(smem_raw + 2 * kRk * kKc * 4);
   const int e = tiles[blockIdx.x * 3], row0 = tiles[blockIdx.x * 3 + 1], nrows = tiles[blockIdx.x * 3 + 2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float acc[4][kRk];
@@ -33,41 +57,48 @@ __global__ void __launch_bounds__(256) rank_down_kernel(const TX* __restrict__ X
 #pragma unroll
     for (int j = 0; j < kRk; ++j) acc[r][j] = 0.f;
   const float* Me = M + (int64_t)e * sE;
-  for (int kc = 0; kc < K; kc += kKc) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kRk * kKc; i += blockDim.x) {
-      const int j = i / kKc, kk = i - j * kKc;
-      ms[j][kk] = (j < rk && kc + kk < K) ? Me[j * sj + (int64_t)(kc + kk) * sk] : 0.f;
+  const bool m_vec = sk == 1 && (sj & 3) == 0 && ((uintptr_t)Me & 15) == 0;  // 16-byte M copies
+  constexpr int kXv = kKc * (int)sizeof(TX) / 16;                           // 16-byte vectors per X row
+  auto issue = [&](int kc, int buf) {
+    if (m_vec) {
+      for (int i = threadIdx.x; i < kRk * kKc / 4; i += 256) {
+        const int j = i / (kKc / 4), c = (i - j * (kKc / 4)) * 4;
+        const bool ok = j < rk && kc + c < K;  // K % 8 == 0: a vector is all in or all out
+        cp_async16(&ms[buf][j][c], ok ? Me + j * sj + kc + c : Me, ok ? 16 : 0);
+      }
+    } else {
+      for (int i = threadIdx.x; i < kRk * kKc; i += 256) {
+        const int j = i / kKc, c = i - j * kKc;
+        const bool ok = j < rk && kc + c < K;
+        cp_async4(&ms[buf][j][c], ok ? Me + j * sj + (int64_t)(kc + c) * sk : Me, ok ? 4 : 0);
+      }
     }
-    __syncthreads();
-    // lane owns 8 consecutive k of the chunk: one 16-byte (two for fp32) load per row
-    const int kk = lane * 8;
+    for (int i = threadIdx.x; i < kTileR * kXv; i += 256) {
+      const int rr = i / kXv, v = i - rr * kXv;
+      const int c = v * (16 / (int)sizeof(TX));
+      const bool ok = rr < nrows && kc + c < K;
+      cp_async16(&xs[buf][rr][c], ok ? X + (int64_t)(row0 + rr) * ldx + kc + c : X, ok ? 16 : 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  const int kk = lane * 8;  // lane owns 8 consecutive k of a chunk
+  issue(0, 0);
+  for (int kc = 0, buf = 0; kc < K; kc += kKc, buf ^= 1) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // chunk kc visible; every thread is done with the other buffer
+    if (kc + kKc < K) issue(kc + kKc, buf ^ 1);
     if (kc + kk < K) {
       float xv[4][8];
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int rr = warp * 4 + r;
-        if (rr < nrows) {
-          const TX* xp = X + (int64_t)(row0 + rr) * ldx + kc + kk;
-          if (sizeof(TX) == 2) {
-            const uint4 u = *reinterpret_cast<const uint4*>(xp);
-            const TX* e = reinterpret_cast<const TX*>(&u);
+        const TX* xp = &xs[buf][warp * 4 + r][kk];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xv[r][i] = to_f32(e[i]);
-          } else {
-            const float4 u0 = reinterpret_cast<const float4*>(xp)[0], u1 = reinterpret_cast<const float4*>(xp)[1];
-            xv[r][0] = u0.x; xv[r][1] = u0.y; xv[r][2] = u0.z; xv[r][3] = u0.w;
-            xv[r][4] = u1.x; xv[r][5] = u1.y; xv[r][6] = u1.z; xv[r][7] = u1.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xv[r][i] = 0.f;
-        }
+        for (int i = 0; i < 8; ++i) xv[r][i] = to_f32(xp[i]);
       }
 #pragma unroll
       for (int j = 0; j < kRk; ++j) {
-        const float4 m0 = *reinterpret_cast<const float4*>(&ms[j][kk]);
-        const float4 m1 = *reinterpret_cast<const float4*>(&ms[j][kk + 4]);
+        const float4 m0 = *reinterpret_cast<const float4*>(&ms[buf][j][kk]);
+        const float4 m1 = *reinterpret_cast<const float4*>(&ms[buf][j][kk + 4]);
         const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -211,16 +242,30 @@ extern "C" e4b_status e4b_lora_rank_down(const void* X, int x_dtype, int ldx, co
   if (!X || !M || !tiles || !Y) return E4B_ERR_INVALID_ARG;
   if (K % 8 || ldx % 8 || !aligned16(X)) return E4B_ERR_UNSUPPORTED;  // 8-element row loads
   cudaStream_t s = (cudaStream_t)stream;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {  // above 48 KB of shared memory (per process; the attribute is per function)
+    cudaError_t a = cudaFuncSetAttribute(rank_down_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         rank_down_smem<__nv_bfloat16>());
+    cudaError_t b = cudaFuncSetAttribute(rank_down_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         rank_down_smem<__half>());
+    cudaError_t c = cudaFuncSetAttribute(rank_down_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         rank_down_smem<float>());
+    attr_err = a != cudaSuccess ? a : b != cudaSuccess ? b : c;
+  });
+  if (attr_err != cudaSuccess) return E4B_ERR_CUDA;
   switch (x_dtype) {
     case E4B_BF16:
-      rank_down_kernel<__nv_bfloat16><<<ntiles, 256, 0, s>>>((const __nv_bfloat16*)X, ldx, M, sE, sj, sk, rk, K, tiles,
-                                                             scale, Y);
+      rank_down_kernel<__nv_bfloat16><<<ntiles, 256, rank_down_smem<__nv_bfloat16>(), s>>>(
+          (const __nv_bfloat16*)X, ldx, M, sE, sj, sk, rk, K, tiles, scale, Y);
       break;
     case E4B_F16:
-      rank_down_kernel<__half><<<ntiles, 256, 0, s>>>((const __half*)X, ldx, M, sE, sj, sk, rk, K, tiles, scale, Y);
+      rank_down_kernel<__half><<<ntiles, 256, rank_down_smem<__half>(), s>>>((const __half*)X, ldx, M, sE, sj, sk, rk,
+                                                                            K, tiles, scale, Y);
       break;
     case E4B_F32:
-      rank_down_kernel<float><<<ntiles, 256, 0, s>>>((const float*)X, ldx, M, sE, sj, sk, rk, K, tiles, scale, Y);
+      rank_down_kernel<float><<<ntiles, 256, rank_down_smem<float>(), s>>>((const float*)X, ldx, M, sE, sj, sk, rk, K,
+                                                                          tiles, scale, Y);
       break;
     default: return E4B_ERR_UNSUPPORTED;
   }
