@@ -10,6 +10,7 @@
 // has a fixed order, so results repeat bit for bit.
 #include <type_traits>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -117,6 +118,112 @@ __global__ void __launch_bounds__(256) rank_down_kernel(const TX* __restrict__ X
       for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane == j && j < rk && rr < nrows) Y[(int64_t)(row0 + rr) * rk + j] = v * scale;
     }
+  }
+}
+
+// bf16 rows on the tensor cores: M (fp32) is split per chunk into three bf16 parts
+// (hi = bf16(M), mid = bf16(M - hi), lo = bf16(M - hi - mid), which sum to M within about 2^-24
+// relative), and each part multiplies the bf16 rows exactly (mma.sync m16n8k16, fp32
+// accumulation), so Y keeps fp32 accuracy at a fraction of the CUDA-core cost. Two warps per
+// 32-row tile, 16 rows each, all 16 rank slots (two n8 tiles); 128-wide K chunks of X arrive by
+// cp.async and of M by registers, both double-buffered with one barrier per chunk.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+constexpr int kMc = 128;         // K per chunk of the tensor-core kernel
+constexpr int kMp = kMc + 8;     // padded row (halves): conflict-free fragment reads
+constexpr int kMPer = kRk * kMc / 64;  // M values per thread per chunk
+
+__global__ void __launch_bounds__(64) rank_down_mma_kernel(const __nv_bfloat16* __restrict__ X, int ldx,
+                                                           const float* __restrict__ M, int64_t sE, int64_t sj,
+                                                           int64_t sk, int rk, int K, const int* __restrict__ tiles,
+                                                           float scale, float* __restrict__ Y) {
+  __shared__ __align__(16) __nv_bfloat16 xs[2][kTileR][kMp];
+  __shared__ __align__(16) __nv_bfloat16 m3[2][3][kRk][kMp];
+  const int e = tiles[blockIdx.x * 3], row0 = tiles[blockIdx.x * 3 + 1], nrows = tiles[blockIdx.x * 3 + 2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const float* Me = M + (int64_t)e * sE;
+  float mr[kMPer];
+  auto issue_x = [&](int kc, int buf) {
+#pragma unroll
+    for (int u = 0; u < kTileR * (kMc / 8) / 64; ++u) {
+      const int i = threadIdx.x + 64 * u, rr = i / (kMc / 8), c = (i % (kMc / 8)) * 8;
+      const bool ok = rr < nrows && kc + c < K;
+      cp_async16(&xs[buf][rr][c], ok ? X + (int64_t)(row0 + rr) * ldx + kc + c : X, ok ? 16 : 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  auto load_m = [&](int kc) {
+#pragma unroll
+    for (int u = 0; u < kMPer; ++u) {
+      const int i = threadIdx.x + 64 * u, j = i / kMc, c = i % kMc;
+      mr[u] = (j < rk && kc + c < K) ? Me[j * sj + (int64_t)(kc + c) * sk] : 0.f;
+    }
+  };
+  auto store_m = [&](int buf) {
+#pragma unroll
+    for (int u = 0; u < kMPer; ++u) {
+      const int i = threadIdx.x + 64 * u, j = i / kMc, c = i % kMc;
+      const float v = mr[u];
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const float r1 = v - __bfloat162float(hi);
+      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+      m3[buf][0][j][c] = hi;
+      m3[buf][1][j][c] = mid;
+      m3[buf][2][j][c] = lo;
+    }
+  };
+  float acc[2][4];
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+  issue_x(0, 0);
+  load_m(0);
+  store_m(0);
+  for (int kc = 0, buf = 0; kc < K; kc += kMc, buf ^= 1) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // chunk kc visible; both warps are done with the other buffers
+    const bool more = kc + kMc < K;
+    if (more) {
+      issue_x(kc + kMc, buf ^ 1);
+      load_m(kc + kMc);
+    }
+    const int rw = warp * 16 + g;
+#pragma unroll
+    for (int ks = 0; ks < kMc; ks += 16) {
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw][ks + 2 * q]);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw + 8][ks + 2 * q]);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw][ks + 2 * q + 8]);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(&xs[buf][rw + 8][ks + 2 * q + 8]);
+#pragma unroll
+      for (int p = 2; p >= 0; --p)  // smallest part first
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&m3[buf][p][n * 8 + g][ks + 2 * q]);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&m3[buf][p][n * 8 + g][ks + 2 * q + 8]);
+          mma_bf16(acc[n], a0, a1, a2, a3, b0, b1);
+        }
+    }
+    if (more) store_m(buf ^ 1);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int rr = warp * 16 + g + 8 * h;
+    if (rr >= nrows) continue;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int j = n * 8 + 2 * q + c;
+        if (j < rk) Y[(int64_t)(row0 + rr) * rk + j] = acc[n][2 * h + c] * scale;
+      }
   }
 }
 
@@ -254,6 +361,15 @@ extern "C" e4b_status e4b_lora_rank_down(const void* X, int x_dtype, int ldx, co
     attr_err = a != cudaSuccess ? a : b != cudaSuccess ? b : c;
   });
   if (attr_err != cudaSuccess) return E4B_ERR_CUDA;
+  // bf16 rows: the tensor-core kernel (E4B_RANK_DOWN_MMA=0: the fp32 CUDA-core kernel)
+  static const bool use_mma = [] {
+    const char* v = getenv("E4B_RANK_DOWN_MMA");
+    return !(v && v[0] == '0');
+  }();
+  if (x_dtype == E4B_BF16 && use_mma) {
+    rank_down_mma_kernel<<<ntiles, 64, 0, s>>>((const __nv_bfloat16*)X, ldx, M, sE, sj, sk, rk, K, tiles, scale, Y);
+    return launch_status();
+  }
   switch (x_dtype) {
     case E4B_BF16:
       rank_down_kernel<__nv_bfloat16><<<ntiles, 256, rank_down_smem<__nv_bfloat16>(), s>>>(
