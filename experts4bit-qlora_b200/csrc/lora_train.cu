@@ -336,6 +336,106 @@ __global__ void __launch_bounds__(256) outer_kernel(const TP* __restrict__ P, in
       if (j < rk) G[(int64_t)e * gE + (int64_t)a * ga + (int64_t)j * gj] = acc[j] * scale;
 }
 
+// bf16 P on the tensor cores: G[a][j] = sum over the segment's rows r of P[r][a] * Y[r][j], with Y
+// (fp32) split into three bf16 parts per chunk (as rank_down_mma_kernel splits M). A CTA of four
+// warps owns 64 columns a (16 per warp, the M = 16 of an m16n8k16 tile) and all 16 rank slots;
+// 32-row chunks of P arrive by cp.async (double-buffered), the A fragments (P transposed) come
+// from ldmatrix .trans, and Y's parts are stored transposed so the B fragments are 32-bit loads.
+constexpr int kOc = 32;      // rows per chunk
+constexpr int kOa = 64;      // columns per CTA
+constexpr int kOap = kOa + 8;
+constexpr int kOrp = kOc + 8;
+
+__global__ void __launch_bounds__(128) outer_mma_kernel(const __nv_bfloat16* __restrict__ P, int ldp, int A,
+                                                        const float* __restrict__ Y, int rk,
+                                                        const int* __restrict__ segs, float scale,
+                                                        float* __restrict__ G, int64_t gE, int64_t ga, int64_t gj) {
+  __shared__ __align__(16) __nv_bfloat16 ps[2][kOc][kOap];
+  __shared__ __align__(16) __nv_bfloat16 yt[2][3][kRk][kOrp];
+  const int e = segs[blockIdx.x * 3], row0 = segs[blockIdx.x * 3 + 1], nrows = segs[blockIdx.x * 3 + 2];
+  const int a0 = blockIdx.y * kOa;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  float yr[kOc * kRk / 128];
+  auto issue_p = [&](int r0, int buf) {
+#pragma unroll
+    for (int u = 0; u < kOc * (kOa / 8) / 128; ++u) {
+      const int i = threadIdx.x + 128 * u, rr = i / (kOa / 8), c = (i % (kOa / 8)) * 8;
+      const bool ok = r0 + rr < nrows;
+      cp_async16(&ps[buf][rr][c], ok ? P + (int64_t)(row0 + r0 + rr) * ldp + a0 + c : P, ok ? 16 : 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  auto load_y = [&](int r0) {
+#pragma unroll
+    for (int u = 0; u < kOc * kRk / 128; ++u) {
+      const int i = threadIdx.x + 128 * u, rr = i / kRk, j = i % kRk;
+      yr[u] = (r0 + rr < nrows && j < rk) ? Y[(int64_t)(row0 + r0 + rr) * rk + j] : 0.f;
+    }
+  };
+  auto store_y = [&](int buf) {
+#pragma unroll
+    for (int u = 0; u < kOc * kRk / 128; ++u) {
+      const int i = threadIdx.x + 128 * u, rr = i / kRk, j = i % kRk;
+      const float v = yr[u];
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const float r1 = v - __bfloat162float(hi);
+      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+      yt[buf][0][j][rr] = hi;
+      yt[buf][1][j][rr] = mid;
+      yt[buf][2][j][rr] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+    }
+  };
+  float acc[2][4];
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+  issue_p(0, 0);
+  load_y(0);
+  store_y(0);
+  for (int r0 = 0, buf = 0; r0 < nrows; r0 += kOc, buf ^= 1) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const bool more = r0 + kOc < nrows;
+    if (more) {
+      issue_p(r0 + kOc, buf ^ 1);
+      load_y(r0 + kOc);
+    }
+#pragma unroll
+    for (int ks = 0; ks < kOc; ks += 16) {
+      // A (16 columns a x 16 rows r) = P^T: matrix i of the x4 load is rows ks + 8 (i >> 1) .. + 7,
+      // columns warp * 16 + 8 (i & 1) .. + 7 of the staged chunk
+      const int mi = lane >> 3;
+      const uint32_t addr = (uint32_t)__cvta_generic_to_shared(
+          &ps[buf][ks + 8 * (mi >> 1) + (lane & 7)][warp * 16 + 8 * (mi & 1)]);
+      uint32_t f0, f1, f2, f3;
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                   : "=r"(f0), "=r"(f1), "=r"(f2), "=r"(f3)
+                   : "r"(addr));
+#pragma unroll
+      for (int p = 2; p >= 0; --p)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&yt[buf][p][n * 8 + g][ks + 2 * q]);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&yt[buf][p][n * 8 + g][ks + 2 * q + 8]);
+          mma_bf16(acc[n], f0, f1, f2, f3, b0, b1);
+        }
+    }
+    if (more) store_y(buf ^ 1);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int a = a0 + warp * 16 + g + 8 * h;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int j = n * 8 + 2 * q + c;
+        if (j < rk && a < A) G[(int64_t)e * gE + (int64_t)a * ga + (int64_t)j * gj] = acc[n][2 * h + c] * scale;
+      }
+  }
+}
+
 }  // namespace
 }  // namespace e4b
 
@@ -420,6 +520,16 @@ extern "C" e4b_status e4b_lora_outer(const void* P, int p_dtype, int ldp, int A,
   if (nsegs == 0) return E4B_OK;
   if (!P || !Y || !segs || !G) return E4B_ERR_INVALID_ARG;
   cudaStream_t s = (cudaStream_t)stream;
+  // bf16 P with 64-column blocks and 16-byte rows: the tensor-core kernel (E4B_OUTER_MMA=0: CUDA cores)
+  static const bool use_mma = [] {
+    const char* v = getenv("E4B_OUTER_MMA");
+    return !(v && v[0] == '0');
+  }();
+  if (p_dtype == E4B_BF16 && use_mma && A % kOa == 0 && ldp % 8 == 0 && aligned16(P)) {
+    outer_mma_kernel<<<dim3(nsegs, A / kOa), 128, 0, s>>>((const __nv_bfloat16*)P, ldp, A, Y, rk, segs, scale, G, gE,
+                                                          ga, gj);
+    return launch_status();
+  }
   const dim3 grid(nsegs, (A + 255) / 256);
   switch (p_dtype) {
     case E4B_BF16:
