@@ -263,10 +263,34 @@ __global__ void __launch_bounds__(256) rank_up_kernel(const float* __restrict__ 
   const int n0 = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (n0 >= N) return;
   float m[4][kRk];
+  const float* Mb = M + (int64_t)e * sE + (int64_t)n0 * sn;
+  if (sn == 1 && (sj & 3) == 0 && ((uintptr_t)Mb & 15) == 0) {  // the 4 columns of a rank slot: one vector
 #pragma unroll
-  for (int c = 0; c < 4; ++c)
+    for (int j = 0; j < kRk; ++j) {
+      const float4 v = j < rk ? *reinterpret_cast<const float4*>(Mb + j * sj) : make_float4(0.f, 0.f, 0.f, 0.f);
+      m[0][j] = v.x;
+      m[1][j] = v.y;
+      m[2][j] = v.z;
+      m[3][j] = v.w;
+    }
+  } else if (sj == 1 && (rk & 3) == 0 && (sn & 3) == 0 && ((uintptr_t)Mb & 15) == 0) {  // a column's rank slots
 #pragma unroll
-    for (int j = 0; j < kRk; ++j) m[c][j] = j < rk ? M[(int64_t)e * sE + j * sj + (int64_t)(n0 + c) * sn] : 0.f;
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int j4 = 0; j4 < kRk; j4 += 4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j4 < rk) v = *reinterpret_cast<const float4*>(Mb + (int64_t)c * sn + j4);  // rk % 4 == 0 here
+        m[c][j4] = v.x;
+        m[c][j4 + 1] = v.y;
+        m[c][j4 + 2] = v.z;
+        m[c][j4 + 3] = v.w;
+      }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int j = 0; j < kRk; ++j) m[c][j] = j < rk ? Mb[j * sj + (int64_t)c * sn] : 0.f;
+  }
   // rows in batches of 8: the batch's read-modify-writes are in flight together
   using V = typename std::conditional<sizeof(TO) == 4, float4, uint2>::type;
   for (int r0 = 0; r0 < nrows; r0 += 8) {
