@@ -157,3 +157,34 @@ def test_fused_train_autograd_matches_loop_on_cpu(e4b, monkeypatch, has_gate):
         assert _rel(got[3][n], ref[3][n]) < 1e-2, n
         # the adapter rows of the expert nobody routed to get exactly zero gradient
         assert got[3][n][5].abs().sum() == 0, n
+
+
+def _split3(v: torch.Tensor):
+    """The adapter kernels' fp32 -> three bf16 parts: hi = bf16(v), mid = bf16(v - hi),
+    lo = bf16(v - hi - mid) (csrc/lora_train.cu, the tensor-core rank-down and outer product)."""
+    hi = v.to(torch.bfloat16)
+    r1 = v - hi.float()
+    mid = r1.to(torch.bfloat16)
+    lo = (r1 - mid.float()).to(torch.bfloat16)
+    return hi, mid, lo
+
+
+def test_three_part_bf16_split_keeps_fp32_accuracy():
+    """The split reconstructs fp32 values to within 2^-24 relative, and a product of bf16 rows with
+    the split adapter (each part exact against bf16, summed smallest first) is as close to the
+    float64 product as an fp32 matmul is."""
+    g = torch.Generator().manual_seed(0)
+    v = torch.randn(200000, generator=g) * torch.logspace(-8, 4, 200000)
+    hi, mid, lo = _split3(v)
+    rec = hi.double() + mid.double() + lo.double()
+    assert ((rec - v.double()).abs() / v.double().abs()).max().item() <= 2.0 ** -24
+    x = (torch.randn(256, 2048, generator=g)).to(torch.bfloat16)
+    m = torch.randn(2048, 16, generator=g) * 0.01
+    exact = x.double() @ m.double()
+    parts = [p.double() for p in _split3(m)]
+    split = x.double() @ parts[2] + x.double() @ parts[1] + x.double() @ parts[0]
+    fp32 = (x.float() @ m).double()
+    scale = exact.abs().max()
+    err_split = ((split - exact).abs().max() / scale).item()
+    err_fp32 = ((fp32 - exact).abs().max() / scale).item()
+    assert err_split <= max(4 * err_fp32, 1e-7), (err_split, err_fp32)
